@@ -1,0 +1,379 @@
+"""Decode benchmark of the W8A8 hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch T] [--impl ours|reference]
+    (N > 1: torchrun --nproc-per-node N ... bench.py --gpus N ...)
+
+One step = one decode step of the Qwen2.5-1.5B-shaped W8A8 workload: 28 layers x
+{qkv 1536x2048, o 1536x1536, gate_up 1536x17920, down 8960x1536} (the seven linears, q|k|v and
+gate|up fused as shared-input subgraphs) + the 1536x151936 LM head with a fused top-40 /
+argmax, vocab-sharded over the N GPUs.  Each GPU decodes its own T tokens (replica of the
+linear stack); the LM head shards its vocab across all N GPUs for all N*T tokens.
+
+Prints one JSON line (rank 0).  `--impl reference` times the reference's CPU path (the C
+restatement of the NPU integer steps around the reference's pack/unpack arithmetic, OpenMP over
+all host cores) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "decode tok/s & HBM GB/s of W8A8 linear + sharded LM-head argmax, 1/2/4/8 B200"
+WORKLOAD = "qwen2.5-1.5b-shaped W8A8 decode: 28 x {qkv,o,gate_up,down} + LM head 1536x151936 top-40"
+# DRAM bytes (read + write) per launch of the gate_up GEMV at T=1 from one ncu capture
+# (profiles/gemv_w8a8_qwen15b_gate_up.md); None until captured.
+GEMV_TRAFFIC_BYTES = None
+
+
+def env_int(name: str, default: int) -> int:
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        self.file.flush()
+        rows = [ln.split(",") for ln in Path(self.file.name).read_text().splitlines() if ln.strip()]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------- CPU paths
+def cpu_model(T: int, layers: int, seed: int = 0):
+    """Host-side synthetic model for the CPU arms (generated on the CPU, same shapes)."""
+    from romanaccio_b200 import synth
+    from romanaccio_b200.quantize import build_linear
+    shape = synth.QWEN25_15B
+    params = []
+    for layer in range(layers):
+        for j, (name, K, N, trunc) in enumerate(shape.subgraphs()):
+            s = seed * 7919 + layer * 16 + j
+            g = torch.Generator().manual_seed(s)
+            w = torch.randn((N, K), generator=g) * 0.02
+            params.append((name, build_linear(w, synth.activations(64, K, s + 1), trunc=trunc)))
+    K, V = shape.hidden, shape.vocab
+    g = torch.Generator().manual_seed(seed + 17)
+    w = torch.randn((V, K), generator=g) * 0.02
+    step = w.double().abs().amax(dim=1, keepdim=True).clamp(min=1e-12) / 127.0
+    wq = torch.clamp(torch.round(w.double() / step), -127, 127).to(torch.int8).numpy()
+    in_step = float(synth.activations(64, K, seed + 23).abs().max()) / 127.0
+    return params, (wq, (in_step * step[:, 0].numpy()).astype(np.float32), in_step)
+
+
+def cpu_step_fn(params, lm, T: int, shape):
+    """Returns a closure running one decode step through the OpenMP oracle baseline."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    lib = O.lib()
+    import ctypes as C
+
+    def p(a):
+        return a.ctypes.data
+
+    x0 = np.random.default_rng(0).standard_normal((T, shape.hidden)).astype(np.float32)
+    bufs = {name: np.empty((T, N), np.float32) for (name, K, N, _) in shape.subgraphs()}
+    qbuf = np.empty((T, max(k for (_, k, _, _) in shape.subgraphs())), np.int8)
+    ratio = np.empty((T,), np.float32)
+    wq_lm, acc_step_lm, in_step_lm = lm
+    V = wq_lm.shape[0]
+    logits = np.empty((T, V), np.float32)
+    val = np.empty((T, 40), np.float32)
+    idx = np.empty((T, 40), np.int32)
+    qlm = np.empty((T, shape.hidden), np.int8)
+    prepared = []
+    for name, prm in params:
+        prepared.append((name, prm.wq.shape[1], prm.wq.shape[0], np.ascontiguousarray(prm.wq),
+                         np.ascontiguousarray(prm.in_inv_smooth, np.float32), prm.in_thresh,
+                         np.ascontiguousarray(prm.quant_m), prm.trunc,
+                         np.ascontiguousarray(prm.out_step_chan, np.float32)))
+
+    def run():
+        x = x0
+        for (name, K, N, wq, inv, thr, qm, tr, osc) in prepared:
+            if name == "o":
+                x = np.ascontiguousarray(bufs["qkv"][:, :shape.q])
+            elif name == "down":
+                x = np.ascontiguousarray(bufs["gate_up"][:, :shape.ffn])
+            elif name == "gate_up":
+                x = bufs["o"]
+            y = bufs[name]
+            lib.orc_linear_dyntok_omp(p(x), T, K, N, p(wq), p(inv), C.c_float(thr), p(qm), tr,
+                                      p(osc), p(y), p(qbuf), p(ratio))
+            x = bufs["down"] if name == "down" else x
+        lib.orc_lmhead_topk_omp(p(bufs["down"]), T, shape.hidden, V, p(wq_lm),
+                                C.c_float(in_step_lm), p(acc_step_lm), 40, p(logits), p(qlm),
+                                p(val), p(idx))
+        return idx[:, 0].copy()
+
+    return run, int(lib.orc_num_threads())
+
+
+def run_reference(args) -> None:
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return
+    from romanaccio_b200 import synth
+    T = args.batch
+    params, lm = cpu_model(T, synth.QWEN25_15B.layers)
+    run, cores = cpu_step_fn(params, lm, T, synth.QWEN25_15B)
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = T / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch_per_gpu": T, "layers": synth.QWEN25_15B.layers,
+                   "vocab": synth.QWEN25_15B.vocab, "parallelism": "host cores (OpenMP)"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} full decode steps (all 28 layers + LM head), "
+                                   "C restatement of the reference path, OpenMP"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- GPU path
+def run_ours(args) -> None:
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    sys.path.insert(0, str(ROOT))
+    from romanaccio_b200 import Context, synth
+    from romanaccio_b200.decode import DecodeStack
+
+    T = args.batch
+    shape = synth.QWEN25_15B
+    ctx = Context(local)
+    stack = DecodeStack(ctx, shape, T, rank=rank, world=world, group=group, seed=0,
+                        layers=args.layers)
+    x_host = torch.from_numpy(
+        np.random.default_rng(rank).standard_normal((T, shape.hidden)).astype(np.float32)).pin_memory()
+    ids_host = torch.empty((T,), dtype=torch.int32).pin_memory()
+    stack.x.copy_(x_host)
+    stack.step()  # eager warm-up (configures every kernel instantiation)
+    torch.cuda.synchronize()
+    stack.capture()
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        stack.step()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            stack.step()
+        ev1.record(stream)
+        barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    # end to end: pinned host input -> step -> sampled ids read back on the host, every step
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        stack.step_host(x_host, ids_host)
+        stream.synchronize()
+    e1.record(stream)
+    barrier()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    times = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, ms_e2e = times.tolist()
+
+    # dominant kernel: the gate_up GEMV (59 % of the linear weight bytes), int8 input in HBM,
+    # one launch per layer over the 28 distinct weight matrices (770 MB > L2), in a graph.
+    sb = stack.step_bytes()
+    gu = [row[2] for row in stack.linears]
+    q_in = torch.zeros((T, shape.hidden), dtype=torch.int8, device=dev)
+    y_out = torch.empty((T, 2 * shape.ffn), dtype=torch.float32, device=dev)
+    from romanaccio_b200 import OUT_F32
+    ratio = torch.ones((T,), dtype=torch.float32, device=dev)
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        for lin in gu:
+            lin.submit(q_in, OUT_F32, dyntok_ratios=ratio, out=y_out)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for lin in gu:
+            lin.submit(q_in, OUT_F32, dyntok_ratios=ratio, out=y_out)
+    for _ in range(3):
+        g.replay()
+    reps = 10
+    torch.cuda.synchronize()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    r1.record(stream)
+    torch.cuda.synchronize()
+    gemv_s = r0.elapsed_time(r1) / 1e3 / (reps * len(gu))
+    del g
+    peak, peak_kind = measured_peaks()
+    achieved = sb.gemv_launch / gemv_s / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        run_cpu, cores = cpu_step_fn(stack.params_host, (stack.lm_host[0], stack.lm_host[1],
+                                                         stack.lm_in_step), T, shape)
+        run_cpu()
+        n, t0 = 0, time.perf_counter()
+        while True:
+            run_cpu()
+            n += 1
+            if time.perf_counter() - t0 > args.cpu_seconds:
+                break
+        dt = (time.perf_counter() - t0) / n
+        cpu = {"value": T / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": f"{n} full decode steps of the same workload (28 layers + LM head), "
+                         "C restatement of the reference path, OpenMP"}
+
+    step_bytes = sb.linear + sb.lm_head
+    value = world * T / (ms / 1e3)
+    per_linear = 2  # act_quant + GEMV
+    groups = (T + 7) // 8
+    launches_per_step = stack.layers * 4 * (1 + groups) + (1 + groups) + (1 if world > 1 else 0)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": T, "layers": stack.layers,
+                       "vocab": shape.vocab, "lm_head_shards": world,
+                       "parallelism": f"linears replicated per GPU, LM head vocab-sharded x{world}",
+                       "l2": f"weights streamed every step: {step_bytes / 1e9:.2f} GB per GPU > 126 MB L2",
+                       "cuda_graph": True},
+            "hbm_gbs_step": step_bytes / (ms / 1e3) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": GEMV_TRAFFIC_BYTES,
+                         "kernel": "gemv_w8a8 gate_up 1536x17920 T=%d" % T,
+                         "peak_kind": peak_kind, "launch_us": gemv_s * 1e6,
+                         "algorithmic_bytes": sb.gemv_launch},
+            "e2e": {"value": world * T / (ms_e2e / 1e3), "unit": "tok/s",
+                    "h2d_bytes_per_step": T * shape.hidden * 4, "d2h_bytes_per_step": T * 4},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    stack.release()
+    del per_linear
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,212 @@
+/*
+ * w8a8.h - C ABI of the B200 (sm_100a) SmoothQuant W8A8 linear and vocab-sharded LM head.
+ *
+ * This library replaces the NPU side of romanaccio's quantised-linear boundary:
+ *
+ *   pack_npu_input(...)          src/LFM3/lfm3_v2.cpp:1186-1204   (fp32 -> int8, static or dyntok)
+ *   WorkerPool::submit_task(...) src/eswin_runtime/src/backend/worker_pool.hpp:232-254
+ *                                (NPU CMAC int8 GEMM -> CACC int32 -> SDP CvtPrecision_QuantM)
+ *   unpack_npu_output(...)       src/LFM3/lfm3_v2.cpp:1207-1225   (int8/int16 -> fp32)
+ *
+ * and the host-side LM-head merge that follows the dual-die vocab split:
+ *
+ *   compute_logits_from_ptr(...)                src/LFM3/lfm3_v2.cpp:2320-2416
+ *   TransformerSession::forward_lm_head_dual_die src/eswin_runtime/src/llm/transformer_session.cpp:538-614
+ *   Sampler::sample greedy / top-k              src/eswin_runtime/src/nlp/sampler.cpp:93-121
+ *
+ * Conventions follow es_runtime.h (src/eswin_runtime/include/es_runtime.h:24-35): every call
+ * returns a status code, no C++ exception crosses this boundary, destroy functions accept NULL,
+ * and the caller owns every buffer it passes in.  Device pointers are plain CUDA device
+ * addresses on the device the context was created for; `stream` is a cudaStream_t passed as
+ * void* (NULL = legacy default stream).  Every forward call is asynchronous on `stream`.
+ *
+ * Thread safety: a w8a8_linear may be used by several host threads only on one stream at a
+ * time (its scratch buffer is per object).  Different objects are independent.
+ */
+#ifndef W8A8_H
+#define W8A8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------------------------------
+ * Status codes: values 0..-9 mirror es_status_t (es_runtime.h:24-35).
+ * ------------------------------------------------------------------------------------- */
+typedef enum {
+    W8A8_SUCCESS               =  0,
+    W8A8_ERR_INVALID_ARG       = -1,
+    W8A8_ERR_NO_MEMORY         = -2,
+    W8A8_ERR_DEVICE_BUSY       = -3,
+    W8A8_ERR_HARDWARE_FAULT    = -4,
+    W8A8_ERR_NOT_INITIALIZED   = -5,
+    W8A8_ERR_NOT_SUPPORTED     = -6,
+    W8A8_ERR_IO                = -7,
+    W8A8_ERR_CHECKSUM_MISMATCH = -8,
+    W8A8_ERR_TIMEOUT           = -9,
+    W8A8_ERR_CUDA              = -10, /* a CUDA runtime call failed; see w8a8_last_error() */
+    W8A8_ERR_PEER_TIMEOUT      = -11  /* a bounded wait on another GPU's flag ran out */
+} w8a8_status;
+
+/* Mirrors es_status_to_string (es_runtime.h:37). */
+const char *w8a8_status_to_string(w8a8_status status);
+/* Detail text of the last failure on the calling host thread ("" if none). */
+const char *w8a8_last_error(void);
+/* Library version string. */
+const char *w8a8_version(void);
+
+/* ---------------------------------------------------------------------------------------
+ * Enumerations
+ * ------------------------------------------------------------------------------------- */
+/* Mirrors BoundaryDtype (lfm3_v2.cpp:550-554).  Only INT8 and INT16 are requant targets. */
+typedef enum {
+    W8A8_DTYPE_FP16  = 0,
+    W8A8_DTYPE_INT8  = 1,
+    W8A8_DTYPE_INT16 = 2
+} w8a8_boundary_dtype;
+
+/* Activation quantisation: pack_npu_input_int8 (static, lfm3_v2.cpp:892-940) or
+ * pack_npu_input_int8_dyntok (per-token amax, lfm3_v2.cpp:1050-1141). */
+typedef enum {
+    W8A8_ACT_STATIC = 0,
+    W8A8_ACT_DYNTOK = 1
+} w8a8_act_mode;
+
+/* What a forward call writes into y:
+ *   ACC_I32  int32 accumulators acc[t,n] = sum_k q[t,k] * Wq[n,k]  (CMAC/CACC, cmac.py:300-383)
+ *   QUANT    int8 (or int16) y_q = clip(RNE(acc * QuantM[n] / 2^trunc), +-Qmax)
+ *            (SDP CvtPrecision_QuantM; attribute_int8_error.py:104-122, FINDINGS.md:2447)
+ *   F32      QUANT followed by the reference unpack: y = float(y_q) * step
+ *            (unpack_npu_output_int8[_dyntok], lfm3_v2.cpp:971-1008, 1143-1183)
+ *   F32_ACC  float(acc) * (ratio[t] * acc_step[n]) without the requant stage (logit mode of the
+ *            LM head: logit = acc * in_step * w_step[n]) */
+typedef enum {
+    W8A8_OUT_ACC_I32 = 0,
+    W8A8_OUT_QUANT   = 1,
+    W8A8_OUT_F32     = 2,
+    W8A8_OUT_F32_ACC = 3
+} w8a8_out_mode;
+
+/* ---------------------------------------------------------------------------------------
+ * Context: one per device.
+ * ------------------------------------------------------------------------------------- */
+typedef struct w8a8_ctx w8a8_ctx;
+
+/* Creates a context on CUDA device `device` (makes it current on the calling thread). */
+w8a8_status w8a8_ctx_create(int device, w8a8_ctx **out_ctx);
+void        w8a8_ctx_destroy(w8a8_ctx *ctx);
+/* Number of SMs of the context's device. */
+int         w8a8_ctx_sm_count(const w8a8_ctx *ctx);
+/* Synchronises the context's device and reports a device-side failure recorded by a kernel
+ * (a bounded wait that ran out: W8A8_ERR_TIMEOUT / W8A8_ERR_PEER_TIMEOUT), then clears it.
+ * Plays the role of the worker liveness checks of worker_pool.cpp:180-193. */
+w8a8_status w8a8_ctx_check(w8a8_ctx *ctx);
+
+/* ---------------------------------------------------------------------------------------
+ * Per-linear scale parameters: mirrors SubgraphScaleInfo (lfm3_v2.cpp:556-565) and the
+ * quant_scales.json entry (build_lfm3_int8_pkg.py:452-463).  Host pointers; copied at create.
+ * ------------------------------------------------------------------------------------- */
+typedef struct {
+    int32_t      out_dtype;      /* w8a8_boundary_dtype: INT8 (Qmax 127) or INT16 (Qmax 32767) */
+    float        in_thresh;      /* dyntok: ratio[t] = amax_t / max(in_thresh, 1e-8) */
+    float        in_step;        /* static: q = RNE(clamp(x * (inv_smooth * (1/in_step)), +-127)) */
+    float        out_thresh;     /* informational (output_threshold) */
+    float        out_step;       /* scalar output step used when out_step_chan == NULL */
+    const float *in_inv_smooth;  /* [K] or NULL: SmoothQuant 1/s_in[c] */
+    const float *out_step_chan;  /* [N] or NULL: per-channel step in_s*w_step*2^trunc/QuantM */
+} w8a8_scale_info;
+
+/* A W8A8 linear: int8 weights [N, K] (row n = output channel, K contiguous), per-channel
+ * QuantM, trunc and the scale info.  Mirrors one INT8 Class-B subgraph of the LFM3 package
+ * (build_single_conv_region, build_lfm3_int8_pkg.py:171-224) with the NVDLA weight tiling
+ * replaced by a row-major device layout. */
+typedef struct {
+    int32_t         K;           /* in-features  (>= 1) */
+    int32_t         N;           /* out-features (>= 1) */
+    const int8_t   *weights;     /* host [N, weights_ld] int8, values in [-127, 127] */
+    int64_t         weights_ld;  /* elements between consecutive rows (>= K) */
+    const int16_t  *quant_m;     /* host [N] QuantM in [1, 32767], or NULL (QUANT/F32 then unsupported) */
+    int32_t         trunc;       /* SDP right shift, 0..62 */
+    const float    *acc_step;    /* host [N] or NULL: step for W8A8_OUT_F32_ACC */
+    w8a8_scale_info scale;
+} w8a8_linear_desc;
+
+typedef struct w8a8_linear w8a8_linear;
+
+/* Uploads the weights and parameters to the context's device.  Replaces the package load of
+ * one subgraph (load_quant_scales / parse_entry, lfm3_v2.cpp:3743, 3807-3826). */
+w8a8_status w8a8_linear_create(w8a8_ctx *ctx, const w8a8_linear_desc *desc, w8a8_linear **out_linear);
+void        w8a8_linear_destroy(w8a8_linear *linear);
+/* Device bytes held by the linear (weights + parameters + scratch). */
+size_t      w8a8_linear_device_bytes(const w8a8_linear *linear);
+
+/* Boundary stage 1 -- replaces pack_npu_input (lfm3_v2.cpp:1186-1204) for INT8 inputs.
+ * x_dev: fp32 [T, K] with row stride ldx (elements).  q_dev: int8 [T, K] with row stride ldq.
+ * ratio_dev: fp32 [T]; written in DYNTOK mode (amax_t / max(in_thresh,1e-8)), ignored (may be
+ * NULL) in STATIC mode.  Layout is [T, K] row-major for every T (the NVDLA [C/32, T, 32]
+ * surface of the reference is not reproduced). */
+w8a8_status w8a8_pack_input(w8a8_linear *linear, const float *x_dev, int64_t ldx, int32_t T,
+                            int32_t act_mode, int8_t *q_dev, int64_t ldq, float *ratio_dev,
+                            void *stream);
+
+/* Boundary stage 2 -- replaces submit_task of the INT8 loadable (CMAC + CACC + SDP).
+ * q_dev: int8 [T, K] (stride ldq).  Writes y_dev [T, N] (stride ldy elements) as int32 (ACC_I32),
+ * int8/int16 per scale.out_dtype (QUANT), or fp32 (F32 / F32_ACC, which need ratio_dev in
+ * DYNTOK mode). */
+w8a8_status w8a8_linear_forward_q(w8a8_linear *linear, const int8_t *q_dev, int64_t ldq, int32_t T,
+                                  int32_t act_mode, const float *ratio_dev, int32_t out_mode,
+                                  void *y_dev, int64_t ldy, void *stream);
+
+/* Boundary stage 3 -- replaces unpack_npu_output (lfm3_v2.cpp:1207-1225) for INT8/INT16
+ * outputs.  yq_dev: [T, N] int8 or int16 per scale.out_dtype (stride ldyq); y_dev fp32 [T, N]
+ * (stride ldy).  ratio_dev is read in DYNTOK mode. */
+w8a8_status w8a8_unpack_output(w8a8_linear *linear, const void *yq_dev, int64_t ldyq, int32_t T,
+                               int32_t act_mode, const float *ratio_dev, float *y_dev, int64_t ldy,
+                               void *stream);
+
+/* The three stages fused: pack -> int8 contraction -> requant -> unpack, one call.
+ * x_dev fp32 [T, K] (stride ldx); y_dev per out_mode (stride ldy); ratio_dev [T] optional
+ * output of the per-token ratios (DYNTOK), may be NULL. */
+w8a8_status w8a8_linear_forward(w8a8_linear *linear, const float *x_dev, int64_t ldx, int32_t T,
+                                int32_t act_mode, int32_t out_mode, void *y_dev, int64_t ldy,
+                                float *ratio_dev, void *stream);
+
+/* ---------------------------------------------------------------------------------------
+ * LM head shard: a linear over a contiguous block of vocab rows [row_offset, row_offset + N)
+ * (the contiguous vocab split of dual_die_splitter.py:63-147 and
+ * transformer_session.cpp:575-596) whose logits never leave the SM: the kernel keeps, per
+ * token, the k largest (logit, vocab id) pairs in the total order (logit desc, id asc).
+ * Greedy argmax (sampler.cpp:93-103, strict '>' keeps the lowest id) is element 0.
+ * ------------------------------------------------------------------------------------- */
+#define W8A8_TOPK_MAX 64
+
+/* x_dev fp32 [T, K] (stride ldx).  out_mode F32 (requant + unpack, the LFM3 INT8 LM head) or
+ * F32_ACC (logit = float(acc) * ratio * acc_step[n]).  k in [1, min(W8A8_TOPK_MAX, N)].
+ * Writes topk_val_dev fp32 [T, k] and topk_idx_dev int32 [T, k] (vocab ids = row_offset + n),
+ * sorted.  logits_dev: optional fp32 [T, N] (stride ldl) copy of the shard's logits, may be
+ * NULL.  Scratch: per-CTA candidate lists held inside the linear. */
+w8a8_status w8a8_linear_forward_topk(w8a8_linear *linear, const float *x_dev, int64_t ldx,
+                                     int32_t T, int32_t act_mode, int32_t out_mode, int32_t k,
+                                     int32_t row_offset, float *topk_val_dev,
+                                     int32_t *topk_idx_dev, float *logits_dev, int64_t ldl,
+                                     void *stream);
+
+/* Merges n_lists candidate lists per token into the global top-k_out (the cross-shard merge
+ * that replaces the logit concatenation + Sampler pass over the full vocab, i.e.
+ * transformer_session.cpp:575-596 followed by sampler.cpp:93-121).  Candidate (t, l, j) is read
+ * at in_val_dev[t * token_stride + l * list_stride + j] (same for in_idx_dev); lists need not
+ * be sorted.  out: [T, k_out] sorted (value desc, id asc); argmax_dev: optional int32 [T]
+ * (= out_idx[t, 0]).  k_out <= n_lists * k_in, k_out <= W8A8_TOPK_MAX, n_lists <= 64. */
+w8a8_status w8a8_topk_merge(w8a8_ctx *ctx, const float *in_val_dev, const int32_t *in_idx_dev,
+                            int32_t T, int32_t n_lists, int32_t k_in, int64_t list_stride,
+                            int64_t token_stride, int32_t k_out, float *out_val_dev,
+                            int32_t *out_idx_dev, int32_t *argmax_dev, void *stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* W8A8_H */

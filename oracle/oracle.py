@@ -1,0 +1,235 @@
+"""TEST INFRASTRUCTURE ONLY: numpy front end of the CPU oracle (liboracle.so) and of the
+reference's own C++ compiled from its sources (_ref/libref.so).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs use this module, and
+only as the checker / the timed CPU baseline.  The product (romanaccio_b200) never imports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_LIB = HERE / "liboracle.so"
+REF_LIB = HERE / "_ref" / "libref.so"
+
+_P, _I32, _I64, _F = C.c_void_p, C.c_int32, C.c_int64, C.c_float
+_ORACLE_SIGS = {
+    "orc_round_clamp": (C.c_int32, [_F, _F]),
+    "orc_pack_static": (None, [_P, _I64, _I32, _I32, _F, _P, _P, _I64]),
+    "orc_pack_dyntok": (None, [_P, _I64, _I32, _I32, _F, _P, _P, _I64, _P]),
+    "orc_gemm_i32": (None, [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _I64]),
+    "orc_requant_one": (C.c_int32, [_I32, _I32, _I32, _I32]),
+    "orc_requant_f64_one": (C.c_int32, [_I32, _I32, _I32, _I32]),
+    "orc_requant": (None, [_P, _I64, _I32, _I32, _P, _I32, _I32, _P, _I64]),
+    "orc_requant_f64": (None, [_P, _I64, _I32, _I32, _P, _I32, _I32, _P, _I64]),
+    "orc_unpack": (None, [_P, _I64, _I32, _I32, _I32, _P, _P, _F, _P, _I64]),
+    "orc_dequant_acc": (None, [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _I64]),
+    "orc_topk": (None, [_P, _I64, _I32, _I32, _I32, _I32, _P, _P]),
+    "orc_argmax": (C.c_int32, [_P, _I32]),
+    "orc_num_threads": (C.c_int, []),
+    "orc_linear_dyntok_omp": (None, [_P, _I32, _I32, _I32, _P, _P, _F, _P, _I32, _P, _P, _P, _P]),
+    "orc_lmhead_topk_omp": (None, [_P, _I32, _I32, _I32, _P, _F, _P, _I32, _P, _P, _P, _P]),
+}
+_REF_SIGS = {
+    "ref_round_clamp_f32": (C.c_int32, [_F, _F]),
+    "ref_pack_int8": (C.c_int, [_P, C.c_int, C.c_int, _F, _P, _P]),
+    "ref_pack_int8_dyntok": (C.c_int, [_P, C.c_int, C.c_int, _F, _P, _P, _P]),
+    "ref_unpack_int8": (C.c_int, [_P, C.c_int, C.c_int, _F, _P, _P, _P]),
+    "ref_unpack_int16": (C.c_int, [_P, C.c_int, C.c_int, _F, _P, _P]),
+    "ref_sampler_greedy": (C.c_int32, [_P, C.c_size_t]),
+}
+
+_orc = None
+_ref = None
+
+
+def build() -> None:
+    """Builds liboracle.so (and _ref/libref.so when the reference tree is present)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+
+
+def _bind(path: Path, sigs: dict) -> C.CDLL:
+    lib = C.CDLL(str(path))
+    for name, (res, args) in sigs.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+def lib() -> C.CDLL:
+    global _orc
+    if _orc is None:
+        if not ORACLE_LIB.exists():
+            build()
+        _orc = _bind(ORACLE_LIB, _ORACLE_SIGS)
+    return _orc
+
+
+def ref_available() -> bool:
+    return REF_LIB.exists()
+
+
+def ref() -> C.CDLL:
+    global _ref
+    if _ref is None:
+        if not REF_LIB.exists():
+            raise FileNotFoundError(f"{REF_LIB} was not built (needs the reference tree)")
+        _ref = _bind(REF_LIB, _REF_SIGS)
+    return _ref
+
+
+def _p(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data
+
+
+def _c(a, dtype):
+    return None if a is None else np.ascontiguousarray(a, dtype=dtype)
+
+
+# ------------------------------------------------------------------ restatement (liboracle)
+def round_clamp(x: float, lim: float = 127.0) -> int:
+    return int(lib().orc_round_clamp(x, lim))
+
+
+def pack_static(x: np.ndarray, in_step: float, inv_smooth: np.ndarray | None = None) -> np.ndarray:
+    x = _c(x, np.float32)
+    T, K = x.shape
+    s = _c(inv_smooth, np.float32)
+    q = np.empty((T, K), np.int8)
+    lib().orc_pack_static(_p(x), K, T, K, in_step, _p(s), _p(q), K)
+    return q
+
+
+def pack_dyntok(x: np.ndarray, in_thresh: float, inv_smooth: np.ndarray | None = None):
+    x = _c(x, np.float32)
+    T, K = x.shape
+    s = _c(inv_smooth, np.float32)
+    q = np.empty((T, K), np.int8)
+    r = np.empty((T,), np.float32)
+    lib().orc_pack_dyntok(_p(x), K, T, K, in_thresh, _p(s), _p(q), K, _p(r))
+    return q, r
+
+
+def gemm_i32(q: np.ndarray, w: np.ndarray) -> np.ndarray:
+    q = _c(q, np.int8)
+    w = _c(w, np.int8)
+    T, K = q.shape
+    N = w.shape[0]
+    acc = np.empty((T, N), np.int32)
+    lib().orc_gemm_i32(_p(q), K, _p(w), K, T, N, K, _p(acc), N)
+    return acc
+
+
+def requant(acc: np.ndarray, quant_m: np.ndarray, trunc: int, qmax: int = 127,
+            f64: bool = False) -> np.ndarray:
+    acc = _c(acc, np.int32)
+    qm = _c(quant_m, np.int16)
+    T, N = acc.shape
+    yq = np.empty((T, N), np.int32)
+    fn = lib().orc_requant_f64 if f64 else lib().orc_requant
+    fn(_p(acc), N, T, N, _p(qm), trunc, qmax, _p(yq), N)
+    return yq
+
+
+def unpack(yq: np.ndarray, out_step: float, out_step_chan: np.ndarray | None = None,
+           ratio: np.ndarray | None = None) -> np.ndarray:
+    yq = _c(yq, np.int32)
+    T, N = yq.shape
+    osc = _c(out_step_chan, np.float32)
+    r = _c(ratio, np.float32)
+    y = np.empty((T, N), np.float32)
+    lib().orc_unpack(_p(yq), N, T, N, 1 if r is not None else 0, _p(r), _p(osc), out_step, _p(y), N)
+    return y
+
+
+def dequant_acc(acc: np.ndarray, acc_step: np.ndarray, ratio: np.ndarray | None = None) -> np.ndarray:
+    acc = _c(acc, np.int32)
+    T, N = acc.shape
+    st = _c(acc_step, np.float32)
+    r = _c(ratio, np.float32)
+    y = np.empty((T, N), np.float32)
+    lib().orc_dequant_acc(_p(acc), N, T, N, 1 if r is not None else 0, _p(r), _p(st), _p(y), N)
+    return y
+
+
+def topk(logits: np.ndarray, k: int, id_offset: int = 0):
+    lg = _c(logits, np.float32)
+    T, V = lg.shape
+    val = np.empty((T, k), np.float32)
+    idx = np.empty((T, k), np.int32)
+    lib().orc_topk(_p(lg), V, T, V, k, id_offset, _p(val), _p(idx))
+    return val, idx
+
+
+def argmax(logits_row: np.ndarray) -> int:
+    lg = _c(logits_row, np.float32)
+    return int(lib().orc_argmax(_p(lg), lg.shape[0]))
+
+
+def linear(x: np.ndarray, wq: np.ndarray, quant_m: np.ndarray, trunc: int, out_step_chan: np.ndarray,
+           inv_smooth: np.ndarray | None, in_thresh: float | None = None, in_step: float | None = None,
+           out_step: float = 0.0, qmax: int = 127):
+    """Full boundary: pack (dyntok when in_thresh is given, else static) -> GEMM -> requant ->
+    unpack.  Returns (q, ratio or None, acc, yq, y)."""
+    if in_thresh is not None:
+        q, r = pack_dyntok(x, in_thresh, inv_smooth)
+    else:
+        q, r = pack_static(x, in_step, inv_smooth), None
+    acc = gemm_i32(q, wq)
+    yq = requant(acc, quant_m, trunc, qmax)
+    y = unpack(yq, out_step, out_step_chan, r)
+    return q, r, acc, yq, y
+
+
+# ------------------------------------------------------------------ reference C++ (_ref)
+def ref_round_clamp(x: float, lim: float = 127.0) -> int:
+    return int(ref().ref_round_clamp_f32(x, lim))
+
+
+def ref_pack(x: np.ndarray, in_step: float, inv_smooth: np.ndarray | None = None) -> np.ndarray:
+    x = _c(x, np.float32)
+    T, K = x.shape
+    s = _c(inv_smooth, np.float32)
+    q = np.empty((T, K), np.int8)
+    assert ref().ref_pack_int8(_p(x), T, K, in_step, _p(s), _p(q)) == 0
+    return q
+
+
+def ref_pack_dyntok(x: np.ndarray, in_thresh: float, inv_smooth: np.ndarray | None = None):
+    x = _c(x, np.float32)
+    T, K = x.shape
+    s = _c(inv_smooth, np.float32)
+    q = np.empty((T, K), np.int8)
+    r = np.empty((max(T, 1),), np.float32)
+    assert ref().ref_pack_int8_dyntok(_p(x), T, K, in_thresh, _p(s), _p(q), _p(r)) == 0
+    return q, r[:T]
+
+
+def ref_unpack(yq: np.ndarray, out_step: float, out_step_chan: np.ndarray | None = None,
+               ratio: np.ndarray | None = None) -> np.ndarray:
+    yq = _c(yq, np.int8)
+    T, N = yq.shape
+    osc = _c(out_step_chan, np.float32)
+    r = _c(ratio, np.float32)
+    y = np.empty((T, N), np.float32)
+    assert ref().ref_unpack_int8(_p(yq), T, N, out_step, _p(osc), _p(r), _p(y)) == 0
+    return y
+
+
+def ref_unpack_i16(yq: np.ndarray, out_step: float, out_step_chan: np.ndarray | None = None) -> np.ndarray:
+    yq = _c(yq, np.int16)
+    T, N = yq.shape
+    osc = _c(out_step_chan, np.float32)
+    y = np.empty((T, N), np.float32)
+    assert ref().ref_unpack_int16(_p(yq), T, N, out_step, _p(osc), _p(y)) == 0
+    return y
+
+
+def ref_greedy(logits_row: np.ndarray) -> int:
+    lg = np.array(logits_row, dtype=np.float32, copy=True)
+    return int(ref().ref_sampler_greedy(_p(lg), lg.shape[0]))

@@ -1,0 +1,196 @@
+/*
+ * w8a8_oracle.c -- TEST INFRASTRUCTURE ONLY (the checker, never the product).
+ *
+ * A plain-C, single-threaded restatement of romanaccio's W8A8 quantised-linear + LM-head hot
+ * path, used by tests/ and by bench.py's CPU-baseline leg to check and time the CUDA path.
+ * Nothing in the shipped library calls this file.
+ *
+ * Each function cites the reference lines it restates (paths relative to the reference tree):
+ *
+ *   orc_round_clamp   src/LFM3/lfm3_v2.cpp:248-257           round_clamp_f32
+ *   orc_pack_static   src/LFM3/lfm3_v2.cpp:892-940            pack_npu_input_int8 ([T, C] layout)
+ *   orc_pack_dyntok   src/LFM3/lfm3_v2.cpp:1050-1141          pack_npu_input_int8_dyntok
+ *   orc_gemm_i32      src/eswin_simulator/eswin_simulator/engines/cmac.py:300-383 (INT8 gemm_1x1)
+ *   orc_requant       src/LFM3/attribute_int8_error.py:104-122, FINDINGS.md:1823-1836, 2443-2456
+ *                     (CvtPrecision_QuantM), exact int64 form
+ *   orc_requant_f64   the same in the reference's float64 form round(acc * (qm / 2^trunc))
+ *   orc_unpack        src/LFM3/lfm3_v2.cpp:971-1046, 1143-1183 unpack_npu_output_int8/_int16/_dyntok
+ *   orc_dequant_acc   logit = float(acc) * (ratio * acc_step) (LM-head logit mode)
+ *   orc_topk          src/eswin_runtime/src/nlp/sampler.cpp:93-121 (greedy keeps the lowest id on
+ *                     ties; top-k ordered value desc, then id asc)
+ *
+ * Compile without fast-math and with -ffp-contract=off so every float step rounds like the
+ * reference's scalar C++.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* std::min(std::max(x, -lim), lim) then nearbyintf (round-half-even under the default mode). */
+int32_t orc_round_clamp(float x, float lim) {
+    float c = (x < -lim) ? -lim : x;
+    c = (lim < c) ? lim : c;
+    if (c != c) return 0; /* NaN: the x86 build converts it to INT32_MIN, whose low byte is 0 */
+    return (int32_t)nearbyintf(c);
+}
+
+/* q[t,c] = round_clamp(x[t,c] * (s[c] * inv_step), 127), inv_step = 1/in_step (0 if tiny). */
+void orc_pack_static(const float *x, int64_t ldx, int32_t T, int32_t K, float in_step,
+                     const float *inv_smooth, int8_t *q, int64_t ldq) {
+    const float inv_step = (in_step > 1e-12f) ? (1.0f / in_step) : 0.0f;
+    for (int32_t t = 0; t < T; ++t) {
+        const float *xr = x + t * ldx;
+        int8_t *qr = q + t * ldq;
+        for (int32_t c = 0; c < K; ++c) {
+            const float v = inv_smooth ? xr[c] * (inv_smooth[c] * inv_step) : xr[c] * inv_step;
+            qr[c] = (int8_t)orc_round_clamp(v, 127.0f);
+        }
+    }
+}
+
+/* Per token: amax = max(max_c |x*s|, 1e-8); ratio = amax / max(in_thresh, 1e-8);
+ * q = round_clamp(x * (s * (127 / amax)), 127). */
+void orc_pack_dyntok(const float *x, int64_t ldx, int32_t T, int32_t K, float in_thresh,
+                     const float *inv_smooth, int8_t *q, int64_t ldq, float *ratio) {
+    const float safe_thresh = in_thresh > 1e-8f ? in_thresh : 1e-8f;
+    for (int32_t t = 0; t < T; ++t) {
+        const float *xr = x + t * ldx;
+        int8_t *qr = q + t * ldq;
+        float amax = 0.0f;
+        for (int32_t c = 0; c < K; ++c) {
+            const float a = inv_smooth ? fabsf(xr[c] * inv_smooth[c]) : fabsf(xr[c]);
+            if (a > amax) amax = a;
+        }
+        amax = (amax < 1e-8f) ? 1e-8f : amax;
+        ratio[t] = amax / safe_thresh;
+        const float inv_step = 127.0f / amax;
+        for (int32_t c = 0; c < K; ++c) {
+            const float v = inv_smooth ? xr[c] * (inv_smooth[c] * inv_step) : xr[c] * inv_step;
+            qr[c] = (int8_t)orc_round_clamp(v, 127.0f);
+        }
+    }
+}
+
+/* acc[t,n] = sum_k q[t,k] * w[n,k] (exact; int64 sum narrowed to int32). */
+void orc_gemm_i32(const int8_t *q, int64_t ldq, const int8_t *w, int64_t ldw, int32_t T, int32_t N,
+                  int32_t K, int32_t *acc, int64_t ldacc) {
+    for (int32_t t = 0; t < T; ++t) {
+        const int8_t *qr = q + t * ldq;
+        for (int32_t n = 0; n < N; ++n) {
+            const int8_t *wr = w + n * ldw;
+            int64_t s = 0;
+            for (int32_t k = 0; k < K; ++k) s += (int32_t)qr[k] * (int32_t)wr[k];
+            acc[t * ldacc + n] = (int32_t)s;
+        }
+    }
+}
+
+/* y_q = clip(RNE(acc * qm / 2^trunc), -qmax, qmax) in exact integer arithmetic. */
+int32_t orc_requant_one(int32_t acc, int32_t qm, int32_t trunc, int32_t qmax) {
+    const int64_t p = (int64_t)acc * (int64_t)qm;
+    int64_t qv = p;
+    if (trunc > 0) {
+        /* floor division by 2^trunc without relying on signed shift behaviour */
+        const int64_t d = (int64_t)1 << trunc;
+        int64_t fl = p / d;
+        if ((p % d) != 0 && p < 0) fl -= 1;
+        const int64_t rem = p - fl * d;
+        const int64_t half = d / 2;
+        qv = fl + ((rem > half || (rem == half && (fl & 1))) ? 1 : 0);
+    }
+    if (qv < -qmax) qv = -qmax;
+    if (qv > qmax) qv = qmax;
+    return (int32_t)qv;
+}
+
+/* The reference's float64 formulation: torch.round(acc * (qm / 2^trunc)) then clamp. */
+int32_t orc_requant_f64_one(int32_t acc, int32_t qm, int32_t trunc, int32_t qmax) {
+    const double v = (double)acc * ((double)qm / ldexp(1.0, trunc));
+    double r = nearbyint(v);
+    if (r < -qmax) r = -qmax;
+    if (r > qmax) r = qmax;
+    return (int32_t)r;
+}
+
+void orc_requant(const int32_t *acc, int64_t ldacc, int32_t T, int32_t N, const int16_t *quant_m,
+                 int32_t trunc, int32_t qmax, int32_t *yq, int64_t ldyq) {
+    for (int32_t t = 0; t < T; ++t)
+        for (int32_t n = 0; n < N; ++n)
+            yq[t * ldyq + n] = orc_requant_one(acc[t * ldacc + n], quant_m[n], trunc, qmax);
+}
+
+void orc_requant_f64(const int32_t *acc, int64_t ldacc, int32_t T, int32_t N, const int16_t *quant_m,
+                     int32_t trunc, int32_t qmax, int32_t *yq, int64_t ldyq) {
+    for (int32_t t = 0; t < T; ++t)
+        for (int32_t n = 0; n < N; ++n)
+            yq[t * ldyq + n] = orc_requant_f64_one(acc[t * ldacc + n], quant_m[n], trunc, qmax);
+}
+
+/* y[t,n] = float(yq[t,n]) * step; step = ratio[t] * (out_step_chan ? out_step_chan[n] : out_step)
+ * in DYNTOK mode (dyn != 0), else out_step_chan[n] or out_step. */
+void orc_unpack(const int32_t *yq, int64_t ldyq, int32_t T, int32_t N, int32_t dyn,
+                const float *ratio, const float *out_step_chan, float out_step, float *y,
+                int64_t ldy) {
+    for (int32_t t = 0; t < T; ++t)
+        for (int32_t n = 0; n < N; ++n) {
+            const float st_c = out_step_chan ? out_step_chan[n] : out_step;
+            const float step = dyn ? ratio[t] * st_c : st_c;
+            y[t * ldy + n] = (float)yq[t * ldyq + n] * step;
+        }
+}
+
+/* logit[t,n] = float(acc) * (dyn ? ratio[t] * acc_step[n] : acc_step[n]). */
+void orc_dequant_acc(const int32_t *acc, int64_t ldacc, int32_t T, int32_t N, int32_t dyn,
+                     const float *ratio, const float *acc_step, float *y, int64_t ldy) {
+    for (int32_t t = 0; t < T; ++t)
+        for (int32_t n = 0; n < N; ++n) {
+            const float step = dyn ? ratio[t] * acc_step[n] : acc_step[n];
+            y[t * ldy + n] = (float)acc[t * ldacc + n] * step;
+        }
+}
+
+typedef struct {
+    float v;
+    int32_t id;
+} orc_pair;
+
+static int orc_pair_cmp(const void *a, const void *b) {
+    const orc_pair *x = (const orc_pair *)a, *y = (const orc_pair *)b;
+    /* -0.0 == +0.0 in C comparisons, as in the reference's '>' */
+    if (x->v > y->v) return -1;
+    if (x->v < y->v) return 1;
+    return (x->id < y->id) ? -1 : (x->id > y->id);
+}
+
+/* Top-k of each row of logits [T, V] (row stride ld) in the order (value desc, id asc); ids
+ * are id_offset + column.  val/idx: [T, k]. */
+void orc_topk(const float *logits, int64_t ld, int32_t T, int32_t V, int32_t k, int32_t id_offset,
+              float *val, int32_t *idx) {
+    orc_pair *buf = (orc_pair *)malloc(sizeof(orc_pair) * (size_t)V);
+    if (!buf) return;
+    for (int32_t t = 0; t < T; ++t) {
+        for (int32_t v = 0; v < V; ++v) {
+            buf[v].v = logits[t * ld + v];
+            buf[v].id = id_offset + v;
+        }
+        qsort(buf, (size_t)V, sizeof(orc_pair), orc_pair_cmp);
+        for (int32_t j = 0; j < k; ++j) {
+            val[t * k + j] = buf[j].v;
+            idx[t * k + j] = buf[j].id;
+        }
+    }
+    free(buf);
+}
+
+/* Greedy argmax as Sampler::sample with temperature <= 0 (strict '>' keeps the lowest id). */
+int32_t orc_argmax(const float *logits, int32_t V) {
+    int32_t best = 0;
+    float m = logits[0];
+    for (int32_t i = 1; i < V; ++i)
+        if (logits[i] > m) {
+            m = logits[i];
+            best = i;
+        }
+    return best;
+}

@@ -1,0 +1,212 @@
+// Boundary kernels around the contraction: activation quantisation (pack), int8 staging copy,
+// output dequantisation (unpack) and the cross-shard top-k merge.
+//
+//   act_quant_kernel  pack_npu_input_int8 (src/LFM3/lfm3_v2.cpp:892-940) and
+//                     pack_npu_input_int8_dyntok (src/LFM3/lfm3_v2.cpp:1050-1141), [T, K] layout
+//   unpack_kernel     unpack_npu_output_int8 / _int16 / _int8_dyntok (src/LFM3/lfm3_v2.cpp:971-1046,
+//                     1143-1183)
+//   topk_merge_kernel merge of per-shard candidates; order (value desc, id asc) as the greedy
+//                     rule of src/eswin_runtime/src/nlp/sampler.cpp:93-103
+#include "common.cuh"
+#include "kernels.h"
+
+namespace w8a8 {
+
+namespace {
+
+constexpr int kActThreads = 256;
+
+struct ActArgs {
+  const float *x;
+  int64_t ldx;
+  int K, k_fill;
+  const float *s;
+  float inv_step, safe_thresh;
+  int8_t *q;
+  int64_t ldq;
+  float *ratio;
+};
+
+// One CTA per token row.  DYN: amax_t = max_c |x*s| (NaN ignored as by `if (a > amax)`),
+// amax_t = max(amax_t, 1e-8), ratio_t = amax_t / max(in_thresh, 1e-8), inv = 127 / amax_t.
+// q = round_clamp(x * (s * inv), 127) with the reference's association of the products.
+template <bool DYN, bool SMOOTH, bool VEC>
+__global__ void __launch_bounds__(kActThreads) act_quant_kernel(const ActArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const float *x = a.x + t * a.ldx;
+  int8_t *q = a.q + t * a.ldq;
+  float inv = a.inv_step;
+  if (DYN) {
+    __shared__ float s_part[kActThreads / 32];
+    float amax = 0.0f;
+    if (VEC) {
+      const float4 *x4 = reinterpret_cast<const float4 *>(x);
+      const float4 *s4 = reinterpret_cast<const float4 *>(a.s);
+      for (int c = threadIdx.x; c < a.K / 4; c += kActThreads) {
+        const float4 v = x4[c];
+        float4 m = v;
+        if (SMOOTH) {
+          const float4 sv = s4[c];
+          m.x = v.x * sv.x; m.y = v.y * sv.y; m.z = v.z * sv.z; m.w = v.w * sv.w;
+        }
+        const float ax = fabsf(m.x), ay = fabsf(m.y), az = fabsf(m.z), aw = fabsf(m.w);
+        if (ax > amax) amax = ax;
+        if (ay > amax) amax = ay;
+        if (az > amax) amax = az;
+        if (aw > amax) amax = aw;
+      }
+    } else {
+      for (int c = threadIdx.x; c < a.K; c += kActThreads) {
+        const float v = SMOOTH ? fabsf(x[c] * a.s[c]) : fabsf(x[c]);
+        if (v > amax) amax = v;
+      }
+    }
+    amax = warp_amax(amax);
+    if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kActThreads / 32; ++w) amax = s_part[w] > amax ? s_part[w] : amax;
+    amax = (amax < 1e-8f) ? 1e-8f : amax;
+    if (threadIdx.x == 0) a.ratio[t] = amax / a.safe_thresh;
+    inv = 127.0f / amax;
+  }
+  if (VEC) {
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    const float4 *s4 = reinterpret_cast<const float4 *>(a.s);
+    char4 *q4 = reinterpret_cast<char4 *>(q);
+    for (int c = threadIdx.x; c < a.K / 4; c += kActThreads) {
+      const float4 v = x4[c];
+      char4 o;
+      if (SMOOTH) {
+        const float4 sv = s4[c];
+        o.x = static_cast<signed char>(round_clamp(v.x * (sv.x * inv), 127.0f));
+        o.y = static_cast<signed char>(round_clamp(v.y * (sv.y * inv), 127.0f));
+        o.z = static_cast<signed char>(round_clamp(v.z * (sv.z * inv), 127.0f));
+        o.w = static_cast<signed char>(round_clamp(v.w * (sv.w * inv), 127.0f));
+      } else {
+        o.x = static_cast<signed char>(round_clamp(v.x * inv, 127.0f));
+        o.y = static_cast<signed char>(round_clamp(v.y * inv, 127.0f));
+        o.z = static_cast<signed char>(round_clamp(v.z * inv, 127.0f));
+        o.w = static_cast<signed char>(round_clamp(v.w * inv, 127.0f));
+      }
+      q4[c] = o;
+    }
+  } else {
+    for (int c = threadIdx.x; c < a.K; c += kActThreads) {
+      const float v = SMOOTH ? x[c] * (a.s[c] * inv) : x[c] * inv;
+      q[c] = static_cast<int8_t>(round_clamp(v, 127.0f));
+    }
+  }
+  for (int c = a.K + threadIdx.x; c < a.k_fill; c += kActThreads) q[c] = 0;
+}
+
+template <bool DYN, bool SMOOTH>
+cudaError_t act_dispatch_vec(const ActArgs &a, int T, bool vec, cudaStream_t st, bool pdl) {
+  if (vec) return launch_ex(act_quant_kernel<DYN, SMOOTH, true>, dim3(T), dim3(kActThreads), 0, st, pdl, a);
+  return launch_ex(act_quant_kernel<DYN, SMOOTH, false>, dim3(T), dim3(kActThreads), 0, st, pdl, a);
+}
+
+__global__ void copy_pad_kernel(const int8_t *src, int64_t lds, int K, int8_t *dst, int64_t ldd,
+                                int k_pad) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.y;
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < k_pad; c += gridDim.x * blockDim.x)
+    dst[t * ldd + c] = c < K ? src[t * lds + c] : static_cast<int8_t>(0);
+}
+
+struct UnpackArgs {
+  const void *yq;
+  int64_t ldyq;
+  int in_i16, N, dyn;
+  const float *ratio, *out_step;
+  float *y;
+  int64_t ldy;
+};
+
+__global__ void unpack_kernel(const UnpackArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.y;
+  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < a.N; n += gridDim.x * blockDim.x) {
+    const int v = a.in_i16 ? static_cast<const int16_t *>(a.yq)[t * a.ldyq + n]
+                           : static_cast<const int8_t *>(a.yq)[t * a.ldyq + n];
+    const float step = a.dyn ? a.ratio[t] * a.out_step[n] : a.out_step[n];
+    a.y[t * a.ldy + n] = static_cast<float>(v) * step;
+  }
+}
+
+struct MergeArgs {
+  const float *in_val;
+  const int32_t *in_idx;
+  int n_lists, k_in, k_out, P;
+  int64_t list_stride, token_stride;
+  float *out_val;
+  int32_t *out_idx;
+  int32_t *argmax;
+};
+
+__global__ void __launch_bounds__(256) topk_merge_kernel(const MergeArgs a) {
+  extern __shared__ __align__(16) uint64_t keys[];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int n = a.n_lists * a.k_in;
+  for (int i = threadIdx.x; i < a.P; i += blockDim.x) {
+    uint64_t key = 0ull;
+    if (i < n) {
+      const int64_t off = t * a.token_stride + (i / a.k_in) * a.list_stride + (i % a.k_in);
+      key = topk_key(a.in_val[off], static_cast<uint32_t>(a.in_idx[off]));
+    }
+    keys[i] = key;
+  }
+  bitonic_sort_desc(keys, a.P);
+  for (int j = threadIdx.x; j < a.k_out; j += blockDim.x) {
+    a.out_val[t * a.k_out + j] = topk_key_value(keys[j]);
+    a.out_idx[t * a.k_out + j] = topk_key_id(keys[j]);
+  }
+  if (a.argmax && threadIdx.x == 0) a.argmax[t] = topk_key_id(keys[0]);
+}
+
+}  // namespace
+
+cudaError_t launch_act_quant(const ActQuantLaunch &L, cudaStream_t st) {
+  ActArgs a{L.x, L.ldx, L.K, L.k_fill, L.inv_smooth, L.inv_step, L.safe_thresh, L.q, L.ldq, L.ratio};
+  const bool vec = (L.K % 4 == 0) && (L.ldx % 4 == 0) && (L.ldq % 4 == 0) &&
+                   (reinterpret_cast<uintptr_t>(L.x) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(L.q) % 4 == 0) &&
+                   (L.inv_smooth == nullptr || reinterpret_cast<uintptr_t>(L.inv_smooth) % 16 == 0);
+  const bool dyn = L.act_mode == kActDyntok;
+  const bool sm = L.inv_smooth != nullptr;
+  if (dyn && sm) return act_dispatch_vec<true, true>(a, L.T, vec, st, L.pdl);
+  if (dyn) return act_dispatch_vec<true, false>(a, L.T, vec, st, L.pdl);
+  if (sm) return act_dispatch_vec<false, true>(a, L.T, vec, st, L.pdl);
+  return act_dispatch_vec<false, false>(a, L.T, vec, st, L.pdl);
+}
+
+cudaError_t launch_copy_pad_i8(const int8_t *src, int64_t lds, int T, int K, int8_t *dst,
+                               int64_t ldd, int k_pad, bool pdl, cudaStream_t st) {
+  const int bx = (k_pad + 255) / 256;
+  return launch_ex(copy_pad_kernel, dim3(bx < 64 ? bx : 64, T), dim3(256), 0, st, pdl, src, lds, K,
+                   dst, ldd, k_pad);
+}
+
+cudaError_t launch_unpack(const UnpackLaunch &L, cudaStream_t st) {
+  UnpackArgs a{L.yq, L.ldyq, L.in_i16, L.N, L.act_mode == kActDyntok ? 1 : 0, L.ratio, L.out_step,
+               L.y, L.ldy};
+  const int bx = (L.N + 255) / 256;
+  return launch_ex(unpack_kernel, dim3(bx < 256 ? bx : 256, L.T), dim3(256), 0, st, L.pdl, a);
+}
+
+cudaError_t launch_topk_merge(const MergeLaunch &L, cudaStream_t st) {
+  int P = 1;
+  while (P < L.n_lists * L.k_in) P <<= 1;
+  MergeArgs a{L.in_val, L.in_idx, L.n_lists, L.k_in, L.k_out, P, L.list_stride, L.token_stride,
+              L.out_val, L.out_idx, L.argmax};
+  return launch_ex(topk_merge_kernel, dim3(L.T), dim3(256), static_cast<size_t>(P) * 8, st, L.pdl, a);
+}
+
+}  // namespace w8a8

@@ -1,0 +1,469 @@
+// Decode-shaped W8A8 contraction (T <= 8 tokens) for sm_100a.
+//
+// One CTA = 8 consumer warps + 1 producer warp.  The CTA owns a contiguous range of row
+// tiles (RB = 8 * RPW output channels each) and streams their int8 weights through an
+// NS-deep ring of shared-memory stages filled by 1-D bulk copies (cp.async.bulk, TMA engine,
+// no tensor map, no multicast) that complete on mbarriers.  Each stage holds an [RB, KC] weight
+// slab plus the matching [T, KC] slab of the int8 activations.  Consumers read 16-byte
+// vectors, accumulate with dp4a into int32 registers, and reduce across the warp with
+// shuffles.  The epilogue applies the reference's SDP requant (QuantM, RNE shift, saturate)
+// and the unpack step (per-channel / per-token dequant), or keeps the logits on chip and
+// selects the per-CTA top-k, which the last CTA to finish merges into the shard's top-k.
+//
+// The weight copies of the first NS stages are issued before griddepcontrol.wait, so under
+// programmatic dependent launch the weight stream of this linear overlaps the tail of the
+// kernel that produces its activations.
+//
+// Reference semantics: CMAC int8 GEMM -> CACC int32 (src/eswin_simulator/eswin_simulator/
+// engines/cmac.py:300-383), SDP CvtPrecision_QuantM (src/LFM3/attribute_int8_error.py:104-122),
+// unpack_npu_output_int8[_dyntok] (src/LFM3/lfm3_v2.cpp:971-1008, 1143-1183), LM-head merge
+// (src/LFM3/lfm3_v2.cpp:2360-2405) + greedy / top-k (src/eswin_runtime/src/nlp/sampler.cpp:93-121).
+#include "common.cuh"
+#include "kernels.h"
+
+#include <algorithm>
+
+namespace w8a8 {
+
+namespace {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMaxStages = 8;
+constexpr size_t kMaxDynSmem = 232448;  // 227 KB opt-in per block on sm_100
+
+struct GemvArgs {
+  const int8_t *w;
+  int64_t ldw;
+  const int8_t *x;
+  int64_t ldx;
+  int T, N, k_pad, kc, nk, ns, num_tiles, tiles_per_cta, cand_cap;
+  uint32_t stage_bytes;
+  Epilogue ep;
+  TopK tk;
+  int *err;
+};
+
+__device__ __forceinline__ void store_output(const Epilogue &ep, int acc, int t, int n) {
+  switch (ep.out_mode) {
+    case kOutAccI32:
+      static_cast<int32_t *>(ep.y)[t * ep.ldy + n] = acc;
+      break;
+    case kOutQuant: {
+      const int yq = requant_quantm(acc, ep.quant_m[n], ep.trunc, ep.qmax);
+      if (ep.out_i16)
+        static_cast<int16_t *>(ep.y)[t * ep.ldy + n] = static_cast<int16_t>(yq);
+      else
+        static_cast<int8_t *>(ep.y)[t * ep.ldy + n] = static_cast<int8_t>(yq);
+      break;
+    }
+    case kOutF32: {
+      const int yq = requant_quantm(acc, ep.quant_m[n], ep.trunc, ep.qmax);
+      const float step = ep.act_mode == kActDyntok ? ep.ratio[t] * ep.out_step[n] : ep.out_step[n];
+      static_cast<float *>(ep.y)[t * ep.ldy + n] = static_cast<float>(yq) * step;
+      break;
+    }
+    default: {
+      const float step = ep.act_mode == kActDyntok ? ep.ratio[t] * ep.acc_step[n] : ep.acc_step[n];
+      static_cast<float *>(ep.y)[t * ep.ldy + n] = __int2float_rn(acc) * step;
+      break;
+    }
+  }
+}
+
+// Float logit of one (token, row) for the top-k path (F32 or F32_ACC).
+__device__ __forceinline__ float logit_value(const Epilogue &ep, int acc, int t, int n) {
+  if (ep.out_mode == kOutF32) {
+    const int yq = requant_quantm(acc, ep.quant_m[n], ep.trunc, ep.qmax);
+    const float step = ep.act_mode == kActDyntok ? ep.ratio[t] * ep.out_step[n] : ep.out_step[n];
+    return static_cast<float>(yq) * step;
+  }
+  const float step = ep.act_mode == kActDyntok ? ep.ratio[t] * ep.acc_step[n] : ep.acc_step[n];
+  return __int2float_rn(acc) * step;
+}
+
+// Merge of the per-CTA sorted lists of one token (run by the last CTA to finish).
+__device__ void merge_lists(const TopK &tk, int t, int G, uint64_t *buf, int buf_cap_pow2) {
+  __shared__ unsigned long long s_red[kConsumerWarps + 1];
+  __shared__ int s_red_g[kConsumerWarps + 1];
+  __shared__ int s_count;
+  __shared__ unsigned long long s_tau;
+  const int k = tk.k;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const uint64_t *lists = tk.lists + static_cast<size_t>(t) * G * k;
+
+  // tau = max over lists of their k-th key: every key of the global top-k is >= tau.
+  uint64_t m = 0;
+  for (int g = tid; g < G; g += blockDim.x) {
+    const uint64_t v = __ldcg(reinterpret_cast<const unsigned long long *>(lists) +
+                              static_cast<size_t>(g) * k + (k - 1));
+    m = v > m ? v : m;
+  }
+  m = warp_max_u64(m);
+  if (lane == 0) s_red[warp] = m;
+  if (tid == 0) s_count = 0;
+  __syncthreads();
+  if (tid == 0) {
+    uint64_t mm = 0;
+    for (int w = 0; w < nwarps; ++w) mm = s_red[w] > mm ? s_red[w] : mm;
+    s_tau = mm < 1 ? 1 : mm;  // key 0 marks an empty slot
+  }
+  __syncthreads();
+  const uint64_t tau = s_tau;
+  for (int g = tid; g < G; g += blockDim.x) {
+    const unsigned long long *lg =
+        reinterpret_cast<const unsigned long long *>(lists) + static_cast<size_t>(g) * k;
+    int c = 0;
+    while (c < k && __ldcg(lg + c) >= tau) ++c;
+    const int base = atomicAdd(&s_count, c);
+    for (int j = 0; j < c && base + j < buf_cap_pow2; ++j) buf[base + j] = __ldcg(lg + j);
+  }
+  __syncthreads();
+  const int C = s_count;
+  if (C <= buf_cap_pow2) {
+    int P = 1;
+    while (P < C) P <<= 1;
+    for (int i = C + tid; i < P; i += blockDim.x) buf[i] = 0;
+    bitonic_sort_desc(buf, P);
+    for (int j = tid; j < k; j += blockDim.x) {
+      tk.val[t * k + j] = topk_key_value(buf[j]);
+      tk.idx[t * k + j] = topk_key_id(buf[j]);
+    }
+    __syncthreads();
+    return;
+  }
+  // Rare path (many lists tie at the threshold): k rounds of a tournament over list heads.
+  int *heads = reinterpret_cast<int *>(buf);
+  for (int g = tid; g < G; g += blockDim.x) heads[g] = 0;
+  __syncthreads();
+  for (int j = 0; j < k; ++j) {
+    uint64_t best = 0;
+    int best_g = -1;
+    for (int g = tid; g < G; g += blockDim.x) {
+      const int h = heads[g];
+      const uint64_t v =
+          h < k ? __ldcg(reinterpret_cast<const unsigned long long *>(lists) +
+                         static_cast<size_t>(g) * k + h)
+                : 0ull;
+      if (v > best) { best = v; best_g = g; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+      const int og = __shfl_xor_sync(0xFFFFFFFFu, best_g, o);
+      if (ov > best) { best = ov; best_g = og; }
+    }
+    if (lane == 0) { s_red[warp] = best; s_red_g[warp] = best_g; }
+    __syncthreads();
+    if (tid == 0) {
+      uint64_t bb = 0;
+      int bg = -1;
+      for (int w = 0; w < nwarps; ++w)
+        if (s_red[w] > bb) { bb = s_red[w]; bg = s_red_g[w]; }
+      tk.val[t * k + j] = topk_key_value(bb);
+      tk.idx[t * k + j] = topk_key_id(bb);
+      if (bg >= 0) heads[bg] += 1;
+    }
+    __syncthreads();
+  }
+}
+
+template <int TT, int RPW, bool TOPK>
+__global__ void __launch_bounds__(kThreads, TOPK ? 1 : 2) gemv_w8a8_kernel(const GemvArgs a) {
+  constexpr int RB = kConsumerWarps * RPW;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t *stages = smem;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + static_cast<size_t>(a.ns) * a.stage_bytes);
+  uint64_t *cand = bars + 2 * kMaxStages;  // TOPK: [TT][cand_cap]
+  __shared__ int s_last;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tile0 = blockIdx.x * a.tiles_per_cta;
+  const int tile_end = min(tile0 + a.tiles_per_cta, a.num_tiles);
+  const int ntiles = tile_end - tile0;
+  const int total = ntiles * a.nk;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.ns; ++s) {
+      mbar_init(smem_addr(&bars[s]), 1);
+      mbar_init(smem_addr(&bars[kMaxStages + s]), kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  if (TOPK) {
+    for (int i = threadIdx.x; i < TT * a.cand_cap; i += blockDim.x) cand[i] = 0ull;
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------- producer warp -------------------------------
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    const int pre = min(a.ns, total);
+    auto stage_geom = [&](int it, int &tile, int &k0, int &bytes, int &rows) {
+      tile = tile0 + it / a.nk;
+      k0 = (it % a.nk) * a.kc;
+      bytes = min(a.kc, a.k_pad - k0);
+      rows = min(RB, a.N - tile * RB);
+    };
+    for (int it = 0; it < pre; ++it) {
+      int tile, k0, bytes, rows;
+      stage_geom(it, tile, k0, bytes, rows);
+      const uint32_t full = smem_addr(&bars[it]);
+      if (lane == 0) mbar_arrive_expect_tx(full, static_cast<uint32_t>((rows + a.T) * bytes));
+      __syncwarp();
+      const uint32_t dst = smem_addr(stages + static_cast<size_t>(it) * a.stage_bytes);
+      for (int r = lane; r < rows; r += 32)
+        bulk_g2s(dst + r * a.kc, a.w + static_cast<int64_t>(tile * RB + r) * a.ldw + k0, bytes,
+                 full, pol_w);
+    }
+    // Activations (and everything written by the previous kernel) are read only after this.
+    pdl_wait();
+    for (int it = 0; it < pre; ++it) {
+      int tile, k0, bytes, rows;
+      stage_geom(it, tile, k0, bytes, rows);
+      const uint32_t full = smem_addr(&bars[it]);
+      const uint32_t dst = smem_addr(stages + static_cast<size_t>(it) * a.stage_bytes) + RB * a.kc;
+      for (int t = lane; t < a.T; t += 32)
+        bulk_g2s(dst + t * a.kc, a.x + t * a.ldx + k0, bytes, full, pol_x);
+    }
+    bool ok = true;
+    for (int it = pre; it < total; ++it) {
+      const int slot = it % a.ns;
+      const int use = it / a.ns;
+      if (ok)
+        ok = mbar_wait_bounded(smem_addr(&bars[kMaxStages + slot]), (use - 1) & 1, a.err,
+                               kDevTimeoutEmpty);
+      if (!ok) break;
+      int tile, k0, bytes, rows;
+      stage_geom(it, tile, k0, bytes, rows);
+      const uint32_t full = smem_addr(&bars[slot]);
+      if (lane == 0) mbar_arrive_expect_tx(full, static_cast<uint32_t>((rows + a.T) * bytes));
+      __syncwarp();
+      const uint32_t dst = smem_addr(stages + static_cast<size_t>(slot) * a.stage_bytes);
+      for (int r = lane; r < rows; r += 32)
+        bulk_g2s(dst + r * a.kc, a.w + static_cast<int64_t>(tile * RB + r) * a.ldw + k0, bytes,
+                 full, pol_w);
+      for (int t = lane; t < a.T; t += 32)
+        bulk_g2s(dst + RB * a.kc + t * a.kc, a.x + t * a.ldx + k0, bytes, full, pol_x);
+    }
+  } else {
+    // ------------------------------- consumer warps -------------------------------
+    pdl_wait();
+    int acc[RPW][TT];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+      for (int t = 0; t < TT; ++t) acc[r][t] = 0;
+    bool ok = true;
+    for (int it = 0; it < total; ++it) {
+      const int slot = it % a.ns;
+      const int use = it / a.ns;
+      if (ok) ok = mbar_wait_bounded(smem_addr(&bars[slot]), use & 1, a.err, kDevTimeoutFull);
+      const int kci = it % a.nk;
+      const int bytes = min(a.kc, a.k_pad - kci * a.kc);
+      const uint8_t *sw = stages + static_cast<size_t>(slot) * a.stage_bytes;
+      const uint8_t *sx = sw + RB * a.kc;
+      if (ok) {
+        for (int kk = lane * 16; kk < bytes; kk += 512) {
+          int4 xv[TT];
+#pragma unroll
+          for (int t = 0; t < TT; ++t) xv[t] = *reinterpret_cast<const int4 *>(sx + t * a.kc + kk);
+#pragma unroll
+          for (int r = 0; r < RPW; ++r) {
+            const int4 wv =
+                *reinterpret_cast<const int4 *>(sw + (warp * RPW + r) * a.kc + kk);
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+              int s = acc[r][t];
+              s = __dp4a(wv.x, xv[t].x, s);
+              s = __dp4a(wv.y, xv[t].y, s);
+              s = __dp4a(wv.z, xv[t].z, s);
+              s = __dp4a(wv.w, xv[t].w, s);
+              acc[r][t] = s;
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&bars[kMaxStages + slot]));
+      if (kci == a.nk - 1) {
+        // Tile finished: butterfly-reduce every (row, token) sum; lane r*TT+t keeps it.
+        const int tile = tile0 + it / a.nk;
+        int mine = 0;
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+          for (int t = 0; t < TT; ++t) {
+            const int s = warp_sum(acc[r][t]);
+            if (lane == r * TT + t) mine = s;
+            acc[r][t] = 0;
+          }
+        if (lane < RPW * TT) {
+          const int r = lane / TT;
+          const int t = lane % TT;
+          const int row = warp * RPW + r;
+          const int n = tile * RB + row;
+          if (t < a.T && n < a.N && ok) {
+            if (TOPK) {
+              const float v = logit_value(a.ep, mine, t, n);
+              if (a.tk.logits) a.tk.logits[t * a.tk.ldl + n] = v;
+              cand[t * a.cand_cap + (tile - tile0) * RB + row] =
+                  topk_key(v, static_cast<uint32_t>(a.tk.row_offset + n));
+            } else {
+              store_output(a.ep, mine, t, n);
+            }
+          }
+        }
+      }
+    }
+  }
+  pdl_launch_dependents();
+  if (!TOPK) return;
+
+  // ------------------------------- top-k epilogue -------------------------------
+  __syncthreads();
+  const int rows_here = min(ntiles * RB, a.N - tile0 * RB);
+  int P = 1;
+  while (P < rows_here) P <<= 1;
+  const int k = a.tk.k;
+  const int G = gridDim.x;
+  for (int t = 0; t < a.T; ++t) {
+    uint64_t *ct = cand + t * a.cand_cap;
+    bitonic_sort_desc(ct, P);
+    for (int j = threadIdx.x; j < k; j += blockDim.x)
+      a.tk.lists[(static_cast<size_t>(t) * G + blockIdx.x) * k + j] = j < P ? ct[j] : 0ull;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(a.tk.counter, 1u) == static_cast<unsigned>(G - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // The whole dynamic shared memory is free now: use it as the merge buffer.
+  const size_t dyn_bytes = static_cast<size_t>(a.ns) * a.stage_bytes + 2 * kMaxStages * 8 +
+                           static_cast<size_t>(TT) * a.cand_cap * 8;
+  int cap = 1;
+  while (static_cast<size_t>(cap) * 2 * 8 <= dyn_bytes) cap <<= 1;
+  uint64_t *buf = reinterpret_cast<uint64_t *>(smem);
+  for (int t = 0; t < a.T; ++t) merge_lists(a.tk, t, G, buf, cap);
+  if (threadIdx.x == 0) *a.tk.counter = 0u;
+}
+
+template <int TT, int RPW, bool TOPK>
+cudaError_t launch_one(const GemvArgs &args, const GemvPlan &plan, cudaStream_t stream, bool pdl) {
+  auto kern = gemv_w8a8_kernel<TT, RPW, TOPK>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDynSmem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  return launch_ex(kern, dim3(plan.grid), dim3(kThreads), plan.smem, stream, pdl, args);
+}
+
+template <int TT>
+cudaError_t dispatch_rpw(const GemvArgs &args, const GemvPlan &plan, cudaStream_t stream, bool pdl,
+                         bool topk) {
+  if (topk) {
+    switch (plan.rpw) {
+      case 1: return launch_one<TT, 1, true>(args, plan, stream, pdl);
+      case 2: return launch_one<TT, 2, true>(args, plan, stream, pdl);
+      default: return launch_one<TT, 4, true>(args, plan, stream, pdl);
+    }
+  }
+  switch (plan.rpw) {
+    case 1: return launch_one<TT, 1, false>(args, plan, stream, pdl);
+    case 2: return launch_one<TT, 2, false>(args, plan, stream, pdl);
+    default: return launch_one<TT, 4, false>(args, plan, stream, pdl);
+  }
+}
+
+size_t pow2_ceil(size_t v) {
+  size_t p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+}  // namespace
+
+bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan *plan) {
+  if (T < 1 || T > 8 || N < 1 || k_pad < 16 || (k_pad % 16) != 0 || sm_count < 1) return false;
+  GemvPlan p = {};
+  p.tt = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
+  auto tiles = [&](int rb) { return (N + rb - 1) / rb; };
+  if (topk) {
+    p.rpw = tiles(32) >= sm_count ? 4 : tiles(16) >= sm_count ? 2 : 1;
+  } else {
+    p.rpw = tiles(32) >= 2 * sm_count ? 4 : tiles(16) >= 2 * sm_count ? 2 : 1;
+  }
+  p.rb = 8 * p.rpw;
+  const int kc_max = 32768 / p.rb;
+  p.kc = std::min(k_pad, kc_max);
+  p.nk = (k_pad + p.kc - 1) / p.kc;
+  const size_t stage = static_cast<size_t>(p.rb + p.tt) * p.kc;
+  p.num_tiles = tiles(p.rb);
+  const size_t bars = 2 * kMaxStages * 8;
+  if (!topk) {
+    const size_t budget = 110 * 1024;
+    p.ns = static_cast<int>(std::min<size_t>(kMaxStages, std::max<size_t>(2, budget / stage)));
+    p.grid = std::min(p.num_tiles, 2 * sm_count);
+    p.tiles_per_cta = (p.num_tiles + p.grid - 1) / p.grid;
+    p.grid = (p.num_tiles + p.tiles_per_cta - 1) / p.tiles_per_cta;
+    p.cand_cap = 0;
+    p.smem = p.ns * stage + bars;
+  } else {
+    if (k < 1 || k > 64 || k > N) return false;
+    int grid = std::min(p.num_tiles, sm_count);
+    size_t cap = 0;
+    while (true) {
+      const int tpc = (p.num_tiles + grid - 1) / grid;
+      cap = pow2_ceil(static_cast<size_t>(tpc) * p.rb);
+      if (static_cast<size_t>(p.tt) * cap * 8 <= 96 * 1024) break;
+      if (grid >= p.num_tiles) return false;
+      grid = std::min(p.num_tiles, grid * 2);
+    }
+    p.tiles_per_cta = (p.num_tiles + grid - 1) / grid;
+    p.grid = (p.num_tiles + p.tiles_per_cta - 1) / p.tiles_per_cta;
+    p.cand_cap = static_cast<int>(cap);
+    const size_t cand_bytes = static_cast<size_t>(p.tt) * cap * 8;
+    const size_t budget = 200 * 1024 - cand_bytes;
+    p.ns = static_cast<int>(std::min<size_t>(kMaxStages, std::max<size_t>(2, budget / stage)));
+    p.smem = p.ns * stage + bars + cand_bytes;
+  }
+  if (p.smem > kMaxDynSmem) return false;
+  *plan = p;
+  return true;
+}
+
+cudaError_t launch_gemv(const GemvLaunch &L, const GemvPlan &plan, cudaStream_t stream) {
+  GemvArgs a;
+  a.w = L.w;
+  a.ldw = L.ldw;
+  a.x = L.x;
+  a.ldx = L.ldx;
+  a.T = L.T;
+  a.N = L.N;
+  a.k_pad = L.k_pad;
+  a.kc = plan.kc;
+  a.nk = plan.nk;
+  a.ns = plan.ns;
+  a.num_tiles = plan.num_tiles;
+  a.tiles_per_cta = plan.tiles_per_cta;
+  a.cand_cap = plan.cand_cap;
+  a.stage_bytes = static_cast<uint32_t>((plan.rb + plan.tt) * plan.kc);
+  a.ep = L.ep;
+  a.tk = L.tk;
+  a.err = L.err;
+  switch (plan.tt) {
+    case 1: return dispatch_rpw<1>(a, plan, stream, L.pdl, L.topk);
+    case 2: return dispatch_rpw<2>(a, plan, stream, L.pdl, L.topk);
+    case 4: return dispatch_rpw<4>(a, plan, stream, L.pdl, L.topk);
+    default: return dispatch_rpw<8>(a, plan, stream, L.pdl, L.topk);
+  }
+}
+
+}  // namespace w8a8

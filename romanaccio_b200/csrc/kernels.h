@@ -1,0 +1,151 @@
+// Internal launch interface between the C-ABI layer (api.cu) and the kernel files.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <utility>
+
+namespace w8a8 {
+
+// Device error codes written into the context's error word.
+enum DeviceError : int {
+  kDevOk = 0,
+  kDevTimeoutFull = 1,   // a consumer waited too long for a bulk copy to land
+  kDevTimeoutEmpty = 2,  // the producer waited too long for a stage to be released
+  kDevPeerTimeout = 3,   // a peer flag never arrived
+};
+
+// Output modes (values of w8a8_out_mode).
+enum OutMode : int { kOutAccI32 = 0, kOutQuant = 1, kOutF32 = 2, kOutF32Acc = 3 };
+// Activation modes (values of w8a8_act_mode).
+enum ActMode : int { kActStatic = 0, kActDyntok = 1 };
+
+// Epilogue parameters shared by every contraction kernel.
+struct Epilogue {
+  int out_mode;
+  int act_mode;
+  const int16_t *quant_m;   // [N]
+  int trunc;
+  int qmax;                 // 127 or 32767
+  int out_i16;              // QUANT output element type: 0 = int8, 1 = int16
+  const float *out_step;    // [N] out_step_chan[n] or the scalar out_step repeated
+  const float *acc_step;    // [N] F32_ACC step
+  const float *ratio;       // [T] dyntok ratios (read in DYNTOK mode)
+  void *y;                  // [T, ldy]
+  int64_t ldy;
+};
+
+// Top-k epilogue (LM head shard).
+struct TopK {
+  int k;                    // 1..64
+  int row_offset;           // vocab id of row 0
+  uint64_t *lists;          // scratch [T, grid, k] per-CTA sorted keys
+  unsigned *counter;        // scratch arrival counter (0 between launches)
+  float *val;               // [T, k]
+  int32_t *idx;             // [T, k]
+  float *logits;            // optional [T, ldl]
+  int64_t ldl;
+};
+
+struct GemvLaunch {
+  const int8_t *w;          // [N, ldw] zero-padded up to k_pad
+  int64_t ldw;
+  const int8_t *x;          // [T, ldx] int8 activations, 16-byte aligned rows, k_pad readable
+  int64_t ldx;
+  int T, N, k_pad;
+  Epilogue ep;
+  bool topk;
+  TopK tk;
+  int *err;
+  int sm_count;
+  bool pdl;
+};
+
+// Shape plan of one GEMV launch (filled by plan_gemv; the scratch sizes of the top-k path
+// depend on it).
+struct GemvPlan {
+  int tt;          // token template (1, 2, 4, 8)
+  int rpw;         // rows per consumer warp (1, 2, 4)
+  int rb;          // rows per tile = 8 * rpw
+  int kc;          // bytes of K per stage
+  int nk;          // stages per tile
+  int ns;          // pipeline depth
+  int num_tiles;
+  int tiles_per_cta;
+  int grid;
+  int cand_cap;    // top-k: power-of-two candidate slots per token per CTA
+  size_t smem;     // dynamic shared memory bytes
+};
+
+bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan *plan);
+cudaError_t launch_gemv(const GemvLaunch &L, const GemvPlan &plan, cudaStream_t stream);
+
+// Activation quantisation (pack) of x [T, K] fp32 into q [T, ldq] int8 (+ ratio [T]).
+struct ActQuantLaunch {
+  const float *x;
+  int64_t ldx;
+  int T, K;
+  int k_fill;               // columns [K, k_fill) of q are zero-filled
+  const float *inv_smooth;  // [K] or null
+  int act_mode;
+  float inv_step;           // static: (in_step > 1e-12f) ? 1/in_step : 0
+  float safe_thresh;        // dyntok: max(in_thresh, 1e-8f)
+  int8_t *q;
+  int64_t ldq;
+  float *ratio;             // [T] (dyntok)
+  bool pdl;
+};
+cudaError_t launch_act_quant(const ActQuantLaunch &L, cudaStream_t stream);
+
+// int8 row copy with zero fill of [K, k_pad) (used when a caller's int8 activations are not
+// 16-byte aligned / padded).
+cudaError_t launch_copy_pad_i8(const int8_t *src, int64_t lds, int T, int K, int8_t *dst,
+                               int64_t ldd, int k_pad, bool pdl, cudaStream_t stream);
+
+// Unpack (dequant) of requantised outputs.
+struct UnpackLaunch {
+  const void *yq;
+  int64_t ldyq;
+  int in_i16;
+  int T, N;
+  int act_mode;
+  const float *ratio;
+  const float *out_step;    // [N]
+  float *y;
+  int64_t ldy;
+  bool pdl;
+};
+cudaError_t launch_unpack(const UnpackLaunch &L, cudaStream_t stream);
+
+// Merge of n_lists candidate lists per token into the top k_out.
+struct MergeLaunch {
+  const float *in_val;
+  const int32_t *in_idx;
+  int T, n_lists, k_in, k_out;
+  int64_t list_stride, token_stride;
+  float *out_val;
+  int32_t *out_idx;
+  int32_t *argmax;
+  bool pdl;
+};
+cudaError_t launch_topk_merge(const MergeLaunch &L, cudaStream_t stream);
+
+// Launch helper: cudaLaunchKernelEx with the programmatic-stream-serialisation attribute.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t stream, bool pdl, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+}  // namespace w8a8

@@ -1,0 +1,193 @@
+"""One decode step of a W8A8 model: every linear of every layer, then the vocab-sharded LM
+head with top-k / argmax -- the hot path of the reference's decode loop
+(Lfm3Engine::forward_chunk, src/LFM3/lfm3_v2.cpp:1743, and TransformerSession::step,
+src/eswin_runtime/src/llm/transformer_session.cpp:616-846), restricted to the quantised
+linears and the LM head.  Attention, norms, residual adds and the SwiGLU product are not part
+of that path: each linear consumes the previous linear's output (o takes the q slice of qkv,
+down takes the gate slice of gate_up), so the chain has real data dependences.
+
+Multi-GPU (one process per GPU): every rank runs its own T tokens through a full replica of the
+linear stack, the final hidden states are all-gathered (the reference broadcasts the final
+hidden state into both dies' buffers, lfm3_v2.cpp:810-831), every rank runs its contiguous
+vocab shard of the LM head over all ranks' tokens, and only the per-shard top-k (value, id)
+pairs are all-gathered and merged.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ._lib import DTYPE_INT8, OUT_F32, OUT_F32_ACC
+from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
+from .lmhead import LmHeadShard, shard_range
+from .quantize import build_linear
+from .synth import DecodeShape, activations, outlier_channels
+
+LM_CHUNK = 4096  # LM-head rows are generated in seeded chunks so every sharding agrees
+
+
+@dataclass
+class StepBytes:
+    linear: int      # algorithmic bytes of all linears (per rank per step)
+    lm_head: int     # algorithmic bytes of this rank's LM-head shard
+    gemv_launch: int  # algorithmic bytes of one launch of the dominant GEMV (gate_up)
+
+
+def _lm_rows(K: int, lo: int, hi: int, seed: int, device) -> tuple[np.ndarray, np.ndarray]:
+    """Rows [lo, hi) of the synthetic LM head: fp32 N(0, 0.02) quantised per row."""
+    wq_parts, step_parts = [], []
+    c0 = lo // LM_CHUNK
+    c1 = (hi + LM_CHUNK - 1) // LM_CHUNK
+    for c in range(c0, c1):
+        g = torch.Generator(device=device).manual_seed(seed * 1_000_003 + c)
+        w = torch.randn((LM_CHUNK, K), generator=g, device=device, dtype=torch.float32) * 0.02
+        r0, r1 = max(lo, c * LM_CHUNK), min(hi, (c + 1) * LM_CHUNK)
+        w = w[r0 - c * LM_CHUNK:r1 - c * LM_CHUNK].double()
+        step = w.abs().amax(dim=1, keepdim=True).clamp(min=1e-12) / 127.0
+        wq = torch.clamp(torch.round(w / step), -127, 127).to(torch.int8)
+        wq_parts.append(wq.cpu().numpy())
+        step_parts.append(step[:, 0].cpu().numpy())
+    return np.concatenate(wq_parts), np.concatenate(step_parts)
+
+
+class DecodeStack:
+    def __init__(self, ctx: Context, shape: DecodeShape, T: int, rank: int = 0, world: int = 1,
+                 group=None, seed: int = 0, layers: int | None = None, k: int = 40,
+                 lm_vocab: int | None = None):
+        self.ctx = ctx
+        self.shape = shape
+        self.T = int(T)
+        self.rank, self.world, self.group = int(rank), int(world), group
+        self.k = int(k)
+        self.layers = shape.layers if layers is None else int(layers)
+        dev = torch.device("cuda", ctx.device)
+        self.dev = dev
+        self.subgraphs = shape.subgraphs()
+        self.linears: list[list[W8A8Linear]] = []
+        self.params_host = []  # kept for the CPU baseline
+        for layer in range(self.layers):
+            row = []
+            for j, (name, K, N, trunc) in enumerate(self.subgraphs):
+                s = seed * 7919 + layer * 16 + j
+                g = torch.Generator(device=dev).manual_seed(s)
+                w = torch.randn((N, K), generator=g, device=dev, dtype=torch.float32) * 0.02
+                calib = activations(64, K, s + 1, device=dev)
+                p = build_linear(w, calib, trunc=trunc)
+                del w, calib
+                scale = SubgraphScaleInfo(in_dtype=DTYPE_INT8, out_dtype=DTYPE_INT8,
+                                          in_thresh=p.in_thresh, in_step=p.in_step,
+                                          in_inv_smooth=p.in_inv_smooth,
+                                          out_step_chan=p.out_step_chan)
+                row.append(W8A8Linear(ctx, p.wq, scale, quant_m=p.quant_m, trunc=p.trunc,
+                                      acc_step=p.acc_step))
+                self.params_host.append((name, p))
+            self.linears.append(row)
+        # LM head: static int8 input (in_step from a calibration of the final hidden state),
+        # logit = float(acc) * in_step * w_step[v].
+        K = shape.hidden
+        V = shape.vocab if lm_vocab is None else int(lm_vocab)
+        self.V = V
+        self.lo, self.hi = shard_range(V, self.world, self.rank)
+        wq, w_step = _lm_rows(K, self.lo, self.hi, seed + 17, dev)
+        calib = activations(64, K, seed + 23, device=dev)
+        self.lm_in_step = float(calib.abs().amax().item()) / 127.0
+        acc_step = (self.lm_in_step * w_step).astype(np.float32)
+        self.lm_host = (wq, acc_step)
+        self.lm = LmHeadShard(ctx, wq, acc_step, self.lm_in_step, row_offset=self.lo)
+        # persistent device buffers
+        T_all = self.T * self.world
+        self.x = torch.zeros((self.T, K), dtype=torch.float32, device=dev)
+        self.outs = [torch.empty((self.T, N), dtype=torch.float32, device=dev)
+                     for (_, _, N, _) in self.subgraphs]
+        self.h_all = torch.empty((T_all, K), dtype=torch.float32, device=dev)
+        self.cand = torch.empty((2, T_all, self.k), dtype=torch.int32, device=dev)
+        self.cand_all = torch.empty((self.world, 2, T_all, self.k), dtype=torch.int32, device=dev)
+        self.ids = torch.empty((self.T,), dtype=torch.int32, device=dev)
+        self.top_val = torch.empty((self.T, self.k), dtype=torch.float32, device=dev)
+        self.top_idx = torch.empty((self.T, self.k), dtype=torch.int32, device=dev)
+        self.graph = None
+        self.graph_lm = None
+
+    # ------------------------------------------------------------------ byte accounting
+    def step_bytes(self) -> StepBytes:
+        T = self.T
+        lin = 0
+        for (_, K, N, _) in self.subgraphs:
+            lin += N * K + T * K * 4 + T * N * 4 + K * 4 + N * (4 + 2 + 4)
+        lin *= self.layers
+        K = self.shape.hidden
+        Vs = self.hi - self.lo
+        T_all = T * self.world
+        lm = Vs * K + T_all * K * 4 + Vs * 4 + T_all * self.k * 8
+        _, K, N, _ = self.subgraphs[2]  # gate_up, the largest subgraph
+        gemv = N * K + T * K + T * N * 4 + N * (2 + 4)
+        return StepBytes(lin, lm, gemv)
+
+    # ------------------------------------------------------------------ the step
+    def run_linears(self) -> None:
+        x = self.x
+        qkv, o, gu, down = self.outs
+        q_width = self.shape.q
+        for row in self.linears:
+            row[0].forward(x, OUT_F32, dyntok=True, out=qkv)
+            row[1].forward(qkv[:, :q_width], OUT_F32, dyntok=True, out=o)
+            row[2].forward(o, OUT_F32, dyntok=True, out=gu)
+            row[3].forward(gu[:, :self.shape.ffn], OUT_F32, dyntok=True, out=down)
+            x = down
+
+    def run_lm_head(self) -> None:
+        h = self.outs[3]
+        if self.world == 1:
+            self.lm.forward(h, self.k, OUT_F32_ACC, val=self.top_val, idx=self.top_idx)
+            self.ids.copy_(self.top_idx[:, 0])
+            return
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(self.h_all, h, group=self.group)
+        self.lm.forward(self.h_all, self.k, OUT_F32_ACC, val=self.cand[0].view(torch.float32),
+                        idx=self.cand[1])
+        dist.all_gather_into_tensor(self.cand_all, self.cand, group=self.group)
+        t0 = self.rank * self.T
+        vals = self.cand_all[:, 0, t0:t0 + self.T].view(torch.float32).permute(1, 0, 2)
+        ids = self.cand_all[:, 1, t0:t0 + self.T].permute(1, 0, 2)
+        v, i, a = topk_merge(self.ctx, vals, ids, self.k)
+        self.top_val.copy_(v)
+        self.top_idx.copy_(i)
+        self.ids.copy_(a)
+
+    def capture(self) -> None:
+        """Captures the device part of the step in CUDA graphs (the LM head + exchange stays
+        eager for world > 1: the NCCL calls are not captured)."""
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            self.run_linears()
+            if self.world == 1:
+                self.run_lm_head()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        torch.cuda.synchronize(self.dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.run_linears()
+            if self.world == 1:
+                self.run_lm_head()
+        self.graph = g
+
+    def step(self) -> None:
+        if self.graph is not None:
+            self.graph.replay()
+            if self.world > 1:
+                self.run_lm_head()
+        else:
+            self.run_linears()
+            self.run_lm_head()
+
+    def step_host(self, x_host: torch.Tensor, ids_host: torch.Tensor) -> None:
+        """End-to-end step through the public API: pinned host activations in, sampled ids out."""
+        self.x.copy_(x_host, non_blocking=True)
+        self.step()
+        ids_host.copy_(self.ids, non_blocking=True)
+
+    def release(self) -> None:
+        self.graph = None

@@ -1,0 +1,100 @@
+"""Vocab-sharded W8A8 LM head with a fused top-k / argmax epilogue.
+
+The reference splits the LM head into contiguous vocab halves across its two NPU dies
+(src/eswin_compiler/passes/dual_die_splitter.py:63-147: die 0 gets rows [0, V//2), die 1 the
+rest), runs both halves concurrently (run_dual_die, src/LFM3/lfm3_v2.cpp:1311-1332;
+forward_lm_head_dual_die, src/eswin_runtime/src/llm/transformer_session.cpp:538-614),
+concatenates the logits on the host and samples over the full vocabulary
+(src/eswin_runtime/src/nlp/sampler.cpp:83-121).
+
+Here each of n ranks (one process per GPU) owns rows [floor(r*V/n), floor((r+1)*V/n)), its
+kernel keeps the shard's logits on chip and emits only the sorted top-k (value, vocab id)
+pairs, the ranks exchange those k*8 bytes, and a merge kernel produces the global top-k and the
+greedy argmax (lowest id on ties, as Sampler::sample's strict '>').
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from ._lib import DTYPE_INT8, OUT_F32_ACC
+from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
+
+
+def shard_range(V: int, n: int, r: int) -> tuple[int, int]:
+    """Contiguous vocab block of shard r of n (n = 2 gives the reference's halves)."""
+    return (r * V) // n, ((r + 1) * V) // n
+
+
+class LmHeadShard:
+    """This rank's block of vocab rows as a W8A8 linear whose output is a top-k list."""
+
+    def __init__(self, ctx: Context, wq_rows: np.ndarray, acc_step_rows: np.ndarray,
+                 in_step: float, row_offset: int, in_inv_smooth: np.ndarray | None = None,
+                 quant_m_rows: np.ndarray | None = None, trunc: int = 22,
+                 out_step_chan_rows: np.ndarray | None = None, out_step: float = 1.0 / 127.0):
+        scale = SubgraphScaleInfo(in_dtype=DTYPE_INT8, out_dtype=DTYPE_INT8, in_step=in_step,
+                                  in_thresh=in_step * 127.0, out_step=out_step,
+                                  in_inv_smooth=in_inv_smooth, out_step_chan=out_step_chan_rows)
+        self.linear = W8A8Linear(ctx, wq_rows, scale, quant_m=quant_m_rows, trunc=trunc,
+                                 acc_step=acc_step_rows)
+        self.row_offset = int(row_offset)
+        self.rows = int(wq_rows.shape[0])
+
+    def forward(self, h: torch.Tensor, k: int, out_mode: int = OUT_F32_ACC, val=None, idx=None,
+                logits=None, stream=None):
+        return self.linear.forward_topk(h, k, row_offset=self.row_offset, out_mode=out_mode,
+                                        dyntok=False, val=val, idx=idx, logits=logits,
+                                        stream=stream)
+
+
+class VocabShardedLmHead:
+    """LM head over `world` ranks; rank `rank` builds only its shard.
+
+    forward(h) -> (top-k values [T, k], top-k vocab ids [T, k], argmax [T]) on every rank.
+    The exchange is one all-gather of the [T, k] (value, id) pairs through torch.distributed
+    (NCCL over NVLink between GPUs); with world == 1 there is no exchange.
+    """
+
+    def __init__(self, ctx: Context, V: int, rank: int = 0, world: int = 1, group=None):
+        self.ctx = ctx
+        self.V = int(V)
+        self.rank = int(rank)
+        self.world = int(world)
+        self.group = group
+        self.lo, self.hi = shard_range(self.V, self.world, self.rank)
+        self.shard: LmHeadShard | None = None
+        self._bufs: dict[tuple[int, int], tuple[torch.Tensor, torch.Tensor]] = {}
+
+    def load_shard(self, wq_full_or_rows: np.ndarray, acc_step: np.ndarray, in_step: float,
+                   rows_are_shard: bool = False, **kw) -> None:
+        """Uploads this rank's rows (pass the full [V, K] matrix or only the shard's rows)."""
+        if rows_are_shard:
+            rows, steps = wq_full_or_rows, acc_step
+        else:
+            rows = wq_full_or_rows[self.lo:self.hi]
+            steps = acc_step[self.lo:self.hi]
+        self.shard = LmHeadShard(self.ctx, rows, steps, in_step, self.lo, **kw)
+
+    def _buffers(self, T: int, k: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+        key = (T, k)
+        if key not in self._bufs:
+            local = torch.empty((2, T, k), dtype=torch.int32, device=device)
+            gathered = torch.empty((self.world, 2, T, k), dtype=torch.int32, device=device)
+            self._bufs[key] = (local, gathered)
+        return self._bufs[key]
+
+    def forward(self, h: torch.Tensor, k: int = 40, out_mode: int = OUT_F32_ACC, stream=None):
+        assert self.shard is not None, "load_shard() first"
+        T = h.shape[0]
+        if self.world == 1:
+            v, i = self.shard.forward(h, k, out_mode=out_mode, stream=stream)
+            return v, i, i[:, 0]
+        local, gathered = self._buffers(T, k, h.device)
+        self.shard.forward(h, k, out_mode=out_mode, val=local[0].view(torch.float32),
+                           idx=local[1], stream=stream)
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(gathered, local, group=self.group)
+        vals = gathered[:, 0].view(torch.float32).permute(1, 0, 2)  # [T, world, k]
+        ids = gathered[:, 1].permute(1, 0, 2)
+        return topk_merge(self.ctx, vals, ids, k, stream=stream)

@@ -1,0 +1,184 @@
+"""Generates the golden fixtures of tests/golden/ from the REFERENCE itself.
+
+Run in a container that has the reference tree (read-only) at REF (default /root/reference):
+
+    python tests/golden/make_golden.py [--ref /root/reference]
+
+Sources of truth, all executed here rather than restated:
+  * quant_linear_*.npz  -- build_single_conv_region / tile_int8_slice of
+    src/LFM3/build_lfm3_int8_pkg.py:95-108, 171-224 (imported with its flatbuffer / compiler
+    dependencies stubbed, since those only serve the .model patching).  The NVDLA-tiled weight
+    bytes it writes are un-tiled with the inverse of its (0, 2, 3, 4, 1, 5) transpose.
+  * boundary_*.npz      -- pack_npu_input_int8[_dyntok] / unpack_npu_output_int8[_dyntok] of
+    src/LFM3/lfm3_v2.cpp (compiled by oracle/Makefile into oracle/_ref/libref.so).
+  * requant_kat.npz     -- the CvtPrecision_QuantM expression as the reference's float64 torch
+    simulation writes it, round(acc * (QuantM / 2^trunc)) clamped to +-Qmax
+    (src/LFM3/attribute_int8_error.py:104-122), over hand-picked edge cases.
+  * sampler_kat.npz     -- Sampler::sample greedy (oracle/_ref/libref.so) on the vector of
+    src/eswin_runtime/tests/test_tokenizer_sampler.cpp:19-31 plus tie cases.
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parent.parent
+sys.path.insert(0, str(ROOT))
+
+from oracle import oracle as O  # noqa: E402
+
+
+class _Region:
+    """Stand-in for the weight region the builder reads from a .model template."""
+
+    def __init__(self, n_rows: int, k: int, slice_rows: int = 512):
+        k_pad = ((k + 95) // 96) * 96
+        self.n_slices = (n_rows + slice_rows - 1) // slice_rows
+        self.offsets, self.contents, off = [], [], 0
+        self.slice_rows = []
+        for s in range(self.n_slices):
+            m = min(slice_rows, n_rows - s * slice_rows)
+            self.slice_rows.append(m)
+            self.offsets += [off, off + m * k_pad]
+            self.contents += ["weights", "quant_m"]
+            off += m * k_pad + 2 * m
+        self.size = off
+        self.k_pad = k_pad
+
+
+def import_builder(ref: Path):
+    sys.path.insert(0, str(ref / "src" / "LFM3"))
+    for name in ("backend", "backend.flatbuffer_emitter", "backend.dynamic_weight_binding"):
+        sys.modules.setdefault(name, types.ModuleType(name))
+    sys.modules["backend.flatbuffer_emitter"].ModelReader = object
+    sys.modules["backend.flatbuffer_emitter"].ModelWriter = object
+    sys.modules["backend.dynamic_weight_binding"].find_weight_regions = lambda m: None
+    import build_lfm3_int8_pkg as builder  # noqa: E402
+    return builder
+
+
+def untile_int8(raw: bytes, m: int, k: int, k_pad: int) -> np.ndarray:
+    """Inverse of reshape(M/8, 8, Kp/96, 3, 8, 4).transpose(0, 2, 3, 4, 1, 5)."""
+    a = np.frombuffer(raw, dtype=np.int8).reshape(m // 8, k_pad // 96, 3, 8, 8, 4)
+    return a.transpose(0, 4, 1, 2, 3, 5).reshape(m, k_pad)[:, :k].copy()
+
+
+def seeded_inputs(n: int, k: int, seed: int):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((64, k)).astype(np.float32)
+    out_ch = rng.choice(k, size=max(1, k // 100), replace=False)
+    x[:, out_ch] *= 20.0
+    return w, x
+
+
+def make_quant_linear(builder, n: int, k: int, trunc: int, seed: int, path: Path) -> None:
+    w, x = seeded_inputs(n, k, seed)
+    reg = _Region(n, k)
+    buf, in_t, in_s, in_inv_smooth, out_step_chan = builder.build_single_conv_region(
+        w, torch.from_numpy(x), None, trunc, cached_reg=reg)
+    wq = np.empty((n, k), np.int8)
+    qm = np.empty((n,), np.int16)
+    for s in range(reg.n_slices):
+        m = reg.slice_rows[s]
+        r0 = s * 512
+        wo, qo = reg.offsets[2 * s], reg.offsets[2 * s + 1]
+        wq[r0:r0 + m] = untile_int8(buf[wo:wo + m * reg.k_pad], m, k, reg.k_pad)
+        qm[r0:r0 + m] = np.frombuffer(buf[qo:qo + 2 * m], dtype=np.int16)
+    np.savez_compressed(path, w=w, calib_x=x, trunc=np.int32(trunc), wq=wq, quant_m=qm,
+                        in_thresh=np.float64(in_t), in_step=np.float64(in_s),
+                        in_inv_smooth=in_inv_smooth.astype(np.float32),
+                        out_step_chan=out_step_chan.astype(np.float32))
+    print(f"{path.name}: N={n} K={k} trunc={trunc} in_t={in_t:.6f} qm[{qm.min()}, {qm.max()}]")
+
+
+def make_boundary(path: Path, T: int, K: int, N: int, seed: int) -> None:
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, K)).astype(np.float32)
+    x[:, rng.choice(K, size=max(1, K // 100), replace=False)] *= 20.0
+    # edge values: exact halves after scaling are produced by in_step = 1 on x = +-k.5
+    x[0, :8] = np.array([0.5, 1.5, 2.5, -0.5, -1.5, 126.5, -126.5, 1000.0], np.float32)
+    s = (rng.random(K).astype(np.float32) * 2.0 + 0.05).astype(np.float32)
+    s[:8] = 1.0
+    q_static = O.ref_pack(x, 1.0, s)
+    q_static_nosmooth = O.ref_pack(x, 0.037, None)
+    q_dyn, ratio = O.ref_pack_dyntok(x, 4.25, s)
+    yq = rng.integers(-127, 128, size=(T, N)).astype(np.int8)
+    osc = (rng.random(N).astype(np.float32) * 0.01 + 1e-4).astype(np.float32)
+    y_static = O.ref_unpack(yq, 0.0123, osc, None)
+    y_static_scalar = O.ref_unpack(yq, 0.0123, None, None)
+    y_dyn = O.ref_unpack(yq, 0.0123, osc, ratio)
+    y_dyn_scalar = O.ref_unpack(yq, 0.0123, None, ratio)
+    yq16 = rng.integers(-32767, 32768, size=(T, N)).astype(np.int16)
+    y16 = O.ref_unpack_i16(yq16, 0.0007, osc)
+    np.savez_compressed(path, x=x, inv_smooth=s, q_static=q_static,
+                        q_static_nosmooth=q_static_nosmooth, q_dyn=q_dyn, ratio=ratio, yq=yq,
+                        out_step_chan=osc, y_static=y_static, y_static_scalar=y_static_scalar,
+                        y_dyn=y_dyn, y_dyn_scalar=y_dyn_scalar, yq16=yq16, y16=y16)
+    print(f"{path.name}: T={T} K={K} N={N}")
+
+
+def make_requant_kat(path: Path) -> None:
+    cases = []
+    for trunc in (0, 1, 14, 15, 22, 23, 25, 26, 28):
+        half = 1 << max(trunc - 1, 0)
+        for qm in (1, 2, 3, 127, 4096, 32767):
+            for acc in (0, 1, -1, half, -half, 3 * half, -3 * half, 2**31 - 1, -2**31, 127 << trunc,
+                        (127 << trunc) + half, -(127 << trunc) - half, 1000, -1000, 123456789):
+                acc = int(np.clip(acc, -2**31, 2**31 - 1))
+                cases.append((acc, qm, trunc))
+    acc = np.array([c[0] for c in cases], np.int64)
+    qm = np.array([c[1] for c in cases], np.int64)
+    tr = np.array([c[2] for c in cases], np.int64)
+    out = {}
+    for qmax in (127, 32767):
+        a = torch.from_numpy(acc).double()
+        scale = torch.from_numpy(qm).double() / torch.from_numpy((1 << tr).astype(np.float64))
+        out[f"yq_{qmax}"] = torch.clamp(torch.round(a * scale), -float(qmax), float(qmax)).long().numpy()
+    # CACC saturation known answer (src/eswin_simulator/tests/test_cmac_cacc.py:137-149):
+    # QuantM = 1, trunc = 0 passes acc through; the SDP rule saturates symmetrically at +-127.
+    cacc = np.array([-1000, -200, -128, 0, 50, 127, 200, 1000], np.int64)
+    np.savez_compressed(path, acc=acc.astype(np.int32), quant_m=qm.astype(np.int16),
+                        trunc=tr.astype(np.int32), cacc_acc=cacc.astype(np.int32), **out)
+    print(f"{path.name}: {len(cases)} cases")
+
+
+def make_sampler_kat(path: Path) -> None:
+    rows = [
+        np.array([1.0, 2.5, 0.5, 8.2, 3.1], np.float32),          # test_tokenizer_sampler.cpp:22
+        np.array([3.0, 7.0, 7.0, 1.0, 7.0], np.float32),          # ties: lowest id wins
+        np.array([-5.0, -1.0, -1.0, -3.0], np.float32),
+        np.array([0.0, -0.0, 0.0], np.float32),
+    ]
+    rng = np.random.default_rng(7)
+    big = rng.integers(-127, 128, size=4096).astype(np.float32) * 0.25  # int8-like logits, many ties
+    rows.append(big)
+    greedy = np.array([O.ref_greedy(r) for r in rows], np.int32)
+    lens = np.array([len(r) for r in rows], np.int32)
+    np.savez_compressed(path, logits=np.concatenate(rows), lens=lens, greedy=greedy)
+    print(f"{path.name}: greedy={greedy.tolist()}")
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    args = ap.parse_args()
+    ref = Path(args.ref)
+    O.build()
+    builder = import_builder(ref)
+    make_quant_linear(builder, 136, 160, 22, 11, HERE / "quant_linear_n136_k160_t22.npz")
+    make_quant_linear(builder, 520, 96, 23, 12, HERE / "quant_linear_n520_k96_t23.npz")
+    make_boundary(HERE / "boundary_t1.npz", 1, 576, 192, 21)
+    make_boundary(HERE / "boundary_t5.npz", 5, 192, 64, 22)
+    make_requant_kat(HERE / "requant_kat.npz")
+    make_sampler_kat(HERE / "sampler_kat.npz")
+
+
+if __name__ == "__main__":
+    main()
