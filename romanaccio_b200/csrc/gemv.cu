@@ -30,7 +30,8 @@ namespace {
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxStages = 8;
-constexpr size_t kMaxDynSmem = 232448;  // 227 KB opt-in per block on sm_100
+// 227 KB opt-in per block on sm_100, less a margin for the kernels' static shared memory.
+constexpr size_t kMaxDynSmem = 232448 - 1024;
 
 struct GemvArgs {
   const int8_t *w;
@@ -355,13 +356,22 @@ __global__ void __launch_bounds__(kThreads, TOPK ? 1 : 2) gemv_w8a8_kernel(const
 template <int TT, int RPW, bool TOPK>
 cudaError_t launch_one(const GemvArgs &args, const GemvPlan &plan, cudaStream_t stream, bool pdl) {
   auto kern = gemv_w8a8_kernel<TT, RPW, TOPK>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDynSmem);
+  // Opt in once to the largest dynamic shared memory the device allows next to this kernel's
+  // static shared memory.
+  static int max_dyn = -1;
+  if (max_dyn < 0) {
+    int dev = 0, optin = 0;
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kern);
     if (e != cudaSuccess) return e;
-    configured = true;
+    const int limit = optin - static_cast<int>(fa.sharedSizeBytes);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
+    if (e != cudaSuccess) return e;
+    max_dyn = limit;
   }
+  if (plan.smem > static_cast<size_t>(max_dyn)) return cudaErrorInvalidValue;
   return launch_ex(kern, dim3(plan.grid), dim3(kThreads), plan.smem, stream, pdl, args);
 }
 

@@ -21,7 +21,8 @@ import torch
 
 from ._lib import DTYPE_INT8, OUT_F32, OUT_F32_ACC
 from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
-from .lmhead import LmHeadShard, shard_range
+from .lmhead import (LmHeadShard, candidate_buffers, exchange_candidates, shard_range,
+                     token_candidates)
 from .quantize import build_linear
 from .synth import DecodeShape, activations, outlier_channels
 
@@ -102,8 +103,7 @@ class DecodeStack:
         self.outs = [torch.empty((self.T, N), dtype=torch.float32, device=dev)
                      for (_, _, N, _) in self.subgraphs]
         self.h_all = torch.empty((T_all, K), dtype=torch.float32, device=dev)
-        self.cand = torch.empty((2, T_all, self.k), dtype=torch.int32, device=dev)
-        self.cand_all = torch.empty((self.world, 2, T_all, self.k), dtype=torch.int32, device=dev)
+        self.cand, self.cand_all = candidate_buffers(T_all, self.k, self.world, dev)
         self.ids = torch.empty((self.T,), dtype=torch.int32, device=dev)
         self.top_val = torch.empty((self.T, self.k), dtype=torch.float32, device=dev)
         self.top_idx = torch.empty((self.T, self.k), dtype=torch.int32, device=dev)
@@ -147,10 +147,8 @@ class DecodeStack:
         dist.all_gather_into_tensor(self.h_all, h, group=self.group)
         self.lm.forward(self.h_all, self.k, OUT_F32_ACC, val=self.cand[0].view(torch.float32),
                         idx=self.cand[1])
-        dist.all_gather_into_tensor(self.cand_all, self.cand, group=self.group)
-        t0 = self.rank * self.T
-        vals = self.cand_all[:, 0, t0:t0 + self.T].view(torch.float32).permute(1, 0, 2)
-        ids = self.cand_all[:, 1, t0:t0 + self.T].permute(1, 0, 2)
+        exchange_candidates(self.cand, self.cand_all, self.group)
+        vals, ids = token_candidates(self.cand_all, self.world, self.rank * self.T, self.T)
         v, i, a = topk_merge(self.ctx, vals, ids, self.k)
         self.top_val.copy_(v)
         self.top_idx.copy_(i)

@@ -26,6 +26,29 @@ def shard_range(V: int, n: int, r: int) -> tuple[int, int]:
     return (r * V) // n, ((r + 1) * V) // n
 
 
+def candidate_buffers(T_all: int, k: int, world: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """(local [2, T_all, k], gathered [world * 2, T_all, k]) int32 exchange buffers; row 0 of a
+    pair holds the float32 values bit-cast, row 1 the vocab ids."""
+    local = torch.empty((2, T_all, k), dtype=torch.int32, device=device)
+    gathered = torch.empty((world * 2, T_all, k), dtype=torch.int32, device=device)
+    return local, gathered
+
+
+def exchange_candidates(local: torch.Tensor, gathered: torch.Tensor, group=None) -> None:
+    """All-gather every shard's [2, T_all, k] candidate block (k * 8 bytes per token per shard)."""
+    import torch.distributed as dist
+
+    dist.all_gather_into_tensor(gathered, local, group=group)
+
+
+def token_candidates(gathered: torch.Tensor, world: int, t0: int, T: int):
+    """[T, world, k] views (values, ids) of tokens [t0, t0 + T) in the gathered block."""
+    g = gathered.view(world, 2, gathered.shape[1], gathered.shape[2])
+    vals = g[:, 0, t0:t0 + T].view(torch.float32).permute(1, 0, 2)
+    ids = g[:, 1, t0:t0 + T].permute(1, 0, 2)
+    return vals, ids
+
+
 class LmHeadShard:
     """This rank's block of vocab rows as a W8A8 linear whose output is a top-k list."""
 
@@ -79,12 +102,12 @@ class VocabShardedLmHead:
     def _buffers(self, T: int, k: int, device) -> tuple[torch.Tensor, torch.Tensor]:
         key = (T, k)
         if key not in self._bufs:
-            local = torch.empty((2, T, k), dtype=torch.int32, device=device)
-            gathered = torch.empty((self.world, 2, T, k), dtype=torch.int32, device=device)
-            self._bufs[key] = (local, gathered)
+            self._bufs[key] = candidate_buffers(T, k, self.world, device)
         return self._bufs[key]
 
     def forward(self, h: torch.Tensor, k: int = 40, out_mode: int = OUT_F32_ACC, stream=None):
+        """h: the same [T, K] hidden states on every rank (the reference broadcasts the final
+        hidden state into both dies' input buffers)."""
         assert self.shard is not None, "load_shard() first"
         T = h.shape[0]
         if self.world == 1:
@@ -93,8 +116,6 @@ class VocabShardedLmHead:
         local, gathered = self._buffers(T, k, h.device)
         self.shard.forward(h, k, out_mode=out_mode, val=local[0].view(torch.float32),
                            idx=local[1], stream=stream)
-        import torch.distributed as dist
-        dist.all_gather_into_tensor(gathered, local, group=self.group)
-        vals = gathered[:, 0].view(torch.float32).permute(1, 0, 2)  # [T, world, k]
-        ids = gathered[:, 1].permute(1, 0, 2)
+        exchange_candidates(local, gathered, self.group)
+        vals, ids = token_candidates(gathered, self.world, 0, T)
         return topk_merge(self.ctx, vals, ids, k, stream=stream)
