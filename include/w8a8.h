@@ -205,6 +205,35 @@ w8a8_status w8a8_topk_merge(w8a8_ctx *ctx, const float *in_val_dev, const int32_
                             int64_t token_stride, int32_t k_out, float *out_val_dev,
                             int32_t *out_idx_dev, int32_t *argmax_dev, void *stream);
 
+/* Allocation-free LM-head shard top-k.  This entry point has no counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc: code running inside an allocator or memory-pool
+ * callback, plugins whose host process owns every device allocation, and hot paths that must
+ * not take the driver's allocation locks.  It computes what w8a8_linear_forward_topk computes
+ * for a static-input shard in F32_ACC mode (logit = float(acc) * acc_step[n]), but takes the
+ * weights and parameters as device pointers (no w8a8_linear, no w8a8_ctx) and keeps its scratch
+ * (int8 activations, per-CTA candidate lists, arrival counter) in one module-scope device array
+ * of about 513 KiB that every GPU loading the library holds until the process exits.  It calls
+ * no cudaMalloc, cudaFree or allocating library routine.
+ *
+ * w_dev: int8 [N, ldw] on the current device, 16-byte aligned, ldw a multiple of 16 and
+ * >= round_up(K, 16) (bytes past K in a row may hold anything).  acc_step_dev: fp32 [N].
+ * x_dev: fp32 [T, ldx].  in_step: static input step (q = RNE(clamp(x * (1 / in_step), +-127))).
+ * Outputs topk_val_dev fp32 [T, k], topk_idx_dev int32 [T, k] (ids = row_offset + n), sorted
+ * (value desc, id asc).  Limits: T <= 8, T * round_up(K, 16) <= 128 KiB, and
+ * T * (CTAs of the launch, at most one per SM) * k <= 49152 candidate keys; larger requests
+ * return W8A8_ERR_INVALID_ARG with the reason in w8a8_last_error().
+ *
+ * The first call on a device resolves the scratch array's device address (with that device
+ * current); make that first call before any stream capture.  Every call on a device shares the
+ * array and it keeps the last call's contents: calls whose executions overlap on the GPU race
+ * and corrupt each other's results, so order them on one stream.  A bounded in-kernel wait that
+ * runs out is not reported by this entry point (it has no context). */
+w8a8_status w8a8_lmhead_topk_noalloc(const int8_t *w_dev, int64_t ldw, int32_t K, int32_t N,
+                                     const float *acc_step_dev, float in_step, const float *x_dev,
+                                     int64_t ldx, int32_t T, int32_t k, int32_t row_offset,
+                                     float *topk_val_dev, int32_t *topk_idx_dev, void *stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

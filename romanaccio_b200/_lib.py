@@ -75,6 +75,8 @@ SIGNATURES = {
     "w8a8_linear_forward_topk": (
         C.c_int, [_P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _I64, _P]),
     "w8a8_topk_merge": (C.c_int, [_P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I32, _P, _P, _P, _P]),
+    "w8a8_lmhead_topk_noalloc": (
+        C.c_int, [_P, _I64, _I32, _I32, _P, C.c_float, _P, _I64, _I32, _I32, _I32, _P, _P, _P]),
 }
 
 

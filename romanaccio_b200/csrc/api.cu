@@ -53,6 +53,10 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
+namespace w8a8 {
+void set_last_error(const char *msg) { g_last_error = msg ? msg : ""; }
+}  // namespace w8a8
+
 struct w8a8_ctx {
   int device = 0;
   int sm_count = 0;

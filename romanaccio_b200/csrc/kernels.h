@@ -131,6 +131,9 @@ struct MergeLaunch {
 };
 cudaError_t launch_topk_merge(const MergeLaunch &L, cudaStream_t stream);
 
+// Records `msg` as the calling thread's w8a8_last_error() text (defined in api.cu).
+void set_last_error(const char *msg);
+
 // Launch helper: cudaLaunchKernelEx with the programmatic-stream-serialisation attribute.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
