@@ -205,6 +205,50 @@ w8a8_status w8a8_topk_merge(w8a8_ctx *ctx, const float *in_val_dev, const int32_
                             int64_t token_stride, int32_t k_out, float *out_val_dev,
                             int32_t *out_idx_dev, int32_t *argmax_dev, void *stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Decode chain: a fixed sequence of linears, optionally ending with an LM-head top-k step, run
+ * by ONE persistent cooperative kernel launch per forward.  Replaces the per-linear
+ * pack -> submit_task -> unpack round trips of the reference's decode loop
+ * (Lfm3Engine::forward_chunk, lfm3_v2.cpp:1743-1990; TransformerSession::step,
+ * transformer_session.cpp:650-844).  All pointers are fixed at create time (like a recorded
+ * graph); a step whose input or output overlaps an earlier step's buffers since the last grid
+ * barrier gets a barrier in front of it.  The linears must outlive the chain.
+ * ------------------------------------------------------------------------------------- */
+typedef struct {
+    w8a8_linear *linear;       /* weights + parameters of this step */
+    const float *x_dev;        /* fp32 [T, ldx] input view (chain input or a slice of an earlier y) */
+    int64_t      ldx;
+    int32_t      act_mode;     /* w8a8_act_mode */
+    int32_t      out_mode;     /* w8a8_out_mode (F32 or F32_ACC for a top-k step) */
+    void        *y_dev;        /* [T, ldy] output per out_mode (unused by a top-k step) */
+    int64_t      ldy;
+    float       *ratio_dev;    /* optional [T] per-token ratios (DYNTOK), may be NULL */
+    int32_t      topk_k;       /* 0, or k (1..64) for an LM-head step; must be the last step */
+    int32_t      row_offset;   /* top-k: vocab id of the linear's row 0 */
+    float       *topk_val_dev; /* top-k: [T, k] */
+    int32_t     *topk_idx_dev; /* top-k: [T, k] */
+} w8a8_chain_step;
+
+typedef struct w8a8_chain w8a8_chain;
+
+/* T in [1, 8].  Returns W8A8_ERR_NOT_SUPPORTED when the steps do not fit the kernel's shared
+ * memory plan. */
+w8a8_status w8a8_chain_create(w8a8_ctx *ctx, const w8a8_chain_step *steps, int32_t n_steps,
+                              int32_t T, w8a8_chain **out_chain);
+/* Runs every step once, asynchronously on `stream` (one memset + one kernel launch). */
+w8a8_status w8a8_chain_forward(w8a8_chain *chain, void *stream);
+void        w8a8_chain_destroy(w8a8_chain *chain);
+/* Number of grid barriers the chain executes per forward. */
+int32_t     w8a8_chain_barriers(const w8a8_chain *chain);
+/* Number of CTAs of the chain kernel (one per SM). */
+int32_t     w8a8_chain_grid(const w8a8_chain *chain);
+/* Per-step stage timers, the counterpart of the reference's StageTimers (lfm3_v2.cpp:431-530):
+ * when trace_dev is non-NULL, every forward writes uint64 %globaltimer stamps (ns) into
+ * trace_dev[(cta * n_steps + step) * 8 + i]: i = 0 step entered (after its grid barrier),
+ * 1 input quantised, 2 outputs written, 3 arrival published, 4 / 5 first / last weight copy of
+ * the step issued, 6 first weight stage of the step landed.  NULL turns tracing off. */
+w8a8_status w8a8_chain_set_trace(w8a8_chain *chain, unsigned long long *trace_dev);
+
 /* Allocation-free LM-head shard top-k.  This entry point has no counterpart in the reference.
  *
  * For callers that cannot call cudaMalloc: code running inside an allocator or memory-pool

@@ -55,6 +55,23 @@ class LinearDesc(C.Structure):
     ]
 
 
+class ChainStep(C.Structure):
+    _fields_ = [
+        ("linear", C.c_void_p),
+        ("x_dev", C.c_void_p),
+        ("ldx", C.c_int64),
+        ("act_mode", C.c_int32),
+        ("out_mode", C.c_int32),
+        ("y_dev", C.c_void_p),
+        ("ldy", C.c_int64),
+        ("ratio_dev", C.c_void_p),
+        ("topk_k", C.c_int32),
+        ("row_offset", C.c_int32),
+        ("topk_val_dev", C.c_void_p),
+        ("topk_idx_dev", C.c_void_p),
+    ]
+
+
 # name -> (restype, argtypes); every symbol include/w8a8.h declares.
 _P, _I32, _I64, _SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_size_t
 SIGNATURES = {
@@ -75,6 +92,12 @@ SIGNATURES = {
     "w8a8_linear_forward_topk": (
         C.c_int, [_P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _I64, _P]),
     "w8a8_topk_merge": (C.c_int, [_P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I32, _P, _P, _P, _P]),
+    "w8a8_chain_create": (C.c_int, [_P, C.POINTER(ChainStep), _I32, _I32, C.POINTER(_P)]),
+    "w8a8_chain_forward": (C.c_int, [_P, _P]),
+    "w8a8_chain_destroy": (None, [_P]),
+    "w8a8_chain_barriers": (_I32, [_P]),
+    "w8a8_chain_grid": (_I32, [_P]),
+    "w8a8_chain_set_trace": (C.c_int, [_P, _P]),
     "w8a8_lmhead_topk_noalloc": (
         C.c_int, [_P, _I64, _I32, _I32, _P, C.c_float, _P, _I64, _I32, _I32, _I32, _P, _P, _P]),
 }

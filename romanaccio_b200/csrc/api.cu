@@ -578,3 +578,205 @@ w8a8_status w8a8_topk_merge(w8a8_ctx *ctx, const float *in_val, const int32_t *i
 }
 
 }  // extern "C"
+
+struct w8a8_chain {
+  w8a8_ctx *ctx = nullptr;
+  int n_ops = 0, T = 0, barriers = 0;
+  size_t clear_bytes = 0;
+  unsigned long long *trace = nullptr;
+  ChainPlan plan = {};
+  ChainOp *ops_dev = nullptr;
+  unsigned *bar = nullptr;
+  unsigned *tk_counter = nullptr;
+  uint64_t *lists = nullptr;
+};
+
+namespace {
+
+struct Range {
+  uintptr_t lo, hi;
+};
+
+Range view_range(const void *p, int64_t ld, int rows, int cols, size_t elem) {
+  const uintptr_t b = reinterpret_cast<uintptr_t>(p);
+  return {b, b + (static_cast<uintptr_t>(rows - 1) * ld + cols) * elem};
+}
+
+bool overlap(const Range &a, const Range &b) { return a.lo < b.hi && b.lo < a.hi; }
+
+void chain_free(w8a8_chain *c) {
+  if (!c) return;
+  DeviceGuard g(c->ctx ? c->ctx->device : 0);
+  cudaFree(c->ops_dev);
+  cudaFree(c->bar);
+  cudaFree(c->tk_counter);
+  cudaFree(c->lists);
+  delete c;
+}
+
+size_t out_elem_bytes(const w8a8_linear *l, int out_mode) {
+  return out_mode == W8A8_OUT_QUANT ? (l->out_i16 ? 2 : 1) : 4;
+}
+
+}  // namespace
+
+extern "C" {
+
+w8a8_status w8a8_chain_create(w8a8_ctx *ctx, const w8a8_chain_step *steps, int32_t n, int32_t T,
+                              w8a8_chain **out) {
+  if (!out) return fail(W8A8_ERR_INVALID_ARG, "out_chain is NULL");
+  *out = nullptr;
+  if (!ctx || !steps || n < 1) return fail(W8A8_ERR_INVALID_ARG, "ctx/steps NULL or n_steps < 1");
+  if (T < 1 || T > 8) return fail(W8A8_ERR_INVALID_ARG, "T=%d outside [1, 8]", T);
+  std::vector<ChainOp> ops(n);
+  std::vector<Range> epoch_in, epoch_out;
+  int barriers = 0;
+  int topk_k = 0;
+  for (int s = 0; s < n; ++s) {
+    const w8a8_chain_step &st = steps[s];
+    const w8a8_linear *l = st.linear;
+    if (!l || l->ctx != ctx) return fail(W8A8_ERR_INVALID_ARG, "step %d: linear NULL or of another context", s);
+    if (!st.x_dev || st.ldx < l->K) return fail(W8A8_ERR_INVALID_ARG, "step %d: x NULL or ldx < K", s);
+    w8a8_status ms = check_modes(l, st.act_mode, st.out_mode);
+    if (ms != W8A8_SUCCESS) return ms;
+    const bool topk = st.topk_k != 0;
+    if (topk) {
+      if (s != n - 1) return fail(W8A8_ERR_INVALID_ARG, "step %d: the top-k step must be last", s);
+      if (st.topk_k < 1 || st.topk_k > W8A8_TOPK_MAX || st.topk_k > l->N)
+        return fail(W8A8_ERR_INVALID_ARG, "step %d: k=%d outside [1, min(64, N)]", s, st.topk_k);
+      if (!st.topk_val_dev || !st.topk_idx_dev) return fail(W8A8_ERR_INVALID_ARG, "step %d: top-k outputs NULL", s);
+      if (st.out_mode != W8A8_OUT_F32 && st.out_mode != W8A8_OUT_F32_ACC)
+        return fail(W8A8_ERR_INVALID_ARG, "step %d: top-k needs F32 or F32_ACC", s);
+      if (st.row_offset < 0) return fail(W8A8_ERR_INVALID_ARG, "step %d: negative row_offset", s);
+      topk_k = st.topk_k;
+    } else if (!st.y_dev || st.ldy < l->N) {
+      return fail(W8A8_ERR_INVALID_ARG, "step %d: y NULL or ldy < N", s);
+    }
+    ChainOp &op = ops[s];
+    op = ChainOp{};
+    op.w = l->w;
+    op.ldw = l->k_pad;
+    op.N = l->N;
+    op.K = l->K;
+    op.k_pad = l->k_pad;
+    op.x = st.x_dev;
+    op.ldx = st.ldx;
+    op.inv_smooth = l->inv_smooth;
+    op.vec_x = (l->K % 4 == 0) && (st.ldx % 4 == 0) && aligned16(st.x_dev) ? 1 : 0;
+    op.act_mode = st.act_mode;
+    op.inv_step = l->inv_step;
+    op.safe_thresh = l->safe_thresh;
+    op.ratio_out = st.ratio_dev;
+    op.out_mode = st.out_mode;
+    op.quant_m = l->quant_m;
+    op.trunc = l->trunc;
+    op.qmax = l->qmax;
+    op.out_i16 = l->out_i16;
+    op.out_step = l->out_step;
+    op.acc_step = l->acc_step;
+    op.y = topk ? nullptr : st.y_dev;
+    op.ldy = st.ldy;
+    op.topk = topk ? 1 : 0;
+    op.tk.k = st.topk_k;
+    op.tk.row_offset = st.row_offset;
+    op.tk.val = st.topk_val_dev;
+    op.tk.idx = st.topk_idx_dev;
+    // hazards against the steps since the last barrier: RAW (x vs y), WAR (y vs x), WAW
+    const Range xin = view_range(st.x_dev, st.ldx, T, l->K, 4);
+    Range yout = {0, 0};
+    if (!topk) yout = view_range(st.y_dev, st.ldy, T, l->N, out_elem_bytes(l, st.out_mode));
+    bool need = false;
+    for (const Range &r : epoch_out) need = need || overlap(r, xin) || (!topk && overlap(r, yout));
+    for (const Range &r : epoch_in) need = need || (!topk && overlap(r, yout));
+    if (need && s > 0) {
+      op.barrier_before = 1;
+      ++barriers;
+      epoch_in.clear();
+      epoch_out.clear();
+    }
+    epoch_in.push_back(xin);
+    if (!topk) epoch_out.push_back(yout);
+  }
+  ChainPlan plan;
+  if (!plan_chain(ops.data(), n, T, ctx->sm_count, &plan))
+    return fail(W8A8_ERR_NOT_SUPPORTED, "the chain does not fit the persistent kernel's shared memory plan");
+  DeviceGuard g(ctx->device);
+  w8a8_chain *c = new (std::nothrow) w8a8_chain();
+  if (!c) return fail(W8A8_ERR_NO_MEMORY, "host allocation failed");
+  c->ctx = ctx;
+  c->n_ops = n;
+  c->T = T;
+  c->barriers = barriers;
+  c->plan = plan;
+  w8a8_status st;
+  // zero-at-launch region: n arrival counters, then n amax slots of 8 floats
+  c->clear_bytes = sizeof(unsigned) * n + sizeof(float) * 8 * n;
+  if ((st = dev_alloc(&c->ops_dev, n, nullptr)) != W8A8_SUCCESS ||
+      (st = dev_alloc(&c->bar, c->clear_bytes / sizeof(unsigned), nullptr)) != W8A8_SUCCESS ||
+      (st = dev_alloc(&c->tk_counter, 1, nullptr)) != W8A8_SUCCESS ||
+      (st = dev_alloc(&c->lists, static_cast<size_t>(T) * plan.grid * std::max(topk_k, 1), nullptr)) !=
+          W8A8_SUCCESS) {
+    chain_free(c);
+    return st;
+  }
+  // amax hand-off: a dyntok step whose input is a column block of exactly one earlier fp32
+  // output (the latest step writing that memory) gets its per-token max |x * s| reduced by
+  // that producer's epilogue, so it reads x once instead of twice.
+  float *amax_dev = reinterpret_cast<float *>(c->bar + n);
+  for (int s = 1; s < n; ++s) {
+    const w8a8_chain_step &cs = steps[s];
+    if (cs.act_mode != W8A8_ACT_DYNTOK) continue;
+    const Range xin = view_range(cs.x_dev, cs.ldx, T, cs.linear->K, 4);
+    int j = -1;
+    for (int q = s - 1; q >= 0 && j < 0; --q) {
+      if (steps[q].topk_k) continue;
+      const Range yq = view_range(steps[q].y_dev, steps[q].ldy, T, steps[q].linear->N,
+                                  out_elem_bytes(steps[q].linear, steps[q].out_mode));
+      if (overlap(xin, yq)) j = q;
+    }
+    if (j < 0 || steps[j].out_mode != W8A8_OUT_F32 || steps[j].ldy != cs.ldx || ops[j].amax_dst)
+      continue;
+    const ptrdiff_t off = static_cast<const float *>(cs.x_dev) - static_cast<const float *>(steps[j].y_dev);
+    if (off < 0 || off + cs.linear->K > steps[j].linear->N) continue;
+    ops[j].amax_dst = amax_dev + 8 * s;
+    ops[j].amax_c0 = static_cast<int>(off);
+    ops[j].amax_cols = cs.linear->K;
+    ops[j].amax_smooth = cs.linear->inv_smooth;
+    ops[s].amax_src = amax_dev + 8 * s;
+  }
+  if (cudaMemcpy(c->ops_dev, ops.data(), sizeof(ChainOp) * n, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemset(c->tk_counter, 0, sizeof(unsigned)) != cudaSuccess) {
+    chain_free(c);
+    return fail(W8A8_ERR_CUDA, "chain upload failed");
+  }
+  const cudaError_t e = configure_chain(plan);
+  if (e != cudaSuccess) {
+    chain_free(c);
+    return cuda_fail(e, "configure_chain");
+  }
+  *out = c;
+  return W8A8_SUCCESS;
+}
+
+w8a8_status w8a8_chain_forward(w8a8_chain *c, void *stream) {
+  if (!c) return fail(W8A8_ERR_INVALID_ARG, "chain is NULL");
+  DeviceGuard g(c->ctx->device);
+  W8A8_CUDA(launch_chain(c->ops_dev, c->n_ops, c->T, c->plan, c->bar, c->clear_bytes,
+                         c->tk_counter, c->lists, c->ctx->d_err, c->trace,
+                         static_cast<cudaStream_t>(stream)));
+  return W8A8_SUCCESS;
+}
+
+w8a8_status w8a8_chain_set_trace(w8a8_chain *c, unsigned long long *trace_dev) {
+  if (!c) return fail(W8A8_ERR_INVALID_ARG, "chain is NULL");
+  c->trace = trace_dev;
+  return W8A8_SUCCESS;
+}
+
+int32_t w8a8_chain_grid(const w8a8_chain *c) { return c ? c->plan.grid : 0; }
+
+void w8a8_chain_destroy(w8a8_chain *c) { chain_free(c); }
+
+int32_t w8a8_chain_barriers(const w8a8_chain *c) { return c ? c->barriers : 0; }
+
+}  // extern "C"

@@ -1,0 +1,733 @@
+// Persistent decode-chain kernel: a whole sequence of W8A8 linears (and optionally the LM-head
+// shard with its top-k) in ONE cooperative launch.
+//
+// It replaces the per-token sequence of NPU submits of the reference's decode loop
+// (Lfm3Engine::forward_chunk, src/LFM3/lfm3_v2.cpp:1743-1990; TransformerSession::step,
+// src/eswin_runtime/src/llm/transformer_session.cpp:650-844), where every linear is a separate
+// pack -> submit_task -> unpack round trip with ~0.41 ms of fixed overhead (FINDINGS.md:1883).
+//
+// One CTA per SM, 8 consumer warps + 1 producer warp.  The producer warp streams the int8
+// weight slabs of every step this CTA owns, step after step, through an NS-deep shared-memory
+// ring with 1-D bulk copies (TMA engine, no tensor map, no multicast) completing on mbarriers.
+// Weights do not depend on activations, so the producer runs ahead into the next linears while
+// the consumers are still busy or waiting: HBM never idles at a linear boundary.  Consumers,
+// per step: wait at a grid barrier when the step reads an earlier step's output, quantise the
+// step's fp32 input into shared memory (dyntok amax / static step, the reference's
+// pack_npu_input_int8[_dyntok] arithmetic), run dp4a over the landed slabs, and apply the
+// requant / unpack epilogue (or keep LM-head logits on chip for the per-CTA top-k and the
+// last-CTA merge).  The grid barrier is a per-step arrival counter (release: fence + atomic
+// add; acquire: ld.acquire spin, bounded by 2 s of %globaltimer).
+#include "common.cuh"
+#include "kernels.h"
+
+#include <algorithm>
+
+namespace w8a8 {
+
+namespace {
+
+constexpr int kCW = 8;              // consumer warps
+constexpr int kCT = kCW * 32;       // consumer threads
+constexpr int kThreads = kCT + 32;  // + producer warp
+constexpr int kMaxStages = 8;
+
+struct ChainArgs {
+  const ChainOp *ops;
+  int n_ops;
+  int T;
+  unsigned *bar;      // [n_ops] arrival counters, zero at launch
+  unsigned *tk_counter;
+  uint64_t *lists;
+  int *err;
+  int ns;
+  uint32_t stage_bytes;
+  int kpad_max;
+  int cand_cap;
+  uint32_t ring_bytes;
+  unsigned long long *trace;  // optional [grid][n_ops][8] %globaltimer stamps
+};
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void split_range(int total, int parts, int idx, int &b, int &e) {
+  b = static_cast<int>((static_cast<long long>(total) * idx) / parts);
+  e = static_cast<int>((static_cast<long long>(total) * (idx + 1)) / parts);
+}
+
+// Descending bitonic sort of n (power of two) keys by the consumer threads only.
+__device__ void consumer_bitonic_desc(uint64_t *s, int n, int tid) {
+  consumer_sync();
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < n; i += kCT) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint64_t a = s[i], b = s[ixj];
+          const bool desc = (i & k) == 0;
+          if (desc ? (a < b) : (a > b)) {
+            s[i] = b;
+            s[ixj] = a;
+          }
+        }
+      }
+      consumer_sync();
+    }
+  }
+}
+
+// Quantises the step's fp32 input [T, K] into xq [TT][kpad_max] (zero past K) and the per-token
+// ratio / inverse step, exactly as pack_npu_input_int8[_dyntok].
+// When the step that produced x already reduced max_c |x*s| per token (amax_src), x is read
+// once; otherwise (the chain's external input) once for the amax and once to quantise.
+__device__ __forceinline__ char4 quant4(const float4 v, const float4 sv, bool smooth, float inv) {
+  char4 o;
+  if (smooth) {
+    o.x = static_cast<signed char>(round_clamp(v.x * (sv.x * inv), 127.0f));
+    o.y = static_cast<signed char>(round_clamp(v.y * (sv.y * inv), 127.0f));
+    o.z = static_cast<signed char>(round_clamp(v.z * (sv.z * inv), 127.0f));
+    o.w = static_cast<signed char>(round_clamp(v.w * (sv.w * inv), 127.0f));
+  } else {
+    o.x = static_cast<signed char>(round_clamp(v.x * inv, 127.0f));
+    o.y = static_cast<signed char>(round_clamp(v.y * inv, 127.0f));
+    o.z = static_cast<signed char>(round_clamp(v.z * inv, 127.0f));
+    o.w = static_cast<signed char>(round_clamp(v.w * inv, 127.0f));
+  }
+  return o;
+}
+
+template <int TT>
+__device__ void quantise_input(const ChainOp &op, int T, int8_t *xq, int kpad_max, float *s_ratio,
+                               float *s_inv, float (*s_part)[TT], int tid) {
+  const int warp = tid >> 5, lane = tid & 31;
+  const bool vec = op.vec_x;
+  float inv_r[TT];
+  if (op.act_mode == kActDyntok && op.amax_src) {
+    // every thread derives the inverse steps itself: no barrier before the x pass
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      float m = t < T ? __ldcg(op.amax_src + t) : 1.0f;
+      m = (m < 1e-8f) ? 1e-8f : m;
+      inv_r[t] = 127.0f / m;
+      if (tid == t && t < T) s_ratio[t] = m / op.safe_thresh;
+    }
+  } else if (op.act_mode == kActDyntok) {
+    float amax[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) amax[t] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      if (t >= T) break;
+      const float *xr = op.x + t * op.ldx;
+      if (vec) {
+        const int n4 = op.K / 4;
+        const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+        const float4 *s4 = reinterpret_cast<const float4 *>(op.inv_smooth);
+        for (int c0 = tid; c0 < n4; c0 += 4 * kCT) {
+          float4 v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int c = c0 + u * kCT;
+            v[u] = c < n4 ? __ldcg(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int c = c0 + u * kCT;
+            if (c >= n4) continue;
+            float4 m = v[u];
+            if (op.inv_smooth) {
+              const float4 sv = s4[c];
+              m.x = m.x * sv.x; m.y = m.y * sv.y; m.z = m.z * sv.z; m.w = m.w * sv.w;
+            }
+            const float a0 = fabsf(m.x), a1 = fabsf(m.y), a2 = fabsf(m.z), a3 = fabsf(m.w);
+            if (a0 > amax[t]) amax[t] = a0;
+            if (a1 > amax[t]) amax[t] = a1;
+            if (a2 > amax[t]) amax[t] = a2;
+            if (a3 > amax[t]) amax[t] = a3;
+          }
+        }
+      } else {
+        for (int c = tid; c < op.K; c += kCT) {
+          const float v = __ldcg(xr + c);
+          const float a = op.inv_smooth ? fabsf(v * op.inv_smooth[c]) : fabsf(v);
+          if (a > amax[t]) amax[t] = a;
+        }
+      }
+      const float m = warp_amax(amax[t]);
+      if (lane == 0) s_part[warp][t] = m;
+    }
+    consumer_sync();
+    if (tid < T) {
+      float m = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kCW; ++w) m = s_part[w][tid] > m ? s_part[w][tid] : m;
+      m = (m < 1e-8f) ? 1e-8f : m;
+      s_ratio[tid] = m / op.safe_thresh;
+      s_inv[tid] = 127.0f / m;
+    }
+    consumer_sync();
+#pragma unroll
+    for (int t = 0; t < TT; ++t) inv_r[t] = t < T ? s_inv[t] : 0.0f;
+  } else {
+    if (tid < T) s_ratio[tid] = 1.0f;
+#pragma unroll
+    for (int t = 0; t < TT; ++t) inv_r[t] = op.inv_step;
+  }
+#pragma unroll
+  for (int t = 0; t < TT; ++t) {
+    if (t >= T) break;
+    const float inv = inv_r[t];
+    const float *xr = op.x + t * op.ldx;
+    int8_t *q = xq + t * kpad_max;
+    if (vec) {
+      // 4 independent 16-byte loads in flight per thread before any use
+      const int n4 = op.K / 4;
+      const bool smooth = op.inv_smooth != nullptr;
+      const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+      const float4 *s4 = reinterpret_cast<const float4 *>(op.inv_smooth);
+      for (int c0 = tid; c0 < n4; c0 += 4 * kCT) {
+        float4 v[4], sv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + u * kCT;
+          v[u] = c < n4 ? __ldcg(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+          sv[u] = (smooth && c < n4) ? s4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + u * kCT;
+          if (c < n4) reinterpret_cast<char4 *>(q)[c] = quant4(v[u], sv[u], smooth, inv);
+        }
+      }
+      for (int c = (op.K & ~3) + tid; c < op.k_pad; c += kCT) q[c] = 0;
+    } else {
+      for (int c = tid; c < op.k_pad; c += kCT) {
+        int8_t v = 0;
+        if (c < op.K) {
+          const float xv = __ldcg(xr + c);
+          v = static_cast<int8_t>(
+              round_clamp(op.inv_smooth ? xv * (op.inv_smooth[c] * inv) : xv * inv, 127.0f));
+        }
+        q[c] = v;
+      }
+    }
+  }
+  consumer_sync();
+}
+
+// Consumes this CTA's tiles [tb, te) of one step.  `it` is the ring iteration counter shared
+// with the producer's issue order.
+template <int TT, int RPW, bool TOPK>
+__device__ void consume_tiles(const ChainOp &op, const ChainArgs &a, int tb, int te, int &it,
+                              const uint8_t *ring, const int8_t *xq, uint64_t *bars,
+                              const float *s_ratio, uint64_t *cand, int *s_amax, int tid,
+                              bool &ok, unsigned long long *tr) {
+  const int warp = tid >> 5, lane = tid & 31;
+  const int it_first = it;
+  constexpr int RB = kCW * RPW;
+  const bool dyn = op.act_mode == kActDyntok;
+  for (int tile = tb; tile < te; ++tile) {
+    int acc[RPW][TT];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+      for (int t = 0; t < TT; ++t) acc[r][t] = 0;
+    // This lane's epilogue parameters (row lane / TT of the warp's rows), loaded while the
+    // tile's weights stream in rather than after the reduction.
+    int e_qm = 1;
+    float e_step = 0.0f, e_smooth = 1.0f;
+    bool e_amax = false;
+    {
+      const int n = tile * RB + warp * RPW + lane / TT;
+      if (lane < RPW * TT && n < op.N) {
+        if (op.out_mode == kOutF32 || op.out_mode == kOutQuant) e_qm = op.quant_m[n];
+        e_step = op.out_mode == kOutF32Acc ? op.acc_step[n] : op.out_step[n];
+        if (op.amax_dst) {
+          const int c = n - op.amax_c0;
+          e_amax = c >= 0 && c < op.amax_cols;
+          if (e_amax && op.amax_smooth) e_smooth = op.amax_smooth[c];
+        }
+      }
+    }
+    for (int kci = 0; kci < op.nk; ++kci, ++it) {
+      const int slot = it % a.ns;
+      const int use = it / a.ns;
+      if (ok) ok = mbar_wait_bounded(smem_addr(&bars[slot]), use & 1, a.err, kDevTimeoutFull);
+      if (tr && it == it_first && tid == 0) tr[6] = global_timer_ns();
+      const int k0 = kci * op.kc;
+      const int bytes = min(op.kc, op.k_pad - k0);
+      const uint8_t *sw = ring + static_cast<size_t>(slot) * a.stage_bytes;
+      if (ok) {
+        for (int kk = lane * 16; kk < bytes; kk += 512) {
+          int4 xv[TT];
+#pragma unroll
+          for (int t = 0; t < TT; ++t)
+            xv[t] = *reinterpret_cast<const int4 *>(xq + t * a.kpad_max + k0 + kk);
+#pragma unroll
+          for (int r = 0; r < RPW; ++r) {
+            const int4 wv = *reinterpret_cast<const int4 *>(sw + (warp * RPW + r) * op.kc + kk);
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+              int s = acc[r][t];
+              s = __dp4a(wv.x, xv[t].x, s);
+              s = __dp4a(wv.y, xv[t].y, s);
+              s = __dp4a(wv.z, xv[t].z, s);
+              s = __dp4a(wv.w, xv[t].w, s);
+              acc[r][t] = s;
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&bars[kMaxStages + slot]));
+    }
+    int mine = 0;
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
+        const int s = warp_sum(acc[r][t]);
+        if (lane == r * TT + t) mine = s;
+      }
+    if (lane < RPW * TT) {
+      const int r = lane / TT, t = lane % TT;
+      const int row = warp * RPW + r;
+      const int n = tile * RB + row;
+      if (t < a.T && n < op.N && ok) {
+        const float step = dyn ? s_ratio[t] * e_step : e_step;
+        if (op.out_mode == kOutAccI32) {
+          static_cast<int32_t *>(op.y)[t * op.ldy + n] = mine;
+        } else if (op.out_mode == kOutQuant) {
+          const int yq = requant_quantm(mine, e_qm, op.trunc, op.qmax);
+          if (op.out_i16)
+            static_cast<int16_t *>(op.y)[t * op.ldy + n] = static_cast<int16_t>(yq);
+          else
+            static_cast<int8_t *>(op.y)[t * op.ldy + n] = static_cast<int8_t>(yq);
+        } else {
+          const float v = op.out_mode == kOutF32
+                              ? static_cast<float>(requant_quantm(mine, e_qm, op.trunc, op.qmax)) * step
+                              : __int2float_rn(mine) * step;
+          if (TOPK) {
+            if (op.tk.logits) op.tk.logits[t * op.tk.ldl + n] = v;
+            cand[t * a.cand_cap + (tile - tb) * RB + row] =
+                topk_key(v, static_cast<uint32_t>(op.tk.row_offset + n));
+          } else {
+            static_cast<float *>(op.y)[t * op.ldy + n] = v;
+            if (e_amax) {
+              // fp32 output consumed by a dyntok step: reduce its amax |y * s_next| per token
+              const float av = op.amax_smooth ? fabsf(v * e_smooth) : fabsf(v);
+              if (av > 0.0f) atomicMax(s_amax + t, __float_as_int(av));
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int TT, bool TOPK>
+__device__ void consume_dispatch(const ChainOp &op, const ChainArgs &a, int tb, int te, int &it,
+                                 const uint8_t *ring, const int8_t *xq, uint64_t *bars,
+                                 const float *s_ratio, uint64_t *cand, int *s_amax, int tid,
+                                 bool &ok, unsigned long long *tr) {
+  switch (op.rpw) {
+    case 1: consume_tiles<TT, 1, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, tid, ok, tr); break;
+    case 2: consume_tiles<TT, 2, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, tid, ok, tr); break;
+    default: consume_tiles<TT, 4, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, tid, ok, tr); break;
+  }
+}
+
+// Per-CTA top-k of the LM-head step, then the merge by the last CTA to finish.
+template <int TT>
+__device__ void topk_finish(const ChainOp &op, const ChainArgs &a, int tb, int te, uint64_t *cand,
+                            uint64_t *merge_buf, int merge_cap, int tid) {
+  __shared__ int s_last;
+  __shared__ int s_count;
+  __shared__ unsigned long long s_red[kCW];
+  __shared__ int s_red_g[kCW];
+  __shared__ unsigned long long s_tau;
+  const int G = gridDim.x;
+  const int k = op.tk.k;
+  const int rb = op.rb;
+  const int rows_here = te > tb ? min((te - tb) * rb, op.N - tb * rb) : 0;
+  int P = 1;
+  while (P < rows_here) P <<= 1;
+  for (int t = 0; t < a.T; ++t) {
+    uint64_t *ct = cand + t * a.cand_cap;
+    if (rows_here > 0) consumer_bitonic_desc(ct, P, tid);
+    for (int j = tid; j < k; j += kCT)
+      a.lists[(static_cast<size_t>(t) * G + blockIdx.x) * k + j] =
+          (rows_here > 0 && j < P) ? ct[j] : 0ull;
+  }
+  __threadfence();
+  consumer_sync();
+  if (tid == 0) s_last = atomicAdd(a.tk_counter, 1u) == static_cast<unsigned>(G - 1);
+  consumer_sync();
+  if (!s_last) return;
+  __threadfence();
+  const int lane = tid & 31, warp = tid >> 5;
+  for (int t = 0; t < a.T; ++t) {
+    const unsigned long long *lists =
+        reinterpret_cast<const unsigned long long *>(a.lists) + static_cast<size_t>(t) * G * k;
+    uint64_t m = 0;
+    for (int g = tid; g < G; g += kCT) {
+      const uint64_t v = __ldcg(lists + static_cast<size_t>(g) * k + (k - 1));
+      m = v > m ? v : m;
+    }
+    m = warp_max_u64(m);
+    if (lane == 0) s_red[warp] = m;
+    if (tid == 0) s_count = 0;
+    consumer_sync();
+    if (tid == 0) {
+      uint64_t mm = 0;
+      for (int w = 0; w < kCW; ++w) mm = s_red[w] > mm ? s_red[w] : mm;
+      s_tau = mm < 1 ? 1 : mm;
+    }
+    consumer_sync();
+    const uint64_t tau = s_tau;
+    // every key >= tau, read as one flat array with 4 independent loads per thread in flight
+    const int total = G * k;
+    for (int i0 = tid; i0 < total; i0 += 4 * kCT) {
+      uint64_t v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * kCT;
+        v[u] = i < total ? __ldcg(lists + i) : 0ull;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (v[u] >= tau) {
+          const int pos = atomicAdd(&s_count, 1);
+          if (pos < merge_cap) merge_buf[pos] = v[u];
+        }
+      }
+    }
+    consumer_sync();
+    const int C = s_count;
+    if (C <= merge_cap) {
+      int P2 = 1;
+      while (P2 < C) P2 <<= 1;
+      for (int i = C + tid; i < P2; i += kCT) merge_buf[i] = 0;
+      consumer_bitonic_desc(merge_buf, P2, tid);
+      for (int j = tid; j < k; j += kCT) {
+        op.tk.val[t * k + j] = topk_key_value(merge_buf[j]);
+        op.tk.idx[t * k + j] = topk_key_id(merge_buf[j]);
+      }
+    } else {
+      // many keys tie at the threshold: k rounds of a tournament over the list heads
+      int *heads = reinterpret_cast<int *>(merge_buf);
+      for (int g = tid; g < G; g += kCT) heads[g] = 0;
+      consumer_sync();
+      for (int j = 0; j < k; ++j) {
+        uint64_t best = 0;
+        int best_g = -1;
+        for (int g = tid; g < G; g += kCT) {
+          const int h = heads[g];
+          const uint64_t v = h < k ? __ldcg(lists + static_cast<size_t>(g) * k + h) : 0ull;
+          if (v > best) { best = v; best_g = g; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const uint64_t ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+          const int og = __shfl_xor_sync(0xFFFFFFFFu, best_g, o);
+          if (ov > best) { best = ov; best_g = og; }
+        }
+        if (lane == 0) { s_red[warp] = best; s_red_g[warp] = best_g; }
+        consumer_sync();
+        if (tid == 0) {
+          uint64_t bb = 0;
+          int bg = -1;
+          for (int w = 0; w < kCW; ++w)
+            if (s_red[w] > bb) { bb = s_red[w]; bg = s_red_g[w]; }
+          op.tk.val[t * k + j] = topk_key_value(bb);
+          op.tk.idx[t * k + j] = topk_key_id(bb);
+          if (bg >= 0) heads[bg] += 1;
+        }
+        consumer_sync();
+      }
+    }
+    consumer_sync();
+  }
+  if (tid == 0) *a.tk_counter = 0u;
+}
+
+template <int TT>
+__global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t *ring = smem;
+  int8_t *xq = reinterpret_cast<int8_t *>(smem + a.ring_bytes);
+  uint64_t *cand = reinterpret_cast<uint64_t *>(smem + a.ring_bytes + TT * a.kpad_max);
+  uint64_t *bars = cand + TT * a.cand_cap;
+  __shared__ float s_part[kCW][TT];
+  __shared__ float s_ratio[TT];
+  __shared__ float s_inv[TT];
+  __shared__ int s_amax[TT];  // float bits of a non-negative max (int order == float order)
+  __shared__ int s_abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < a.ns; ++s) {
+      mbar_init(smem_addr(&bars[s]), 1);
+      mbar_init(smem_addr(&bars[kMaxStages + s]), kCW);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kCW) {
+    // ------------------------------- producer warp -------------------------------
+    const uint64_t pol = policy_evict_first();
+    int it = 0;
+    bool ok = true;
+    for (int s = 0; s < a.n_ops && ok; ++s) {
+      const ChainOp &op = a.ops[s];
+      int tb, te;
+      split_range(op.num_tiles, G, blockIdx.x, tb, te);
+      unsigned long long *ptr =
+          a.trace ? a.trace + (static_cast<size_t>(blockIdx.x) * a.n_ops + s) * 8 : nullptr;
+      if (ptr && lane == 0) ptr[4] = global_timer_ns();
+      for (int tile = tb; tile < te && ok; ++tile) {
+        const int rows = min(op.rb, op.N - tile * op.rb);
+        for (int kci = 0; kci < op.nk; ++kci, ++it) {
+          const int slot = it % a.ns;
+          const int use = it / a.ns;
+          if (it >= a.ns) {
+            ok = mbar_wait_bounded(smem_addr(&bars[kMaxStages + slot]), (use - 1) & 1, a.err,
+                                   kDevTimeoutEmpty);
+            if (!ok) break;
+          }
+          const int k0 = kci * op.kc;
+          const int bytes = min(op.kc, op.k_pad - k0);
+          const uint32_t full = smem_addr(&bars[slot]);
+          const uint32_t dst = smem_addr(ring + static_cast<size_t>(slot) * a.stage_bytes);
+          const int8_t *src = op.w + static_cast<int64_t>(tile * op.rb) * op.ldw + k0;
+          if (op.nk == 1 && op.kc == op.ldw) {
+            // whole rows: the tile is one contiguous block of rows * k_pad bytes, one copy
+            if (lane == 0) {
+              mbar_arrive_expect_tx(full, static_cast<uint32_t>(rows * bytes));
+              bulk_g2s(dst, src, static_cast<uint32_t>(rows * bytes), full, pol);
+            }
+          } else {
+            if (lane == 0) mbar_arrive_expect_tx(full, static_cast<uint32_t>(rows * bytes));
+            __syncwarp();
+            for (int r = lane; r < rows; r += 32)
+              bulk_g2s(dst + r * op.kc, src + static_cast<int64_t>(r) * op.ldw, bytes, full, pol);
+          }
+          __syncwarp();
+        }
+      }
+      if (ptr && lane == 0) ptr[5] = global_timer_ns();
+    }
+    return;
+  }
+
+  // ------------------------------- consumer warps -------------------------------
+  const int tid = threadIdx.x;
+  int it = 0;
+  bool ok = true;
+  for (int s = 0; s < a.n_ops; ++s) {
+    const ChainOp &op = a.ops[s];
+    // the next step's descriptor into L1 while this one runs
+    if (tid < 3 && s + 1 < a.n_ops)
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char *>(a.ops + s + 1) + tid * 128));
+    int tb, te;
+    split_range(op.num_tiles, G, blockIdx.x, tb, te);
+    if (op.barrier_before && s > 0) {
+      // Once one grid wait has run out, later ones are skipped so the kernel still ends.
+      if (tid == 0 && !s_abort) {
+        const unsigned *cnt = a.bar + (s - 1);
+        if (ld_acquire_gpu(cnt) < static_cast<unsigned>(G)) {
+          const unsigned long long t0 = global_timer_ns();
+          for (uint32_t i = 1; ld_acquire_gpu(cnt) < static_cast<unsigned>(G); ++i) {
+            if ((i & 255u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+              atomicExch(a.err, kDevPeerTimeout);
+              s_abort = 1;
+              break;
+            }
+          }
+        }
+      }
+      consumer_sync();
+    }
+    unsigned long long *tr =
+        a.trace ? a.trace + (static_cast<size_t>(blockIdx.x) * a.n_ops + s) * 8 : nullptr;
+    if (tr && tid == 0) tr[0] = global_timer_ns();
+    if (tid < TT) s_amax[tid] = 0;
+    if (te > tb || op.topk) {
+      if (te > tb) quantise_input<TT>(op, a.T, xq, a.kpad_max, s_ratio, s_inv, s_part, tid);
+      if (tr && tid == 0) tr[1] = global_timer_ns();
+      // the CTA owning tile 0 publishes the per-token ratios
+      if (tb == 0 && te > 0 && op.ratio_out && tid < a.T && op.act_mode == kActDyntok)
+        op.ratio_out[tid] = s_ratio[tid];
+      if (op.topk) {
+        for (int i = tid; i < TT * a.cand_cap; i += kCT) cand[i] = 0ull;
+        consumer_sync();
+        consume_dispatch<TT, true>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, tid, ok, tr);
+        consumer_sync();
+        int cap = 1;
+        while (static_cast<size_t>(cap) * 2 * 8 <= a.ring_bytes) cap <<= 1;
+        topk_finish<TT>(op, a, tb, te, cand, reinterpret_cast<uint64_t *>(ring), cap, tid);
+      } else {
+        consume_dispatch<TT, false>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, tid, ok, tr);
+      }
+    }
+    // arrival: every output of this CTA for step s is written (and its amax share reduced)
+    consumer_sync();
+    if (tr && tid == 0) tr[2] = global_timer_ns();
+    if (op.amax_dst) {
+      if (tid < a.T && s_amax[tid] > 0) atomicMax(reinterpret_cast<int *>(op.amax_dst) + tid, s_amax[tid]);
+      consumer_sync();
+    }
+    if (tid == 0) {
+      // release: the CTA's writes (ordered before this by the consumer barrier) become
+      // visible to any CTA that acquires the counter
+      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.bar + s), "r"(1u) : "memory");
+      if (tr) tr[3] = global_timer_ns();
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t configure_chain(const ChainPlan &plan) {
+  // Opt every instantiation in once to the largest dynamic shared memory the device allows.
+  static bool done[4] = {false, false, false, false};
+  const int slot = plan.tt == 1 ? 0 : plan.tt == 2 ? 1 : plan.tt == 4 ? 2 : 3;
+  if (done[slot]) return cudaSuccess;
+  void (*kern)(ChainArgs) = slot == 0 ? chain_kernel<1> : slot == 1 ? chain_kernel<2>
+                          : slot == 2 ? chain_kernel<4> : chain_kernel<8>;
+  int dev = 0, optin = 0;
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kern);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - static_cast<int>(fa.sharedSizeBytes));
+  if (e != cudaSuccess) return e;
+  if (plan.smem > static_cast<size_t>(optin) - fa.sharedSizeBytes) return cudaErrorInvalidValue;
+  done[slot] = true;
+  return cudaSuccess;
+}
+
+namespace {
+
+// Plans the chain for `cps` co-resident CTAs per SM; false when it does not fit.
+bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, ChainPlan *plan) {
+  ChainPlan p = {};
+  p.tt = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
+  p.grid = cps * sm_count;
+  int kpad_max = 16;
+  size_t stage = 0;
+  size_t cand_cap = 0;
+  for (int s = 0; s < n_ops; ++s) {
+    ChainOp &op = ops[s];
+    if (op.topk && s != n_ops - 1) return false;  // the LM-head step must be last
+    auto tiles = [&](int rb) { return (op.N + rb - 1) / rb; };
+    constexpr int kMaxStage = 32768;
+    const int min_tiles = op.topk ? p.grid : 2 * p.grid;
+    if (op.k_pad * 8 <= kMaxStage) {
+      // whole-row tiles: a tile is one contiguous rb x k_pad block (one bulk copy per stage)
+      op.rpw = 1;
+      for (int r : {4, 2})
+        if (8 * r * op.k_pad <= kMaxStage && tiles(8 * r) >= min_tiles) {
+          op.rpw = r;
+          break;
+        }
+      op.kc = op.k_pad;
+    } else {
+      // long rows: 8-row tiles streamed in K chunks of 4 KB per row
+      op.rpw = 1;
+      op.kc = kMaxStage / 8;
+    }
+    op.rb = 8 * op.rpw;
+    op.nk = (op.k_pad + op.kc - 1) / op.kc;
+    op.num_tiles = tiles(op.rb);
+    stage = std::max(stage, static_cast<size_t>(op.rb) * op.kc);
+    kpad_max = std::max(kpad_max, op.k_pad);
+    if (op.topk) {
+      const int max_tiles = (op.num_tiles + p.grid - 1) / p.grid;
+      size_t c = 1;
+      while (c < static_cast<size_t>(max_tiles) * op.rb) c <<= 1;
+      cand_cap = c;
+    }
+  }
+  p.kpad_max = (kpad_max + 15) / 16 * 16;
+  p.cand_cap = static_cast<int>(cand_cap);
+  p.stage_bytes = static_cast<uint32_t>(stage);
+  const size_t fixed = static_cast<size_t>(p.tt) * p.kpad_max + static_cast<size_t>(p.tt) * cand_cap * 8 +
+                      2 * kMaxStages * 8;
+  // the SM's 228 KB split between the co-resident CTAs, less the per-CTA reservation and
+  // static shared memory
+  const size_t budget = 233472 / cps - 1024 - 2048;
+  if (fixed + 2 * stage > budget) return false;
+  p.ns = static_cast<int>(std::min<size_t>(kMaxStages, (budget - fixed) / stage));
+  p.ring_bytes = static_cast<uint32_t>(p.ns * stage);
+  p.smem = p.ring_bytes + fixed;
+  *plan = p;
+  return true;
+}
+
+}  // namespace
+
+bool plan_chain(ChainOp *ops, int n_ops, int T, int sm_count, ChainPlan *plan) {
+  if (n_ops < 1 || T < 1 || T > 8 || sm_count < 1) return false;
+  // Two co-resident CTAs per SM give two independent weight pipelines per SM (more bytes in
+  // flight than one CTA whose 8 warps release each stage together); large T x K inputs fall
+  // back to one CTA per SM with the whole shared memory.
+  return plan_chain_cps(ops, n_ops, T, sm_count, 2, plan) ||
+         plan_chain_cps(ops, n_ops, T, sm_count, 1, plan);
+}
+
+cudaError_t launch_chain(const ChainOp *ops_dev, int n_ops, int T, const ChainPlan &plan,
+                         unsigned *bar, size_t clear_bytes, unsigned *tk_counter,
+                         uint64_t *lists, int *err, unsigned long long *trace,
+                         cudaStream_t stream) {
+  ChainArgs a;
+  a.ops = ops_dev;
+  a.n_ops = n_ops;
+  a.T = T;
+  a.bar = bar;
+  a.tk_counter = tk_counter;
+  a.lists = lists;
+  a.err = err;
+  a.ns = plan.ns;
+  a.stage_bytes = plan.stage_bytes;
+  a.kpad_max = plan.kpad_max;
+  a.cand_cap = plan.cand_cap;
+  a.ring_bytes = plan.ring_bytes;
+  a.trace = trace;
+  void (*kern)(ChainArgs) = nullptr;
+  switch (plan.tt) {
+    case 1: kern = chain_kernel<1>; break;
+    case 2: kern = chain_kernel<2>; break;
+    case 4: kern = chain_kernel<4>; break;
+    default: kern = chain_kernel<8>; break;
+  }
+  cudaError_t e = configure_chain(plan);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(bar, 0, clear_bytes, stream);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+}  // namespace w8a8

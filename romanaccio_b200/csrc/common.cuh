@@ -65,10 +65,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int *err,
                                                   int code) {
   if (mbar_try_wait(bar, parity)) return true;
+  // %globaltimer is slow to read: poll the barrier, and look at the clock every 512 polls.
   const unsigned long long t0 = global_timer_ns();
-  while (true) {
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if ((i & 511u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
       if (err) atomicExch(err, code);
       return false;
     }

@@ -209,16 +209,24 @@ __global__ void __launch_bounds__(kThreads, TOPK ? 1 : 2) gemv_w8a8_kernel(const
       bytes = min(a.kc, a.k_pad - k0);
       rows = min(RB, a.N - tile * RB);
     };
+    // Whole-row tiles are one contiguous rows x k_pad block: one copy; else one per row.
+    const bool whole_rows = a.nk == 1 && a.kc == a.ldw;
+    auto copy_w = [&](uint32_t dst, int tile, int k0, int bytes, int rows, uint32_t full) {
+      const int8_t *src = a.w + static_cast<int64_t>(tile * RB) * a.ldw + k0;
+      if (whole_rows) {
+        if (lane == 0) bulk_g2s(dst, src, static_cast<uint32_t>(rows * bytes), full, pol_w);
+      } else {
+        for (int r = lane; r < rows; r += 32)
+          bulk_g2s(dst + r * a.kc, src + static_cast<int64_t>(r) * a.ldw, bytes, full, pol_w);
+      }
+    };
     for (int it = 0; it < pre; ++it) {
       int tile, k0, bytes, rows;
       stage_geom(it, tile, k0, bytes, rows);
       const uint32_t full = smem_addr(&bars[it]);
       if (lane == 0) mbar_arrive_expect_tx(full, static_cast<uint32_t>((rows + a.T) * bytes));
       __syncwarp();
-      const uint32_t dst = smem_addr(stages + static_cast<size_t>(it) * a.stage_bytes);
-      for (int r = lane; r < rows; r += 32)
-        bulk_g2s(dst + r * a.kc, a.w + static_cast<int64_t>(tile * RB + r) * a.ldw + k0, bytes,
-                 full, pol_w);
+      copy_w(smem_addr(stages + static_cast<size_t>(it) * a.stage_bytes), tile, k0, bytes, rows, full);
     }
     // Activations (and everything written by the previous kernel) are read only after this.
     pdl_wait();
@@ -244,9 +252,7 @@ __global__ void __launch_bounds__(kThreads, TOPK ? 1 : 2) gemv_w8a8_kernel(const
       if (lane == 0) mbar_arrive_expect_tx(full, static_cast<uint32_t>((rows + a.T) * bytes));
       __syncwarp();
       const uint32_t dst = smem_addr(stages + static_cast<size_t>(slot) * a.stage_bytes);
-      for (int r = lane; r < rows; r += 32)
-        bulk_g2s(dst + r * a.kc, a.w + static_cast<int64_t>(tile * RB + r) * a.ldw + k0, bytes,
-                 full, pol_w);
+      copy_w(dst, tile, k0, bytes, rows, full);
       for (int t = lane; t < a.T; t += 32)
         bulk_g2s(dst + RB * a.kc + t * a.kc, a.x + t * a.ldx + k0, bytes, full, pol_x);
     }
@@ -405,14 +411,21 @@ bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan
   GemvPlan p = {};
   p.tt = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
   auto tiles = [&](int rb) { return (N + rb - 1) / rb; };
-  if (topk) {
-    p.rpw = tiles(32) >= sm_count ? 4 : tiles(16) >= sm_count ? 2 : 1;
+  const int min_tiles = topk ? sm_count : 2 * sm_count;
+  constexpr int kMaxStage = 32768;
+  p.rpw = 1;
+  if (k_pad * 8 <= kMaxStage) {
+    // whole-row tiles (one contiguous block per stage), as many rows as balance allows
+    for (int r : {4, 2})
+      if (8 * r * k_pad <= kMaxStage && tiles(8 * r) >= min_tiles) {
+        p.rpw = r;
+        break;
+      }
+    p.kc = k_pad;
   } else {
-    p.rpw = tiles(32) >= 2 * sm_count ? 4 : tiles(16) >= 2 * sm_count ? 2 : 1;
+    p.kc = kMaxStage / 8;
   }
   p.rb = 8 * p.rpw;
-  const int kc_max = 32768 / p.rb;
-  p.kc = std::min(k_pad, kc_max);
   p.nk = (k_pad + p.kc - 1) / p.kc;
   const size_t stage = static_cast<size_t>(p.rb + p.tt) * p.kc;
   p.num_tiles = tiles(p.rb);

@@ -131,6 +131,55 @@ struct MergeLaunch {
 };
 cudaError_t launch_topk_merge(const MergeLaunch &L, cudaStream_t stream);
 
+// One step of the persistent decode-chain kernel (device-resident op table).  128-byte aligned:
+// an op is exactly three cache lines, which the kernel prefetches ahead of use.
+struct alignas(128) ChainOp {
+  // weights and tiling
+  const int8_t *w;
+  int64_t ldw;
+  int N, K, k_pad;
+  int rpw, rb, kc, nk, num_tiles;  // filled by plan_chain
+  // input view and activation quantisation
+  const float *x;
+  int64_t ldx;
+  int vec_x;                 // x rows 16-byte aligned, K % 4 == 0
+  const float *inv_smooth;   // [K] or null (16-byte aligned)
+  int act_mode;
+  float inv_step, safe_thresh;
+  float *ratio_out;          // optional [T]
+  // epilogue
+  int out_mode;
+  const int16_t *quant_m;
+  int trunc, qmax, out_i16;
+  const float *out_step;
+  const float *acc_step;
+  void *y;
+  int64_t ldy;
+  // per-token amax hand-off between a producing step and the dyntok step that reads its output
+  const float *amax_src;     // this step's amax [T] was reduced by its producer (or null)
+  float *amax_dst;           // reduce max |y[:, c0 + c] * amax_smooth[c]| into [T] (or null)
+  int amax_c0, amax_cols;
+  const float *amax_smooth;  // the consuming step's in_inv_smooth (or null)
+  // scheduling
+  int barrier_before;        // wait for every CTA to finish the previous steps first
+  int topk;                  // LM-head step (must be the last step)
+  TopK tk;                   // k, row_offset, val, idx, logits, ldl (lists / counter unused)
+};
+
+struct ChainPlan {
+  int tt, grid, kpad_max, cand_cap, ns;
+  uint32_t stage_bytes, ring_bytes;
+  size_t smem;
+};
+
+bool plan_chain(ChainOp *ops, int n_ops, int T, int sm_count, ChainPlan *plan);
+cudaError_t configure_chain(const ChainPlan &plan);
+// `bar` starts a zero-at-launch region of clear_bytes (arrival counters, then amax slots).
+cudaError_t launch_chain(const ChainOp *ops_dev, int n_ops, int T, const ChainPlan &plan,
+                         unsigned *bar, size_t clear_bytes, unsigned *tk_counter,
+                         uint64_t *lists, int *err, unsigned long long *trace,
+                         cudaStream_t stream);
+
 // Records `msg` as the calling thread's w8a8_last_error() text (defined in api.cu).
 void set_last_error(const char *msg);
 

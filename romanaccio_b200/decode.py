@@ -19,7 +19,8 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from ._lib import DTYPE_INT8, OUT_F32, OUT_F32_ACC
+from ._lib import ACT_STATIC, DTYPE_INT8, OUT_F32, OUT_F32_ACC
+from .chain import ChainStepSpec, DecodeChain
 from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
 from .lmhead import (LmHeadShard, candidate_buffers, exchange_candidates, shard_range,
                      token_candidates)
@@ -56,7 +57,7 @@ def _lm_rows(K: int, lo: int, hi: int, seed: int, device) -> tuple[np.ndarray, n
 class DecodeStack:
     def __init__(self, ctx: Context, shape: DecodeShape, T: int, rank: int = 0, world: int = 1,
                  group=None, seed: int = 0, layers: int | None = None, k: int = 40,
-                 lm_vocab: int | None = None):
+                 lm_vocab: int | None = None, use_chain: bool = True):
         self.ctx = ctx
         self.shape = shape
         self.T = int(T)
@@ -108,7 +109,34 @@ class DecodeStack:
         self.top_val = torch.empty((self.T, self.k), dtype=torch.float32, device=dev)
         self.top_idx = torch.empty((self.T, self.k), dtype=torch.int32, device=dev)
         self.graph = None
-        self.graph_lm = None
+        self.chain = self._build_chain() if use_chain else None
+
+    def _build_chain(self) -> DecodeChain:
+        """The whole linear stack (+ the LM head when it is not sharded) as one persistent
+        kernel: same buffers and the same data dependences as run_linears / run_lm_head."""
+        qkv, o, gu, down = self.outs
+        x = self.x
+        steps = []
+        for row in self.linears:
+            steps.append(ChainStepSpec(row[0], x, qkv))
+            steps.append(ChainStepSpec(row[1], qkv[:, :self.shape.q], o))
+            steps.append(ChainStepSpec(row[2], o, gu))
+            steps.append(ChainStepSpec(row[3], gu[:, :self.shape.ffn], down))
+            x = down
+        if self.world == 1:
+            steps.append(ChainStepSpec(self.lm.linear, down, None, act_mode=ACT_STATIC,
+                                       out_mode=OUT_F32_ACC, topk_k=self.k,
+                                       row_offset=self.lo, topk_val=self.top_val,
+                                       topk_idx=self.top_idx))
+        return DecodeChain(self.ctx, steps, self.T)
+
+    def launches_per_step(self) -> int:
+        """Kernels of this library launched per step."""
+        lm = 0 if self.world == 1 else 3  # act_quant + top-k GEMV + merge
+        if self.chain is not None:
+            return 1 + lm
+        groups = (self.T + 7) // 8
+        return self.layers * 4 * (1 + groups) + (1 + groups if self.world == 1 else lm)
 
     # ------------------------------------------------------------------ byte accounting
     def step_bytes(self) -> StepBytes:
@@ -154,31 +182,37 @@ class DecodeStack:
         self.top_idx.copy_(i)
         self.ids.copy_(a)
 
+    def run_device(self) -> None:
+        """The part of the step that needs no collective (everything when world == 1)."""
+        if self.chain is not None:
+            self.chain.forward()
+            if self.world == 1:
+                self.ids.copy_(self.top_idx[:, 0])
+            return
+        self.run_linears()
+        if self.world == 1:
+            self.run_lm_head()
+
     def capture(self) -> None:
-        """Captures the device part of the step in CUDA graphs (the LM head + exchange stays
+        """Captures the device part of the step in a CUDA graph (the LM head + exchange stays
         eager for world > 1: the NCCL calls are not captured)."""
         s = torch.cuda.Stream(device=self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(s):
-            self.run_linears()
-            if self.world == 1:
-                self.run_lm_head()
+            self.run_device()
         torch.cuda.current_stream(self.dev).wait_stream(s)
         torch.cuda.synchronize(self.dev)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            self.run_linears()
-            if self.world == 1:
-                self.run_lm_head()
+            self.run_device()
         self.graph = g
 
     def step(self) -> None:
         if self.graph is not None:
             self.graph.replay()
-            if self.world > 1:
-                self.run_lm_head()
         else:
-            self.run_linears()
+            self.run_device()
+        if self.world > 1:
             self.run_lm_head()
 
     def step_host(self, x_host: torch.Tensor, ids_host: torch.Tensor) -> None:

@@ -1,0 +1,111 @@
+"""The persistent decode-chain kernel (one cooperative launch for a whole stack of linears and
+the LM-head top-k) must produce exactly the per-linear path's outputs, which are themselves
+bit-exact against the CPU oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+import romanaccio_b200 as rb
+from romanaccio_b200 import synth
+from romanaccio_b200.chain import ChainStepSpec, DecodeChain
+from romanaccio_b200.decode import DecodeStack
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("shape,T,layers,vocab", [
+    (synth.SMOLLM_135M, 1, 3, 49152),
+    (synth.SMOLLM_135M, 3, 2, 8192),
+    (synth.QWEN25_15B, 1, 2, 151936),
+    (synth.QWEN25_15B, 8, 1, 20000),
+    (synth.GEMMA_12B, 1, 1, 32768),
+])
+def test_chain_matches_per_linear_path(ctx, shape, T, layers, vocab):
+    st = DecodeStack(ctx, shape, T, layers=layers, lm_vocab=vocab, use_chain=True, seed=3)
+    x = synth.activations(T, shape.hidden, seed=5).to(st.dev)
+    st.x.copy_(x)
+    assert st.chain.barriers == 4 * layers  # every step reads the previous step's output
+    st.run_device()
+    torch.cuda.synchronize()
+    chain_outs = [o.clone() for o in st.outs]
+    chain_val, chain_idx = st.top_val.clone(), st.top_idx.clone()
+    # per-linear launches over the same buffers
+    st.run_linears()
+    st.run_lm_head()
+    torch.cuda.synchronize()
+    for a, b in zip(chain_outs, st.outs):
+        assert torch.equal(a, b)
+    assert torch.equal(chain_idx, st.top_idx)
+    assert torch.equal(chain_val, st.top_val)
+    # and against the oracle: the final hidden state's LM head
+    h = st.outs[3].cpu().numpy()
+    wq, acc_step = st.lm_host
+    lg = O.dequant_acc(O.gemm_i32(O.pack_static(h, st.lm_in_step), wq), acc_step)
+    wv, wi = O.topk(lg, st.k)
+    assert np.array_equal(chain_idx.cpu().numpy(), wi)
+    assert np.array_equal(chain_val.cpu().numpy(), wv)
+    # repeated launches are stable (arrival counters and top-k counter reset correctly)
+    for _ in range(5):
+        st.run_device()
+    torch.cuda.synchronize()
+    assert torch.equal(st.top_idx, chain_idx)
+    ctx.check()
+
+
+def test_chain_oracle_chain_bit_exact(ctx):
+    """Two dependent linears with requant outputs checked step by step against the oracle."""
+    T = 2
+    p1 = synth.make_linear(576, 1536, seed=1)
+    p2 = synth.make_linear(1536, 576, seed=2)
+
+    def lin(p):
+        s = rb.SubgraphScaleInfo(in_dtype=rb.DTYPE_INT8, out_dtype=rb.DTYPE_INT8,
+                                 in_thresh=p.in_thresh, in_step=p.in_step,
+                                 in_inv_smooth=p.in_inv_smooth, out_step_chan=p.out_step_chan)
+        return rb.W8A8Linear(ctx, p.wq, s, quant_m=p.quant_m, trunc=p.trunc, acc_step=p.acc_step)
+
+    l1, l2 = lin(p1), lin(p2)
+    x = synth.activations(T, 576, seed=9)
+    xd = x.cuda()
+    y1 = torch.empty((T, 1536), dtype=torch.float32, device="cuda")
+    y2 = torch.empty((T, 576), dtype=torch.float32, device="cuda")
+    r1 = torch.empty(T, dtype=torch.float32, device="cuda")
+    r2 = torch.empty(T, dtype=torch.float32, device="cuda")
+    ch = DecodeChain(ctx, [ChainStepSpec(l1, xd, y1, ratio=r1), ChainStepSpec(l2, y1, y2, ratio=r2)], T)
+    assert ch.barriers == 1
+    ch.forward()
+    torch.cuda.synchronize()
+    *_, yy1 = O.linear(x.numpy(), p1.wq, p1.quant_m, p1.trunc, p1.out_step_chan, p1.in_inv_smooth,
+                       in_thresh=p1.in_thresh)
+    q2, rr2, _, _, yy2 = O.linear(yy1, p2.wq, p2.quant_m, p2.trunc, p2.out_step_chan,
+                                  p2.in_inv_smooth, in_thresh=p2.in_thresh)
+    assert np.array_equal(y1.cpu().numpy(), yy1)
+    assert np.array_equal(y2.cpu().numpy(), yy2)
+    assert np.array_equal(r2.cpu().numpy(), rr2)
+
+
+def test_independent_steps_need_no_barrier(ctx):
+    """Steps that share an input and write disjoint outputs run without a grid barrier."""
+    T, K = 1, 1536
+    ps = [synth.make_linear(K, n, seed=20 + i) for i, n in enumerate((1536, 256, 256))]
+    lins = []
+    for p in ps:
+        s = rb.SubgraphScaleInfo(in_dtype=rb.DTYPE_INT8, out_dtype=rb.DTYPE_INT8,
+                                 in_thresh=p.in_thresh, in_step=p.in_step,
+                                 in_inv_smooth=p.in_inv_smooth, out_step_chan=p.out_step_chan)
+        lins.append(rb.W8A8Linear(ctx, p.wq, s, quant_m=p.quant_m, trunc=p.trunc))
+    x = synth.activations(T, K, seed=4)
+    xd = x.cuda()
+    out = torch.empty((T, 2048), dtype=torch.float32, device="cuda")
+    views = [out[:, :1536], out[:, 1536:1792], out[:, 1792:]]
+    ch = DecodeChain(ctx, [ChainStepSpec(l, xd, v) for l, v in zip(lins, views)], T)
+    assert ch.barriers == 0
+    ch.forward()
+    torch.cuda.synchronize()
+    for p, v in zip(ps, views):
+        *_, y = O.linear(x.numpy(), p.wq, p.quant_m, p.trunc, p.out_step_chan, p.in_inv_smooth,
+                         in_thresh=p.in_thresh)
+        assert np.array_equal(v.cpu().numpy(), y)
