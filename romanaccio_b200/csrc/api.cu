@@ -68,6 +68,7 @@ struct w8a8_linear {
   int K = 0, N = 0, k_pad = 0;
   int8_t *w = nullptr;          // [N, k_pad]
   int16_t *quant_m = nullptr;   // [N]
+  int32_t *quant_m32 = nullptr; // [N] widened copy
   float *out_step = nullptr;    // [N]
   float *acc_step = nullptr;    // [N]
   float *inv_smooth = nullptr;  // [K] or null
@@ -115,6 +116,7 @@ void linear_free(w8a8_linear *l) {
   DeviceGuard g(l->ctx ? l->ctx->device : 0);
   cudaFree(l->w);
   cudaFree(l->quant_m);
+  cudaFree(l->quant_m32);
   cudaFree(l->out_step);
   cudaFree(l->acc_step);
   cudaFree(l->inv_smooth);
@@ -328,17 +330,20 @@ w8a8_status w8a8_linear_create(w8a8_ctx *ctx, const w8a8_linear_desc *d, w8a8_li
     }
   }
   TRY(dev_alloc(&l->quant_m, l->N, &l->device_bytes));
+  TRY(dev_alloc(&l->quant_m32, l->N, &l->device_bytes));
   TRY(dev_alloc(&l->out_step, l->N, &l->device_bytes));
   TRY(dev_alloc(&l->acc_step, l->N, &l->device_bytes));
   {
     std::vector<int16_t> qm(l->N, 1);
     std::vector<float> os(l->N), as(l->N, 0.0f);
     if (d->quant_m) std::memcpy(qm.data(), d->quant_m, sizeof(int16_t) * l->N);
+    std::vector<int32_t> qm32(qm.begin(), qm.end());
     for (int n = 0; n < l->N; ++n) os[n] = d->scale.out_step_chan ? d->scale.out_step_chan[n] : d->scale.out_step;
     if (d->acc_step) std::memcpy(as.data(), d->acc_step, sizeof(float) * l->N);
     l->has_quant_m = d->quant_m != nullptr;
     l->has_acc_step = d->acc_step != nullptr;
     if (cudaMemcpy(l->quant_m, qm.data(), sizeof(int16_t) * l->N, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(l->quant_m32, qm32.data(), sizeof(int32_t) * l->N, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(l->out_step, os.data(), sizeof(float) * l->N, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(l->acc_step, as.data(), sizeof(float) * l->N, cudaMemcpyHostToDevice) != cudaSuccess) {
       linear_free(l);
@@ -669,6 +674,7 @@ w8a8_status w8a8_chain_create(w8a8_ctx *ctx, const w8a8_chain_step *steps, int32
     op.ratio_out = st.ratio_dev;
     op.out_mode = st.out_mode;
     op.quant_m = l->quant_m;
+    op.quant_m32 = l->quant_m32;
     op.trunc = l->trunc;
     op.qmax = l->qmax;
     op.out_i16 = l->out_i16;

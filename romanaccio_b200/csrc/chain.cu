@@ -43,6 +43,7 @@ struct ChainArgs {
   uint32_t stage_bytes;
   int kpad_max;
   int cand_cap;
+  int max_rows;       // most rows one CTA owns in any step (epilogue parameter staging)
   uint32_t ring_bytes;
   unsigned long long *trace;  // optional [grid][n_ops][8] %globaltimer stamps
 };
@@ -101,9 +102,25 @@ __device__ __forceinline__ char4 quant4(const float4 v, const float4 sv, bool sm
   return o;
 }
 
+// Smoothing factors of this thread's first 4 float4 columns, loaded before the grid barrier
+// (they do not depend on the previous step).
+__device__ __forceinline__ void preload_smooth(const ChainOp &op, int tid, float4 (&s_pre)[4]) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) s_pre[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (!op.vec_x || !op.inv_smooth) return;
+  const int n4 = op.K / 4;
+  const float4 *s4 = reinterpret_cast<const float4 *>(op.inv_smooth);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int c = tid + u * kCT;
+    if (c < n4) s_pre[u] = s4[c];
+  }
+}
+
 template <int TT>
 __device__ void quantise_input(const ChainOp &op, int T, int8_t *xq, int kpad_max, float *s_ratio,
-                               float *s_inv, float (*s_part)[TT], int tid) {
+                               float *s_inv, float (*s_part)[TT], int tid,
+                               const float4 (&s_pre)[4]) {
   const int warp = tid >> 5, lane = tid & 31;
   const bool vec = op.vec_x;
   float inv_r[TT];
@@ -196,7 +213,8 @@ __device__ void quantise_input(const ChainOp &op, int T, int8_t *xq, int kpad_ma
         for (int u = 0; u < 4; ++u) {
           const int c = c0 + u * kCT;
           v[u] = c < n4 ? __ldcg(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-          sv[u] = (smooth && c < n4) ? s4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+          sv[u] = c0 == tid ? s_pre[u]
+                            : ((smooth && c < n4) ? s4[c] : make_float4(0.f, 0.f, 0.f, 0.f));
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -220,13 +238,76 @@ __device__ void quantise_input(const ChainOp &op, int T, int8_t *xq, int kpad_ma
   consumer_sync();
 }
 
+// Per-row epilogue parameters of the CTA's rows of the current step, in shared memory.
+struct EpiSmem {
+  int *qm;        // QuantM
+  float *step;    // out_step_chan / out_step / acc_step
+  float *smooth;  // the consuming dyntok step's smoothing factor, or -1 outside its columns
+};
+
+__device__ __forceinline__ void cp_async4(void *smem_dst, const void *gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all_but_newest() {
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+}
+
+// Stages the epilogue parameters of rows [tb*rb, min(te*rb, N)) with asynchronous copies
+// (cp.async): the issuing threads do not wait for the loads, so staging the next step's
+// parameters costs the current step nothing.  The caller commits the copy group.
+__device__ void stage_epilogue_params(const ChainOp &op, int tb, int te, const EpiSmem &ep,
+                                      int tid) {
+  const int r0 = tb * op.rb;
+  const int rows = te > tb ? min((te - tb) * op.rb, op.N - r0) : 0;
+  const float *step = op.out_mode == kOutF32Acc ? op.acc_step : op.out_step;
+  for (int i = tid; i < rows; i += kCT) {
+    const int n = r0 + i;
+    cp_async4(ep.qm + i, op.quant_m32 + n);
+    cp_async4(ep.step + i, step + n);
+    const int c = n - op.amax_c0;
+    if (op.amax_dst && c >= 0 && c < op.amax_cols) {
+      if (op.amax_smooth)
+        cp_async4(ep.smooth + i, op.amax_smooth + c);
+      else
+        ep.smooth[i] = 1.0f;
+    } else {
+      ep.smooth[i] = -1.0f;
+    }
+  }
+}
+
+// Step descriptors live in a window of kWindow shared-memory slots, refilled kWindow - 1
+// steps ahead with asynchronous copies, so the consumers never wait on a descriptor load.
+constexpr int kWindow = 8;
+constexpr int kOpChunks = static_cast<int>(sizeof(ChainOp) / 16);
+
+__device__ __forceinline__ void fetch_descriptor(ChainOp *window, const ChainOp *ops, int s,
+                                                 int lane) {
+  const uint4 *src = reinterpret_cast<const uint4 *>(ops + s);
+  uint4 *dst = reinterpret_cast<uint4 *>(window + (s % kWindow));
+  for (int c = lane; c < kOpChunks; c += 32) cp_async16(dst + c, src + c);
+}
+
 // Consumes this CTA's tiles [tb, te) of one step.  `it` is the ring iteration counter shared
 // with the producer's issue order.
 template <int TT, int RPW, bool TOPK>
 __device__ void consume_tiles(const ChainOp &op, const ChainArgs &a, int tb, int te, int &it,
                               const uint8_t *ring, const int8_t *xq, uint64_t *bars,
-                              const float *s_ratio, uint64_t *cand, int *s_amax, int tid,
-                              bool &ok, unsigned long long *tr) {
+                              const float *s_ratio, uint64_t *cand, int *s_amax,
+                              const EpiSmem &ep, int tid, bool &ok, unsigned long long *tr) {
   const int warp = tid >> 5, lane = tid & 31;
   const int it_first = it;
   constexpr int RB = kCW * RPW;
@@ -237,23 +318,6 @@ __device__ void consume_tiles(const ChainOp &op, const ChainArgs &a, int tb, int
     for (int r = 0; r < RPW; ++r)
 #pragma unroll
       for (int t = 0; t < TT; ++t) acc[r][t] = 0;
-    // This lane's epilogue parameters (row lane / TT of the warp's rows), loaded while the
-    // tile's weights stream in rather than after the reduction.
-    int e_qm = 1;
-    float e_step = 0.0f, e_smooth = 1.0f;
-    bool e_amax = false;
-    {
-      const int n = tile * RB + warp * RPW + lane / TT;
-      if (lane < RPW * TT && n < op.N) {
-        if (op.out_mode == kOutF32 || op.out_mode == kOutQuant) e_qm = op.quant_m[n];
-        e_step = op.out_mode == kOutF32Acc ? op.acc_step[n] : op.out_step[n];
-        if (op.amax_dst) {
-          const int c = n - op.amax_c0;
-          e_amax = c >= 0 && c < op.amax_cols;
-          if (e_amax && op.amax_smooth) e_smooth = op.amax_smooth[c];
-        }
-      }
-    }
     for (int kci = 0; kci < op.nk; ++kci, ++it) {
       const int slot = it % a.ns;
       const int use = it / a.ns;
@@ -299,6 +363,12 @@ __device__ void consume_tiles(const ChainOp &op, const ChainArgs &a, int tb, int
       const int row = warp * RPW + r;
       const int n = tile * RB + row;
       if (t < a.T && n < op.N && ok) {
+        // per-row parameters staged in shared memory before the step's grid barrier
+        const int lr = (tile - tb) * RB + row;
+        const int e_qm = ep.qm[lr];
+        const float e_step = ep.step[lr];
+        const float e_smooth = ep.smooth[lr];
+        const bool e_amax = e_smooth >= 0.0f;
         const float step = dyn ? s_ratio[t] * e_step : e_step;
         if (op.out_mode == kOutAccI32) {
           static_cast<int32_t *>(op.y)[t * op.ldy + n] = mine;
@@ -320,7 +390,8 @@ __device__ void consume_tiles(const ChainOp &op, const ChainArgs &a, int tb, int
             static_cast<float *>(op.y)[t * op.ldy + n] = v;
             if (e_amax) {
               // fp32 output consumed by a dyntok step: reduce its amax |y * s_next| per token
-              const float av = op.amax_smooth ? fabsf(v * e_smooth) : fabsf(v);
+              // (e_smooth is 1 when that step has no smoothing: v * 1 == v exactly)
+              const float av = fabsf(v * e_smooth);
               if (av > 0.0f) atomicMax(s_amax + t, __float_as_int(av));
             }
           }
@@ -333,12 +404,12 @@ __device__ void consume_tiles(const ChainOp &op, const ChainArgs &a, int tb, int
 template <int TT, bool TOPK>
 __device__ void consume_dispatch(const ChainOp &op, const ChainArgs &a, int tb, int te, int &it,
                                  const uint8_t *ring, const int8_t *xq, uint64_t *bars,
-                                 const float *s_ratio, uint64_t *cand, int *s_amax, int tid,
-                                 bool &ok, unsigned long long *tr) {
+                                 const float *s_ratio, uint64_t *cand, int *s_amax,
+                                 const EpiSmem &ep, int tid, bool &ok, unsigned long long *tr) {
   switch (op.rpw) {
-    case 1: consume_tiles<TT, 1, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, tid, ok, tr); break;
-    case 2: consume_tiles<TT, 2, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, tid, ok, tr); break;
-    default: consume_tiles<TT, 4, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, tid, ok, tr); break;
+    case 1: consume_tiles<TT, 1, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, ep, tid, ok, tr); break;
+    case 2: consume_tiles<TT, 2, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, ep, tid, ok, tr); break;
+    default: consume_tiles<TT, 4, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, ep, tid, ok, tr); break;
   }
 }
 
@@ -459,10 +530,21 @@ __device__ void topk_finish(const ChainOp &op, const ChainArgs &a, int tb, int t
 template <int TT>
 __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t *ring = smem;
-  int8_t *xq = reinterpret_cast<int8_t *>(smem + a.ring_bytes);
-  uint64_t *cand = reinterpret_cast<uint64_t *>(smem + a.ring_bytes + TT * a.kpad_max);
+  ChainOp *window = reinterpret_cast<ChainOp *>(smem);
+  uint8_t *ring = smem + kWindow * sizeof(ChainOp);
+  int8_t *xq = reinterpret_cast<int8_t *>(ring + a.ring_bytes);
+  uint64_t *cand = reinterpret_cast<uint64_t *>(ring + a.ring_bytes + TT * a.kpad_max);
   uint64_t *bars = cand + TT * a.cand_cap;
+  EpiSmem ep_buf[2];
+  {
+    int *p = reinterpret_cast<int *>(bars + 2 * kMaxStages);
+    for (int b = 0; b < 2; ++b) {
+      ep_buf[b].qm = p;
+      ep_buf[b].step = reinterpret_cast<float *>(p + a.max_rows);
+      ep_buf[b].smooth = ep_buf[b].step + a.max_rows;
+      p += 3 * a.max_rows;
+    }
+  }
   __shared__ float s_part[kCW][TT];
   __shared__ float s_ratio[TT];
   __shared__ float s_inv[TT];
@@ -475,6 +557,7 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
 
   if (threadIdx.x == 0) {
     s_abort = 0;
+    for (int t = 0; t < TT; ++t) s_amax[t] = 0;
     for (int s = 0; s < a.ns; ++s) {
       mbar_init(smem_addr(&bars[s]), 1);
       mbar_init(smem_addr(&bars[kMaxStages + s]), kCW);
@@ -489,15 +572,23 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
     int it = 0;
     bool ok = true;
     for (int s = 0; s < a.n_ops && ok; ++s) {
+      // The producer runs ahead of the consumers: fetch the next descriptor into L1 now, and
+      // keep this one's fields in registers (the barrier asm would otherwise force reloads).
+      if (lane < 3 && s + 1 < a.n_ops)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char *>(a.ops + s + 1) + lane * 128));
       const ChainOp &op = a.ops[s];
+      const int8_t *w = op.w;
+      const int64_t ldw = op.ldw;
+      const int N = op.N, rb = op.rb, kc = op.kc, nk = op.nk, k_pad = op.k_pad;
+      const bool whole_rows = nk == 1 && kc == ldw;
       int tb, te;
       split_range(op.num_tiles, G, blockIdx.x, tb, te);
       unsigned long long *ptr =
           a.trace ? a.trace + (static_cast<size_t>(blockIdx.x) * a.n_ops + s) * 8 : nullptr;
       if (ptr && lane == 0) ptr[4] = global_timer_ns();
       for (int tile = tb; tile < te && ok; ++tile) {
-        const int rows = min(op.rb, op.N - tile * op.rb);
-        for (int kci = 0; kci < op.nk; ++kci, ++it) {
+        const int rows = min(rb, N - tile * rb);
+        for (int kci = 0; kci < nk; ++kci, ++it) {
           const int slot = it % a.ns;
           const int use = it / a.ns;
           if (it >= a.ns) {
@@ -505,12 +596,12 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
                                    kDevTimeoutEmpty);
             if (!ok) break;
           }
-          const int k0 = kci * op.kc;
-          const int bytes = min(op.kc, op.k_pad - k0);
+          const int k0 = kci * kc;
+          const int bytes = min(kc, k_pad - k0);
           const uint32_t full = smem_addr(&bars[slot]);
           const uint32_t dst = smem_addr(ring + static_cast<size_t>(slot) * a.stage_bytes);
-          const int8_t *src = op.w + static_cast<int64_t>(tile * op.rb) * op.ldw + k0;
-          if (op.nk == 1 && op.kc == op.ldw) {
+          const int8_t *src = w + static_cast<int64_t>(tile * rb) * ldw + k0;
+          if (whole_rows) {
             // whole rows: the tile is one contiguous block of rows * k_pad bytes, one copy
             if (lane == 0) {
               mbar_arrive_expect_tx(full, static_cast<uint32_t>(rows * bytes));
@@ -520,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
             if (lane == 0) mbar_arrive_expect_tx(full, static_cast<uint32_t>(rows * bytes));
             __syncwarp();
             for (int r = lane; r < rows; r += 32)
-              bulk_g2s(dst + r * op.kc, src + static_cast<int64_t>(r) * op.ldw, bytes, full, pol);
+              bulk_g2s(dst + r * kc, src + static_cast<int64_t>(r) * ldw, bytes, full, pol);
           }
           __syncwarp();
         }
@@ -534,13 +625,43 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
   const int tid = threadIdx.x;
   int it = 0;
   bool ok = true;
+  // descriptors 0 .. kWindow-2 into the window, then step 0's per-row epilogue parameters;
+  // every later descriptor is fetched kWindow-1 steps ahead and every later step's
+  // parameters one step ahead
+  if (tid < 32)
+    for (int s = 0; s < kWindow - 1 && s < a.n_ops; ++s) fetch_descriptor(window, a.ops, s, tid);
+  cp_async_commit();
+  cp_async_wait_all();
+  consumer_sync();
+  {
+    int tb0, te0;
+    split_range(window[0].num_tiles, G, blockIdx.x, tb0, te0);
+    stage_epilogue_params(window[0], tb0, te0, ep_buf[0], tid);
+    cp_async_commit();
+  }
   for (int s = 0; s < a.n_ops; ++s) {
-    const ChainOp &op = a.ops[s];
-    // the next step's descriptor into L1 while this one runs
-    if (tid < 3 && s + 1 < a.n_ops)
-      asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char *>(a.ops + s + 1) + tid * 128));
+    const ChainOp &op = window[s % kWindow];
+    const EpiSmem &ep = ep_buf[s & 1];
     int tb, te;
     split_range(op.num_tiles, G, blockIdx.x, tb, te);
+    // Work that does not depend on the previous step goes before its grid barrier: the
+    // descriptor kWindow-1 steps ahead, the next step's per-row epilogue parameters into the
+    // other shared-memory buffer, this thread's first smoothing factors into registers, the
+    // candidate slots of a top-k step.  Exactly one copy group is committed per step, so
+    // "all but the newest group" is this step's parameters (and older descriptors).
+    if (tid < 32 && s + kWindow - 1 < a.n_ops) fetch_descriptor(window, a.ops, s + kWindow - 1, tid);
+    if (s + 1 < a.n_ops) {
+      const ChainOp &op1 = window[(s + 1) % kWindow];
+      int tb1, te1;
+      split_range(op1.num_tiles, G, blockIdx.x, tb1, te1);
+      stage_epilogue_params(op1, tb1, te1, ep_buf[(s + 1) & 1], tid);
+    }
+    cp_async_commit();
+    cp_async_wait_all_but_newest();
+    float4 s_pre[4];
+    preload_smooth(op, tid, s_pre);
+    if (op.topk)
+      for (int i = tid; i < TT * a.cand_cap; i += kCT) cand[i] = 0ull;
     if (op.barrier_before && s > 0) {
       // Once one grid wait has run out, later ones are skipped so the kernel still ends.
       if (tid == 0 && !s_abort) {
@@ -561,35 +682,37 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
     unsigned long long *tr =
         a.trace ? a.trace + (static_cast<size_t>(blockIdx.x) * a.n_ops + s) * 8 : nullptr;
     if (tr && tid == 0) tr[0] = global_timer_ns();
-    if (tid < TT) s_amax[tid] = 0;
     if (te > tb || op.topk) {
-      if (te > tb) quantise_input<TT>(op, a.T, xq, a.kpad_max, s_ratio, s_inv, s_part, tid);
+      // (quantise_input ends with a consumer barrier: the staged parameters are visible)
+      if (te > tb) quantise_input<TT>(op, a.T, xq, a.kpad_max, s_ratio, s_inv, s_part, tid, s_pre);
+      else consumer_sync();
       if (tr && tid == 0) tr[1] = global_timer_ns();
       // the CTA owning tile 0 publishes the per-token ratios
       if (tb == 0 && te > 0 && op.ratio_out && tid < a.T && op.act_mode == kActDyntok)
         op.ratio_out[tid] = s_ratio[tid];
       if (op.topk) {
-        for (int i = tid; i < TT * a.cand_cap; i += kCT) cand[i] = 0ull;
-        consumer_sync();
-        consume_dispatch<TT, true>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, tid, ok, tr);
+        consume_dispatch<TT, true>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, ep, tid, ok, tr);
         consumer_sync();
         int cap = 1;
         while (static_cast<size_t>(cap) * 2 * 8 <= a.ring_bytes) cap <<= 1;
         topk_finish<TT>(op, a, tb, te, cand, reinterpret_cast<uint64_t *>(ring), cap, tid);
       } else {
-        consume_dispatch<TT, false>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, tid, ok, tr);
+        consume_dispatch<TT, false>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, ep, tid, ok, tr);
       }
     }
-    // arrival: every output of this CTA for step s is written (and its amax share reduced)
+    // arrival: every output of this CTA for step s is written (and its amax share reduced).
+    // (read from the descriptor before the barrier: its window slot is refilled right after)
+    float *const amax_dst = op.amax_dst;
     consumer_sync();
-    if (tr && tid == 0) tr[2] = global_timer_ns();
-    if (op.amax_dst) {
-      if (tid < a.T && s_amax[tid] > 0) atomicMax(reinterpret_cast<int *>(op.amax_dst) + tid, s_amax[tid]);
-      consumer_sync();
-    }
     if (tid == 0) {
-      // release: the CTA's writes (ordered before this by the consumer barrier) become
-      // visible to any CTA that acquires the counter
+      if (tr) tr[2] = global_timer_ns();
+      if (amax_dst)
+        for (int t = 0; t < a.T; ++t)
+          if (s_amax[t] > 0) atomicMax(reinterpret_cast<int *>(amax_dst) + t, s_amax[t]);
+      // only this thread touches s_amax between the consume phases: reset for the next step
+      for (int t = 0; t < TT; ++t) s_amax[t] = 0;
+      // release: the CTA's writes (ordered before this by the consumer barrier, and this
+      // thread's amax reductions) become visible to any CTA that acquires the counter
       asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.bar + s), "r"(1u) : "memory");
       if (tr) tr[3] = global_timer_ns();
     }
@@ -629,11 +752,14 @@ bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, Chain
   int kpad_max = 16;
   size_t stage = 0;
   size_t cand_cap = 0;
+  int max_rows = 8;
+  // Stage size target: every stage carries ~24 KB (whole-row tiles of up to 32 rows, or 8-row
+  // K chunks of 3 KB per row for long rows), so the fixed-size ring slots stay full.
+  constexpr int kMaxStage = 24576;
   for (int s = 0; s < n_ops; ++s) {
     ChainOp &op = ops[s];
     if (op.topk && s != n_ops - 1) return false;  // the LM-head step must be last
     auto tiles = [&](int rb) { return (op.N + rb - 1) / rb; };
-    constexpr int kMaxStage = 32768;
     const int min_tiles = op.topk ? p.grid : 2 * p.grid;
     if (op.k_pad * 8 <= kMaxStage) {
       // whole-row tiles: a tile is one contiguous rb x k_pad block (one bulk copy per stage)
@@ -645,7 +771,7 @@ bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, Chain
         }
       op.kc = op.k_pad;
     } else {
-      // long rows: 8-row tiles streamed in K chunks of 4 KB per row
+      // long rows: 8-row tiles streamed in K chunks
       op.rpw = 1;
       op.kc = kMaxStage / 8;
     }
@@ -654,8 +780,9 @@ bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, Chain
     op.num_tiles = tiles(op.rb);
     stage = std::max(stage, static_cast<size_t>(op.rb) * op.kc);
     kpad_max = std::max(kpad_max, op.k_pad);
+    const int max_tiles = (op.num_tiles + p.grid - 1) / p.grid;
+    max_rows = std::max(max_rows, max_tiles * op.rb);
     if (op.topk) {
-      const int max_tiles = (op.num_tiles + p.grid - 1) / p.grid;
       size_t c = 1;
       while (c < static_cast<size_t>(max_tiles) * op.rb) c <<= 1;
       cand_cap = c;
@@ -663,9 +790,11 @@ bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, Chain
   }
   p.kpad_max = (kpad_max + 15) / 16 * 16;
   p.cand_cap = static_cast<int>(cand_cap);
+  p.max_rows = (max_rows + 3) / 4 * 4;
   p.stage_bytes = static_cast<uint32_t>(stage);
   const size_t fixed = static_cast<size_t>(p.tt) * p.kpad_max + static_cast<size_t>(p.tt) * cand_cap * 8 +
-                      2 * kMaxStages * 8;
+                      2 * kMaxStages * 8 + 2 * static_cast<size_t>(p.max_rows) * 12 +
+                      kWindow * sizeof(ChainOp);
   // the SM's 228 KB split between the co-resident CTAs, less the per-CTA reservation and
   // static shared memory
   const size_t budget = 233472 / cps - 1024 - 2048;
@@ -704,6 +833,7 @@ cudaError_t launch_chain(const ChainOp *ops_dev, int n_ops, int T, const ChainPl
   a.stage_bytes = plan.stage_bytes;
   a.kpad_max = plan.kpad_max;
   a.cand_cap = plan.cand_cap;
+  a.max_rows = plan.max_rows;
   a.ring_bytes = plan.ring_bytes;
   a.trace = trace;
   void (*kern)(ChainArgs) = nullptr;

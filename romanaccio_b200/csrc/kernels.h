@@ -150,6 +150,7 @@ struct alignas(128) ChainOp {
   // epilogue
   int out_mode;
   const int16_t *quant_m;
+  const int32_t *quant_m32;  // the same values widened (4-byte asynchronous staging)
   int trunc, qmax, out_i16;
   const float *out_step;
   const float *acc_step;
@@ -167,7 +168,7 @@ struct alignas(128) ChainOp {
 };
 
 struct ChainPlan {
-  int tt, grid, kpad_max, cand_cap, ns;
+  int tt, grid, kpad_max, cand_cap, max_rows, ns;
   uint32_t stage_bytes, ring_bytes;
   size_t smem;
 };
