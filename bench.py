@@ -34,6 +34,9 @@ WORKLOAD = "qwen2.5-1.5b-shaped W8A8 decode: 28 x {qkv,o,gate_up,down} + LM head
 # DRAM bytes (read + write) per launch of the gate_up GEMV at T=1 from one ncu capture
 # (profiles/gemv_w8a8_gate_up_qwen15b_t1.md): 27.666688 MB read + 0 B written.
 GEMV_TRAFFIC_BYTES = 27666688
+# DRAM bytes per algorithmic byte of the chain kernel from one ncu capture of a 4-layer,
+# 1024-vocab chain (profiles/chain_kernel_qwen15b_4layer.md): 189.84 MB read / 188.7 MB.
+CHAIN_TRAFFIC_RATIO = 1.006
 
 
 def env_int(name: str, default: int) -> int:
@@ -226,7 +229,7 @@ def run_ours(args) -> None:
     shape = synth.QWEN25_15B
     ctx = Context(local)
     stack = DecodeStack(ctx, shape, T, rank=rank, world=world, group=group, seed=0,
-                        layers=args.layers, use_chain=args.chain)
+                        layers=args.layers, use_chain=not args.per_linear)
     x_host = torch.from_numpy(
         np.random.default_rng(rank).standard_normal((T, shape.hidden)).astype(np.float32)).pin_memory()
     ids_host = torch.empty((T,), dtype=torch.int32).pin_memory()
@@ -306,7 +309,32 @@ def run_ours(args) -> None:
     gemv_s = r0.elapsed_time(r1) / 1e3 / (reps * len(gu))
     del g
     peak, peak_kind = measured_peaks()
-    achieved = sb.gemv_launch / gemv_s / 1e9
+    gemv_achieved = sb.gemv_launch / gemv_s / 1e9
+    gemv_roof = {"kernel": "gemv_w8a8 gate_up 1536x17920 T=%d (standalone launches)" % T,
+                 "achieved": gemv_achieved, "frac": gemv_achieved / peak,
+                 "launch_us": gemv_s * 1e6, "algorithmic_bytes": sb.gemv_launch,
+                 "traffic": GEMV_TRAFFIC_BYTES}
+    if stack.chain is not None:
+        # dominant (only) kernel of the step: the persistent chain kernel; one launch moves the
+        # whole step's algorithmic bytes (world == 1: linears + LM head)
+        chain_bytes = sb.linear + (sb.lm_head if world == 1 else 0)
+        for _ in range(3):
+            stack.chain.forward()
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(reps):
+            stack.chain.forward()
+        c1.record(stream)
+        torch.cuda.synchronize()
+        chain_s = c0.elapsed_time(c1) / 1e3 / reps
+        roof_kernel = "chain_kernel (whole decode step, 1 launch)"
+        roof_bytes, roof_s = chain_bytes, chain_s
+        roof_traffic = int(chain_bytes * CHAIN_TRAFFIC_RATIO) if CHAIN_TRAFFIC_RATIO else None
+    else:
+        roof_kernel = gemv_roof["kernel"]
+        roof_bytes, roof_s, roof_traffic = sb.gemv_launch, gemv_s, GEMV_TRAFFIC_BYTES
+    achieved = roof_bytes / roof_s / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -338,14 +366,14 @@ def run_ours(args) -> None:
                        "parallelism": f"linears replicated per GPU, LM head vocab-sharded x{world}",
                        "l2": f"weights streamed every step: {step_bytes / 1e9:.2f} GB per GPU > 126 MB L2",
                        "cuda_graph": graph_note,
-                       "kernel": "per-linear GEMV launches" if not args.chain else
+                       "kernel": "per-linear GEMV launches" if args.per_linear else
                                  "persistent decode-chain kernel (1 cooperative launch per step)"},
             "hbm_gbs_step": step_bytes / (ms / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": GEMV_TRAFFIC_BYTES,
-                         "kernel": "gemv_w8a8 gate_up 1536x17920 T=%d" % T,
-                         "peak_kind": peak_kind, "launch_us": gemv_s * 1e6,
-                         "algorithmic_bytes": sb.gemv_launch},
+                         "frac": achieved / peak, "traffic": roof_traffic,
+                         "kernel": roof_kernel, "peak_kind": peak_kind,
+                         "launch_us": roof_s * 1e6, "algorithmic_bytes": roof_bytes,
+                         "secondary": gemv_roof},
             "e2e": {"value": world * T / (ms_e2e / 1e3), "unit": "tok/s",
                     "h2d_bytes_per_step": T * shape.hidden * 4, "d2h_bytes_per_step": T * 4},
             "gpu_launches": launches_per_step * args.steps,
@@ -368,8 +396,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=None)
-    ap.add_argument("--chain", action="store_true",
-                    help="run the step as the persistent decode-chain kernel (one launch)")
+    ap.add_argument("--per-linear", action="store_true",
+                    help="launch each linear separately instead of the persistent decode-chain "
+                         "kernel (one cooperative launch per step)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
