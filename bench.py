@@ -135,6 +135,9 @@ def cpu_step_fn(params, lm, T: int, shape):
     from oracle import oracle as O
     lib = O.lib()
     import ctypes as C
+    # every host core this process may run on (launchers such as torchrun export
+    # OMP_NUM_THREADS=1 to their workers)
+    lib.orc_set_threads(len(os.sched_getaffinity(0)))
 
     def p(a):
         return a.ctypes.data

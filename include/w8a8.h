@@ -174,6 +174,18 @@ w8a8_status w8a8_linear_forward(w8a8_linear *linear, const float *x_dev, int64_t
                                 int32_t act_mode, int32_t out_mode, void *y_dev, int64_t ldy,
                                 float *ratio_dev, void *stream);
 
+/* Contraction engine used by forward / forward_q (no reference counterpart: the reference has
+ * one NPU engine).  AUTO streams the weights through the GEMV kernels for small token counts and
+ * switches to the tcgen05 tensor-core GEMM above W8A8_TC_MIN_TOKENS; GEMV and TENSOR force one.
+ * Both give bit-identical results. */
+typedef enum {
+    W8A8_PATH_AUTO   = 0,
+    W8A8_PATH_GEMV   = 1,
+    W8A8_PATH_TENSOR = 2
+} w8a8_path;
+#define W8A8_TC_MIN_TOKENS 16
+w8a8_status w8a8_linear_set_path(w8a8_linear *linear, int32_t path);
+
 /* ---------------------------------------------------------------------------------------
  * LM head shard: a linear over a contiguous block of vocab rows [row_offset, row_offset + N)
  * (the contiguous vocab split of dual_die_splitter.py:63-147 and

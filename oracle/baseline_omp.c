@@ -32,6 +32,16 @@ int orc_num_threads(void) {
 #endif
 }
 
+/* Thread count of the parallel regions that follow (a launcher may have set OMP_NUM_THREADS=1
+ * for its worker processes; the timed CPU baseline uses every host core it was given). */
+void orc_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 static int32_t dot_i8(const int8_t *a, const int8_t *b, int32_t K) {
     int32_t s = 0;
     for (int32_t k = 0; k < K; ++k) s += (int32_t)a[k] * (int32_t)b[k];

@@ -31,6 +31,7 @@ _ORACLE_SIGS = {
     "orc_topk": (None, [_P, _I64, _I32, _I32, _I32, _I32, _P, _P]),
     "orc_argmax": (C.c_int32, [_P, _I32]),
     "orc_num_threads": (C.c_int, []),
+    "orc_set_threads": (None, [C.c_int]),
     "orc_linear_dyntok_omp": (None, [_P, _I32, _I32, _I32, _P, _P, _F, _P, _I32, _P, _P, _P, _P]),
     "orc_lmhead_topk_omp": (None, [_P, _I32, _I32, _I32, _P, _F, _P, _I32, _P, _P, _P, _P]),
 }

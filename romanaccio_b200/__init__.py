@@ -4,13 +4,15 @@ The compute path is libw8a8.so (hand-written CUDA kernels behind the C ABI in
 include/w8a8.h); this package is its host-side mirror of romanaccio's operator surface.
 """
 from ._lib import (ACT_DYNTOK, ACT_STATIC, DTYPE_FP16, DTYPE_INT8, DTYPE_INT16, OUT_ACC_I32,
-                   OUT_F32, OUT_F32_ACC, OUT_QUANT, TOPK_MAX, W8A8Error)
+                   OUT_F32, OUT_F32_ACC, OUT_QUANT, PATH_AUTO, PATH_GEMV, PATH_TENSOR, TOPK_MAX,
+                   W8A8Error)
 from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
 from .lmhead import LmHeadShard, VocabShardedLmHead, shard_range
 
 __all__ = [
     "ACT_DYNTOK", "ACT_STATIC", "DTYPE_FP16", "DTYPE_INT8", "DTYPE_INT16", "OUT_ACC_I32",
-    "OUT_F32", "OUT_F32_ACC", "OUT_QUANT", "TOPK_MAX", "W8A8Error", "Context",
+    "OUT_F32", "OUT_F32_ACC", "OUT_QUANT", "PATH_AUTO", "PATH_GEMV", "PATH_TENSOR", "TOPK_MAX",
+    "W8A8Error", "Context",
     "SubgraphScaleInfo", "W8A8Linear", "topk_merge", "LmHeadShard", "VocabShardedLmHead",
     "shard_range",
 ]

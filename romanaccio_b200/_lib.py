@@ -28,6 +28,8 @@ DTYPE_FP16, DTYPE_INT8, DTYPE_INT16 = 0, 1, 2
 ACT_STATIC, ACT_DYNTOK = 0, 1
 OUT_ACC_I32, OUT_QUANT, OUT_F32, OUT_F32_ACC = 0, 1, 2, 3
 TOPK_MAX = 64
+PATH_AUTO, PATH_GEMV, PATH_TENSOR = 0, 1, 2
+TC_MIN_TOKENS = 16
 
 
 class ScaleInfo(C.Structure):
@@ -85,6 +87,7 @@ SIGNATURES = {
     "w8a8_linear_create": (C.c_int, [_P, C.POINTER(LinearDesc), C.POINTER(_P)]),
     "w8a8_linear_destroy": (None, [_P]),
     "w8a8_linear_device_bytes": (_SZ, [_P]),
+    "w8a8_linear_set_path": (C.c_int, [_P, _I32]),
     "w8a8_pack_input": (C.c_int, [_P, _P, _I64, _I32, _I32, _P, _I64, _P, _P]),
     "w8a8_linear_forward_q": (C.c_int, [_P, _P, _I64, _I32, _I32, _P, _I32, _P, _I64, _P]),
     "w8a8_unpack_output": (C.c_int, [_P, _P, _I64, _I32, _I32, _P, _P, _I64, _P]),

@@ -82,6 +82,12 @@ struct w8a8_linear {
   uint64_t *lists = nullptr;    // top-k per-CTA candidate lists
   size_t lists_keys = 0;
   unsigned *counter = nullptr;
+  // tensor-core path: split-K workspace and per-tile counters (zero between launches)
+  int path = W8A8_PATH_AUTO;
+  int32_t *tc_ws = nullptr;
+  size_t tc_ws_elems = 0;
+  unsigned *tc_count = nullptr;
+  size_t tc_count_n = 0;
   size_t device_bytes = 0;
 };
 
@@ -124,7 +130,33 @@ void linear_free(w8a8_linear *l) {
   cudaFree(l->ratio);
   cudaFree(l->lists);
   cudaFree(l->counter);
+  cudaFree(l->tc_ws);
+  cudaFree(l->tc_count);
   delete l;
+}
+
+// Grows the split-K partial planes / per-tile arrival counters of the tensor-core path (the
+// counters start at zero and the kernel leaves them zero again).
+w8a8_status ensure_tc_scratch(w8a8_linear *l, size_t ws_elems, size_t count_n) {
+  if (ws_elems > l->tc_ws_elems) {
+    cudaFree(l->tc_ws);
+    l->tc_ws = nullptr;
+    l->tc_ws_elems = 0;
+    w8a8_status st = dev_alloc(&l->tc_ws, ws_elems, nullptr);
+    if (st != W8A8_SUCCESS) return st;
+    W8A8_CUDA(cudaMemset(l->tc_ws, 0, ws_elems * sizeof(int32_t)));
+    l->tc_ws_elems = ws_elems;
+  }
+  if (count_n > l->tc_count_n) {
+    cudaFree(l->tc_count);
+    l->tc_count = nullptr;
+    l->tc_count_n = 0;
+    w8a8_status st = dev_alloc(&l->tc_count, count_n, nullptr);
+    if (st != W8A8_SUCCESS) return st;
+    W8A8_CUDA(cudaMemset(l->tc_count, 0, count_n * sizeof(unsigned)));
+    l->tc_count_n = count_n;
+  }
+  return W8A8_SUCCESS;
 }
 
 // Grows the activation staging buffers to hold T tokens (allocates only when T exceeds the
@@ -178,6 +210,34 @@ w8a8_status check_modes(const w8a8_linear *l, int act_mode, int out_mode) {
 w8a8_status run_gemv(w8a8_linear *l, const int8_t *xq, int64_t ldx, int T, int act_mode,
                      const float *ratio, int out_mode, void *y, int64_t ldy, bool pdl,
                      cudaStream_t st) {
+  const bool tensor = l->path == W8A8_PATH_TENSOR ||
+                      (l->path == W8A8_PATH_AUTO && T >= W8A8_TC_MIN_TOKENS);
+  if (tensor) {
+    TcPlan plan;
+    if (!plan_tc(T, l->N, l->k_pad, l->ctx->sm_count, &plan))
+      return fail(W8A8_ERR_NOT_SUPPORTED, "no tensor-core plan for T=%d N=%d K=%d", T, l->N, l->K);
+    if (plan.splits > 1) {
+      w8a8_status s = ensure_tc_scratch(l, static_cast<size_t>(plan.splits) * T * l->N,
+                                        static_cast<size_t>(plan.tiles_n) * plan.tiles_t);
+      if (s != W8A8_SUCCESS) return s;
+    }
+    TcLaunch L = {};
+    L.w = l->w;
+    L.ldw = l->k_pad;
+    L.k_extent_w = l->k_pad;
+    L.x = xq;
+    L.ldx = ldx;
+    L.k_extent_x = l->k_pad;
+    L.T = T;
+    L.N = l->N;
+    L.ep = make_epilogue(l, out_mode, act_mode, ratio, y, ldy);
+    L.ws = l->tc_ws;
+    L.tile_count = l->tc_count;
+    L.err = l->ctx->d_err;
+    L.pdl = pdl;
+    W8A8_CUDA(launch_tc(L, plan, st));
+    return W8A8_SUCCESS;
+  }
   const size_t out_elem = out_mode == W8A8_OUT_ACC_I32 ? 4
                           : out_mode == W8A8_OUT_QUANT ? (l->out_i16 ? 2 : 1)
                                                         : 4;
@@ -381,6 +441,14 @@ w8a8_status w8a8_linear_create(w8a8_ctx *ctx, const w8a8_linear_desc *d, w8a8_li
 void w8a8_linear_destroy(w8a8_linear *l) { linear_free(l); }
 
 size_t w8a8_linear_device_bytes(const w8a8_linear *l) { return l ? l->device_bytes : 0; }
+
+w8a8_status w8a8_linear_set_path(w8a8_linear *l, int32_t path) {
+  if (!l) return fail(W8A8_ERR_INVALID_ARG, "linear is NULL");
+  if (path != W8A8_PATH_AUTO && path != W8A8_PATH_GEMV && path != W8A8_PATH_TENSOR)
+    return fail(W8A8_ERR_INVALID_ARG, "path %d is not a w8a8_path", path);
+  l->path = path;
+  return W8A8_SUCCESS;
+}
 
 w8a8_status w8a8_pack_input(w8a8_linear *l, const float *x, int64_t ldx, int32_t T, int32_t act_mode,
                             int8_t *q, int64_t ldq, float *ratio, void *stream) {

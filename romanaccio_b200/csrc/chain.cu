@@ -8,7 +8,7 @@
 //
 // One CTA per SM, 8 consumer warps + 1 producer warp.  The producer warp streams the int8
 // weight slabs of every step this CTA owns, step after step, through an NS-deep shared-memory
-// ring with 1-D bulk copies (TMA engine, no tensor map, no multicast) completing on mbarriers.
+// ring with 1-D bulk copies (TMA engine, no tensor map, one CTA per copy) completing on mbarriers.
 // Weights do not depend on activations, so the producer runs ahead into the next linears while
 // the consumers are still busy or waiting: HBM never idles at a linear boundary.  Consumers,
 // per step: wait at a grid barrier when the step reads an earlier step's output, quantise the

@@ -29,7 +29,7 @@ __device__ __forceinline__ uint32_t smem_addr(const void *p) {
 }
 
 // ---------------------------------------------------------------------------------------
-// mbarrier + bulk copy (TMA 1-D, no tensor map, no multicast)
+// mbarrier + bulk copy (TMA 1-D, no tensor map, one CTA per copy)
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -119,15 +119,16 @@ __device__ __forceinline__ int32_t round_clamp(float x, float lim) {
   return __float2int_rn(c);
 }
 
+// Round-half-even of p / 2^trunc with one add and one arithmetic shift: with p = f * 2^t + r
+// (0 <= r < 2^t), adding 2^(t-1) - 1 + (f & 1) carries into f exactly when r > 2^(t-1), or when
+// r == 2^(t-1) and f is odd.
 __device__ __forceinline__ int32_t requant_quantm(int32_t acc, int32_t qm, int32_t trunc,
                                                   int32_t qmax) {
   const long long p = static_cast<long long>(acc) * static_cast<long long>(qm);
   long long q = p;
   if (trunc > 0) {
-    q = p >> trunc;  // floor
-    const long long rem = p - (q << trunc);
-    const long long half = 1LL << (trunc - 1);
-    q += (rem > half || (rem == half && (q & 1))) ? 1 : 0;
+    const long long odd = (p >> trunc) & 1LL;
+    q = (p + ((1LL << (trunc - 1)) - 1) + odd) >> trunc;
   }
   q = q < -qmax ? -qmax : (q > qmax ? qmax : q);
   return static_cast<int32_t>(q);

@@ -1,0 +1,591 @@
+// Tensor-core W8A8 contraction for token counts above the GEMV range (prefill, batched decode):
+// tcgen05.mma kind::i8 with int32 accumulators in TMEM, operands staged by 2-D TMA tiles with the
+// 128-byte swizzle (plain per-CTA loads).
+//
+// Math: acc[t, n] = sum_k q[t, k] * Wq[n, k] in exact int32 (the CMAC step, cmac.py:300-383 of
+// the reference's NPU model), then the per-output-channel epilogue shared with the GEMV kernels:
+// CvtPrecision_QuantM requant (attribute_int8_error.py:104-122) and the out_step / acc_step
+// dequant with the dyntok ratio (src/LFM3/lfm3_v2.cpp:971-1008, 1143-1183).
+//
+// Orientation: the weight tile is the MMA's A operand (M = 128 output channels = the 128 TMEM
+// lanes) and the token tile is B (N = BT tokens = TMEM columns).  Each epilogue thread owns one
+// output channel, so QuantM / out_step are per-thread constants and one warp's stores for one
+// token are 32 consecutive channels.
+//
+// Work split: units of (channel block, token block, K split), walked persistently by the CTAs
+// (unit = blockIdx.x + i * gridDim.x).  The accumulator is double-buffered in TMEM, so the
+// epilogue of one unit overlaps the main loop of the next.  When the channel x token tiles do not
+// fill the SMs, K is split: each split stores its int32 partial tile into its own plane of a
+// workspace, and the last split of a tile to arrive (an arrival counter per tile) adds the other
+// planes to its TMEM accumulator and runs the epilogue.  Integer sums are exact in any order.
+//
+// Warp roles (320 threads): warp 0 issues the TMA copies, warp 1 owns TMEM and issues the MMAs
+// (one thread), warps 2..9 run the epilogue; warp w reads TMEM lanes 32*(w%4)..+31 (the lane
+// quarter a warp may access is fixed by its id modulo 4) and the column chunks of parity (w-2)/4.
+#include <cuda.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace w8a8 {
+namespace {
+
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kBM = 128;                       // output channels per tile (MMA M)
+constexpr int kBK = 128;                       // K bytes per stage = one 128-byte swizzle row
+constexpr int kMmaK = 32;                      // K of one tcgen05.mma kind::i8
+constexpr uint32_t kTileWBytes = kBM * kBK;    // weight bytes per stage
+constexpr int kMaxStages = 16;
+constexpr int kMaxBT = 256;
+constexpr int kMaxDynSmem = 232448;            // sm_100 opt-in limit per block
+
+struct TcArgs {
+  int N, T, BT;
+  int tiles_t, splits, k_iters, ips, units, ns;
+  uint32_t stage_bytes, buf_stride, tmem_cols, idesc;
+  Epilogue ep;
+  int32_t *ws;            // split-K partial planes [splits, T, N]
+  unsigned *tile_count;   // split-K arrival counters [tiles] (all zero between launches)
+  int *err;
+  uint64_t pol_w;         // L2 policy selector for the weight copies: 0 normal, 1 evict-first
+};
+
+// ------------------------------------------------------------------------------------------
+// tcgen05 / TMA wrappers
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, int8 x int8 -> int32.
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on `bar` once every tcgen05 operation issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns; the wait is inside the same statement so no use of
+// the registers can be scheduled before the data has arrived.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap *map, int c0,
+                                                 int c1, uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile written by TMA with the 128-byte swizzle:
+// rows of 128 bytes, 8-row swizzle atoms 1024 bytes apart (stride byte offset), leading byte
+// offset unused (encoded 1), descriptor version 1, layout type 2 = SWIZZLE_128B.  The tile base
+// is 1024-byte aligned, so the base-offset field is 0.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (1ull << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void epi_bar_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+}
+
+// ------------------------------------------------------------------------------------------
+// Epilogue: one thread = one output channel n; TMEM columns = tokens.  Specialised per output
+// mode so that the per-element code is a short straight line.
+// ------------------------------------------------------------------------------------------
+struct ChanParams {
+  int32_t qm;
+  float step;   // out_step[n] (F32) or acc_step[n] (F32_ACC)
+};
+
+template <int MODE>
+__device__ __forceinline__ ChanParams chan_params(const Epilogue &ep, int n, bool n_ok) {
+  ChanParams cp{0, 0.0f};
+  if (!n_ok) return cp;
+  if (MODE == kOutQuant || MODE == kOutF32) cp.qm = ep.quant_m[n];
+  if (MODE == kOutF32) cp.step = ep.out_step[n];
+  if (MODE == kOutF32Acc) cp.step = ep.acc_step[n];
+  return cp;
+}
+
+template <int MODE>
+__device__ __forceinline__ int out_size(const Epilogue &ep) {
+  return MODE == kOutQuant ? (ep.out_i16 ? 2 : 1) : 4;
+}
+
+// Output value of (channel, token t) written at p.
+template <int MODE>
+__device__ __forceinline__ void emit(const Epilogue &ep, const ChanParams &cp, int32_t acc, int t,
+                                     char *p) {
+  if (MODE == kOutAccI32) {
+    *reinterpret_cast<int32_t *>(p) = acc;
+  } else if (MODE == kOutQuant) {
+    const int yq = requant_quantm(acc, cp.qm, ep.trunc, ep.qmax);
+    if (ep.out_i16)
+      *reinterpret_cast<int16_t *>(p) = static_cast<int16_t>(yq);
+    else
+      *reinterpret_cast<int8_t *>(p) = static_cast<int8_t>(yq);
+  } else if (MODE == kOutF32) {
+    const int yq = requant_quantm(acc, cp.qm, ep.trunc, ep.qmax);
+    const float step = ep.act_mode == kActDyntok ? ep.ratio[t] * cp.step : cp.step;
+    *reinterpret_cast<float *>(p) = static_cast<float>(yq) * step;
+  } else {
+    const float step = ep.act_mode == kActDyntok ? ep.ratio[t] * cp.step : cp.step;
+    *reinterpret_cast<float *>(p) = __int2float_rn(acc) * step;
+  }
+}
+
+// 32 lanes x CW consecutive 32-bit TMEM columns (CW = 16 or 32), load and wait in one statement.
+template <int CW>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[CW]);
+
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&v)[16]) {
+  tmem_ld16(taddr, v);
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Split-K: this split's partial tile into its plane of the workspace.
+template <int CW>
+__device__ __forceinline__ void store_partials(int32_t *plane_n, int N, uint32_t trow, int c_first,
+                                               int t_base, int t_lim, bool n_ok) {
+  for (int c = c_first; c < t_lim; c += 2 * CW) {
+    uint32_t v[CW];
+    tmem_ld<CW>(trow + c, v);
+    if (!n_ok) continue;
+    int32_t *p = plane_n + static_cast<size_t>(t_base + c) * N;
+#pragma unroll
+    for (int i = 0; i < CW; ++i)
+      if (c + i < t_lim) __stcg(p + static_cast<size_t>(i) * N, static_cast<int32_t>(v[i]));
+  }
+}
+
+// Final values of this thread's channel for its columns: accumulator (+ the other splits'
+// partial planes) through the output mode.
+template <int MODE, int CW>
+__device__ __forceinline__ void finish_columns(const Epilogue &ep, const ChanParams &cp,
+                                               uint32_t trow, int c_first, int t_base, int t_lim,
+                                               int n, bool n_ok, const int32_t *ws, int N,
+                                               int splits, int split, size_t plane) {
+  const int esize = out_size<MODE>(ep);
+  char *col = static_cast<char *>(ep.y) + static_cast<size_t>(n) * esize;
+  const size_t ldb = static_cast<size_t>(ep.ldy) * esize;
+  for (int c = c_first; c < t_lim; c += 2 * CW) {
+    uint32_t v[CW];
+    tmem_ld<CW>(trow + c, v);
+    if (!n_ok) continue;
+    if (splits > 1) {
+      // One plane at a time, all CW loads of it in flight together.
+      const int32_t *p = ws + static_cast<size_t>(t_base + c) * N + n;
+      for (int s = 0; s < splits; ++s) {
+        if (s == split) continue;
+        const int32_t *ps = p + s * plane;
+        int32_t part[CW];
+#pragma unroll
+        for (int i = 0; i < CW; ++i)
+          part[i] = (c + i < t_lim) ? __ldcg(ps + static_cast<size_t>(i) * N) : 0;
+#pragma unroll
+        for (int i = 0; i < CW; ++i) v[i] += static_cast<uint32_t>(part[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < CW; ++i) {
+      if (c + i < t_lim) {
+        const int t = t_base + c + i;
+        emit<MODE>(ep, cp, static_cast<int32_t>(v[i]), t, col + static_cast<size_t>(t) * ldb);
+      }
+    }
+  }
+}
+
+struct Unit {
+  int nb, tb, split, tile, k_begin, k_end;
+};
+
+__device__ __forceinline__ Unit decode_unit(const TcArgs &a, int u) {
+  Unit r;
+  r.split = u % a.splits;
+  r.tile = u / a.splits;
+  r.tb = r.tile % a.tiles_t;
+  r.nb = r.tile / a.tiles_t;
+  r.k_begin = r.split * a.ips;
+  r.k_end = min(r.k_begin + a.ips, a.k_iters);
+  return r;
+}
+
+// The epilogue warps' loop over this CTA's units.
+template <int MODE>
+__device__ __forceinline__ void epilogue_role(const TcArgs &a, uint32_t tmem, uint32_t tfull0,
+                                              uint32_t tempty0, int warp, int lane, int *s_last) {
+  const Epilogue &ep = a.ep;
+  const int q = warp & 3;
+  const int parity = (warp - 2) >> 2;
+  const bool cw32 = (a.BT % 32) == 0;
+  const size_t plane = static_cast<size_t>(a.T) * a.N;
+  bool ok = true;
+  int j = 0;
+  for (int u = blockIdx.x; u < a.units; u += gridDim.x, ++j) {
+    const Unit un = decode_unit(a, u);
+    const int buf = j & 1, use = j >> 1;
+    if (ok) ok = mbar_wait_bounded(tfull0 + 8 * buf, use & 1, a.err, kDevTimeoutFull);
+    // tcgen05.ld is warp-collective: the whole warp takes the same branch.
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    const int n = un.nb * kBM + q * 32 + lane;
+    const bool n_ok = n < a.N;
+    const int t_base = un.tb * a.BT;
+    const int t_lim = min(a.BT, a.T - t_base);
+    const uint32_t trow = tmem + buf * a.buf_stride + (static_cast<uint32_t>(q * 32) << 16);
+    bool finish = true;
+    if (a.splits > 1) {
+      // Split-K: every split stores its partial tile (plain coalesced stores into its own plane
+      // of the workspace); the last split of the tile to arrive adds the other planes to its
+      // own accumulator, still in TMEM, and runs the epilogue.
+      if (ok) {
+        int32_t *mine = a.ws + un.split * plane + n;
+        if (cw32)
+          store_partials<32>(mine, a.N, trow, parity * 32, t_base, t_lim, n_ok);
+        else
+          store_partials<16>(mine, a.N, trow, parity * 16, t_base, t_lim, n_ok);
+      }
+      __threadfence();
+      epi_bar_sync();
+      if (threadIdx.x == 64) {
+        const unsigned prev = atomicAdd(a.tile_count + un.tile, 1u);
+        *s_last = (prev == static_cast<unsigned>(a.splits - 1)) ? 1 : 0;
+        if (*s_last) a.tile_count[un.tile] = 0u;
+      }
+      epi_bar_sync();
+      finish = *s_last != 0;
+      if (finish) __threadfence();
+    }
+    if (ok && finish) {
+      const ChanParams cp = chan_params<MODE>(ep, n, n_ok);
+      if (cw32)
+        finish_columns<MODE, 32>(ep, cp, trow, parity * 32, t_base, t_lim, n, n_ok, a.ws, a.N,
+                                 a.splits, un.split, plane);
+      else
+        finish_columns<MODE, 16>(ep, cp, trow, parity * 16, t_base, t_lim, n, n_ok, a.ws, a.N,
+                                 a.splits, un.split, plane);
+    }
+    // TMEM buffer free for the next unit's MMAs.
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
+                        const __grid_constant__ CUtensorMap tm_x, const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 4];
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_last;
+
+  // Tiles start on a 1024-byte boundary (the 128-byte swizzle pattern repeats every 1024 bytes).
+  const uint32_t raw = smem_addr(smem_raw);
+  const uint32_t tiles = (raw + 1023u) & ~1023u;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t full0 = smem_addr(&bars[0]);
+  const uint32_t empty0 = smem_addr(&bars[kMaxStages]);
+  const uint32_t tfull0 = smem_addr(&bars[2 * kMaxStages]);
+  const uint32_t tempty0 = smem_addr(&bars[2 * kMaxStages + 2]);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.ns; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);
+      mbar_init(tempty0 + 8 * b, kEpiWarps);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(smem_addr(&s_tmem), a.tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 0) {
+    // ------------------------------- TMA producer -------------------------------
+    if (lane == 0) {
+      prefetch_tensormap(&tm_w);
+      prefetch_tensormap(&tm_x);
+      const uint64_t pol_first = policy_evict_first();
+      bool ok = true, dep_done = false;
+      uint32_t g = 0;
+      for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+        const Unit un = decode_unit(a, u);
+        for (int kit = un.k_begin; kit < un.k_end; ++kit, ++g) {
+          const uint32_t s = g % a.ns, use = g / a.ns;
+          if (use > 0) ok = mbar_wait_bounded(empty0 + 8 * s, (use - 1) & 1, a.err, kDevTimeoutEmpty);
+          if (!ok) break;
+          const uint32_t full = full0 + 8 * s;
+          const uint32_t dst = tiles + s * a.stage_bytes;
+          mbar_arrive_expect_tx(full, a.stage_bytes);
+          if (a.pol_w)
+            tma_load_2d_hint(dst, &tm_w, kit * kBK, un.nb * kBM, full, pol_first);
+          else
+            tma_load_2d(dst, &tm_w, kit * kBK, un.nb * kBM, full);
+          // Activations are written by the previous kernel in the stream: wait for it only now,
+          // after the first weight copy is in flight.
+          if (!dep_done) {
+            pdl_wait();
+            dep_done = true;
+          }
+          tma_load_2d(dst + kTileWBytes, &tm_x, kit * kBK, un.tb * a.BT, full);
+        }
+      }
+      // Copies still in flight target this CTA's shared memory: let the last ones land before
+      // the CTA may exit (the earlier ones were waited for by the MMA issuer).
+      const uint32_t first = g > static_cast<uint32_t>(a.ns) ? g - a.ns : 0u;
+      for (uint32_t i = first; i < g; ++i)
+        if (!mbar_wait_bounded(full0 + 8 * (i % a.ns), (i / a.ns) & 1, a.err, kDevTimeoutFull)) break;
+    }
+  } else if (warp == 1) {
+    // ------------------------------- MMA issuer -------------------------------
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t g = 0;
+      int j = 0;
+      for (int u = blockIdx.x; u < a.units; u += gridDim.x, ++j) {
+        const Unit un = decode_unit(a, u);
+        const int buf = j & 1, use = j >> 1;
+        if (ok && use > 0)
+          ok = mbar_wait_bounded(tempty0 + 8 * buf, (use - 1) & 1, a.err, kDevTimeoutEmpty);
+        tc_fence_after();
+        const uint32_t d = tmem + buf * a.buf_stride;
+        for (int kit = un.k_begin; kit < un.k_end && ok; ++kit, ++g) {
+          const uint32_t s = g % a.ns, su = g / a.ns;
+          ok = mbar_wait_bounded(full0 + 8 * s, su & 1, a.err, kDevTimeoutFull);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t base = tiles + s * a.stage_bytes;
+          const uint64_t adesc = smem_desc_sw128(base);
+          const uint64_t bdesc = smem_desc_sw128(base + kTileWBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / kMmaK; ++kk) {
+            // +32 bytes along K inside the swizzled row = +2 in the descriptor's address field.
+            mma_i8(d, adesc + 2 * kk, bdesc + 2 * kk, a.idesc,
+                   (kit > un.k_begin || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(empty0 + 8 * s);
+        }
+        // Always released (also after a timeout) so that the epilogue warps do not wait twice.
+        mma_commit(tfull0 + 8 * buf);
+        if (!ok) break;
+      }
+    }
+  } else {
+    // ------------------------------- epilogue -------------------------------
+    pdl_wait();
+    switch (a.ep.out_mode) {
+      case kOutAccI32: epilogue_role<kOutAccI32>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+      case kOutQuant: epilogue_role<kOutQuant>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+      case kOutF32: epilogue_role<kOutF32>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+      default: epilogue_role<kOutF32Acc>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, a.tmem_cols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Host side: tensor maps through the driver entry point (no link-time libcuda dependency).
+// ------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Row-major int8 matrix [rows, cols] (row stride ld bytes) read in boxes of box_rows x 128.
+bool encode_i8_rows(CUtensorMap *map, const int8_t *base, int64_t rows, int64_t cols, int64_t ld,
+                    int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool plan_tc(int T, int N, int k_pad, int sm_count, TcPlan *p) {
+  if (T < 1 || N < 1 || k_pad < 16 || sm_count < 1) return false;
+  TcPlan r = {};
+  r.tiles_t = (T + kMaxBT - 1) / kMaxBT;
+  const int per = (T + r.tiles_t - 1) / r.tiles_t;
+  r.BT = (per + 15) / 16 * 16;
+  r.tiles_n = (N + kBM - 1) / kBM;
+  r.k_iters = (k_pad + kBK - 1) / kBK;
+  const int tiles = r.tiles_n * r.tiles_t;
+  r.splits = 1;
+  if (tiles < sm_count) {
+    // Fill the SMs, but keep each split's operand bytes ((128 + BT) * K / splits) well above the
+    // partial tile it writes and the last split reads back (4 * BT * 128 bytes per split).
+    int s = sm_count / tiles;
+    if (s > r.k_iters / 4) s = r.k_iters / 4;  // at least 4 K stages per split
+    const int by_bytes = k_pad / (2 * r.BT);
+    if (s > by_bytes) s = by_bytes;
+    if (s < 1) s = 1;
+    r.splits = s;
+  }
+  r.ips = (r.k_iters + r.splits - 1) / r.splits;
+  r.splits = (r.k_iters + r.ips - 1) / r.ips;  // no empty split
+  r.units = tiles * r.splits;
+  r.grid = r.units < sm_count ? r.units : sm_count;
+  r.stage_bytes = kTileWBytes + static_cast<uint32_t>(r.BT) * kBK;
+  const size_t budget = kMaxDynSmem - 1024 - 1024;  // alignment slack + static barriers
+  int ns = static_cast<int>(budget / r.stage_bytes);
+  if (ns > kMaxStages) ns = kMaxStages;
+  const int total_iters = r.ips * ((r.units + r.grid - 1) / r.grid);
+  if (ns > total_iters && total_iters >= 2) ns = total_iters;
+  if (ns < 2) return false;
+  r.ns = ns;
+  r.smem = static_cast<size_t>(ns) * r.stage_bytes + 1024;
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(2 * r.BT)) cols <<= 1;
+  r.tmem_cols = cols;
+  *p = r;
+  return true;
+}
+
+cudaError_t launch_tc(const TcLaunch &L, const TcPlan &p, cudaStream_t stream) {
+  CUtensorMap tm_w, tm_x;
+  if (!encode_i8_rows(&tm_w, L.w, L.N, L.k_extent_w, L.ldw, kBM) ||
+      !encode_i8_rows(&tm_x, L.x, L.T, L.k_extent_x, L.ldx, p.BT)) {
+    set_last_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad operand)");
+    return cudaErrorInvalidValue;
+  }
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(gemm_w8a8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kMaxDynSmem - 1024);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  TcArgs a = {};
+  a.N = L.N;
+  a.T = L.T;
+  a.BT = p.BT;
+  a.tiles_t = p.tiles_t;
+  a.splits = p.splits;
+  a.k_iters = p.k_iters;
+  a.ips = p.ips;
+  a.units = p.units;
+  a.ns = p.ns;
+  a.stage_bytes = p.stage_bytes;
+  a.buf_stride = static_cast<uint32_t>(p.BT);
+  a.tmem_cols = p.tmem_cols;
+  // Instruction descriptor: D int32 (bits 4-5 = 2), A and B signed int8 (bits 7-9, 10-12 = 1),
+  // both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+  a.idesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(p.BT >> 3) << 17) |
+            (static_cast<uint32_t>(kBM >> 4) << 24);
+  a.ep = L.ep;
+  a.ws = L.ws;
+  a.tile_count = L.tile_count;
+  a.err = L.err;
+  a.pol_w = p.tiles_t == 1 ? 1 : 0;
+  return launch_ex(gemm_w8a8_tc_kernel, dim3(p.grid), dim3(kThreads), p.smem, stream, L.pdl, tm_w,
+                   tm_x, a);
+}
+
+}  // namespace w8a8

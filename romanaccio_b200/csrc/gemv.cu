@@ -3,7 +3,7 @@
 // One CTA = 8 consumer warps + 1 producer warp.  The CTA owns a contiguous range of row
 // tiles (RB = 8 * RPW output channels each) and streams their int8 weights through an
 // NS-deep ring of shared-memory stages filled by 1-D bulk copies (cp.async.bulk, TMA engine,
-// no tensor map, no multicast) that complete on mbarriers.  Each stage holds an [RB, KC] weight
+// no tensor map, one CTA per copy) that complete on mbarriers.  Each stage holds an [RB, KC] weight
 // slab plus the matching [T, KC] slab of the int8 activations.  Consumers read 16-byte
 // vectors, accumulate with dp4a into int32 registers, and reduce across the warp with
 // shuffles.  The epilogue applies the reference's SDP requant (QuantM, RNE shift, saturate)

@@ -81,6 +81,39 @@ struct GemvPlan {
 bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan *plan);
 cudaError_t launch_gemv(const GemvLaunch &L, const GemvPlan &plan, cudaStream_t stream);
 
+// Tensor-core (tcgen05 kind::i8) contraction for larger token counts.
+struct TcPlan {
+  int BT;          // tokens per tile (multiple of 16, <= 256) = MMA N
+  int tiles_n;     // 128-channel blocks
+  int tiles_t;     // token blocks
+  int splits;      // K splits per tile
+  int k_iters;     // 128-byte K stages per tile
+  int ips;         // K stages per split
+  int units;       // tiles * splits
+  int grid;        // persistent CTAs
+  int ns;          // pipeline depth
+  uint32_t stage_bytes, tmem_cols;
+  size_t smem;
+};
+
+struct TcLaunch {
+  const int8_t *w;          // [N, ldw]
+  int64_t ldw;
+  int k_extent_w;           // readable columns of w (zero padded up to it)
+  const int8_t *x;          // [T, ldx] int8 activations (16-byte aligned base, ldx % 16 == 0)
+  int64_t ldx;
+  int k_extent_x;           // readable columns of x; columns beyond read as zero
+  int T, N;
+  Epilogue ep;
+  int32_t *ws;              // split-K partial planes [splits, T, N] (plan.splits > 1)
+  unsigned *tile_count;     // split-K counters [tiles_n * tiles_t], zero between launches
+  int *err;
+  bool pdl;
+};
+
+bool plan_tc(int T, int N, int k_pad, int sm_count, TcPlan *plan);
+cudaError_t launch_tc(const TcLaunch &L, const TcPlan &plan, cudaStream_t stream);
+
 // Activation quantisation (pack) of x [T, K] fp32 into q [T, ldq] int8 (+ ratio [T]).
 struct ActQuantLaunch {
   const float *x;

@@ -133,6 +133,18 @@ class W8A8Linear:
     def device_bytes(self) -> int:
         return int(self._lib.w8a8_linear_device_bytes(self.handle))
 
+    @classmethod
+    def from_params(cls, ctx: Context, p) -> "W8A8Linear":
+        """From quantize.LinearParams (one quant_scales.json entry + its int8 weights)."""
+        scale = SubgraphScaleInfo(in_dtype=DTYPE_INT8, out_dtype=DTYPE_INT8,
+                                  in_thresh=p.in_thresh, in_step=p.in_step,
+                                  in_inv_smooth=p.in_inv_smooth, out_step_chan=p.out_step_chan)
+        return cls(ctx, p.wq, scale, quant_m=p.quant_m, trunc=p.trunc, acc_step=p.acc_step)
+
+    def set_path(self, path: int) -> None:
+        """Contraction engine: PATH_AUTO, PATH_GEMV (weight streaming) or PATH_TENSOR (tcgen05)."""
+        check(self._lib.w8a8_linear_set_path(self.handle, int(path)), "w8a8_linear_set_path")
+
     def close(self) -> None:
         if getattr(self, "handle", None):
             self._lib.w8a8_linear_destroy(self.handle)
