@@ -185,6 +185,11 @@ typedef enum {
 } w8a8_path;
 #define W8A8_TC_MIN_TOKENS 16
 w8a8_status w8a8_linear_set_path(w8a8_linear *linear, int32_t path);
+/* Diagnostics (no reference counterpart): attaches a device buffer of sm_count x 8 uint64 that
+ * each tensor-core launch of this linear fills with per-CTA %globaltimer stamps (entry, setup
+ * done, first stage issued, first stage landed, first MMAs committed, first accumulator seen by
+ * the epilogue, released, exit).  NULL detaches. */
+w8a8_status w8a8_linear_set_trace(w8a8_linear *linear, unsigned long long *trace_dev);
 
 /* ---------------------------------------------------------------------------------------
  * LM head shard: a linear over a contiguous block of vocab rows [row_offset, row_offset + N)

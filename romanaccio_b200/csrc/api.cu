@@ -4,7 +4,8 @@
 // (weights + QuantM blob + quant_scales.json entry, lfm3_v2.cpp:3743-3826), the DmaBuffer
 // staging of activations (lfm3_v2.cpp:1186-1225) and WorkerPool::submit_task
 // (worker_pool.hpp:232-254).  Everything runs in-process on CUDA streams; no call allocates
-// device memory after create, except a forward with T above the preallocated token budget.
+// device memory after create, except a forward with T above the preallocated token budget and
+// the first tensor-core forward of a linear (its tile-ordered weight copy and split-K scratch).
 #include "../../include/w8a8.h"
 #include "kernels.h"
 
@@ -82,8 +83,10 @@ struct w8a8_linear {
   uint64_t *lists = nullptr;    // top-k per-CTA candidate lists
   size_t lists_keys = 0;
   unsigned *counter = nullptr;
-  // tensor-core path: split-K workspace and per-tile counters (zero between launches)
+  // tensor-core path: tile-ordered weights, split-K partial planes, per-tile arrival counters
   int path = W8A8_PATH_AUTO;
+  int8_t *w_tiles = nullptr;    // weights in tensor-core tile order (built on first use)
+  unsigned long long *tc_trace = nullptr;  // optional per-CTA timeline of tensor-core launches
   int32_t *tc_ws = nullptr;
   size_t tc_ws_elems = 0;
   unsigned *tc_count = nullptr;
@@ -130,9 +133,23 @@ void linear_free(w8a8_linear *l) {
   cudaFree(l->ratio);
   cudaFree(l->lists);
   cudaFree(l->counter);
+  cudaFree(l->w_tiles);
   cudaFree(l->tc_ws);
   cudaFree(l->tc_count);
   delete l;
+}
+
+// Builds the tensor-core tile copy of the weights on the first tensor-core launch (stream
+// ordered before it).  It doubles the linear's weight bytes, so decode-only linears never pay it.
+w8a8_status ensure_tc_weights(w8a8_linear *l, cudaStream_t st, bool *built) {
+  *built = false;
+  if (l->w_tiles) return W8A8_SUCCESS;
+  *built = true;
+  const size_t bytes = tc_tile_bytes(l->N, l->k_pad);
+  w8a8_status s = dev_alloc(&l->w_tiles, bytes, &l->device_bytes);
+  if (s != W8A8_SUCCESS) return s;
+  W8A8_CUDA(launch_tile_weights(l->w, l->k_pad, l->N, l->k_pad, l->w_tiles, st));
+  return W8A8_SUCCESS;
 }
 
 // Grows the split-K partial planes / per-tile arrival counters of the tensor-core path (the
@@ -221,10 +238,11 @@ w8a8_status run_gemv(w8a8_linear *l, const int8_t *xq, int64_t ldx, int T, int a
                                         static_cast<size_t>(plan.tiles_n) * plan.tiles_t);
       if (s != W8A8_SUCCESS) return s;
     }
+    bool built = false;
+    w8a8_status s = ensure_tc_weights(l, st, &built);
+    if (s != W8A8_SUCCESS) return s;
     TcLaunch L = {};
-    L.w = l->w;
-    L.ldw = l->k_pad;
-    L.k_extent_w = l->k_pad;
+    L.w_tiles = l->w_tiles;
     L.x = xq;
     L.ldx = ldx;
     L.k_extent_x = l->k_pad;
@@ -234,7 +252,9 @@ w8a8_status run_gemv(w8a8_linear *l, const int8_t *xq, int64_t ldx, int T, int a
     L.ws = l->tc_ws;
     L.tile_count = l->tc_count;
     L.err = l->ctx->d_err;
-    L.pdl = pdl;
+    L.trace = l->tc_trace;
+    // The GEMM reads weight tiles before its dependency wait: not right after they were built.
+    L.pdl = pdl && !built;
     W8A8_CUDA(launch_tc(L, plan, st));
     return W8A8_SUCCESS;
   }
@@ -441,6 +461,12 @@ w8a8_status w8a8_linear_create(w8a8_ctx *ctx, const w8a8_linear_desc *d, w8a8_li
 void w8a8_linear_destroy(w8a8_linear *l) { linear_free(l); }
 
 size_t w8a8_linear_device_bytes(const w8a8_linear *l) { return l ? l->device_bytes : 0; }
+
+w8a8_status w8a8_linear_set_trace(w8a8_linear *l, unsigned long long *trace_dev) {
+  if (!l) return fail(W8A8_ERR_INVALID_ARG, "linear is NULL");
+  l->tc_trace = trace_dev;
+  return W8A8_SUCCESS;
+}
 
 w8a8_status w8a8_linear_set_path(w8a8_linear *l, int32_t path) {
   if (!l) return fail(W8A8_ERR_INVALID_ARG, "linear is NULL");

@@ -18,9 +18,10 @@ namespace w8a8 {
 // Upper bound for any spin wait inside a kernel: 2 seconds of %globaltimer.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
+// The "memory" clobber keeps the read in program order with barriers and memory operations.
 __device__ __forceinline__ unsigned long long global_timer_ns() {
   unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t)::"memory");
   return t;
 }
 
@@ -132,6 +133,37 @@ __device__ __forceinline__ int32_t requant_quantm(int32_t acc, int32_t qm, int32
   }
   q = q < -qmax ? -qmax : (q > qmax ? qmax : q);
   return static_cast<int32_t>(q);
+}
+
+// requant_quantm for 15 <= trunc <= 31, where the quotient fits 32 bits (|acc * QuantM| < 2^46):
+// the low words of the shifts come from 32-bit funnel shifts of the 64-bit product (the low 32
+// bits of a logical and an arithmetic shift agree).  bias = 2^(trunc-1) - 1.
+__device__ __forceinline__ int32_t requant_quantm_t15(int32_t acc, int32_t qm, int32_t trunc,
+                                                      long long bias, int32_t qmax) {
+  const long long p = static_cast<long long>(acc) * static_cast<long long>(qm);
+  const uint32_t odd =
+      __funnelshift_r(static_cast<uint32_t>(p), static_cast<uint32_t>(p >> 32), trunc) & 1u;
+  const long long r = p + bias + odd;
+  int32_t q = static_cast<int32_t>(
+      __funnelshift_r(static_cast<uint32_t>(r), static_cast<uint32_t>(r >> 32), trunc));
+  q = q < -qmax ? -qmax : (q > qmax ? qmax : q);
+  return q;
+}
+
+// The same requant in float64, the reference's own formulation (round(acc * (QuantM / 2^trunc))):
+// scale = QuantM * 2^-trunc is exact, and so is acc * scale because |acc * QuantM| < 2^46 fits
+// the 53-bit significand; clamping to the integer bound before the round-half-even conversion
+// gives the same integer as clipping after it.  Five instructions instead of the int64 chain.
+__device__ __forceinline__ double quantm_scale(int32_t qm, int32_t trunc) {
+  // 2^-trunc built from its exponent bits (trunc in [0, 62])
+  return static_cast<double>(qm) * __longlong_as_double(static_cast<long long>(1023 - trunc) << 52);
+}
+
+__device__ __forceinline__ int32_t requant_f64(int32_t acc, double scale, double qmax) {
+  double x = static_cast<double>(acc) * scale;
+  x = x < -qmax ? -qmax : x;
+  x = x > qmax ? qmax : x;
+  return __double2int_rn(x);
 }
 
 __device__ __forceinline__ uint64_t topk_key(float v, uint32_t id) {

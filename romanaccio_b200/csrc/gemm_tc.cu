@@ -1,6 +1,8 @@
 // Tensor-core W8A8 contraction for token counts above the GEMV range (prefill, batched decode):
-// tcgen05.mma kind::i8 with int32 accumulators in TMEM, operands staged by 2-D TMA tiles with the
-// 128-byte swizzle (plain per-CTA loads).
+// tcgen05.mma kind::i8 with int32 accumulators in TMEM.  Weights live in HBM as contiguous 16 KB
+// tiles already in the 128-byte-swizzled shared-memory image (launch_tile_weights), so one 1-D bulk
+// copy per stage streams them at full DRAM efficiency; activations arrive by 2-D TMA tiles with the
+// 128-byte swizzle.  Every copy is a plain per-CTA load.
 //
 // Math: acc[t, n] = sum_k q[t, k] * Wq[n, k] in exact int32 (the CMAC step, cmac.py:300-383 of
 // the reference's NPU model), then the per-output-channel epilogue shared with the GEMV kernels:
@@ -19,9 +21,9 @@
 // workspace, and the last split of a tile to arrive (an arrival counter per tile) adds the other
 // planes to its TMEM accumulator and runs the epilogue.  Integer sums are exact in any order.
 //
-// Warp roles (320 threads): warp 0 issues the TMA copies, warp 1 owns TMEM and issues the MMAs
-// (one thread), warps 2..9 run the epilogue; warp w reads TMEM lanes 32*(w%4)..+31 (the lane
-// quarter a warp may access is fixed by its id modulo 4) and the column chunks of parity (w-2)/4.
+// Warp roles (576 threads): warp 0 issues the TMA copies, warp 1 owns TMEM and issues the MMAs
+// (one thread), warps 2..17 run the epilogue; warp w reads TMEM lanes 32*(w%4)..+31 (the lane
+// quarter a warp may access is fixed by its id modulo 4) and every 4th column chunk from (w-2)/4.
 #include <cuda.h>
 
 #include <cstdint>
@@ -34,8 +36,9 @@
 namespace w8a8 {
 namespace {
 
-constexpr int kThreads = 320;
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer warp, MMA warp, epilogue warps
+constexpr int kColGroups = kEpiWarps / 4;    // epilogue warps sharing one TMEM lane quarter
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kBM = 128;                       // output channels per tile (MMA M)
 constexpr int kBK = 128;                       // K bytes per stage = one 128-byte swizzle row
@@ -50,11 +53,20 @@ struct TcArgs {
   int tiles_t, splits, k_iters, ips, units, ns;
   uint32_t stage_bytes, buf_stride, tmem_cols, idesc;
   Epilogue ep;
+  const int8_t *w_tiles;  // [tiles_n][k_iters] contiguous 16 KB swizzled weight tiles
   int32_t *ws;            // split-K partial planes [splits, T, N]
   unsigned *tile_count;   // split-K arrival counters [tiles] (all zero between launches)
   int *err;
-  uint64_t pol_w;         // L2 policy selector for the weight copies: 0 normal, 1 evict-first
+  int w_stream;           // weights read once (one token block): evict-first L2 policy
+  unsigned long long *trace;  // optional [grid, 8] %globaltimer stamps (see stamp())
 };
+
+// Diagnostic timeline of a CTA (only when a trace buffer is attached): 0 entry, 1 setup done,
+// 2 first stage issued, 3 first stage landed (MMA issuer), 4 first unit's MMAs committed,
+// 5 epilogue saw the first accumulator, 6 epilogue released it, 7 exit.
+__device__ __forceinline__ void stamp(const TcArgs &a, int i) {
+  if (a.trace) a.trace[blockIdx.x * 8 + i] = global_timer_ns();
+}
 
 // ------------------------------------------------------------------------------------------
 // tcgen05 / TMA wrappers
@@ -99,6 +111,7 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 // 32 lanes x 16 consecutive 32-bit columns; the wait is inside the same statement so no use of
 // the registers can be scheduled before the data has arrived.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  __syncwarp();  // .sync.aligned: the whole warp executes it together
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
       "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
@@ -116,15 +129,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
       "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(map), "r"(c0), "r"(c1), "r"(bar)
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap *map, int c0,
-                                                 int c1, uint32_t bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
-      "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
-      "l"(map), "r"(c0), "r"(c1), "r"(bar), "l"(policy)
       : "memory");
 }
 
@@ -147,42 +151,61 @@ __device__ __forceinline__ void epi_bar_sync() {
 
 // ------------------------------------------------------------------------------------------
 // Epilogue: one thread = one output channel n; TMEM columns = tokens.  Specialised per output
-// mode so that the per-element code is a short straight line.
+// mode so that the per-element code is a short straight line.  MODE = w8a8_out_mode, plus
+// kRqInt when the requant runs in 32-bit funnel-shift arithmetic (15 <= trunc <= 31) rather than
+// in float64; both give the exact integer of requant_quantm.
 // ------------------------------------------------------------------------------------------
+constexpr int kRqInt = 4;
+
 struct ChanParams {
   int32_t qm;
-  float step;   // out_step[n] (F32) or acc_step[n] (F32_ACC)
+  long long bias;  // 2^(trunc-1) - 1
+  double scale;    // QuantM[n] * 2^-trunc
+  double qmax;
+  float step;      // out_step[n] (F32) or acc_step[n] (F32_ACC)
 };
 
 template <int MODE>
 __device__ __forceinline__ ChanParams chan_params(const Epilogue &ep, int n, bool n_ok) {
-  ChanParams cp{0, 0.0f};
+  constexpr int base = MODE & 3;
+  ChanParams cp{0, (1LL << (ep.trunc > 0 ? ep.trunc - 1 : 0)) - 1, 0.0,
+                static_cast<double>(ep.qmax), 0.0f};
   if (!n_ok) return cp;
-  if (MODE == kOutQuant || MODE == kOutF32) cp.qm = ep.quant_m[n];
-  if (MODE == kOutF32) cp.step = ep.out_step[n];
-  if (MODE == kOutF32Acc) cp.step = ep.acc_step[n];
+  if (base == kOutQuant || base == kOutF32) {
+    cp.qm = ep.quant_m[n];
+    cp.scale = quantm_scale(cp.qm, ep.trunc);
+  }
+  if (base == kOutF32) cp.step = ep.out_step[n];
+  if (base == kOutF32Acc) cp.step = ep.acc_step[n];
   return cp;
 }
 
 template <int MODE>
 __device__ __forceinline__ int out_size(const Epilogue &ep) {
-  return MODE == kOutQuant ? (ep.out_i16 ? 2 : 1) : 4;
+  return (MODE & 3) == kOutQuant ? (ep.out_i16 ? 2 : 1) : 4;
+}
+
+template <int MODE>
+__device__ __forceinline__ int32_t requant(const Epilogue &ep, const ChanParams &cp, int32_t acc) {
+  if (MODE & kRqInt) return requant_quantm_t15(acc, cp.qm, ep.trunc, cp.bias, ep.qmax);
+  return requant_f64(acc, cp.scale, cp.qmax);
 }
 
 // Output value of (channel, token t) written at p.
 template <int MODE>
 __device__ __forceinline__ void emit(const Epilogue &ep, const ChanParams &cp, int32_t acc, int t,
                                      char *p) {
-  if (MODE == kOutAccI32) {
+  constexpr int base = MODE & 3;
+  if (base == kOutAccI32) {
     *reinterpret_cast<int32_t *>(p) = acc;
-  } else if (MODE == kOutQuant) {
-    const int yq = requant_quantm(acc, cp.qm, ep.trunc, ep.qmax);
+  } else if (base == kOutQuant) {
+    const int yq = requant<MODE>(ep, cp, acc);
     if (ep.out_i16)
       *reinterpret_cast<int16_t *>(p) = static_cast<int16_t>(yq);
     else
       *reinterpret_cast<int8_t *>(p) = static_cast<int8_t>(yq);
-  } else if (MODE == kOutF32) {
-    const int yq = requant_quantm(acc, cp.qm, ep.trunc, ep.qmax);
+  } else if (base == kOutF32) {
+    const int yq = requant<MODE>(ep, cp, acc);
     const float step = ep.act_mode == kActDyntok ? ep.ratio[t] * cp.step : cp.step;
     *reinterpret_cast<float *>(p) = static_cast<float>(yq) * step;
   } else {
@@ -191,36 +214,21 @@ __device__ __forceinline__ void emit(const Epilogue &ep, const ChanParams &cp, i
   }
 }
 
-// 32 lanes x CW consecutive 32-bit TMEM columns (CW = 16 or 32), load and wait in one statement.
+// Epilogue column chunk: 16 TMEM columns per tcgen05.ld (keeps the 16 epilogue warps within
+// their register budget).
+constexpr int kCW = 16;
+
 template <int CW>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[CW]);
-
-template <>
-__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&v)[16]) {
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[CW]) {
+  static_assert(CW == 16, "16-column TMEM loads");
   tmem_ld16(taddr, v);
-}
-
-template <>
-__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
-        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
-        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(taddr)
-      : "memory");
 }
 
 // Split-K: this split's partial tile into its plane of the workspace.
 template <int CW>
 __device__ __forceinline__ void store_partials(int32_t *plane_n, int N, uint32_t trow, int c_first,
                                                int t_base, int t_lim, bool n_ok) {
-  for (int c = c_first; c < t_lim; c += 2 * CW) {
+  for (int c = c_first; c < t_lim; c += kColGroups * CW) {
     uint32_t v[CW];
     tmem_ld<CW>(trow + c, v);
     if (!n_ok) continue;
@@ -241,7 +249,7 @@ __device__ __forceinline__ void finish_columns(const Epilogue &ep, const ChanPar
   const int esize = out_size<MODE>(ep);
   char *col = static_cast<char *>(ep.y) + static_cast<size_t>(n) * esize;
   const size_t ldb = static_cast<size_t>(ep.ldy) * esize;
-  for (int c = c_first; c < t_lim; c += 2 * CW) {
+  for (int c = c_first; c < t_lim; c += kColGroups * CW) {
     uint32_t v[CW];
     tmem_ld<CW>(trow + c, v);
     if (!n_ok) continue;
@@ -290,8 +298,7 @@ __device__ __forceinline__ void epilogue_role(const TcArgs &a, uint32_t tmem, ui
                                               uint32_t tempty0, int warp, int lane, int *s_last) {
   const Epilogue &ep = a.ep;
   const int q = warp & 3;
-  const int parity = (warp - 2) >> 2;
-  const bool cw32 = (a.BT % 32) == 0;
+  const int group = (warp - 2) >> 2;  // column group of this warp
   const size_t plane = static_cast<size_t>(a.T) * a.N;
   bool ok = true;
   int j = 0;
@@ -302,6 +309,7 @@ __device__ __forceinline__ void epilogue_role(const TcArgs &a, uint32_t tmem, ui
     // tcgen05.ld is warp-collective: the whole warp takes the same branch.
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
+    if (j == 0 && threadIdx.x == 64) stamp(a, 5);
     const int n = un.nb * kBM + q * 32 + lane;
     const bool n_ok = n < a.N;
     const int t_base = un.tb * a.BT;
@@ -314,10 +322,7 @@ __device__ __forceinline__ void epilogue_role(const TcArgs &a, uint32_t tmem, ui
       // own accumulator, still in TMEM, and runs the epilogue.
       if (ok) {
         int32_t *mine = a.ws + un.split * plane + n;
-        if (cw32)
-          store_partials<32>(mine, a.N, trow, parity * 32, t_base, t_lim, n_ok);
-        else
-          store_partials<16>(mine, a.N, trow, parity * 16, t_base, t_lim, n_ok);
+        store_partials<kCW>(mine, a.N, trow, group * kCW, t_base, t_lim, n_ok);
       }
       __threadfence();
       epi_bar_sync();
@@ -332,25 +337,21 @@ __device__ __forceinline__ void epilogue_role(const TcArgs &a, uint32_t tmem, ui
     }
     if (ok && finish) {
       const ChanParams cp = chan_params<MODE>(ep, n, n_ok);
-      if (cw32)
-        finish_columns<MODE, 32>(ep, cp, trow, parity * 32, t_base, t_lim, n, n_ok, a.ws, a.N,
-                                 a.splits, un.split, plane);
-      else
-        finish_columns<MODE, 16>(ep, cp, trow, parity * 16, t_base, t_lim, n, n_ok, a.ws, a.N,
-                                 a.splits, un.split, plane);
+      finish_columns<MODE, kCW>(ep, cp, trow, group * kCW, t_base, t_lim, n, n_ok, a.ws, a.N,
+                                a.splits, un.split, plane);
     }
     // TMEM buffer free for the next unit's MMAs.
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
+    if (j == 0 && threadIdx.x == 64) stamp(a, 6);
   }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
-                        const __grid_constant__ CUtensorMap tm_x, const TcArgs a) {
+    gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 4];
+  __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 5];
   __shared__ uint32_t s_tmem;
   __shared__ int s_last;
 
@@ -362,8 +363,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t empty0 = smem_addr(&bars[kMaxStages]);
   const uint32_t tfull0 = smem_addr(&bars[2 * kMaxStages]);
   const uint32_t tempty0 = smem_addr(&bars[2 * kMaxStages + 2]);
+  const uint32_t epi_done = smem_addr(&bars[2 * kMaxStages + 4]);
 
   if (threadIdx.x == 0) {
+    stamp(a, 0);
     for (int s = 0; s < a.ns; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
@@ -372,20 +375,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(tfull0 + 8 * b, 1);
       mbar_init(tempty0 + 8 * b, kEpiWarps);
     }
+    mbar_init(epi_done, kEpiWarps);
     fence_barrier_init();
   }
+  __syncwarp();
   if (warp == 1) tmem_alloc(smem_addr(&s_tmem), a.tmem_cols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
+  if (threadIdx.x == 0) stamp(a, 1);
 
   if (warp == 0) {
     // ------------------------------- TMA producer -------------------------------
     if (lane == 0) {
-      prefetch_tensormap(&tm_w);
       prefetch_tensormap(&tm_x);
-      const uint64_t pol_first = policy_evict_first();
+      const uint64_t pol_w = a.w_stream ? policy_evict_first() : policy_evict_last();
       bool ok = true, dep_done = false;
       uint32_t g = 0;
       for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
@@ -397,10 +402,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t full = full0 + 8 * s;
           const uint32_t dst = tiles + s * a.stage_bytes;
           mbar_arrive_expect_tx(full, a.stage_bytes);
-          if (a.pol_w)
-            tma_load_2d_hint(dst, &tm_w, kit * kBK, un.nb * kBM, full, pol_first);
-          else
-            tma_load_2d(dst, &tm_w, kit * kBK, un.nb * kBM, full);
+          // One contiguous 16 KB weight tile, already in the swizzled shared-memory image.
+          bulk_g2s(dst, a.w_tiles + (static_cast<size_t>(un.nb) * a.k_iters + kit) * kTileWBytes,
+                   kTileWBytes, full, pol_w);
           // Activations are written by the previous kernel in the stream: wait for it only now,
           // after the first weight copy is in flight.
           if (!dep_done) {
@@ -408,6 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             dep_done = true;
           }
           tma_load_2d(dst + kTileWBytes, &tm_x, kit * kBK, un.tb * a.BT, full);
+          if (g == 0) stamp(a, 2);
         }
       }
       // Copies still in flight target this CTA's shared memory: let the last ones land before
@@ -433,6 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t s = g % a.ns, su = g / a.ns;
           ok = mbar_wait_bounded(full0 + 8 * s, su & 1, a.err, kDevTimeoutFull);
           if (!ok) break;
+          if (g == 0) stamp(a, 3);
           tc_fence_after();
           const uint32_t base = tiles + s * a.stage_bytes;
           const uint64_t adesc = smem_desc_sw128(base);
@@ -447,27 +453,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // Always released (also after a timeout) so that the epilogue warps do not wait twice.
         mma_commit(tfull0 + 8 * buf);
+        if (j == 0) stamp(a, 4);
         if (!ok) break;
       }
     }
   } else {
     // ------------------------------- epilogue -------------------------------
     pdl_wait();
-    switch (a.ep.out_mode) {
-      case kOutAccI32: epilogue_role<kOutAccI32>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+    const int rq_int = (a.ep.trunc >= 15 && a.ep.trunc <= 31) ? kRqInt : 0;
+    switch (a.ep.out_mode | rq_int) {
+      case kOutAccI32:
+      case kOutAccI32 | kRqInt:
+        epilogue_role<kOutAccI32>(a, tmem, tfull0, tempty0, warp, lane, &s_last);
+        break;
       case kOutQuant: epilogue_role<kOutQuant>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+      case kOutQuant | kRqInt:
+        epilogue_role<kOutQuant | kRqInt>(a, tmem, tfull0, tempty0, warp, lane, &s_last);
+        break;
       case kOutF32: epilogue_role<kOutF32>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+      case kOutF32 | kRqInt:
+        epilogue_role<kOutF32 | kRqInt>(a, tmem, tfull0, tempty0, warp, lane, &s_last);
+        break;
       default: epilogue_role<kOutF32Acc>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
     }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(epi_done);
   }
 
-  tc_fence_before();
-  __syncthreads();
+  // TMEM is released only after every epilogue warp has signalled, through an mbarrier, that its
+  // last TMEM read completed (the block barrier alone was seen to let the producer and MMA warps
+  // through while the epilogue was still draining).
+  __syncwarp();
   if (warp == 1) {
+    mbar_wait_bounded(epi_done, 0, a.err, kDevTimeoutFull);
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, a.tmem_cols);
   }
+  __syncthreads();
+  if (threadIdx.x == 0) stamp(a, 7);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -504,6 +529,23 @@ bool encode_i8_rows(CUtensorMap *map, const int8_t *base, int64_t rows, int64_t 
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(base), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// One CTA per 128 x 128-byte tile: 16-byte chunk c of row r goes to chunk c ^ (r % 8) of the
+// row, the pattern TMA writes for CU_TENSOR_MAP_SWIZZLE_128B into a 1024-byte aligned tile.
+__global__ void tile_weights_kernel(const int8_t *__restrict__ w, int64_t ldw, int N, int k_pad,
+                                    int k_iters, int8_t *__restrict__ tiles) {
+  const int tile = blockIdx.x;
+  const int nb = tile / k_iters, kb = tile % k_iters;
+  int8_t *dst = tiles + static_cast<size_t>(tile) * kTileWBytes;
+  for (int i = threadIdx.x; i < kBM * (kBK / 16); i += blockDim.x) {
+    const int r = i >> 3, c = i & 7;
+    const int row = nb * kBM + r, col = kb * kBK + c * 16;
+    int4 v = make_int4(0, 0, 0, 0);
+    if (row < N && col < k_pad)
+      v = *reinterpret_cast<const int4 *>(w + static_cast<size_t>(row) * ldw + col);
+    *reinterpret_cast<int4 *>(dst + r * kBK + ((c ^ (r & 7)) << 4)) = v;
+  }
 }
 
 }  // namespace
@@ -549,9 +591,8 @@ bool plan_tc(int T, int N, int k_pad, int sm_count, TcPlan *p) {
 }
 
 cudaError_t launch_tc(const TcLaunch &L, const TcPlan &p, cudaStream_t stream) {
-  CUtensorMap tm_w, tm_x;
-  if (!encode_i8_rows(&tm_w, L.w, L.N, L.k_extent_w, L.ldw, kBM) ||
-      !encode_i8_rows(&tm_x, L.x, L.T, L.k_extent_x, L.ldx, p.BT)) {
+  CUtensorMap tm_x;
+  if (!encode_i8_rows(&tm_x, L.x, L.T, L.k_extent_x, L.ldx, p.BT)) {
     set_last_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad operand)");
     return cudaErrorInvalidValue;
   }
@@ -583,9 +624,23 @@ cudaError_t launch_tc(const TcLaunch &L, const TcPlan &p, cudaStream_t stream) {
   a.ws = L.ws;
   a.tile_count = L.tile_count;
   a.err = L.err;
-  a.pol_w = p.tiles_t == 1 ? 1 : 0;
-  return launch_ex(gemm_w8a8_tc_kernel, dim3(p.grid), dim3(kThreads), p.smem, stream, L.pdl, tm_w,
-                   tm_x, a);
+  a.w_tiles = L.w_tiles;
+  a.trace = L.trace;
+  a.w_stream = p.tiles_t == 1 ? 1 : 0;
+  return launch_ex(gemm_w8a8_tc_kernel, dim3(p.grid), dim3(kThreads), p.smem, stream, L.pdl, tm_x,
+                   a);
+}
+
+size_t tc_tile_bytes(int N, int k_pad) {
+  return static_cast<size_t>((N + kBM - 1) / kBM) * ((k_pad + kBK - 1) / kBK) * kTileWBytes;
+}
+
+cudaError_t launch_tile_weights(const int8_t *w, int64_t ldw, int N, int k_pad, int8_t *tiles,
+                                cudaStream_t stream) {
+  const int k_iters = (k_pad + kBK - 1) / kBK;
+  const int n_tiles = ((N + kBM - 1) / kBM) * k_iters;
+  tile_weights_kernel<<<n_tiles, 256, 0, stream>>>(w, ldw, N, k_pad, k_iters, tiles);
+  return cudaGetLastError();
 }
 
 }  // namespace w8a8

@@ -97,9 +97,7 @@ struct TcPlan {
 };
 
 struct TcLaunch {
-  const int8_t *w;          // [N, ldw]
-  int64_t ldw;
-  int k_extent_w;           // readable columns of w (zero padded up to it)
+  const int8_t *w_tiles;    // weights in tensor-core tile order (launch_tile_weights)
   const int8_t *x;          // [T, ldx] int8 activations (16-byte aligned base, ldx % 16 == 0)
   int64_t ldx;
   int k_extent_x;           // readable columns of x; columns beyond read as zero
@@ -108,11 +106,18 @@ struct TcLaunch {
   int32_t *ws;              // split-K partial planes [splits, T, N] (plan.splits > 1)
   unsigned *tile_count;     // split-K counters [tiles_n * tiles_t], zero between launches
   int *err;
+  unsigned long long *trace;  // optional per-CTA timeline [grid, 8]
   bool pdl;
 };
 
 bool plan_tc(int T, int N, int k_pad, int sm_count, TcPlan *plan);
 cudaError_t launch_tc(const TcLaunch &L, const TcPlan &plan, cudaStream_t stream);
+// Weights [N, ldw] (k_pad readable columns) re-laid as contiguous 128 x 128-byte tiles
+// [ceil(N/128)][ceil(k_pad/128)], each stored exactly as the 128-byte-swizzled shared-memory
+// image the MMA reads, zero-filled past N and k_pad.
+size_t tc_tile_bytes(int N, int k_pad);
+cudaError_t launch_tile_weights(const int8_t *w, int64_t ldw, int N, int k_pad, int8_t *tiles,
+                                cudaStream_t stream);
 
 // Activation quantisation (pack) of x [T, K] fp32 into q [T, ldq] int8 (+ ratio [T]).
 struct ActQuantLaunch {

@@ -141,6 +141,13 @@ class W8A8Linear:
                                   in_inv_smooth=p.in_inv_smooth, out_step_chan=p.out_step_chan)
         return cls(ctx, p.wq, scale, quant_m=p.quant_m, trunc=p.trunc, acc_step=p.acc_step)
 
+    def enable_trace(self, sm_count: int, device) -> torch.Tensor:
+        """Per-CTA timeline [sm_count, 8] (int64 %globaltimer ns) of tensor-core launches."""
+        buf = torch.zeros((sm_count, 8), dtype=torch.int64, device=device)
+        check(self._lib.w8a8_linear_set_trace(self.handle, buf.data_ptr()), "w8a8_linear_set_trace")
+        self._trace = buf
+        return buf
+
     def set_path(self, path: int) -> None:
         """Contraction engine: PATH_AUTO, PATH_GEMV (weight streaming) or PATH_TENSOR (tcgen05)."""
         check(self._lib.w8a8_linear_set_path(self.handle, int(path)), "w8a8_linear_set_path")
