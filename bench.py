@@ -37,6 +37,9 @@ GEMV_TRAFFIC_BYTES = 27666688
 # DRAM bytes per algorithmic byte of the chain kernel from one ncu capture of a 4-layer,
 # 1024-vocab chain (profiles/chain_kernel_qwen15b_4layer.md): 189.84 MB read / 188.7 MB.
 CHAIN_TRAFFIC_RATIO = 1.006
+# DRAM bytes (read + write) of one launch of the M=2048, K=N=8192 tensor-core GEMM from one ncu
+# capture (profiles/gemm_w8a8_tc_prefill_2048x8192x8192.md); None until captured.
+PREFILL_GEMM_TRAFFIC_BYTES = None
 
 
 def env_int(name: str, default: int) -> int:
@@ -392,6 +395,231 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------- prefill sweep
+PREFILL_METRIC = "prefill int8 GEMM TOPS (W8A8 linear: dyntok act quant + int8 GEMM + int8 requant)"
+PREFILL_SHAPES = [(m, k, n) for m in (128, 512, 2048)
+                  for (k, n) in ((2048, 2048), (8192, 8192), (2048, 8192), (8192, 2048))]
+PREFILL_WORKLOAD = ("prefill sweep: M in {128,512,2048} x (K,N) in {(2048,2048),(8192,8192),"
+                    "(2048,8192),(8192,2048)}, SmoothQuant W8A8, per-channel requant to int8")
+
+
+def prefill_ops(shapes) -> int:
+    return sum(2 * m * n * k for (m, k, n) in shapes)
+
+
+def cpu_prefill_fn(shapes, seed: int = 0):
+    """OpenMP oracle linear (dyntok pack + int32 GEMM + QuantM requant + dequant) over shapes."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    from romanaccio_b200 import synth
+    lib = O.lib()
+    lib.orc_set_threads(len(os.sched_getaffinity(0)))
+    import ctypes as C
+    jobs = []
+    for i, (M, K, N) in enumerate(shapes):
+        p = synth.make_linear(K, N, seed=seed + i)
+        x = synth.activations(M, K, seed=seed + 100 + i).numpy()
+        jobs.append((M, K, N, x, np.ascontiguousarray(p.wq), p.in_inv_smooth.astype(np.float32),
+                     p.in_thresh, p.quant_m, p.trunc, p.out_step_chan.astype(np.float32),
+                     np.empty((M, N), np.float32), np.empty((M, K), np.int8),
+                     np.empty(M, np.float32)))
+
+    def run():
+        for (M, K, N, x, wq, inv, thr, qm, tr, osc, y, q, r) in jobs:
+            lib.orc_linear_dyntok_omp(x.ctypes.data, M, K, N, wq.ctypes.data, inv.ctypes.data,
+                                      C.c_float(thr), qm.ctypes.data, tr, osc.ctypes.data,
+                                      y.ctypes.data, q.ctypes.data, r.ctypes.data)
+
+    return run, int(lib.orc_num_threads())
+
+
+def run_prefill_reference(args) -> None:
+    if env_int("RANK", 0) != 0:
+        return
+    sample = [s for s in PREFILL_SHAPES if s[0] == 128]  # bounded sample: the M=128 row
+    run, cores = cpu_prefill_fn(sample)
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = prefill_ops(sample) / dt / 1e12
+    line = {
+        "impl": "reference", "metric": PREFILL_METRIC, "value": value, "unit": "TOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": PREFILL_WORKLOAD, "parallelism": "host cores (OpenMP)"},
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": cores, "kind": "port",
+                         "sample": "the four M=128 GEMMs of the sweep per step, C restatement "
+                                   "of the reference linear, OpenMP"},
+        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_prefill(args) -> None:
+    """One step = the 12 prefill linears of the sweep, each a fused W8A8 forward (dyntok act
+    quant kernel + tcgen05 GEMM with the requant epilogue) from fp32 activations in HBM to int8
+    outputs.  Every GEMM runs on a cold L2 (a 256 MB write before it, outside the timed events)."""
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    sys.path.insert(0, str(ROOT))
+    from romanaccio_b200 import OUT_QUANT, PATH_TENSOR, Context, W8A8Linear, synth
+
+    ctx = Context(local)
+    jobs = []
+    for i, (M, K, N) in enumerate(PREFILL_SHAPES):
+        p = synth.make_linear(K, N, seed=i, device=dev)
+        lin = W8A8Linear.from_params(ctx, p)
+        lin.set_path(PATH_TENSOR)
+        x = synth.activations(M, K, seed=100 + i, device=dev)
+        y = torch.empty((M, N), dtype=torch.int8, device=dev)
+        jobs.append((M, K, N, lin, x, y))
+    flush = torch.empty(256 << 20, dtype=torch.int8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def step(events=None):
+        for j, (M, K, N, lin, x, y) in enumerate(jobs):
+            flush.zero_()
+            if events is not None:
+                events[j][0].record(stream)
+            lin.forward(x, OUT_QUANT, dyntok=True, out=y)
+            if events is not None:
+                events[j][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in jobs] for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        barrier()
+        for s in range(args.steps):
+            step(evs[s])
+        barrier()
+    per_shape = [0.0] * len(jobs)
+    for s in range(args.steps):
+        for j, (a, b) in enumerate(evs[s]):
+            per_shape[j] += a.elapsed_time(b) / args.steps
+    ms = sum(per_shape)
+
+    # end to end through the public API: pinned fp32 activations in, int8 outputs back
+    x_host = [torch.empty((M, K), dtype=torch.float32).pin_memory() for (M, K, N, *_ ) in jobs]
+    y_host = [torch.empty((M, N), dtype=torch.int8).pin_memory() for (M, K, N, *_ ) in jobs]
+    for h, (M, K, N, lin, x, y) in zip(x_host, jobs):
+        h.copy_(x)
+    h2d = sum(h.numel() * 4 for h in x_host)
+    d2h = sum(h.numel() for h in y_host)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        for h, o, (M, K, N, lin, x, y) in zip(x_host, y_host, jobs):
+            x.copy_(h, non_blocking=True)
+            lin.forward(x, OUT_QUANT, dyntok=True, out=y)
+            o.copy_(y, non_blocking=True)
+        stream.synchronize()
+    e1.record(stream)
+    barrier()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+
+    # dominant kernel: the tensor-core GEMM of M=2048, K=N=8192 alone (int8 input in HBM)
+    M, K, N, lin, x, y = jobs[PREFILL_SHAPES.index((2048, 8192, 8192))]
+    q = torch.empty((M, K), dtype=torch.int8, device=dev)
+    ratio = torch.empty((M,), dtype=torch.float32, device=dev)
+    lin.pack_npu_input(x, dyntok_ratios=ratio, out=q)
+    reps = 10
+    gemm_ms = []
+    for r in range(reps + 3):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        lin.submit(q, OUT_QUANT, out=y)
+        b.record(stream)
+        torch.cuda.synchronize()
+        if r >= 3:
+            gemm_ms.append(a.elapsed_time(b))
+    gemm_s = statistics.median(gemm_ms) / 1e3
+
+    times = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, ms_e2e = times.tolist()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        sample = [s for s in PREFILL_SHAPES if s[0] == 128]
+        run_cpu, cores = cpu_prefill_fn(sample)
+        run_cpu()
+        n, t0 = 0, time.perf_counter()
+        while True:
+            run_cpu()
+            n += 1
+            if time.perf_counter() - t0 > args.cpu_seconds:
+                break
+        dt = (time.perf_counter() - t0) / n
+        cpu = {"value": prefill_ops(sample) / dt / 1e12, "unit": "TOPS", "cores": cores,
+               "kind": "port", "sample": f"{n} passes over the four M=128 linears of the sweep, "
+                                         "C restatement of the reference linear, OpenMP"}
+
+    ops = prefill_ops(PREFILL_SHAPES)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    peak = 2.0 * bf16
+    achieved = 2 * M * N * K / gemm_s / 1e12
+    if rank == 0:
+        line = {
+            "metric": PREFILL_METRIC, "value": world * ops / (ms / 1e3) / 1e12, "unit": "TOPS",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": PREFILL_WORKLOAD,
+                       "parallelism": f"replicas: every GPU runs the whole sweep (x{world})",
+                       "l2": "256 MB written before every GEMM (outside the timed events)",
+                       "per_shape_us": {f"{m}x{k}x{n}": round(t * 1e3, 2)
+                                        for (m, k, n), t in zip(PREFILL_SHAPES, per_shape)},
+                       "per_shape_tops": {f"{m}x{k}x{n}": round(2 * m * n * k / (t / 1e3) / 1e12, 1)
+                                          for (m, k, n), t in zip(PREFILL_SHAPES, per_shape)}},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS",
+                         "frac": achieved / peak, "traffic": PREFILL_GEMM_TRAFFIC_BYTES,
+                         "kernel": "gemm_w8a8_tc_kernel M=2048 K=N=8192 (int8 in, int8 out)",
+                         "peak_kind": "2 x measured bf16 burst (B200 int8 dense rate = 2 x bf16)"
+                                      if "bf16_tflops" in peaks else "2 x fallback bf16",
+                         "nominal_peak": 4500.0, "frac_of_nominal": achieved / 4500.0,
+                         "launch_us": gemm_s * 1e6},
+            "e2e": {"value": world * ops / (ms_e2e / 1e3) / 1e12, "unit": "TOPS",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": 2 * len(jobs) * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -403,12 +631,16 @@ def main() -> None:
                     help="launch each linear separately instead of the persistent decode-chain "
                          "kernel (one cooperative launch per step)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode: the headline decode step; prefill: the int8 GEMM sweep")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.workload == "prefill":
+        run_prefill_reference(args) if args.impl == "reference" else run_prefill(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

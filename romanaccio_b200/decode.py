@@ -19,7 +19,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from ._lib import ACT_STATIC, DTYPE_INT8, OUT_F32, OUT_F32_ACC
+from ._lib import ACT_STATIC, DTYPE_INT8, OUT_F32, OUT_F32_ACC, TC_MIN_TOKENS
 from .chain import ChainStepSpec, DecodeChain
 from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
 from .lmhead import (LmHeadShard, candidate_buffers, exchange_candidates, shard_range,
@@ -109,7 +109,9 @@ class DecodeStack:
         self.top_val = torch.empty((self.T, self.k), dtype=torch.float32, device=dev)
         self.top_idx = torch.empty((self.T, self.k), dtype=torch.int32, device=dev)
         self.graph = None
-        self.chain = self._build_chain() if use_chain else None
+        # the persistent chain kernel covers decode batches of up to 8 tokens; larger batches run
+        # each linear as act_quant + tensor-core GEMM
+        self.chain = self._build_chain() if use_chain and self.T <= 8 else None
 
     def _build_chain(self) -> DecodeChain:
         """The whole linear stack (+ the LM head when it is not sharded) as one persistent
@@ -132,11 +134,14 @@ class DecodeStack:
 
     def launches_per_step(self) -> int:
         """Kernels of this library launched per step."""
-        lm = 0 if self.world == 1 else 3  # act_quant + top-k GEMV + merge
+        T_all = self.T * self.world
+        # LM head: act_quant + top-k GEMV per group of 8 tokens (+ merge when sharded)
+        lm = 1 + (T_all + 7) // 8 + (1 if self.world > 1 else 0)
         if self.chain is not None:
-            return 1 + lm
-        groups = (self.T + 7) // 8
-        return self.layers * 4 * (1 + groups) + (1 + groups if self.world == 1 else lm)
+            return 1 + (0 if self.world == 1 else lm)
+        # each linear: act_quant + one tensor-core GEMM, or a GEMV per group of 8 tokens
+        contraction = 1 if self.T >= TC_MIN_TOKENS else (self.T + 7) // 8
+        return self.layers * 4 * (1 + contraction) + lm
 
     # ------------------------------------------------------------------ byte accounting
     def step_bytes(self) -> StepBytes:
