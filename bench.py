@@ -38,8 +38,9 @@ GEMV_TRAFFIC_BYTES = 27666688
 # 1024-vocab chain (profiles/chain_kernel_qwen15b_4layer.md): 189.84 MB read / 188.7 MB.
 CHAIN_TRAFFIC_RATIO = 1.006
 # DRAM bytes (read + write) of one launch of the M=2048, K=N=8192 tensor-core GEMM from one ncu
-# capture (profiles/gemm_w8a8_tc_prefill_2048x8192x8192.md); None until captured.
-PREFILL_GEMM_TRAFFIC_BYTES = None
+# capture (profiles/gemm_w8a8_tc_prefill_2048x8192x8192.md): 84.005632 MB read + 6.348032 MB
+# written.
+PREFILL_GEMM_TRAFFIC_BYTES = 90353664
 
 
 def env_int(name: str, default: int) -> int:
