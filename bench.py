@@ -621,6 +621,86 @@ def run_prefill(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------- LM-head latency
+LMHEAD_METRIC = ("LM-head latency per decode step (hidden state in HBM -> top-40 ids and argmax "
+                 "on the host), vocab-sharded over n GPUs of one process")
+
+
+def run_lmhead(args) -> None:
+    """Qwen2.5-1.5B LM head (1536 x 151936, static int8 input, logits = acc * in_step * w_step)
+    sharded over n = 1, 2, 4, ... up to --gpus devices driven by this one process
+    (w8a8_lmhead_*): every step is one CUDA-graph replay of the sharded forward + merge and a
+    device-to-host copy of the ids, timed with CUDA events on GPU 0."""
+    if env_int("WORLD_SIZE", 1) > 1:
+        raise SystemExit("--workload lmhead drives every GPU from one process; run it without "
+                         "torchrun")
+    sys.path.insert(0, str(ROOT))
+    from romanaccio_b200 import Context, MultiDeviceLmHead, synth
+    n_max = min(args.gpus, torch.cuda.device_count())
+    ctxs = [Context(d) for d in range(n_max)]
+    torch.cuda.set_device(0)
+    K, V, k, T = synth.QWEN25_15B.hidden, synth.QWEN25_15B.vocab, 40, args.batch
+    rng = np.random.default_rng(17)
+    wq = rng.integers(-127, 128, size=(V, K), dtype=np.int16).astype(np.int8)
+    w_step = (rng.random(V) * 0.02 / 127 + 1e-5)
+    in_step = float(synth.activations(64, K, 23).abs().max()) / 127.0
+    acc_step = (in_step * w_step).astype(np.float32)
+    h = synth.activations(T, K, seed=5).cuda()
+    ids_host = torch.empty((T,), dtype=torch.int32).pin_memory()
+    counts = [n for n in (1, 2, 4, 8) if n <= n_max]
+    result, ids_ref = {}, None
+    for n in counts:
+        lm = MultiDeviceLmHead(ctxs[:n], wq, acc_step, in_step, max_tokens=max(T, 8), k_max=k)
+        val = torch.empty((T, k), dtype=torch.float32, device="cuda")
+        idx = torch.empty((T, k), dtype=torch.int32, device="cuda")
+        am = torch.empty((T,), dtype=torch.int32, device="cuda")
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            lm.forward(h, k, val, idx, am)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            lm.forward(h, k, val, idx, am)
+        stream = torch.cuda.current_stream()
+        for _ in range(args.warmup):
+            g.replay()
+            ids_host.copy_(am, non_blocking=True)
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            g.replay()
+            ids_host.copy_(am, non_blocking=True)
+            b.record(stream)
+            b.synchronize()
+            times.append(a.elapsed_time(b) * 1e3)
+        ids = ids_host.clone()
+        if ids_ref is None:
+            ids_ref = ids
+        result[n] = {"us_median": statistics.median(times), "us_min": min(times),
+                     "ids_equal_1gpu": bool(torch.equal(ids, ids_ref))}
+        del g, lm
+        torch.cuda.synchronize()
+    for c in ctxs:
+        c.check()
+    lat = [result[n]["us_median"] for n in counts]
+    line = {
+        "metric": LMHEAD_METRIC, "value": result[counts[-1]]["us_median"], "unit": "us",
+        "n_gpus": counts[-1], "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": result[counts[-1]]["us_median"] / 1e3, "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": f"LM head {K}x{V} top-{k} + argmax, T={T}",
+                   "by_shards": {str(n): result[n] for n in counts},
+                   "monotonic_decreasing": all(x > y for x, y in zip(lat, lat[1:])),
+                   "parallelism": "vocab-sharded, one process, peer stores into GPU 0"},
+        "e2e": {"value": result[counts[-1]]["us_median"], "unit": "us",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": T * 4},
+        "gpu_launches": counts[-1] * 2 + 1,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -632,8 +712,9 @@ def main() -> None:
                     help="launch each linear separately instead of the persistent decode-chain "
                          "kernel (one cooperative launch per step)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
-                    help="decode: the headline decode step; prefill: the int8 GEMM sweep")
+    ap.add_argument("--workload", choices=["decode", "prefill", "lmhead"], default="decode",
+                    help="decode: the headline decode step; prefill: the int8 GEMM sweep; "
+                         "lmhead: sharded LM-head latency over 1, 2, 4, 8 GPUs of one process")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
@@ -641,6 +722,8 @@ def main() -> None:
         raise SystemExit("--warmup must be >= 3")
     if args.workload == "prefill":
         run_prefill_reference(args) if args.impl == "reference" else run_prefill(args)
+    elif args.workload == "lmhead":
+        run_lmhead(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -100,6 +100,8 @@ w8a8_status w8a8_ctx_create(int device, w8a8_ctx **out_ctx);
 void        w8a8_ctx_destroy(w8a8_ctx *ctx);
 /* Number of SMs of the context's device. */
 int         w8a8_ctx_sm_count(const w8a8_ctx *ctx);
+/* CUDA device ordinal of the context (-1 for NULL). */
+int         w8a8_ctx_device(const w8a8_ctx *ctx);
 /* Synchronises the context's device and reports a device-side failure recorded by a kernel
  * (a bounded wait that ran out: W8A8_ERR_TIMEOUT / W8A8_ERR_PEER_TIMEOUT), then clears it.
  * Plays the role of the worker liveness checks of worker_pool.cpp:180-193. */
@@ -223,6 +225,35 @@ w8a8_status w8a8_topk_merge(w8a8_ctx *ctx, const float *in_val_dev, const int32_
                             int32_t *out_idx_dev, int32_t *argmax_dev, void *stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Vocab-sharded LM head over several devices driven by one process: the single-process form of
+ * the dual-die LM head (TransformerSession::forward_lm_head_dual_die,
+ * transformer_session.cpp:538-614; run_dual_die, lfm3_v2.cpp:1311-1332) for n = 1..8 shards.
+ * Shard s holds the contiguous vocab rows [s*V/n, (s+1)*V/n) (floor split; n = 2 gives the
+ * reference's halves, dual_die_splitter.py:95-141) on the device of ctxs[s].
+ *
+ * forward: h_dev lives on the device of ctxs[0].  Every shard quantises h itself (static
+ * in_step, the broadcast of fused_emb_norm_broadcast_t1, lfm3_v2.cpp:810-831) reading it over
+ * NVLink, runs its top-k GEMV, and stores its k (logit, vocab id) pairs straight into a gather
+ * buffer on device 0 (peer stores); device 0 merges them (value desc, id asc).  Streams of the
+ * shards are ordered after `stream` and back by events, so the call is asynchronous on
+ * `stream` and can be captured in a CUDA graph.  Logits: float(acc) * in_step * w_step[v]
+ * (acc_step = in_step * w_step).  Devices other than ctxs[0]'s need peer access to it.
+ * ------------------------------------------------------------------------------------- */
+typedef struct w8a8_lmhead w8a8_lmhead;
+
+w8a8_status w8a8_lmhead_create(w8a8_ctx *const *ctxs, int32_t n_shards, int32_t K, int32_t V,
+                               const int8_t *weights_host, int64_t weights_ld,
+                               const float *acc_step_host, float in_step, int32_t max_tokens,
+                               int32_t k_max, w8a8_lmhead **out_lmhead);
+/* topk_val_dev fp32 [T, k], topk_idx_dev int32 [T, k] (sorted), argmax_dev int32 [T] or NULL,
+ * all on the device of ctxs[0].  1 <= T <= max_tokens, 1 <= k <= k_max. */
+w8a8_status w8a8_lmhead_forward(w8a8_lmhead *lmhead, const float *h_dev, int32_t T, int32_t k,
+                                float *topk_val_dev, int32_t *topk_idx_dev, int32_t *argmax_dev,
+                                void *stream);
+void        w8a8_lmhead_destroy(w8a8_lmhead *lmhead);
+int32_t     w8a8_lmhead_shards(const w8a8_lmhead *lmhead);
+
+/* ---------------------------------------------------------------------------------------
  * Decode chain: a fixed sequence of linears, optionally ending with an LM-head top-k step, run
  * by ONE persistent cooperative kernel launch per forward.  Replaces the per-linear
  * pack -> submit_task -> unpack round trips of the reference's decode loop
@@ -274,7 +305,7 @@ w8a8_status w8a8_chain_set_trace(w8a8_chain *chain, unsigned long long *trace_de
  * for a static-input shard in F32_ACC mode (logit = float(acc) * acc_step[n]), but takes the
  * weights and parameters as device pointers (no w8a8_linear, no w8a8_ctx) and keeps its scratch
  * (int8 activations, per-CTA candidate lists, arrival counter) in one module-scope device array
- * of about 513 KiB that every GPU loading the library holds until the process exits.  It calls
+ * of about 1.4 MiB that every GPU loading the library holds until the process exits.  It calls
  * no cudaMalloc, cudaFree or allocating library routine.
  *
  * w_dev: int8 [N, ldw] on the current device, 16-byte aligned, ldw a multiple of 16 and
@@ -282,7 +313,7 @@ w8a8_status w8a8_chain_set_trace(w8a8_chain *chain, unsigned long long *trace_de
  * x_dev: fp32 [T, ldx].  in_step: static input step (q = RNE(clamp(x * (1 / in_step), +-127))).
  * Outputs topk_val_dev fp32 [T, k], topk_idx_dev int32 [T, k] (ids = row_offset + n), sorted
  * (value desc, id asc).  Limits: T <= 8, T * round_up(K, 16) <= 128 KiB, and
- * T * (CTAs of the launch, at most one per SM) * k <= 49152 candidate keys; larger requests
+ * T * (CTAs of the launch, at most two per SM) * k <= 163840 candidate keys; larger requests
  * return W8A8_ERR_INVALID_ARG with the reason in w8a8_last_error().
  *
  * The first call on a device resolves the scratch array's device address (with that device

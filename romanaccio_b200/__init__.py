@@ -7,12 +7,13 @@ from ._lib import (ACT_DYNTOK, ACT_STATIC, DTYPE_FP16, DTYPE_INT8, DTYPE_INT16, 
                    OUT_F32, OUT_F32_ACC, OUT_QUANT, PATH_AUTO, PATH_GEMV, PATH_TENSOR, TOPK_MAX,
                    W8A8Error)
 from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
-from .lmhead import LmHeadShard, VocabShardedLmHead, shard_range
+from .lmhead import LmHeadShard, MultiDeviceLmHead, VocabShardedLmHead, shard_range
 
 __all__ = [
     "ACT_DYNTOK", "ACT_STATIC", "DTYPE_FP16", "DTYPE_INT8", "DTYPE_INT16", "OUT_ACC_I32",
     "OUT_F32", "OUT_F32_ACC", "OUT_QUANT", "PATH_AUTO", "PATH_GEMV", "PATH_TENSOR", "TOPK_MAX",
     "W8A8Error", "Context",
-    "SubgraphScaleInfo", "W8A8Linear", "topk_merge", "LmHeadShard", "VocabShardedLmHead",
+    "SubgraphScaleInfo", "W8A8Linear", "topk_merge", "LmHeadShard", "MultiDeviceLmHead",
+    "VocabShardedLmHead",
     "shard_range",
 ]

@@ -83,6 +83,7 @@ SIGNATURES = {
     "w8a8_ctx_create": (C.c_int, [C.c_int, C.POINTER(_P)]),
     "w8a8_ctx_destroy": (None, [_P]),
     "w8a8_ctx_sm_count": (C.c_int, [_P]),
+    "w8a8_ctx_device": (C.c_int, [_P]),
     "w8a8_ctx_check": (C.c_int, [_P]),
     "w8a8_linear_create": (C.c_int, [_P, C.POINTER(LinearDesc), C.POINTER(_P)]),
     "w8a8_linear_destroy": (None, [_P]),
@@ -96,6 +97,11 @@ SIGNATURES = {
     "w8a8_linear_forward_topk": (
         C.c_int, [_P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _I64, _P]),
     "w8a8_topk_merge": (C.c_int, [_P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I32, _P, _P, _P, _P]),
+    "w8a8_lmhead_create": (C.c_int, [C.POINTER(_P), _I32, _I32, _I32, _P, _I64, _P, C.c_float,
+                                     _I32, _I32, C.POINTER(_P)]),
+    "w8a8_lmhead_forward": (C.c_int, [_P, _P, _I32, _I32, _P, _P, _P, _P]),
+    "w8a8_lmhead_destroy": (None, [_P]),
+    "w8a8_lmhead_shards": (_I32, [_P]),
     "w8a8_chain_create": (C.c_int, [_P, C.POINTER(ChainStep), _I32, _I32, C.POINTER(_P)]),
     "w8a8_chain_forward": (C.c_int, [_P, _P]),
     "w8a8_chain_destroy": (None, [_P]),

@@ -348,6 +348,8 @@ void w8a8_ctx_destroy(w8a8_ctx *ctx) {
 
 int w8a8_ctx_sm_count(const w8a8_ctx *ctx) { return ctx ? ctx->sm_count : 0; }
 
+int w8a8_ctx_device(const w8a8_ctx *ctx) { return ctx ? ctx->device : -1; }
+
 w8a8_status w8a8_ctx_check(w8a8_ctx *ctx) {
   if (!ctx) return fail(W8A8_ERR_INVALID_ARG, "ctx is NULL");
   DeviceGuard g(ctx->device);

@@ -83,8 +83,13 @@ __device__ __forceinline__ float logit_value(const Epilogue &ep, int acc, int t,
   return __int2float_rn(acc) * step;
 }
 
+struct BlockSync {
+  __device__ void operator()() const { __syncthreads(); }
+};
+
 // Merge of the per-CTA sorted lists of one token (run by the last CTA to finish).
-__device__ void merge_lists(const TopK &tk, int t, int G, uint64_t *buf, int buf_cap_pow2) {
+__device__ void merge_lists(const TopK &tk, int t, int G, uint64_t *buf, int buf_cap_pow2,
+                            TopkScratch *sc) {
   __shared__ unsigned long long s_red[kConsumerWarps + 1];
   __shared__ int s_red_g[kConsumerWarps + 1];
   __shared__ int s_count;
@@ -112,21 +117,28 @@ __device__ void merge_lists(const TopK &tk, int t, int G, uint64_t *buf, int buf
   }
   __syncthreads();
   const uint64_t tau = s_tau;
-  for (int g = tid; g < G; g += blockDim.x) {
-    const unsigned long long *lg =
-        reinterpret_cast<const unsigned long long *>(lists) + static_cast<size_t>(g) * k;
-    int c = 0;
-    while (c < k && __ldcg(lg + c) >= tau) ++c;
-    const int base = atomicAdd(&s_count, c);
-    for (int j = 0; j < c && base + j < buf_cap_pow2; ++j) buf[base + j] = __ldcg(lg + j);
+  // every key >= tau, read as one flat array with 4 independent loads per thread in flight
+  const unsigned long long *flat = reinterpret_cast<const unsigned long long *>(lists);
+  const int total = G * k;
+  for (int i0 = tid; i0 < total; i0 += 4 * kThreads) {
+    uint64_t v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * kThreads;
+      v[u] = i < total ? __ldcg(flat + i) : 0ull;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (v[u] >= tau) {
+        const int pos = atomicAdd(&s_count, 1);
+        if (pos < buf_cap_pow2) buf[pos] = v[u];
+      }
+    }
   }
   __syncthreads();
   const int C = s_count;
   if (C <= buf_cap_pow2) {
-    int P = 1;
-    while (P < C) P <<= 1;
-    for (int i = C + tid; i < P; i += blockDim.x) buf[i] = 0;
-    bitonic_sort_desc(buf, P);
+    block_topk<kThreads>(buf, C, k, buf, sc, tid, BlockSync{});
     for (int j = tid; j < k; j += blockDim.x) {
       tk.val[t * k + j] = topk_key_value(buf[j]);
       tk.idx[t * k + j] = topk_key_id(buf[j]);
@@ -171,7 +183,7 @@ __device__ void merge_lists(const TopK &tk, int t, int G, uint64_t *buf, int buf
 }
 
 template <int TT, int RPW, bool TOPK>
-__global__ void __launch_bounds__(kThreads, TOPK ? 1 : 2) gemv_w8a8_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a) {
   constexpr int RB = kConsumerWarps * RPW;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t *stages = smem;
@@ -331,18 +343,16 @@ __global__ void __launch_bounds__(kThreads, TOPK ? 1 : 2) gemv_w8a8_kernel(const
   if (!TOPK) return;
 
   // ------------------------------- top-k epilogue -------------------------------
+  __shared__ TopkScratch s_tk;
   __syncthreads();
   const int rows_here = min(ntiles * RB, a.N - tile0 * RB);
-  int P = 1;
-  while (P < rows_here) P <<= 1;
   const int k = a.tk.k;
   const int G = gridDim.x;
-  for (int t = 0; t < a.T; ++t) {
-    uint64_t *ct = cand + t * a.cand_cap;
-    bitonic_sort_desc(ct, P);
-    for (int j = threadIdx.x; j < k; j += blockDim.x)
-      a.tk.lists[(static_cast<size_t>(t) * G + blockIdx.x) * k + j] = j < P ? ct[j] : 0ull;
-  }
+  // this CTA's k best of its rows, sorted, per token (radix selection, not a full sort)
+  for (int t = 0; t < a.T; ++t)
+    block_topk<kThreads>(cand + t * a.cand_cap, rows_here, k,
+                         a.tk.lists + (static_cast<size_t>(t) * G + blockIdx.x) * k, &s_tk,
+                         threadIdx.x, BlockSync{});
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(a.tk.counter, 1u) == static_cast<unsigned>(G - 1);
@@ -355,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, TOPK ? 1 : 2) gemv_w8a8_kernel(const
   int cap = 1;
   while (static_cast<size_t>(cap) * 2 * 8 <= dyn_bytes) cap <<= 1;
   uint64_t *buf = reinterpret_cast<uint64_t *>(smem);
-  for (int t = 0; t < a.T; ++t) merge_lists(a.tk, t, G, buf, cap);
+  for (int t = 0; t < a.T; ++t) merge_lists(a.tk, t, G, buf, cap, &s_tk);
   if (threadIdx.x == 0) *a.tk.counter = 0u;
 }
 
@@ -411,7 +421,7 @@ bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan
   GemvPlan p = {};
   p.tt = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
   auto tiles = [&](int rb) { return (N + rb - 1) / rb; };
-  const int min_tiles = topk ? sm_count : 2 * sm_count;
+  const int min_tiles = 2 * sm_count;
   constexpr int kMaxStage = 32768;
   p.rpw = 1;
   if (k_pad * 8 <= kMaxStage) {
@@ -440,7 +450,7 @@ bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan
     p.smem = p.ns * stage + bars;
   } else {
     if (k < 1 || k > 64 || k > N) return false;
-    int grid = std::min(p.num_tiles, sm_count);
+    int grid = std::min(p.num_tiles, 2 * sm_count);
     size_t cap = 0;
     while (true) {
       const int tpc = (p.num_tiles + grid - 1) / grid;
@@ -453,7 +463,7 @@ bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan
     p.grid = (p.num_tiles + p.tiles_per_cta - 1) / p.tiles_per_cta;
     p.cand_cap = static_cast<int>(cap);
     const size_t cand_bytes = static_cast<size_t>(p.tt) * cap * 8;
-    const size_t budget = 200 * 1024 - cand_bytes;
+    const size_t budget = 110 * 1024 > cand_bytes + 2 * stage ? 110 * 1024 - cand_bytes : 2 * stage;
     p.ns = static_cast<int>(std::min<size_t>(kMaxStages, std::max<size_t>(2, budget / stage)));
     p.smem = p.ns * stage + bars + cand_bytes;
   }

@@ -9,7 +9,7 @@
 // keeps that scratch in one module-scope device array instead, so the entry point below
 // allocates nothing.
 //
-// The array (kScratchBytes, about 513 KiB) is held by every GPU that loads the library until
+// The array (kScratchBytes, about 1.4 MiB) is held by every GPU that loads the library until
 // the process exits.  All calls on a device share it and it keeps the last call's contents, so
 // calls whose executions overlap on the GPU (different streams, or different host threads
 // without ordering) race and corrupt each other's results; the arrival counter, which must
@@ -28,7 +28,7 @@ namespace {
 constexpr int kMaxTokens = 8;
 constexpr size_t kXqBytes = 128 * 1024;     // int8 activations: T * round_up(K, 16) bytes
 constexpr size_t kMiscBytes = 256;          // ratios [8] fp32, counter, error word
-constexpr size_t kListKeys = 48 * 1024;     // per-CTA candidate keys (u64): 384 KiB
+constexpr size_t kListKeys = 160 * 1024;    // per-CTA candidate keys (u64): 1.25 MiB
 constexpr size_t kScratchBytes = kXqBytes + kMiscBytes + kListKeys * 8;
 constexpr int kMaxDevices = 64;
 

@@ -119,3 +119,58 @@ class VocabShardedLmHead:
         exchange_candidates(local, gathered, self.group)
         vals, ids = token_candidates(gathered, self.world, 0, T)
         return topk_merge(self.ctx, vals, ids, k, stream=stream)
+
+
+class MultiDeviceLmHead:
+    """Vocab-sharded LM head over several devices driven by this process (w8a8_lmhead_*).
+
+    Shard s holds vocab rows shard_range(V, n, s) on the device of ctxs[s]; forward(h) with h
+    on ctxs[0]'s device returns (top-k values [T, k], top-k vocab ids [T, k], argmax [T]) there.
+    The shards read h and store their candidates over NVLink; one merge kernel finishes.
+    """
+
+    def __init__(self, ctxs: list[Context], wq: np.ndarray, acc_step: np.ndarray,
+                 in_step: float, max_tokens: int = 64, k_max: int = 64):
+        import ctypes as C
+        from ._lib import check
+        self._lib = ctxs[0]._lib
+        self.ctxs = list(ctxs)
+        self.device = ctxs[0].device
+        w = np.ascontiguousarray(wq, dtype=np.int8)
+        st = np.ascontiguousarray(acc_step, dtype=np.float32)
+        self.V, self.K = map(int, w.shape)
+        arr = (C.c_void_p * len(ctxs))(*[c.handle.value for c in ctxs])
+        h = C.c_void_p()
+        check(self._lib.w8a8_lmhead_create(arr, len(ctxs), self.K, self.V, w.ctypes.data,
+                                           self.K, st.ctypes.data, float(in_step),
+                                           int(max_tokens), int(k_max), C.byref(h)),
+              "w8a8_lmhead_create")
+        self.handle = h
+        self._check = check
+
+    @property
+    def shards(self) -> int:
+        return int(self._lib.w8a8_lmhead_shards(self.handle))
+
+    def forward(self, h: torch.Tensor, k: int, val=None, idx=None, argmax=None, stream=None):
+        from .linear import _stream
+        T = h.shape[0]
+        dev = h.device
+        v = val if val is not None else torch.empty((T, k), dtype=torch.float32, device=dev)
+        i = idx if idx is not None else torch.empty((T, k), dtype=torch.int32, device=dev)
+        a = argmax if argmax is not None else torch.empty((T,), dtype=torch.int32, device=dev)
+        self._check(self._lib.w8a8_lmhead_forward(self.handle, h.data_ptr(), T, int(k),
+                                                  v.data_ptr(), i.data_ptr(), a.data_ptr(),
+                                                  _stream(stream)), "w8a8_lmhead_forward")
+        return v, i, a
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self._lib.w8a8_lmhead_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

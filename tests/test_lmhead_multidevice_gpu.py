@@ -1,0 +1,85 @@
+"""The single-process, multi-device LM head (w8a8_lmhead_*): shards on one device (every shard
+count) and, when the box has them, on several devices; the merged top-k and argmax must equal
+the oracle's top-k over the full vocabulary (bit-exact values, identical ids)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+import romanaccio_b200 as rb
+from romanaccio_b200 import synth
+
+from test_lmhead_gpu import lm_params, oracle_logits
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(lm, x, wq, in_step, acc_step, k):
+    val, idx, am = lm.forward(torch.from_numpy(x).cuda(lm.device), k)
+    torch.cuda.synchronize()
+    lg = oracle_logits(x, wq, in_step, acc_step)
+    wv, wi = O.topk(lg, k)
+    assert np.array_equal(idx.cpu().numpy(), wi)
+    assert np.array_equal(val.cpu().numpy(), wv)
+    assert np.array_equal(am.cpu().numpy(), wi[:, 0])
+
+
+@pytest.mark.parametrize("n,V,K,T,k", [
+    (1, 49152, 576, 1, 40), (2, 49152, 576, 1, 40), (3, 20000, 1536, 2, 40),
+    (4, 151936, 1536, 1, 40), (8, 151936, 1536, 3, 64), (2, 1000, 64, 5, 7),
+])
+def test_shards_on_one_device(ctx, n, V, K, T, k):
+    wq, w_step = lm_params(V, K, seed=V + n)
+    in_step = 0.031
+    acc_step = (in_step * w_step).astype(np.float32)
+    lm = rb.MultiDeviceLmHead([ctx] * n, wq, acc_step, in_step, max_tokens=8, k_max=64)
+    assert lm.shards == n
+    x = synth.activations(T, K, seed=n + T).numpy()
+    _check(lm, x, wq, in_step, acc_step, k)
+    # repeated calls reuse the gather buffers and streams
+    _check(lm, synth.activations(T, K, seed=99).numpy(), wq, in_step, acc_step, k)
+
+
+def test_graph_capture(ctx):
+    """The whole forward (fork to the shard streams, join, merge) is capturable."""
+    V, K, T, k, n = 65536, 1536, 1, 40, 4
+    wq, w_step = lm_params(V, K, seed=5)
+    in_step = 0.02
+    acc_step = (in_step * w_step).astype(np.float32)
+    lm = rb.MultiDeviceLmHead([ctx] * n, wq, acc_step, in_step, max_tokens=4, k_max=40)
+    x = torch.from_numpy(synth.activations(T, K, seed=7).numpy()).cuda()
+    val = torch.empty((T, k), dtype=torch.float32, device="cuda")
+    idx = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    am = torch.empty((T,), dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        lm.forward(x, k, val, idx, am)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        lm.forward(x, k, val, idx, am)
+    val.zero_()
+    idx.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    lg = oracle_logits(x.cpu().numpy(), wq, in_step, acc_step)
+    wv, wi = O.topk(lg, k)
+    assert np.array_equal(idx.cpu().numpy(), wi)
+    assert np.array_equal(val.cpu().numpy(), wv)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 or more GPUs")
+def test_shards_on_several_devices():
+    n = min(torch.cuda.device_count(), 8)
+    ctxs = [rb.Context(d) for d in range(n)]
+    V, K, T, k = 151936, 1536, 2, 40
+    wq, w_step = lm_params(V, K, seed=11)
+    in_step = 0.031
+    acc_step = (in_step * w_step).astype(np.float32)
+    lm = rb.MultiDeviceLmHead(ctxs, wq, acc_step, in_step, max_tokens=8, k_max=64)
+    x = synth.activations(T, K, seed=12).numpy()
+    _check(lm, x, wq, in_step, acc_step, k)
+    for c in ctxs:
+        c.check()
