@@ -131,3 +131,23 @@ def build_linear(w: np.ndarray | torch.Tensor, calib_x: torch.Tensor, trunc: int
                         quant_m=qm_f.to(torch.int16).cpu().numpy(),
                         out_step_chan=out_step_chan.cpu().numpy(), in_thresh=in_t,
                         in_step=in_s, trunc=trunc)
+
+
+def split_columns(p: LinearParams, n: int) -> list[LinearParams]:
+    """Column-split tensor parallelism of one linear over n shards (lfm3_v2.cpp:1920-1975,
+    build_lfm3_tp2_pkg.py:80-160): shard s keeps the contiguous output channels
+    [s*N/n, (s+1)*N/n) with their weight rows, QuantM and out_step_chan (the per-die
+    out_step_chan offset of lfm3_v2.cpp:3852-3860) and shares the input side (in_inv_smooth,
+    in_thresh, in_step, trunc).  Every output channel's arithmetic is unchanged, so the shards'
+    outputs concatenated along N equal the unsplit linear's outputs bit for bit."""
+    N = p.wq.shape[0]
+    if not 1 <= n <= N:
+        raise ValueError(f"cannot split {N} output channels into {n} shards")
+    out = []
+    for s in range(n):
+        lo, hi = (s * N) // n, ((s + 1) * N) // n
+        out.append(LinearParams(wq=np.ascontiguousarray(p.wq[lo:hi]), w_step=p.w_step[lo:hi].copy(),
+                                in_inv_smooth=p.in_inv_smooth, quant_m=p.quant_m[lo:hi].copy(),
+                                out_step_chan=p.out_step_chan[lo:hi].copy(),
+                                in_thresh=p.in_thresh, in_step=p.in_step, trunc=p.trunc))
+    return out

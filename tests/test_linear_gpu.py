@@ -190,3 +190,23 @@ def test_repeated_calls_and_errors(ctx):
     with pytest.raises(rb.W8A8Error):
         nolin.forward(x, rb.OUT_QUANT)
     ctx.check()
+
+
+@pytest.mark.parametrize("n", [2, 3, 4])
+def test_column_split_tensor_parallel(ctx, n):
+    """Column-split TP (output-channel shards sharing the input side): the shards' outputs,
+    concatenated, equal the unsplit linear's and the oracle's, for every output mode."""
+    from romanaccio_b200.quantize import split_columns
+    T, K, N = 5, 1536, 2304
+    p = synth.make_linear(K, N, seed=40 + n)
+    full = rb.W8A8Linear.from_params(ctx, p)
+    shards = [rb.W8A8Linear.from_params(ctx, s) for s in split_columns(p, n)]
+    x = synth.activations(T, K, seed=n).cuda()
+    for mode in (rb.OUT_ACC_I32, rb.OUT_QUANT, rb.OUT_F32, rb.OUT_F32_ACC):
+        want = full.forward(x, out_mode=mode, dyntok=True).cpu()
+        got = torch.cat([s.forward(x, out_mode=mode, dyntok=True).cpu() for s in shards], dim=1)
+        assert torch.equal(got, want)
+    q, r = O.pack_dyntok(x.cpu().numpy(), p.in_thresh, p.in_inv_smooth)
+    yq = O.requant(O.gemm_i32(q, p.wq), p.quant_m, p.trunc, 127)
+    got = torch.cat([s.forward(x, out_mode=rb.OUT_QUANT, dyntok=True).cpu() for s in shards], dim=1)
+    assert np.array_equal(got.numpy().astype(np.int32), yq)
