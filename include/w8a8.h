@@ -254,6 +254,68 @@ void        w8a8_lmhead_destroy(w8a8_lmhead *lmhead);
 int32_t     w8a8_lmhead_shards(const w8a8_lmhead *lmhead);
 
 /* ---------------------------------------------------------------------------------------
+ * Mixture-of-experts layer (decode): router + W8A8 experts + weighted combine, all on the
+ * device (no host round trip between routing and the experts).
+ *
+ *   route:   MoERouter::route (src/eswin_runtime/src/llm/moe_router.cpp:211-260): fp32 logits
+ *            W_gate . h (+ bias), softmax (max subtracted, float exp, double sum,
+ *            scores_from_logits :108-130), top-k by (score desc, expert index asc), weights =
+ *            the probabilities (renormalised only when norm_topk_prob), times routed_scaling.
+ *   experts: every (token, slot) pair, slots = top_k routed experts then n_shared shared ones
+ *            (weight 1): gate|up W8A8 linear (dyntok input, F32 output) -> silu(gate) * up ->
+ *            down W8A8 linear (static input, QUANT int8/int16 output y_q).
+ *   combine: out[t, c] = sum over the token's slots in order of
+ *            float(y_q[c]) * (w_slot * down_out_step_chan[e, c])
+ *            (src/LFM2.5-8B-A1B/lfm2_moe.cpp:2300-2318).
+ * Expert e (0 <= e < n_routed + n_shared) parameters are expert-major host arrays, copied at
+ * create.  The router's logits are a warp-parallel fp32 sum (not the reference's serial
+ * order), so routing weights agree within float rounding; the expert stages and the combine
+ * are exact given the routing.
+ * ------------------------------------------------------------------------------------- */
+typedef struct {
+    int32_t        hidden;            /* H <= 4096 */
+    int32_t        inter;             /* I <= 4096, expert intermediate size */
+    int32_t        n_routed;          /* E */
+    int32_t        n_shared;          /* S */
+    int32_t        top_k;             /* k <= 16 */
+    int32_t        norm_topk_prob;    /* 0: raw softmax probabilities (DeepSeek-V2-Lite) */
+    float          routed_scaling;    /* routed_scaling_factor (1.0 for none) */
+    int32_t        max_tokens;        /* largest T of a forward */
+    const float   *gate_w;            /* [E, H] router weights */
+    const float   *gate_bias;         /* [E] or NULL */
+    const int8_t  *gu_weights;        /* [E+S, 2I, H]: gate rows then up rows */
+    const int16_t *gu_quant_m;        /* [E+S, 2I] */
+    const float   *gu_out_step_chan;  /* [E+S, 2I] */
+    const float   *gu_inv_smooth;     /* [E+S, H] */
+    const float   *gu_in_thresh;      /* [E+S] dyntok input threshold */
+    int32_t        gu_trunc;
+    const int8_t  *dn_weights;        /* [E+S, H, I] */
+    const int16_t *dn_quant_m;        /* [E+S, H] */
+    const float   *dn_out_step_chan;  /* [E+S, H] */
+    const float   *dn_inv_smooth;     /* [E+S, I] */
+    const float   *dn_in_step;        /* [E+S] static input step */
+    int32_t        dn_trunc;
+    int32_t        dn_out_dtype;      /* W8A8_DTYPE_INT8 or W8A8_DTYPE_INT16 */
+} w8a8_moe_desc;
+
+typedef struct w8a8_moe w8a8_moe;
+
+w8a8_status w8a8_moe_create(w8a8_ctx *ctx, const w8a8_moe_desc *desc, w8a8_moe **out_moe);
+void        w8a8_moe_destroy(w8a8_moe *moe);
+/* Router only: idx_dev int32 [T, k], w_dev fp32 [T, k]. */
+w8a8_status w8a8_moe_route(w8a8_moe *moe, const float *hidden_dev, int64_t ldh, int32_t T,
+                           int32_t *idx_dev, float *w_dev, void *stream);
+/* Whole layer: hidden_dev fp32 [T, ldh] -> out_dev fp32 [T, ldo] (T <= max_tokens). */
+w8a8_status w8a8_moe_forward(w8a8_moe *moe, const float *hidden_dev, int64_t ldh, int32_t T,
+                             float *out_dev, int64_t ldo, void *stream);
+/* Device views of the last forward's intermediates (for tests and tracing): routed ids
+ * [T, k], weights [T, k], gate|up outputs fp32 [T*slots, 2I], silu(gate)*up fp32
+ * [T*slots, I], down requantised outputs [T*slots, H] (int16 or int8 per dn_out_dtype). */
+w8a8_status w8a8_moe_views(const w8a8_moe *moe, const int32_t **idx_dev, const float **w_dev,
+                           const float **gate_up_dev, const float **act_dev,
+                           const void **down_q_dev);
+
+/* ---------------------------------------------------------------------------------------
  * Decode chain: a fixed sequence of linears, optionally ending with an LM-head top-k step, run
  * by ONE persistent cooperative kernel launch per forward.  Replaces the per-linear
  * pack -> submit_task -> unpack round trips of the reference's decode loop

@@ -30,6 +30,8 @@ _ORACLE_SIGS = {
     "orc_dequant_acc": (None, [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _I64]),
     "orc_topk": (None, [_P, _I64, _I32, _I32, _I32, _I32, _P, _P]),
     "orc_argmax": (C.c_int32, [_P, _I32]),
+    "orc_moe_route": (None, [_P, _I64, _I32, _I32, _P, _P, _I32, _I32, _I32, _F, _P, _P]),
+    "orc_moe_combine": (None, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P]),
     "orc_num_threads": (C.c_int, []),
     "orc_set_threads": (None, [C.c_int]),
     "orc_linear_dyntok_omp": (None, [_P, _I32, _I32, _I32, _P, _P, _F, _P, _I32, _P, _P, _P, _P]),
@@ -42,6 +44,7 @@ _REF_SIGS = {
     "ref_unpack_int8": (C.c_int, [_P, C.c_int, C.c_int, _F, _P, _P, _P]),
     "ref_unpack_int16": (C.c_int, [_P, C.c_int, C.c_int, _F, _P, _P]),
     "ref_sampler_greedy": (C.c_int32, [_P, C.c_size_t]),
+    "ref_moe_route": (C.c_int, [_P, C.c_int, C.c_int, _P, _P, C.c_int, C.c_int, C.c_int, _F, _P, _P]),
 }
 
 _orc = None
@@ -172,6 +175,35 @@ def argmax(logits_row: np.ndarray) -> int:
     return int(lib().orc_argmax(_p(lg), lg.shape[0]))
 
 
+def moe_route(hidden: np.ndarray, gate_w: np.ndarray, k: int, bias: np.ndarray | None = None,
+              norm_topk: bool = False, scaling: float = 1.0):
+    """MoERouter::route for every row of hidden [T, H]: (expert ids [T, k], weights [T, k])."""
+    h = _c(hidden, np.float32)
+    gw = _c(gate_w, np.float32)
+    b = _c(bias, np.float32)
+    T, H = h.shape
+    E = gw.shape[0]
+    idx = np.empty((T, k), np.int32)
+    w = np.empty((T, k), np.float32)
+    lib().orc_moe_route(_p(h), H, T, H, _p(gw), _p(b), E, k, int(norm_topk), float(scaling),
+                        _p(idx), _p(w))
+    return idx, w
+
+
+def moe_combine(yq: np.ndarray, idx: np.ndarray, w: np.ndarray, out_step_chan: np.ndarray,
+                n_routed: int, slots: int) -> np.ndarray:
+    """Weighted combine of the experts' requantised outputs yq [T*slots, H] into [T, H]."""
+    y = _c(yq, np.int32)
+    ix = _c(idx, np.int32)
+    ww = _c(w, np.float32)
+    osc = _c(out_step_chan, np.float32)
+    T, k = ix.shape
+    H = y.shape[1]
+    out = np.empty((T, H), np.float32)
+    lib().orc_moe_combine(_p(y), T, k, slots, n_routed, H, _p(ix), _p(ww), _p(osc), _p(out))
+    return out
+
+
 def linear(x: np.ndarray, wq: np.ndarray, quant_m: np.ndarray, trunc: int, out_step_chan: np.ndarray,
            inv_smooth: np.ndarray | None, in_thresh: float | None = None, in_step: float | None = None,
            out_step: float = 0.0, qmax: int = 127):
@@ -234,3 +266,19 @@ def ref_unpack_i16(yq: np.ndarray, out_step: float, out_step_chan: np.ndarray | 
 def ref_greedy(logits_row: np.ndarray) -> int:
     lg = np.array(logits_row, dtype=np.float32, copy=True)
     return int(ref().ref_sampler_greedy(_p(lg), lg.shape[0]))
+
+
+def ref_moe_route(hidden: np.ndarray, gate_w: np.ndarray, k: int, bias: np.ndarray | None = None,
+                  norm_topk: bool = False, scaling: float = 1.0):
+    """The reference's MoERouter::route (compiled from its sources) on every row of hidden."""
+    h = _c(hidden, np.float32)
+    gw = _c(gate_w, np.float32)
+    b = _c(bias, np.float32)
+    T, H = h.shape
+    idx = np.empty((T, k), np.int32)
+    w = np.empty((T, k), np.float32)
+    rc = ref().ref_moe_route(_p(h), T, H, _p(gw), _p(b), gw.shape[0], k, int(norm_topk),
+                             float(scaling), _p(idx), _p(w))
+    if rc != 0:
+        raise RuntimeError(f"ref_moe_route failed ({rc})")
+    return idx, w

@@ -9,6 +9,7 @@
 //                          (:1050-1141), unpack_npu_output_int8 (:971-1008), _int16 (:1011-1046),
 //                          _int8_dyntok (:1143-1183), round_clamp_f32 (:248-257)
 //   src/eswin_runtime/src/nlp/sampler.cpp   Sampler::sample greedy path (:93-103)
+//   src/eswin_runtime/src/llm/moe_router.cpp MoERouter::route (:211-260)
 //
 // lfm3_v2.cpp is a program: its main() is renamed so this shim can include it as a
 // translation unit and call its file-static functions.  For T > 1 the reference packs into
@@ -18,7 +19,10 @@
 #include "lfm3_v2.cpp"
 #undef main
 
+#include <string>
 #include <vector>
+
+#include "llm/moe_router.hpp"
 
 extern "C" {
 
@@ -99,6 +103,30 @@ int32_t ref_sampler_greedy(float *logits, size_t vocab) {
     p.seed = 1;
     eswin::Sampler s(p);
     return s.sample(logits, vocab);
+}
+
+// MoERouter::route over T tokens (softmax scoring, greedy top-k): ids [T, k], weights [T, k].
+int ref_moe_route(const float *hidden, int T, int H, const float *gate_w, const float *bias, int E,
+                  int k, int norm_topk, float scaling, int32_t *idx, float *w) {
+    eswin::MoERouterConfig cfg;
+    cfg.hidden_size = static_cast<uint32_t>(H);
+    cfg.num_experts = static_cast<uint32_t>(E);
+    cfg.top_k = static_cast<uint32_t>(k);
+    cfg.norm_topk_prob = norm_topk != 0;
+    cfg.routed_scaling_factor = scaling;
+    cfg.has_gate_bias = bias != nullptr;
+    eswin::MoERouter r;
+    std::string err;
+    if (!r.init(cfg, gate_w, bias, err)) return -1;
+    eswin::MoERouterResult res;
+    for (int t = 0; t < T; ++t) {
+        if (!r.route(hidden + static_cast<size_t>(t) * H, res)) return -2;
+        for (int j = 0; j < k; ++j) {
+            idx[t * k + j] = static_cast<int32_t>(res.routed[j].index);
+            w[t * k + j] = res.routed[j].score;
+        }
+    }
+    return 0;
 }
 
 }  // extern "C"

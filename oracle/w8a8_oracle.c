@@ -18,6 +18,8 @@
  *   orc_dequant_acc   logit = float(acc) * (ratio * acc_step) (LM-head logit mode)
  *   orc_topk          src/eswin_runtime/src/nlp/sampler.cpp:93-121 (greedy keeps the lowest id on
  *                     ties; top-k ordered value desc, then id asc)
+ *   orc_moe_route     src/eswin_runtime/src/llm/moe_router.cpp:92-130, 211-260 (MoERouter::route)
+ *   orc_moe_combine   src/LFM2.5-8B-A1B/lfm2_moe.cpp:2300-2318 (weighted expert combine)
  *
  * Compile without fast-math and with -ffp-contract=off so every float step rounds like the
  * reference's scalar C++.
@@ -193,4 +195,82 @@ int32_t orc_argmax(const float *logits, int32_t V) {
             best = i;
         }
     return best;
+}
+
+/* ------------------------------------------------------------------------------------------
+ * Mixture of experts (decode)
+ * ---------------------------------------------------------------------------------------- */
+
+/* MoERouter::route (src/eswin_runtime/src/llm/moe_router.cpp:211-260) for T tokens:
+ * logits[e] = sum_i w[e,i] * h[i] in float, serial over i (MoERouter::logits, :92-105), + bias;
+ * softmax with the max subtracted, float exp, double sum, float inverse (scores_from_logits,
+ * :108-130); top-k by (score desc, index asc) (the partial_sort comparator); weights = scores,
+ * renormalised by their float sum only when norm_topk, then times scaling. */
+void orc_moe_route(const float *hidden, int64_t ldh, int32_t T, int32_t H, const float *gate_w,
+                   const float *bias, int32_t E, int32_t k, int32_t norm_topk, float scaling,
+                   int32_t *idx, float *w) {
+    float *logit = (float *)malloc(sizeof(float) * (size_t)E);
+    float *score = (float *)malloc(sizeof(float) * (size_t)E);
+    for (int32_t t = 0; t < T; ++t) {
+        const float *h = hidden + (int64_t)t * ldh;
+        for (int32_t e = 0; e < E; ++e) {
+            float acc = 0.0f;
+            const float *we = gate_w + (int64_t)e * H;
+            for (int32_t i = 0; i < H; ++i) acc += we[i] * h[i];
+            logit[e] = bias ? acc + bias[e] : acc;
+        }
+        float mx = logit[0];
+        for (int32_t e = 1; e < E; ++e)
+            if (logit[e] > mx) mx = logit[e];
+        double sum = 0.0;
+        for (int32_t e = 0; e < E; ++e) {
+            score[e] = expf(logit[e] - mx);
+            sum += score[e];
+        }
+        if (sum > 0.0) {
+            const float inv = (float)(1.0 / sum);
+            for (int32_t e = 0; e < E; ++e) score[e] *= inv;
+        }
+        float wsum = 0.0f;
+        for (int32_t j = 0; j < k; ++j) {
+            int32_t best = -1;
+            for (int32_t e = 0; e < E; ++e) {
+                if (score[e] < 0.0f) continue;
+                if (best < 0 || score[e] > score[best]) best = e;
+            }
+            idx[t * k + j] = best;
+            w[t * k + j] = score[best];
+            wsum += score[best];
+            score[best] = -1.0f;
+        }
+        if (norm_topk && wsum > 0.0f) {
+            const float inv = 1.0f / wsum;
+            for (int32_t j = 0; j < k; ++j) w[t * k + j] *= inv;
+        }
+        if (scaling != 1.0f)
+            for (int32_t j = 0; j < k; ++j) w[t * k + j] *= scaling;
+    }
+    free(logit);
+    free(score);
+}
+
+/* Expert combine (src/LFM2.5-8B-A1B/lfm2_moe.cpp:2300-2318):
+ * out[t,c] = sum over slots j in order, from 0, of float(yq[p,c]) * (w_j * out_step_chan[e_j,c]),
+ * p = t * slots + j; slots j < k are routed (expert idx[t,j], weight w[t,j]), the rest shared
+ * (expert n_routed + j - k, weight 1). */
+void orc_moe_combine(const int32_t *yq, int32_t T, int32_t k, int32_t slots, int32_t n_routed,
+                     int32_t H, const int32_t *idx, const float *w, const float *out_step_chan,
+                     float *out) {
+    for (int32_t t = 0; t < T; ++t) {
+        for (int32_t c = 0; c < H; ++c) {
+            float acc = 0.0f;
+            for (int32_t j = 0; j < slots; ++j) {
+                const int32_t p = t * slots + j;
+                const int32_t e = j < k ? idx[t * k + j] : n_routed + (j - k);
+                const float wj = j < k ? w[t * k + j] : 1.0f;
+                acc += (float)yq[(int64_t)p * H + c] * (wj * out_step_chan[(int64_t)e * H + c]);
+            }
+            out[(int64_t)t * H + c] = acc;
+        }
+    }
 }

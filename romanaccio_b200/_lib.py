@@ -57,6 +57,34 @@ class LinearDesc(C.Structure):
     ]
 
 
+class MoeDesc(C.Structure):
+    _fields_ = [
+        ("hidden", C.c_int32),
+        ("inter", C.c_int32),
+        ("n_routed", C.c_int32),
+        ("n_shared", C.c_int32),
+        ("top_k", C.c_int32),
+        ("norm_topk_prob", C.c_int32),
+        ("routed_scaling", C.c_float),
+        ("max_tokens", C.c_int32),
+        ("gate_w", C.c_void_p),
+        ("gate_bias", C.c_void_p),
+        ("gu_weights", C.c_void_p),
+        ("gu_quant_m", C.c_void_p),
+        ("gu_out_step_chan", C.c_void_p),
+        ("gu_inv_smooth", C.c_void_p),
+        ("gu_in_thresh", C.c_void_p),
+        ("gu_trunc", C.c_int32),
+        ("dn_weights", C.c_void_p),
+        ("dn_quant_m", C.c_void_p),
+        ("dn_out_step_chan", C.c_void_p),
+        ("dn_inv_smooth", C.c_void_p),
+        ("dn_in_step", C.c_void_p),
+        ("dn_trunc", C.c_int32),
+        ("dn_out_dtype", C.c_int32),
+    ]
+
+
 class ChainStep(C.Structure):
     _fields_ = [
         ("linear", C.c_void_p),
@@ -102,6 +130,12 @@ SIGNATURES = {
     "w8a8_lmhead_forward": (C.c_int, [_P, _P, _I32, _I32, _P, _P, _P, _P]),
     "w8a8_lmhead_destroy": (None, [_P]),
     "w8a8_lmhead_shards": (_I32, [_P]),
+    "w8a8_moe_create": (C.c_int, [_P, C.POINTER(MoeDesc), C.POINTER(_P)]),
+    "w8a8_moe_destroy": (None, [_P]),
+    "w8a8_moe_route": (C.c_int, [_P, _P, _I64, _I32, _P, _P, _P]),
+    "w8a8_moe_forward": (C.c_int, [_P, _P, _I64, _I32, _P, _I64, _P]),
+    "w8a8_moe_views": (C.c_int, [_P, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(_P),
+                                 C.POINTER(_P)]),
     "w8a8_chain_create": (C.c_int, [_P, C.POINTER(ChainStep), _I32, _I32, C.POINTER(_P)]),
     "w8a8_chain_forward": (C.c_int, [_P, _P]),
     "w8a8_chain_destroy": (None, [_P]),

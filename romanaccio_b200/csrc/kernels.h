@@ -119,6 +119,75 @@ size_t tc_tile_bytes(int N, int k_pad);
 cudaError_t launch_tile_weights(const int8_t *w, int64_t ldw, int N, int k_pad, int8_t *tiles,
                                 cudaStream_t stream);
 
+// ---- mixture of experts (decode) ----
+// Pair p = t * slots + j: slot j < k is the token's j-th routed expert, the rest are the shared
+// experts (stored after the n_routed routed ones).
+struct MoePairs {
+  int T, k, slots, n_routed;
+  const int32_t *routed_idx;  // [T, k]
+  const float *routed_w;      // [T, k]
+};
+
+struct MoeRouteLaunch {
+  const float *hidden;  // [T, ldh]
+  int64_t ldh;
+  const float *gate_w;  // [E, H]
+  const float *bias;    // [E] or null
+  int T, H, E, k, norm_topk;
+  float scaling;
+  int32_t *idx;         // [T, k]
+  float *w;             // [T, k]
+  bool pdl;
+};
+
+struct MoeActLaunch {
+  MoePairs pairs;
+  const float *src;          // rows: token t (per_pair_rows = 0) or pair p (1)
+  int64_t ld;
+  int per_pair_rows;
+  int K;
+  const float *inv_smooth;   // [E_total, K]
+  const float *inv_step;     // [E_total] static 1/in_step, or null in dyntok mode
+  const float *safe_thresh;  // [E_total] max(in_thresh, 1e-8) (dyntok)
+  int8_t *q;                 // [pairs, ldq], ldq = round_up(K, 16)
+  int64_t ldq;
+  float *ratio;              // [pairs] (dyntok)
+  bool pdl;
+};
+
+struct MoeGemvLaunch {
+  MoePairs pairs;
+  const int8_t *q;          // [pairs, ldq]
+  int64_t ldq;
+  const int8_t *w;          // [E_total, N, k_pad]
+  int N, k_pad;
+  const int16_t *quant_m;   // [E_total, N]
+  int trunc, qmax;
+  const float *out_step;    // [E_total, N]
+  const float *ratio;       // [pairs] (dyntok unpack) or null
+  int out_f32, out_i16;     // F32 (unpack) or QUANT int16 / int8
+  void *y;                  // [pairs, N]
+  bool pdl;
+};
+
+struct MoeCombineLaunch {
+  MoePairs pairs;
+  const void *yq;           // [pairs, H] int16 or int8
+  int in_i16;
+  int H;
+  const float *out_step;    // [E_total, H]
+  float *out;               // [T, ldo]
+  int64_t ldo;
+  bool pdl;
+};
+
+cudaError_t launch_moe_route(const MoeRouteLaunch &L, cudaStream_t stream);
+cudaError_t launch_moe_act_quant(const MoeActLaunch &L, bool dyn, cudaStream_t stream);
+cudaError_t launch_moe_gemv(const MoeGemvLaunch &L, cudaStream_t stream);
+cudaError_t launch_moe_swiglu(const float *gu, int I, int pairs, float *h, bool pdl,
+                              cudaStream_t stream);
+cudaError_t launch_moe_combine(const MoeCombineLaunch &L, cudaStream_t stream);
+
 // Activation quantisation (pack) of x [T, K] fp32 into q [T, ldq] int8 (+ ratio [T]).
 struct ActQuantLaunch {
   const float *x;

@@ -16,6 +16,9 @@ Sources of truth, all executed here rather than restated:
     (src/LFM3/attribute_int8_error.py:104-122), over hand-picked edge cases.
   * sampler_kat.npz     -- Sampler::sample greedy (oracle/_ref/libref.so) on the vector of
     src/eswin_runtime/tests/test_tokenizer_sampler.cpp:19-31 plus tie cases.
+  * moe_route.npz       -- MoERouter::route (src/eswin_runtime/src/llm/moe_router.cpp:211-260,
+    compiled into oracle/_ref/libref.so) on seeded gate logits (64 experts, top-6): raw
+    softmax weights (norm_topk_prob = false), renormalised weights, and a gate bias.
 """
 from __future__ import annotations
 
@@ -165,12 +168,31 @@ def make_sampler_kat(path: Path) -> None:
     print(f"{path.name}: greedy={greedy.tolist()}")
 
 
+def make_moe_route(path: Path) -> None:
+    rng = np.random.default_rng(31)
+    T, H, E, k = 6, 512, 64, 6
+    hidden = rng.standard_normal((T, H)).astype(np.float32)
+    gate_w = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    bias = (rng.standard_normal(E) * 0.01).astype(np.float32)
+    idx_raw, w_raw = O.ref_moe_route(hidden, gate_w, k)
+    idx_norm, w_norm = O.ref_moe_route(hidden, gate_w, k, norm_topk=True, scaling=2.5)
+    idx_bias, w_bias = O.ref_moe_route(hidden, gate_w, k, bias=bias)
+    np.savez_compressed(path, hidden=hidden, gate_w=gate_w, bias=bias, k=np.int32(k),
+                        idx_raw=idx_raw, w_raw=w_raw, idx_norm=idx_norm, w_norm=w_norm,
+                        idx_bias=idx_bias, w_bias=w_bias)
+    print(f"{path.name}: ids {idx_raw[0].tolist()}")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", default=None, help="generate one fixture family (e.g. moe)")
     args = ap.parse_args()
     ref = Path(args.ref)
     O.build()
+    if args.only == "moe":
+        make_moe_route(HERE / "moe_route.npz")
+        return
     builder = import_builder(ref)
     make_quant_linear(builder, 136, 160, 22, 11, HERE / "quant_linear_n136_k160_t22.npz")
     make_quant_linear(builder, 520, 96, 23, 12, HERE / "quant_linear_n520_k96_t23.npz")
@@ -178,6 +200,7 @@ def main() -> None:
     make_boundary(HERE / "boundary_t5.npz", 5, 192, 64, 22)
     make_requant_kat(HERE / "requant_kat.npz")
     make_sampler_kat(HERE / "sampler_kat.npz")
+    make_moe_route(HERE / "moe_route.npz")
 
 
 if __name__ == "__main__":
