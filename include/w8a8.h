@@ -95,7 +95,7 @@ typedef enum {
  * ------------------------------------------------------------------------------------- */
 typedef struct w8a8_ctx w8a8_ctx;
 
-/* Creates a context on CUDA device `device` (makes it current on the calling thread). */
+/* Creates a context on CUDA device `device`; the calling thread's current device is left as it was. */
 w8a8_status w8a8_ctx_create(int device, w8a8_ctx **out_ctx);
 void        w8a8_ctx_destroy(w8a8_ctx *ctx);
 /* Number of SMs of the context's device. */

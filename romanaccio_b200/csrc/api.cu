@@ -320,7 +320,9 @@ w8a8_status w8a8_ctx_create(int device, w8a8_ctx **out_ctx) {
     return fail(W8A8_ERR_NOT_INITIALIZED, "no CUDA device: %s", cudaGetErrorString(e));
   if (device < 0 || device >= ndev)
     return fail(W8A8_ERR_INVALID_ARG, "device %d out of range [0, %d)", device, ndev);
-  W8A8_CUDA(cudaSetDevice(device));
+  // The caller's current device is restored on return: every call on this context's objects
+  // selects the device itself.
+  DeviceGuard guard(device);
   cudaDeviceProp prop;
   W8A8_CUDA(cudaGetDeviceProperties(&prop, device));
   if (prop.major != 10 || prop.minor != 0)

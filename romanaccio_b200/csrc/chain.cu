@@ -722,23 +722,17 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
 }  // namespace
 
 cudaError_t configure_chain(const ChainPlan &plan) {
-  // Opt every instantiation in once to the largest dynamic shared memory the device allows.
-  static bool done[4] = {false, false, false, false};
-  const int slot = plan.tt == 1 ? 0 : plan.tt == 2 ? 1 : plan.tt == 4 ? 2 : 3;
-  if (done[slot]) return cudaSuccess;
-  void (*kern)(ChainArgs) = slot == 0 ? chain_kernel<1> : slot == 1 ? chain_kernel<2>
-                          : slot == 2 ? chain_kernel<4> : chain_kernel<8>;
-  int dev = 0, optin = 0;
-  cudaFuncAttributes fa;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kern);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             optin - static_cast<int>(fa.sharedSizeBytes));
+  // Opt the instantiation in (once per device) to the largest dynamic shared memory allowed.
+  int limit = 0;
+  cudaError_t e;
+  switch (plan.tt) {
+    case 1: e = opt_in_dyn_smem<chain_kernel<1>>(&limit); break;
+    case 2: e = opt_in_dyn_smem<chain_kernel<2>>(&limit); break;
+    case 4: e = opt_in_dyn_smem<chain_kernel<4>>(&limit); break;
+    default: e = opt_in_dyn_smem<chain_kernel<8>>(&limit); break;
+  }
   if (e != cudaSuccess) return e;
-  if (plan.smem > static_cast<size_t>(optin) - fa.sharedSizeBytes) return cudaErrorInvalidValue;
-  done[slot] = true;
+  if (plan.smem > static_cast<size_t>(limit)) return cudaErrorInvalidValue;
   return cudaSuccess;
 }
 

@@ -596,13 +596,10 @@ cudaError_t launch_tc(const TcLaunch &L, const TcPlan &p, cudaStream_t stream) {
     set_last_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad operand)");
     return cudaErrorInvalidValue;
   }
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_w8a8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    kMaxDynSmem - 1024);
-  });
+  int limit = 0;
+  cudaError_t attr_err = opt_in_dyn_smem<gemm_w8a8_tc_kernel>(&limit);
   if (attr_err != cudaSuccess) return attr_err;
+  if (p.smem > static_cast<size_t>(limit)) return cudaErrorInvalidValue;
   TcArgs a = {};
   a.N = L.N;
   a.T = L.T;

@@ -372,21 +372,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
 template <int TT, int RPW, bool TOPK>
 cudaError_t launch_one(const GemvArgs &args, const GemvPlan &plan, cudaStream_t stream, bool pdl) {
   auto kern = gemv_w8a8_kernel<TT, RPW, TOPK>;
-  // Opt in once to the largest dynamic shared memory the device allows next to this kernel's
-  // static shared memory.
-  static int max_dyn = -1;
-  if (max_dyn < 0) {
-    int dev = 0, optin = 0;
-    cudaFuncAttributes fa;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kern);
-    if (e != cudaSuccess) return e;
-    const int limit = optin - static_cast<int>(fa.sharedSizeBytes);
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
-    if (e != cudaSuccess) return e;
-    max_dyn = limit;
-  }
+  int max_dyn = 0;
+  cudaError_t e = opt_in_dyn_smem<gemv_w8a8_kernel<TT, RPW, TOPK>>(&max_dyn);
+  if (e != cudaSuccess) return e;
   if (plan.smem > static_cast<size_t>(max_dyn)) return cudaErrorInvalidValue;
   return launch_ex(kern, dim3(plan.grid), dim3(kThreads), plan.smem, stream, pdl, args);
 }

@@ -4,6 +4,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
+#include <mutex>
 #include <utility>
 
 namespace w8a8 {
@@ -290,6 +291,34 @@ cudaError_t launch_chain(const ChainOp *ops_dev, int n_ops, int T, const ChainPl
 
 // Records `msg` as the calling thread's w8a8_last_error() text (defined in api.cu).
 void set_last_error(const char *msg);
+
+// Opts kernel Kern in, once per device (function attributes belong to a device's context), to
+// the largest dynamic shared memory the device allows next to the kernel's static shared
+// memory; *limit receives that size for the current device.
+template <auto Kern>
+cudaError_t opt_in_dyn_smem(int *limit) {
+  constexpr int kDevices = 64;
+  static int cached[kDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == 0) {
+    int optin = 0;
+    cudaFuncAttributes fa;
+    e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, Kern);
+    if (e != cudaSuccess) return e;
+    const int lim = optin - static_cast<int>(fa.sharedSizeBytes);
+    e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if (e != cudaSuccess) return e;
+    cached[dev] = lim;
+  }
+  *limit = cached[dev];
+  return cudaSuccess;
+}
 
 // Launch helper: cudaLaunchKernelEx with the programmatic-stream-serialisation attribute.
 template <typename... KArgs, typename... Args>

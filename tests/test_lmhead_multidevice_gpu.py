@@ -73,7 +73,10 @@ def test_graph_capture(ctx):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 or more GPUs")
 def test_shards_on_several_devices():
     n = min(torch.cuda.device_count(), 8)
+    before = torch.cuda.current_device()
     ctxs = [rb.Context(d) for d in range(n)]
+    # Creating contexts on other devices leaves the caller's current device alone.
+    assert torch.cuda.current_device() == before
     V, K, T, k = 151936, 1536, 2, 40
     wq, w_step = lm_params(V, K, seed=11)
     in_step = 0.031
