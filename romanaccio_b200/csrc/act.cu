@@ -9,6 +9,7 @@
 //                     rule of src/eswin_runtime/src/nlp/sampler.cpp:93-103
 #include "common.cuh"
 #include "kernels.h"
+#include "topk.cuh"
 
 namespace w8a8 {
 
@@ -149,26 +150,44 @@ struct MergeArgs {
   int32_t *argmax;
 };
 
-__global__ void __launch_bounds__(256) topk_merge_kernel(const MergeArgs a) {
+constexpr int kMergeWarps = 8;
+
+// One CTA per token: the candidates' order keys into shared memory, then the warp-list top-k
+// (topk.cuh) of all of them.
+__global__ void __launch_bounds__(kMergeWarps * 32) topk_merge_kernel(const MergeArgs a) {
   extern __shared__ __align__(16) uint64_t keys[];
+  uint64_t *stage = keys + a.P;  // kMergeWarps * 64 keys
   pdl_launch_dependents();
   pdl_wait();
   const int t = blockIdx.x;
   const int n = a.n_lists * a.k_in;
-  for (int i = threadIdx.x; i < a.P; i += blockDim.x) {
-    uint64_t key = 0ull;
-    if (i < n) {
-      const int64_t off = t * a.token_stride + (i / a.k_in) * a.list_stride + (i % a.k_in);
-      key = topk_key(a.in_val[off], static_cast<uint32_t>(a.in_idx[off]));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int64_t off = t * a.token_stride + (i / a.k_in) * a.list_stride + (i % a.k_in);
+    keys[i] = topk_key(a.in_val[off], static_cast<uint32_t>(a.in_idx[off]));
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto sync = [] { __syncthreads(); };
+  uint64_t v[2];
+  if (a.k_out > 32) {
+    cta_top_keys<2, kMergeWarps, false>(keys, n, stage, warp, lane, sync, v);
+  } else {
+    uint64_t v1[1];
+    cta_top_keys<1, kMergeWarps, false>(keys, n, stage, warp, lane, sync, v1);
+    v[0] = v1[0];
+    v[1] = 0ull;
+  }
+  if (warp == 0) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int e = lane + 32 * j;
+      if (e < a.k_out) {
+        a.out_val[t * a.k_out + e] = topk_key_value(v[j]);
+        a.out_idx[t * a.k_out + e] = topk_key_id(v[j]);
+      }
     }
-    keys[i] = key;
+    if (a.argmax && lane == 0) a.argmax[t] = topk_key_id(v[0]);
   }
-  bitonic_sort_desc(keys, a.P);
-  for (int j = threadIdx.x; j < a.k_out; j += blockDim.x) {
-    a.out_val[t * a.k_out + j] = topk_key_value(keys[j]);
-    a.out_idx[t * a.k_out + j] = topk_key_id(keys[j]);
-  }
-  if (a.argmax && threadIdx.x == 0) a.argmax[t] = topk_key_id(keys[0]);
 }
 
 }  // namespace
@@ -202,11 +221,12 @@ cudaError_t launch_unpack(const UnpackLaunch &L, cudaStream_t st) {
 }
 
 cudaError_t launch_topk_merge(const MergeLaunch &L, cudaStream_t st) {
-  int P = 1;
-  while (P < L.n_lists * L.k_in) P <<= 1;
+  // keys, rounded up to an even count, then the warp lists' staging area
+  const int P = (L.n_lists * L.k_in + 1) & ~1;
   MergeArgs a{L.in_val, L.in_idx, L.n_lists, L.k_in, L.k_out, P, L.list_stride, L.token_stride,
               L.out_val, L.out_idx, L.argmax};
-  return launch_ex(topk_merge_kernel, dim3(L.T), dim3(256), static_cast<size_t>(P) * 8, st, L.pdl, a);
+  const size_t smem = (static_cast<size_t>(P) + kMergeWarps * 64) * 8;
+  return launch_ex(topk_merge_kernel, dim3(L.T), dim3(kMergeWarps * 32), smem, st, L.pdl, a);
 }
 
 }  // namespace w8a8

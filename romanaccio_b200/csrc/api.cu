@@ -448,7 +448,7 @@ w8a8_status w8a8_linear_create(w8a8_ctx *ctx, const w8a8_linear_desc *d, w8a8_li
   for (int T = 1; T <= 8; ++T) {
     GemvPlan p;
     if (plan_gemv(T, l->N, l->k_pad, true, std::min(64, l->N), ctx->sm_count, &p))
-      max_keys = std::max(max_keys, static_cast<size_t>(T) * p.grid * 64);
+      max_keys = std::max(max_keys, static_cast<size_t>(T) * p.grid * 65);
   }
   l->lists_keys = std::max<size_t>(max_keys, 64);
   TRY(dev_alloc(&l->lists, l->lists_keys, &l->device_bytes));
@@ -623,7 +623,7 @@ w8a8_status w8a8_linear_forward_topk(w8a8_linear *l, const float *x, int64_t ldx
     GemvPlan plan;
     if (!plan_gemv(tg, l->N, l->k_pad, true, k, l->ctx->sm_count, &plan))
       return fail(W8A8_ERR_NOT_SUPPORTED, "no top-k plan for T=%d N=%d K=%d k=%d", tg, l->N, l->K, k);
-    if (static_cast<size_t>(tg) * plan.grid * k > l->lists_keys)
+    if (static_cast<size_t>(tg) * plan.grid * (k + 1) > l->lists_keys)
       return fail(W8A8_ERR_NOT_SUPPORTED, "top-k scratch too small");
     GemvLaunch L = {};
     L.w = l->w;
@@ -818,7 +818,7 @@ w8a8_status w8a8_chain_create(w8a8_ctx *ctx, const w8a8_chain_step *steps, int32
   if ((st = dev_alloc(&c->ops_dev, n, nullptr)) != W8A8_SUCCESS ||
       (st = dev_alloc(&c->bar, c->clear_bytes / sizeof(unsigned), nullptr)) != W8A8_SUCCESS ||
       (st = dev_alloc(&c->tk_counter, 1, nullptr)) != W8A8_SUCCESS ||
-      (st = dev_alloc(&c->lists, static_cast<size_t>(T) * plan.grid * std::max(topk_k, 1), nullptr)) !=
+      (st = dev_alloc(&c->lists, static_cast<size_t>(T) * plan.grid * (std::max(topk_k, 1) + 1), nullptr)) !=
           W8A8_SUCCESS) {
     chain_free(c);
     return st;

@@ -14,11 +14,11 @@
 // per step: wait at a grid barrier when the step reads an earlier step's output, quantise the
 // step's fp32 input into shared memory (dyntok amax / static step, the reference's
 // pack_npu_input_int8[_dyntok] arithmetic), run dp4a over the landed slabs, and apply the
-// requant / unpack epilogue (or keep LM-head logits on chip for the per-CTA top-k and the
-// last-CTA merge).  The grid barrier is a per-step arrival counter (release: fence + atomic
+// requant / unpack epilogue (or keep LM-head logits on chip for the grid top-k of topk.cuh).  The grid barrier is a per-step arrival counter (release: fence + atomic
 // add; acquire: ld.acquire spin, bounded by 2 s of %globaltimer).
 #include "common.cuh"
 #include "kernels.h"
+#include "topk.cuh"
 
 #include <algorithm>
 
@@ -36,8 +36,8 @@ struct ChainArgs {
   int n_ops;
   int T;
   unsigned *bar;      // [n_ops] arrival counters, zero at launch
-  unsigned *tk_counter;
-  uint64_t *lists;
+  unsigned *tk_counter;  // top-k arrival counter (zero between launches)
+  uint64_t *lists;       // [T][grid * (k + 1)] top-k lists, then heads
   int *err;
   int ns;
   uint32_t stage_bytes;
@@ -59,27 +59,6 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
 __device__ __forceinline__ void split_range(int total, int parts, int idx, int &b, int &e) {
   b = static_cast<int>((static_cast<long long>(total) * idx) / parts);
   e = static_cast<int>((static_cast<long long>(total) * (idx + 1)) / parts);
-}
-
-// Descending bitonic sort of n (power of two) keys by the consumer threads only.
-__device__ void consumer_bitonic_desc(uint64_t *s, int n, int tid) {
-  consumer_sync();
-  for (int k = 2; k <= n; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < n; i += kCT) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint64_t a = s[i], b = s[ixj];
-          const bool desc = (i & k) == 0;
-          if (desc ? (a < b) : (a > b)) {
-            s[i] = b;
-            s[ixj] = a;
-          }
-        }
-      }
-      consumer_sync();
-    }
-  }
 }
 
 // Quantises the step's fp32 input [T, K] into xq [TT][kpad_max] (zero past K) and the per-token
@@ -413,118 +392,28 @@ __device__ void consume_dispatch(const ChainOp &op, const ChainArgs &a, int tb, 
   }
 }
 
-// Per-CTA top-k of the LM-head step, then the merge by the last CTA to finish.
-template <int TT>
-__device__ void topk_finish(const ChainOp &op, const ChainArgs &a, int tb, int te, uint64_t *cand,
-                            uint64_t *merge_buf, int merge_cap, int tid) {
+// The LM-head step's grid top-k (topk.cuh): every CTA writes its sorted top-k list per token,
+// and the last CTA to arrive selects the shard's top-k.  Consumer warps only; the drained weight
+// ring holds the warps' staged lists and the gathered candidates.
+template <int R>
+__device__ void topk_finish(const ChainOp &op, const ChainArgs &a, int tb, int te, const uint64_t *cand,
+                            uint64_t *ring, int tid) {
   __shared__ int s_last;
-  __shared__ int s_count;
-  __shared__ unsigned long long s_red[kCW];
-  __shared__ int s_red_g[kCW];
-  __shared__ unsigned long long s_tau;
-  const int G = gridDim.x;
+  __shared__ int s_n;
   const int k = op.tk.k;
-  const int rb = op.rb;
-  const int rows_here = te > tb ? min((te - tb) * rb, op.N - tb * rb) : 0;
-  int P = 1;
-  while (P < rows_here) P <<= 1;
-  for (int t = 0; t < a.T; ++t) {
-    uint64_t *ct = cand + t * a.cand_cap;
-    if (rows_here > 0) consumer_bitonic_desc(ct, P, tid);
-    for (int j = tid; j < k; j += kCT)
-      a.lists[(static_cast<size_t>(t) * G + blockIdx.x) * k + j] =
-          (rows_here > 0 && j < P) ? ct[j] : 0ull;
-  }
-  __threadfence();
-  consumer_sync();
-  if (tid == 0) s_last = atomicAdd(a.tk_counter, 1u) == static_cast<unsigned>(G - 1);
-  consumer_sync();
-  if (!s_last) return;
-  __threadfence();
-  const int lane = tid & 31, warp = tid >> 5;
-  for (int t = 0; t < a.T; ++t) {
-    const unsigned long long *lists =
-        reinterpret_cast<const unsigned long long *>(a.lists) + static_cast<size_t>(t) * G * k;
-    uint64_t m = 0;
-    for (int g = tid; g < G; g += kCT) {
-      const uint64_t v = __ldcg(lists + static_cast<size_t>(g) * k + (k - 1));
-      m = v > m ? v : m;
-    }
-    m = warp_max_u64(m);
-    if (lane == 0) s_red[warp] = m;
-    if (tid == 0) s_count = 0;
-    consumer_sync();
-    if (tid == 0) {
-      uint64_t mm = 0;
-      for (int w = 0; w < kCW; ++w) mm = s_red[w] > mm ? s_red[w] : mm;
-      s_tau = mm < 1 ? 1 : mm;
-    }
-    consumer_sync();
-    const uint64_t tau = s_tau;
-    // every key >= tau, read as one flat array with 4 independent loads per thread in flight
-    const int total = G * k;
-    for (int i0 = tid; i0 < total; i0 += 4 * kCT) {
-      uint64_t v[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = i0 + u * kCT;
-        v[u] = i < total ? __ldcg(lists + i) : 0ull;
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (v[u] >= tau) {
-          const int pos = atomicAdd(&s_count, 1);
-          if (pos < merge_cap) merge_buf[pos] = v[u];
-        }
-      }
-    }
-    consumer_sync();
-    const int C = s_count;
-    if (C <= merge_cap) {
-      int P2 = 1;
-      while (P2 < C) P2 <<= 1;
-      for (int i = C + tid; i < P2; i += kCT) merge_buf[i] = 0;
-      consumer_bitonic_desc(merge_buf, P2, tid);
-      for (int j = tid; j < k; j += kCT) {
-        op.tk.val[t * k + j] = topk_key_value(merge_buf[j]);
-        op.tk.idx[t * k + j] = topk_key_id(merge_buf[j]);
-      }
-    } else {
-      // many keys tie at the threshold: k rounds of a tournament over the list heads
-      int *heads = reinterpret_cast<int *>(merge_buf);
-      for (int g = tid; g < G; g += kCT) heads[g] = 0;
-      consumer_sync();
-      for (int j = 0; j < k; ++j) {
-        uint64_t best = 0;
-        int best_g = -1;
-        for (int g = tid; g < G; g += kCT) {
-          const int h = heads[g];
-          const uint64_t v = h < k ? __ldcg(lists + static_cast<size_t>(g) * k + h) : 0ull;
-          if (v > best) { best = v; best_g = g; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const uint64_t ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
-          const int og = __shfl_xor_sync(0xFFFFFFFFu, best_g, o);
-          if (ov > best) { best = ov; best_g = og; }
-        }
-        if (lane == 0) { s_red[warp] = best; s_red_g[warp] = best_g; }
-        consumer_sync();
-        if (tid == 0) {
-          uint64_t bb = 0;
-          int bg = -1;
-          for (int w = 0; w < kCW; ++w)
-            if (s_red[w] > bb) { bb = s_red[w]; bg = s_red_g[w]; }
-          op.tk.val[t * k + j] = topk_key_value(bb);
-          op.tk.idx[t * k + j] = topk_key_id(bb);
-          if (bg >= 0) heads[bg] += 1;
-        }
-        consumer_sync();
-      }
-    }
-    consumer_sync();
-  }
-  if (tid == 0) *a.tk_counter = 0u;
+  const int rows_here = te > tb ? min((te - tb) * op.rb, op.N - tb * op.rb) : 0;
+  const int warp = tid >> 5, lane = tid & 31;
+  const GridTopkState st{a.tk_counter, a.lists};
+  uint64_t *stage = ring;
+  uint64_t *gather = ring + kCW * 64;
+  auto sync = [] { consumer_sync(); };
+  for (int t = 0; t < a.T; ++t)
+    grid_topk_offer<R, kCW>(cand + t * a.cand_cap, rows_here, k, t, st, stage, warp, lane, sync);
+  if (!grid_topk_arrive(st, tid, &s_last, sync)) return;
+  for (int t = 0; t < a.T; ++t)
+    grid_topk_select<R, kCW>(k, t, st, op.tk.val, op.tk.idx, stage, gather, &s_n, warp, lane,
+                             sync);
+  if (tid == 0) *st.arrive = 0u;
 }
 
 template <int TT>
@@ -693,9 +582,11 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
       if (op.topk) {
         consume_dispatch<TT, true>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, ep, tid, ok, tr);
         consumer_sync();
-        int cap = 1;
-        while (static_cast<size_t>(cap) * 2 * 8 <= a.ring_bytes) cap <<= 1;
-        topk_finish<TT>(op, a, tb, te, cand, reinterpret_cast<uint64_t *>(ring), cap, tid);
+        uint64_t *ring64 = reinterpret_cast<uint64_t *>(ring);
+        if (op.tk.k > 32)
+          topk_finish<2>(op, a, tb, te, cand, ring64, tid);
+        else
+          topk_finish<1>(op, a, tb, te, cand, ring64, tid);
       } else {
         consume_dispatch<TT, false>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, ep, tid, ok, tr);
       }
@@ -795,6 +686,10 @@ bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, Chain
   if (fixed + 2 * stage > budget) return false;
   p.ns = static_cast<int>(std::min<size_t>(kMaxStages, (budget - fixed) / stage));
   p.ring_bytes = static_cast<uint32_t>(p.ns * stage);
+  // the top-k step reuses the drained ring for its staged lists and gathered candidates
+  bool any_topk = false;
+  for (int s = 0; s < n_ops; ++s) any_topk = any_topk || ops[s].topk;
+  if (any_topk && p.ring_bytes < (kCW * 64 + kTopkGatherKeys) * 8) return false;
   p.smem = p.ring_bytes + fixed;
   *plan = p;
   return true;

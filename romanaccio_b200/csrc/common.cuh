@@ -183,144 +183,6 @@ __device__ __forceinline__ int32_t topk_key_id(uint64_t key) {
   return static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(key));
 }
 
-// In-place descending bitonic sort of n (power of two) keys in shared memory by all threads
-// of the block.  Ends with a __syncthreads().
-__device__ __forceinline__ void bitonic_sort_desc(uint64_t *s, int n) {
-  __syncthreads();
-  for (int k = 2; k <= n; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint64_t a = s[i];
-          const uint64_t b = s[ixj];
-          const bool desc = (i & k) == 0;
-          if (desc ? (a < b) : (a > b)) {
-            s[i] = b;
-            s[ixj] = a;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-}
-
-// Descending bitonic sort of n (power of two) keys by NT threads (tid < NT) with sync() a barrier
-// over exactly those threads.
-template <int NT, typename Sync>
-__device__ __forceinline__ void block_bitonic_desc(uint64_t *s, int n, int tid, Sync sync) {
-  for (int k = 2; k <= n; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < n; i += NT) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint64_t a = s[i], b = s[ixj];
-          const bool desc = (i & k) == 0;
-          if (desc ? (a < b) : (a > b)) {
-            s[i] = b;
-            s[ixj] = a;
-          }
-        }
-      }
-      sync();
-    }
-  }
-}
-
-struct TopkScratch {
-  int hist[256];
-  uint64_t sel[64];
-  uint64_t prefix, mask;
-  int remaining, count, eq;
-};
-
-// The k (<= 64) largest of n 64-bit keys in shared memory, in descending order, into out[0..k)
-// (key 0 past n).  Radix selection of the k-th largest key, 8 bits per pass from the top (each
-// pass: a 256-bin histogram of the keys that match the digits chosen so far, then one warp finds
-// the bin holding the k-th key), then one compaction of the keys above it and a bitonic sort of
-// at most 64 keys: O(8 n / NT) work per thread instead of the O(n log^2 n) of a full sort.
-// NT threads take part (tid < NT, NT >= 32); sync() is a barrier over exactly them; warp 0 of
-// them scans the histogram.
-template <int NT, typename Sync>
-__device__ void block_topk(const uint64_t *keys, int n, int k, uint64_t *out, TopkScratch *sc,
-                           int tid, Sync sync) {
-  const int kk = n < k ? n : k;
-  if (tid == 0) {
-    sc->prefix = 0;
-    sc->mask = 0;
-    sc->remaining = kk;
-    sc->count = 0;
-    sc->eq = 0;
-  }
-  sync();
-  const bool all = n <= k;
-  if (!all) {
-    for (int shift = 56; shift >= 0; shift -= 8) {
-      for (int b = tid; b < 256; b += NT) sc->hist[b] = 0;
-      const uint64_t prefix = sc->prefix, mask = sc->mask;
-      sync();
-      for (int i = tid; i < n; i += NT) {
-        const uint64_t key = keys[i];
-        if ((key & mask) == prefix) atomicAdd(&sc->hist[(key >> shift) & 255], 1);
-      }
-      sync();
-      if (tid < 32) {
-        // lane l owns bins 255 - 8l .. 248 - 8l (largest first)
-        int c[8], tot = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          c[j] = sc->hist[255 - (tid * 8 + j)];
-          tot += c[j];
-        }
-        int incl = tot;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-          if (tid >= o) incl += y;
-        }
-        const int excl = incl - tot;
-        const int rem = sc->remaining;
-        __syncwarp();  // every lane has read `remaining` before the owner lane rewrites it
-        if (excl < rem && rem <= incl) {
-          int above = excl;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            if (above < rem && rem <= above + c[j]) {
-              const uint64_t bin = static_cast<uint64_t>(255 - (tid * 8 + j));
-              sc->remaining = rem - above;
-              sc->prefix = prefix | (bin << shift);
-              sc->mask = mask | (255ull << shift);
-            }
-            above += c[j];
-          }
-        }
-      }
-      sync();
-    }
-  }
-  // prefix is now the k-th largest key itself; `remaining` copies of it belong to the top k.
-  const uint64_t kth = sc->prefix;
-  const int need = sc->remaining;
-  for (int i = tid; i < n; i += NT) {
-    const uint64_t key = keys[i];
-    if (all || key > kth) {
-      sc->sel[atomicAdd(&sc->count, 1)] = key;
-    } else if (key == kth) {
-      const int e = atomicAdd(&sc->eq, 1);
-      if (e < need) sc->sel[kk - need + e] = key;
-    }
-  }
-  sync();
-  int P = 1;
-  while (P < kk) P <<= 1;
-  for (int i = kk + tid; i < P; i += NT) sc->sel[i] = 0ull;
-  sync();
-  block_bitonic_desc<NT>(sc->sel, P, tid, sync);
-  for (int j = tid; j < k; j += NT) out[j] = j < kk ? sc->sel[j] : 0ull;
-  sync();
-}
-
 __device__ __forceinline__ int warp_sum(int v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);

@@ -7,8 +7,9 @@
 // slab plus the matching [T, KC] slab of the int8 activations.  Consumers read 16-byte
 // vectors, accumulate with dp4a into int32 registers, and reduce across the warp with
 // shuffles.  The epilogue applies the reference's SDP requant (QuantM, RNE shift, saturate)
-// and the unpack step (per-channel / per-token dequant), or keeps the logits on chip and
-// selects the per-CTA top-k, which the last CTA to finish merges into the shard's top-k.
+// and the unpack step (per-channel / per-token dequant), or keeps the logits on chip: each CTA
+// writes its sorted top-k (warp bitonic networks, topk.cuh) and the last CTA to finish selects
+// the shard's top-k from the few list prefixes that can hold it.
 //
 // The weight copies of the first NS stages are issued before griddepcontrol.wait, so under
 // programmatic dependent launch the weight stream of this linear overlaps the tail of the
@@ -20,6 +21,7 @@
 // (src/LFM3/lfm3_v2.cpp:2360-2405) + greedy / top-k (src/eswin_runtime/src/nlp/sampler.cpp:93-121).
 #include "common.cuh"
 #include "kernels.h"
+#include "topk.cuh"
 
 #include <algorithm>
 
@@ -40,6 +42,7 @@ struct GemvArgs {
   int64_t ldx;
   int T, N, k_pad, kc, nk, ns, num_tiles, tiles_per_cta, cand_cap;
   uint32_t stage_bytes;
+  uint32_t ring_bytes;  // stage ring (top-k: at least kTopkStageBytes); barriers follow it
   Epilogue ep;
   TopK tk;
   int *err;
@@ -87,99 +90,27 @@ struct BlockSync {
   __device__ void operator()() const { __syncthreads(); }
 };
 
-// Merge of the per-CTA sorted lists of one token (run by the last CTA to finish).
-__device__ void merge_lists(const TopK &tk, int t, int G, uint64_t *buf, int buf_cap_pow2,
-                            TopkScratch *sc) {
-  __shared__ unsigned long long s_red[kConsumerWarps + 1];
-  __shared__ int s_red_g[kConsumerWarps + 1];
-  __shared__ int s_count;
-  __shared__ unsigned long long s_tau;
-  const int k = tk.k;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nwarps = blockDim.x >> 5;
-  const uint64_t *lists = tk.lists + static_cast<size_t>(t) * G * k;
+// Shared memory of the top-k epilogue (in the drained stage ring): the warps' staged lists (64
+// keys each), then the last CTA's gathered candidates.
+constexpr uint32_t kTopkStageBytes = ((kConsumerWarps + 1) * 64 + kTopkGatherKeys) * 8;
 
-  // tau = max over lists of their k-th key: every key of the global top-k is >= tau.
-  uint64_t m = 0;
-  for (int g = tid; g < G; g += blockDim.x) {
-    const uint64_t v = __ldcg(reinterpret_cast<const unsigned long long *>(lists) +
-                              static_cast<size_t>(g) * k + (k - 1));
-    m = v > m ? v : m;
-  }
-  m = warp_max_u64(m);
-  if (lane == 0) s_red[warp] = m;
-  if (tid == 0) s_count = 0;
-  __syncthreads();
-  if (tid == 0) {
-    uint64_t mm = 0;
-    for (int w = 0; w < nwarps; ++w) mm = s_red[w] > mm ? s_red[w] : mm;
-    s_tau = mm < 1 ? 1 : mm;  // key 0 marks an empty slot
-  }
-  __syncthreads();
-  const uint64_t tau = s_tau;
-  // every key >= tau, read as one flat array with 4 independent loads per thread in flight
-  const unsigned long long *flat = reinterpret_cast<const unsigned long long *>(lists);
-  const int total = G * k;
-  for (int i0 = tid; i0 < total; i0 += 4 * kThreads) {
-    uint64_t v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = i0 + u * kThreads;
-      v[u] = i < total ? __ldcg(flat + i) : 0ull;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (v[u] >= tau) {
-        const int pos = atomicAdd(&s_count, 1);
-        if (pos < buf_cap_pow2) buf[pos] = v[u];
-      }
-    }
-  }
-  __syncthreads();
-  const int C = s_count;
-  if (C <= buf_cap_pow2) {
-    block_topk<kThreads>(buf, C, k, buf, sc, tid, BlockSync{});
-    for (int j = tid; j < k; j += blockDim.x) {
-      tk.val[t * k + j] = topk_key_value(buf[j]);
-      tk.idx[t * k + j] = topk_key_id(buf[j]);
-    }
-    __syncthreads();
-    return;
-  }
-  // Rare path (many lists tie at the threshold): k rounds of a tournament over list heads.
-  int *heads = reinterpret_cast<int *>(buf);
-  for (int g = tid; g < G; g += blockDim.x) heads[g] = 0;
-  __syncthreads();
-  for (int j = 0; j < k; ++j) {
-    uint64_t best = 0;
-    int best_g = -1;
-    for (int g = tid; g < G; g += blockDim.x) {
-      const int h = heads[g];
-      const uint64_t v =
-          h < k ? __ldcg(reinterpret_cast<const unsigned long long *>(lists) +
-                         static_cast<size_t>(g) * k + h)
-                : 0ull;
-      if (v > best) { best = v; best_g = g; }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const uint64_t ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
-      const int og = __shfl_xor_sync(0xFFFFFFFFu, best_g, o);
-      if (ov > best) { best = ov; best_g = og; }
-    }
-    if (lane == 0) { s_red[warp] = best; s_red_g[warp] = best_g; }
-    __syncthreads();
-    if (tid == 0) {
-      uint64_t bb = 0;
-      int bg = -1;
-      for (int w = 0; w < nwarps; ++w)
-        if (s_red[w] > bb) { bb = s_red[w]; bg = s_red_g[w]; }
-      tk.val[t * k + j] = topk_key_value(bb);
-      tk.idx[t * k + j] = topk_key_id(bb);
-      if (bg >= 0) heads[bg] += 1;
-    }
-    __syncthreads();
-  }
+// Every token's share of the grid top-k from this CTA's candidate keys, then, in the CTA that
+// arrives last, the selection of the shard's top-k (R = 1 for k <= 32, else 2).
+template <int R>
+__device__ void topk_epilogue(const GemvArgs &a, const GridTopkState &st, const uint64_t *cand,
+                              int rows_here, uint64_t *stage, int *s_last) {
+  constexpr int NW = kConsumerWarps + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = 0; t < a.T; ++t)
+    grid_topk_offer<R, NW>(cand + t * a.cand_cap, rows_here, a.tk.k, t, st, stage, warp, lane,
+                           BlockSync{});
+  if (!grid_topk_arrive(st, threadIdx.x, s_last, BlockSync{})) return;
+  __shared__ int s_n;
+  uint64_t *gather = stage + NW * 64;
+  for (int t = 0; t < a.T; ++t)
+    grid_topk_select<R, NW>(a.tk.k, t, st, a.tk.val, a.tk.idx, stage, gather, &s_n, warp, lane,
+                            BlockSync{});
+  if (threadIdx.x == 0) *st.arrive = 0u;
 }
 
 template <int TT, int RPW, bool TOPK>
@@ -187,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
   constexpr int RB = kConsumerWarps * RPW;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t *stages = smem;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + static_cast<size_t>(a.ns) * a.stage_bytes);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.ring_bytes);
   uint64_t *cand = bars + 2 * kMaxStages;  // TOPK: [TT][cand_cap]
   __shared__ int s_last;
 
@@ -343,30 +274,15 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
   if (!TOPK) return;
 
   // ------------------------------- top-k epilogue -------------------------------
-  __shared__ TopkScratch s_tk;
+  // The drained stage ring (at least kTopkStageBytes) stages the warps' sorted lists.
   __syncthreads();
   const int rows_here = min(ntiles * RB, a.N - tile0 * RB);
-  const int k = a.tk.k;
-  const int G = gridDim.x;
-  // this CTA's k best of its rows, sorted, per token (radix selection, not a full sort)
-  for (int t = 0; t < a.T; ++t)
-    block_topk<kThreads>(cand + t * a.cand_cap, rows_here, k,
-                         a.tk.lists + (static_cast<size_t>(t) * G + blockIdx.x) * k, &s_tk,
-                         threadIdx.x, BlockSync{});
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(a.tk.counter, 1u) == static_cast<unsigned>(G - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  // The whole dynamic shared memory is free now: use it as the merge buffer.
-  const size_t dyn_bytes = static_cast<size_t>(a.ns) * a.stage_bytes + 2 * kMaxStages * 8 +
-                           static_cast<size_t>(TT) * a.cand_cap * 8;
-  int cap = 1;
-  while (static_cast<size_t>(cap) * 2 * 8 <= dyn_bytes) cap <<= 1;
-  uint64_t *buf = reinterpret_cast<uint64_t *>(smem);
-  for (int t = 0; t < a.T; ++t) merge_lists(a.tk, t, G, buf, cap, &s_tk);
-  if (threadIdx.x == 0) *a.tk.counter = 0u;
+  const GridTopkState st{a.tk.counter, a.tk.lists};
+  uint64_t *stage = reinterpret_cast<uint64_t *>(smem);
+  if (a.tk.k > 32)
+    topk_epilogue<2>(a, st, cand, rows_here, stage, &s_last);
+  else
+    topk_epilogue<1>(a, st, cand, rows_here, stage, &s_last);
 }
 
 template <int TT, int RPW, bool TOPK>
@@ -453,7 +369,7 @@ bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan
     const size_t cand_bytes = static_cast<size_t>(p.tt) * cap * 8;
     const size_t budget = 110 * 1024 > cand_bytes + 2 * stage ? 110 * 1024 - cand_bytes : 2 * stage;
     p.ns = static_cast<int>(std::min<size_t>(kMaxStages, std::max<size_t>(2, budget / stage)));
-    p.smem = p.ns * stage + bars + cand_bytes;
+    p.smem = std::max<size_t>(p.ns * stage, kTopkStageBytes) + bars + cand_bytes;
   }
   if (p.smem > kMaxDynSmem) return false;
   *plan = p;
@@ -476,6 +392,8 @@ cudaError_t launch_gemv(const GemvLaunch &L, const GemvPlan &plan, cudaStream_t 
   a.tiles_per_cta = plan.tiles_per_cta;
   a.cand_cap = plan.cand_cap;
   a.stage_bytes = static_cast<uint32_t>((plan.rb + plan.tt) * plan.kc);
+  a.ring_bytes = static_cast<uint32_t>(plan.ns) * a.stage_bytes;
+  if (L.topk) a.ring_bytes = std::max(a.ring_bytes, kTopkStageBytes);
   a.ep = L.ep;
   a.tk = L.tk;
   a.err = L.err;

@@ -41,7 +41,7 @@ struct Epilogue {
 struct TopK {
   int k;                    // 1..64
   int row_offset;           // vocab id of row 0
-  uint64_t *lists;          // scratch [T, grid, k] per-CTA sorted keys
+  uint64_t *lists;          // scratch [T][grid * (k + 1)]: per-CTA sorted lists, then heads
   unsigned *counter;        // scratch arrival counter (0 between launches)
   float *val;               // [T, k]
   int32_t *idx;             // [T, k]

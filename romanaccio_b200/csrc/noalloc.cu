@@ -122,10 +122,11 @@ extern "C" w8a8_status w8a8_lmhead_topk_noalloc(const int8_t *w_dev, int64_t ldw
   GemvPlan plan;
   if (!plan_gemv(T, N, k_pad, true, k, slot.sm_count, &plan))
     return reject(W8A8_ERR_NOT_SUPPORTED, "no top-k plan for T=%lld N=%lld", T, N);
-  if (static_cast<size_t>(T) * plan.grid * k > kListKeys)
+  if (static_cast<size_t>(T) * plan.grid * (k + 1) > kListKeys)
     return reject(W8A8_ERR_INVALID_ARG,
-                  "T * grid * k = %lld candidate keys exceed the scratch maximum of %lld",
-                  static_cast<long long>(T) * plan.grid * k, static_cast<long long>(kListKeys));
+                  "T * grid * (k + 1) = %lld candidate keys exceed the scratch maximum of %lld",
+                  static_cast<long long>(T) * plan.grid * (k + 1),
+                  static_cast<long long>(kListKeys));
 
   int8_t *xq = reinterpret_cast<int8_t *>(slot.scratch);
   float *ratio = reinterpret_cast<float *>(slot.scratch + kXqBytes);
