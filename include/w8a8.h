@@ -187,10 +187,12 @@ typedef enum {
 } w8a8_path;
 #define W8A8_TC_MIN_TOKENS 16
 w8a8_status w8a8_linear_set_path(w8a8_linear *linear, int32_t path);
-/* Diagnostics (no reference counterpart): attaches a device buffer of sm_count x 8 uint64 that
- * each tensor-core launch of this linear fills with per-CTA %globaltimer stamps (entry, setup
- * done, first stage issued, first stage landed, first MMAs committed, first accumulator seen by
- * the epilogue, released, exit).  NULL detaches. */
+/* Diagnostics (no reference counterpart): attaches a device buffer of 2 x sm_count x 8 uint64
+ * that each launch of this linear fills with per-CTA %globaltimer stamps.  Tensor-core launches
+ * (grid <= sm_count): entry, setup done, first stage issued, first stage landed, first MMAs
+ * committed, first accumulator seen by the epilogue, released, exit.  GEMV launches (when their
+ * grid is at most 2 x sm_count): entry, setup done, first stage landed, streaming done, top-k
+ * lists written, arrived, top-k selected (last CTA), exit.  NULL detaches. */
 w8a8_status w8a8_linear_set_trace(w8a8_linear *linear, unsigned long long *trace_dev);
 
 /* ---------------------------------------------------------------------------------------
@@ -231,13 +233,20 @@ w8a8_status w8a8_topk_merge(w8a8_ctx *ctx, const float *in_val_dev, const int32_
  * Shard s holds the contiguous vocab rows [s*V/n, (s+1)*V/n) (floor split; n = 2 gives the
  * reference's halves, dual_die_splitter.py:95-141) on the device of ctxs[s].
  *
- * forward: h_dev lives on the device of ctxs[0].  Every shard quantises h itself (static
- * in_step, the broadcast of fused_emb_norm_broadcast_t1, lfm3_v2.cpp:810-831) reading it over
- * NVLink, runs its top-k GEMV, and stores its k (logit, vocab id) pairs straight into a gather
- * buffer on device 0 (peer stores); device 0 merges them (value desc, id asc).  Streams of the
- * shards are ordered after `stream` and back by events, so the call is asynchronous on
- * `stream` and can be captured in a CUDA graph.  Logits: float(acc) * in_step * w_step[v]
- * (acc_step = in_step * w_step).  Devices other than ctxs[0]'s need peer access to it.
+ * forward: h_dev lives on the device of ctxs[0] ("device 0").  Device 0 quantises h once
+ * (static in_step, the broadcast of fused_emb_norm_broadcast_t1, lfm3_v2.cpp:810-831) and
+ * stores the int8 rows into every shard's staging buffer over NVLink; each shard runs its top-k
+ * GEMV and stores its k (logit, vocab id) pairs into a gather buffer on device 0; device 0
+ * merges them (value desc, id asc).  Shards on other devices synchronise with device 0 through
+ * counters in device memory (no host or cross-device stream dependency): they are launched on
+ * their own streams first, stream their first weight stages at once, and wait (at most 1 s) for
+ * device 0's activations, so device 0's `stream` must reach the forward within 1 s of the call;
+ * a wait that runs out records W8A8_ERR_PEER_TIMEOUT (w8a8_ctx_check) and the head must then be
+ * destroyed.  Forwards of one head are issued on one stream, one at a time.  A head with every
+ * shard on device 0 is ordered on `stream` alone and can be captured in a CUDA graph; one with
+ * shards elsewhere cannot (W8A8_ERR_NOT_SUPPORTED while `stream` is capturing) and takes at most
+ * 8 tokens a forward (max_tokens <= 8).  Logits: float(acc) * in_step * w_step[v]
+ * (acc_step = in_step * w_step).  Shard devices need peer access to and from device 0.
  * ------------------------------------------------------------------------------------- */
 typedef struct w8a8_lmhead w8a8_lmhead;
 

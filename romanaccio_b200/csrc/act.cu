@@ -26,7 +26,25 @@ struct ActArgs {
   int8_t *q;
   int64_t ldq;
   float *ratio;
+  const PublishPeer *peers;
+  int n_peers;
+  unsigned *pub_seq, *pub_arrive;
 };
+
+// Publication of the quantised rows to other devices: every CTA's stores are fenced at system
+// scope before it arrives; the last CTA to arrive bumps the forward counter and stores it into
+// each peer's flag with release semantics (the peer reads the rows after an acquire of it).
+__device__ void publish_arrive(const ActArgs &a) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(a.pub_arrive, 1u) == gridDim.x - 1) {
+    __threadfence_system();
+    const unsigned e = *a.pub_seq + 1u;
+    *a.pub_seq = e;
+    *a.pub_arrive = 0u;
+    for (int p = 0; p < a.n_peers; ++p) st_release_sys(a.peers[p].flag, e);
+  }
+}
 
 // One CTA per token row.  DYN: amax_t = max_c |x*s| (NaN ignored as by `if (a > amax)`),
 // amax_t = max(amax_t, 1e-8), ratio_t = amax_t / max(in_thresh, 1e-8), inv = 127 / amax_t.
@@ -94,14 +112,22 @@ __global__ void __launch_bounds__(kActThreads) act_quant_kernel(const ActArgs a)
         o.w = static_cast<signed char>(round_clamp(v.w * inv, 127.0f));
       }
       q4[c] = o;
+      for (int p = 0; p < a.n_peers; ++p)
+        reinterpret_cast<char4 *>(a.peers[p].q + t * a.ldq)[c] = o;
     }
   } else {
     for (int c = threadIdx.x; c < a.K; c += kActThreads) {
       const float v = SMOOTH ? x[c] * (a.s[c] * inv) : x[c] * inv;
-      q[c] = static_cast<int8_t>(round_clamp(v, 127.0f));
+      const int8_t o = static_cast<int8_t>(round_clamp(v, 127.0f));
+      q[c] = o;
+      for (int p = 0; p < a.n_peers; ++p) a.peers[p].q[t * a.ldq + c] = o;
     }
   }
-  for (int c = a.K + threadIdx.x; c < a.k_fill; c += kActThreads) q[c] = 0;
+  for (int c = a.K + threadIdx.x; c < a.k_fill; c += kActThreads) {
+    q[c] = 0;
+    for (int p = 0; p < a.n_peers; ++p) a.peers[p].q[t * a.ldq + c] = 0;
+  }
+  if (a.pub_seq) publish_arrive(a);
 }
 
 template <bool DYN, bool SMOOTH>
@@ -148,6 +174,10 @@ struct MergeArgs {
   float *out_val;
   int32_t *out_idx;
   int32_t *argmax;
+  const unsigned *done;
+  uint64_t remote_mask;
+  const unsigned *pub_seq;
+  int *err;
 };
 
 constexpr int kMergeWarps = 8;
@@ -159,6 +189,13 @@ __global__ void __launch_bounds__(kMergeWarps * 32) topk_merge_kernel(const Merg
   uint64_t *stage = keys + a.P;  // kMergeWarps * 64 keys
   pdl_launch_dependents();
   pdl_wait();
+  if (a.done) {
+    // lists stored by other devices: wait until each has reached this forward's count
+    const unsigned e = *a.pub_seq;
+    for (int s = threadIdx.x; s < 64; s += blockDim.x)
+      if ((a.remote_mask >> s) & 1ull) wait_flag_reached(a.done + s, e, kWaitLimitNs, a.err, kDevPeerTimeout);
+    __syncthreads();
+  }
   const int t = blockIdx.x;
   const int n = a.n_lists * a.k_in;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -193,7 +230,8 @@ __global__ void __launch_bounds__(kMergeWarps * 32) topk_merge_kernel(const Merg
 }  // namespace
 
 cudaError_t launch_act_quant(const ActQuantLaunch &L, cudaStream_t st) {
-  ActArgs a{L.x, L.ldx, L.K, L.k_fill, L.inv_smooth, L.inv_step, L.safe_thresh, L.q, L.ldq, L.ratio};
+  ActArgs a{L.x,     L.ldx,   L.K,       L.k_fill,  L.inv_smooth, L.inv_step,  L.safe_thresh,
+            L.q,     L.ldq,   L.ratio,   L.peers,   L.n_peers,    L.pub_seq,   L.pub_arrive};
   const bool vec = (L.K % 4 == 0) && (L.ldx % 4 == 0) && (L.ldq % 4 == 0) &&
                    (reinterpret_cast<uintptr_t>(L.x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(L.q) % 4 == 0) &&
@@ -223,8 +261,9 @@ cudaError_t launch_unpack(const UnpackLaunch &L, cudaStream_t st) {
 cudaError_t launch_topk_merge(const MergeLaunch &L, cudaStream_t st) {
   // keys, rounded up to an even count, then the warp lists' staging area
   const int P = (L.n_lists * L.k_in + 1) & ~1;
-  MergeArgs a{L.in_val, L.in_idx, L.n_lists, L.k_in, L.k_out, P, L.list_stride, L.token_stride,
-              L.out_val, L.out_idx, L.argmax};
+  MergeArgs a{L.in_val,  L.in_idx,  L.n_lists, L.k_in,        L.k_out,   P,
+              L.list_stride, L.token_stride, L.out_val, L.out_idx, L.argmax,
+              L.done,    L.remote_mask, L.pub_seq, L.err};
   const size_t smem = (static_cast<size_t>(P) + kMergeWarps * 64) * 8;
   return launch_ex(topk_merge_kernel, dim3(L.T), dim3(kMergeWarps * 32), smem, st, L.pdl, a);
 }

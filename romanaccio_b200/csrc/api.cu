@@ -8,6 +8,7 @@
 // the first tensor-core forward of a linear (its tile-ordered weight copy and split-K scratch).
 #include "../../include/w8a8.h"
 #include "kernels.h"
+#include "linear_internal.h"
 
 #include <cuda_runtime.h>
 
@@ -280,12 +281,95 @@ w8a8_status run_gemv(w8a8_linear *l, const int8_t *xq, int64_t ldx, int T, int a
     L.err = l->ctx->d_err;
     L.sm_count = l->ctx->sm_count;
     L.pdl = pdl;
+    L.trace = plan.grid <= 2 * l->ctx->sm_count ? l->tc_trace : nullptr;
     W8A8_CUDA(launch_gemv(L, plan, st));
   }
   return W8A8_SUCCESS;
 }
 
 }  // namespace
+
+namespace w8a8 {
+
+w8a8_status linear_quant_input(w8a8_linear *l, const float *x, int64_t ldx, int T, int act_mode,
+                               const PublishPeer *peers, int n_peers, unsigned *pub_seq,
+                               unsigned *pub_arrive, cudaStream_t s) {
+  ActQuantLaunch A = {};
+  A.x = x;
+  A.ldx = ldx;
+  A.T = T;
+  A.K = l->K;
+  A.k_fill = l->k_pad;
+  A.inv_smooth = l->inv_smooth;
+  A.act_mode = act_mode;
+  A.inv_step = l->inv_step;
+  A.safe_thresh = l->safe_thresh;
+  A.q = l->xq;
+  A.ldq = l->k_pad;
+  A.ratio = l->ratio;
+  A.pdl = true;
+  A.peers = peers;
+  A.n_peers = n_peers;
+  A.pub_seq = pub_seq;
+  A.pub_arrive = pub_arrive;
+  W8A8_CUDA(launch_act_quant(A, s));
+  return W8A8_SUCCESS;
+}
+
+w8a8_status linear_topk_quantized(w8a8_linear *l, int T, int act_mode, int out_mode, int k,
+                                  int row_offset, float *topk_val, int32_t *topk_idx,
+                                  float *logits, int64_t ldl, const ShardSync &sync, bool pdl,
+                                  cudaStream_t s) {
+  if (sync.seq && T > 8)
+    return fail(W8A8_ERR_INVALID_ARG, "a shard on another device takes at most 8 tokens a forward");
+  for (int t0 = 0; t0 < T; t0 += 8) {
+    const int tg = std::min(8, T - t0);
+    GemvPlan plan;
+    if (!plan_gemv(tg, l->N, l->k_pad, true, k, l->ctx->sm_count, &plan))
+      return fail(W8A8_ERR_NOT_SUPPORTED, "no top-k plan for T=%d N=%d K=%d k=%d", tg, l->N, l->K, k);
+    if (static_cast<size_t>(tg) * plan.grid * (k + 1) > l->lists_keys)
+      return fail(W8A8_ERR_NOT_SUPPORTED, "top-k scratch too small");
+    GemvLaunch L = {};
+    L.w = l->w;
+    L.ldw = l->k_pad;
+    L.x = l->xq + static_cast<size_t>(t0) * l->k_pad;
+    L.ldx = l->k_pad;
+    L.T = tg;
+    L.N = l->N;
+    L.k_pad = l->k_pad;
+    L.ep = make_epilogue(l, out_mode, act_mode, l->ratio + t0, nullptr, 0);
+    L.topk = true;
+    L.tk.k = k;
+    L.tk.row_offset = row_offset;
+    L.tk.lists = l->lists;
+    L.tk.counter = l->counter;
+    L.tk.val = topk_val + static_cast<size_t>(t0) * k;
+    L.tk.idx = topk_idx + static_cast<size_t>(t0) * k;
+    L.tk.logits = logits ? logits + static_cast<size_t>(t0) * ldl : nullptr;
+    L.tk.ldl = ldl;
+    L.err = l->ctx->d_err;
+    L.sm_count = l->ctx->sm_count;
+    L.pdl = pdl;
+    L.trace = plan.grid <= 2 * l->ctx->sm_count ? l->tc_trace : nullptr;
+    L.sync = sync;
+    W8A8_CUDA(launch_gemv(L, plan, s));
+  }
+  return W8A8_SUCCESS;
+}
+
+int8_t *linear_staging(w8a8_linear *l) { return l->xq; }
+
+int linear_staging_ld(const w8a8_linear *l) { return l->k_pad; }
+
+w8a8_status linear_reserve_tokens(w8a8_linear *l, int T) {
+  DeviceGuard g(l->ctx->device);
+  return ensure_tokens(l, T);
+}
+
+int *linear_error_word(w8a8_linear *l) { return l->ctx->d_err; }
+
+}  // namespace w8a8
+
 
 extern "C" {
 
@@ -603,52 +687,10 @@ w8a8_status w8a8_linear_forward_topk(w8a8_linear *l, const float *x, int64_t ldx
   st = ensure_tokens(l, T);
   if (st != W8A8_SUCCESS) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ActQuantLaunch A = {};
-  A.x = x;
-  A.ldx = ldx;
-  A.T = T;
-  A.K = l->K;
-  A.k_fill = l->k_pad;
-  A.inv_smooth = l->inv_smooth;
-  A.act_mode = act_mode;
-  A.inv_step = l->inv_step;
-  A.safe_thresh = l->safe_thresh;
-  A.q = l->xq;
-  A.ldq = l->k_pad;
-  A.ratio = l->ratio;
-  A.pdl = true;
-  W8A8_CUDA(launch_act_quant(A, s));
-  for (int t0 = 0; t0 < T; t0 += 8) {
-    const int tg = std::min(8, T - t0);
-    GemvPlan plan;
-    if (!plan_gemv(tg, l->N, l->k_pad, true, k, l->ctx->sm_count, &plan))
-      return fail(W8A8_ERR_NOT_SUPPORTED, "no top-k plan for T=%d N=%d K=%d k=%d", tg, l->N, l->K, k);
-    if (static_cast<size_t>(tg) * plan.grid * (k + 1) > l->lists_keys)
-      return fail(W8A8_ERR_NOT_SUPPORTED, "top-k scratch too small");
-    GemvLaunch L = {};
-    L.w = l->w;
-    L.ldw = l->k_pad;
-    L.x = l->xq + static_cast<size_t>(t0) * l->k_pad;
-    L.ldx = l->k_pad;
-    L.T = tg;
-    L.N = l->N;
-    L.k_pad = l->k_pad;
-    L.ep = make_epilogue(l, out_mode, act_mode, l->ratio + t0, nullptr, 0);
-    L.topk = true;
-    L.tk.k = k;
-    L.tk.row_offset = row_offset;
-    L.tk.lists = l->lists;
-    L.tk.counter = l->counter;
-    L.tk.val = topk_val + static_cast<size_t>(t0) * k;
-    L.tk.idx = topk_idx + static_cast<size_t>(t0) * k;
-    L.tk.logits = logits ? logits + static_cast<size_t>(t0) * ldl : nullptr;
-    L.tk.ldl = ldl;
-    L.err = l->ctx->d_err;
-    L.sm_count = l->ctx->sm_count;
-    L.pdl = true;
-    W8A8_CUDA(launch_gemv(L, plan, s));
-  }
-  return W8A8_SUCCESS;
+  st = w8a8::linear_quant_input(l, x, ldx, T, act_mode, nullptr, 0, nullptr, nullptr, s);
+  if (st != W8A8_SUCCESS) return st;
+  return w8a8::linear_topk_quantized(l, T, act_mode, out_mode, k, row_offset, topk_val, topk_idx,
+                                     logits, ldl, w8a8::ShardSync{}, true, s);
 }
 
 w8a8_status w8a8_topk_merge(w8a8_ctx *ctx, const float *in_val, const int32_t *in_idx, int32_t T,

@@ -410,9 +410,17 @@ __device__ void topk_finish(const ChainOp &op, const ChainArgs &a, int tb, int t
   for (int t = 0; t < a.T; ++t)
     grid_topk_offer<R, kCW>(cand + t * a.cand_cap, rows_here, k, t, st, stage, warp, lane, sync);
   if (!grid_topk_arrive(st, tid, &s_last, sync)) return;
+  // CTA g owns the tiles split_range(num_tiles, G, g): tile i belongs to
+  // g = ceil((i + 1) * G / num_tiles) - 1
+  const int row_offset = op.tk.row_offset, rb = op.rb, num_tiles = op.num_tiles;
+  const long long G = gridDim.x;
+  auto list_of = [row_offset, rb, num_tiles, G](uint64_t key) {
+    const long long tile = (topk_key_id(key) - row_offset) / rb;
+    return static_cast<int>(((tile + 1) * G + num_tiles - 1) / num_tiles - 1);
+  };
   for (int t = 0; t < a.T; ++t)
     grid_topk_select<R, kCW>(k, t, st, op.tk.val, op.tk.idx, stage, gather, &s_n, warp, lane,
-                             sync);
+                             sync, list_of);
   if (tid == 0) *st.arrive = 0u;
 }
 

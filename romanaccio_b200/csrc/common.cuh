@@ -77,6 +77,40 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Cross-device flags (counters that only grow; compared modulo 2^32)
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders this thread's earlier generic-proxy accesses (an acquire included) before its later
+// bulk copies, which read global memory through the async proxy.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Bounded wait until *flag reaches `target`.  Returns false (and records `code` in *err) after
+// limit_ns of %globaltimer.
+__device__ __forceinline__ bool wait_flag_reached(const unsigned *flag, unsigned target,
+                                                  unsigned long long limit_ns, int *err, int code) {
+  if (static_cast<int>(ld_acquire_sys(flag) - target) >= 0) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (static_cast<int>(ld_acquire_sys(flag) - target) >= 0) return true;
+    if ((i & 255u) == 0 && global_timer_ns() - t0 > limit_ns) {
+      if (err) atomicExch(err, code);
+      return false;
+    }
+  }
+}
+
 // Global -> shared bulk copy completing on an mbarrier (bytes multiple of 16, both addresses
 // 16-byte aligned).  Streamed operands use an evict-first L2 policy.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,

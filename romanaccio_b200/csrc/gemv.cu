@@ -46,7 +46,20 @@ struct GemvArgs {
   Epilogue ep;
   TopK tk;
   int *err;
+  unsigned long long *trace;
+  ShardSync sync;
 };
+
+// A shard on another device than GPU 0 waits at most this long for GPU 0 to store its
+// activations (less than the consumers' 2 s stage wait, so the producer gives up first).
+constexpr unsigned long long kXReadyLimitNs = 1000000000ull;
+
+// Diagnostic timeline of a CTA (only when a trace buffer is attached): 0 entry, 1 setup done,
+// 2 first stage landed (consumer warp 0), 3 streaming done, 4 top-k lists written, 5 arrived,
+// 6 top-k selected (last CTA only), 7 exit.
+__device__ __forceinline__ void stamp(const GemvArgs &a, int i) {
+  if (a.trace && (threadIdx.x & 31) == 0) a.trace[blockIdx.x * 8 + i] = global_timer_ns();
+}
 
 __device__ __forceinline__ void store_output(const Epilogue &ep, int acc, int t, int n) {
   switch (ep.out_mode) {
@@ -98,19 +111,44 @@ constexpr uint32_t kTopkStageBytes = ((kConsumerWarps + 1) * 64 + kTopkGatherKey
 // arrives last, the selection of the shard's top-k (R = 1 for k <= 32, else 2).
 template <int R>
 __device__ void topk_epilogue(const GemvArgs &a, const GridTopkState &st, const uint64_t *cand,
-                              int rows_here, uint64_t *stage, int *s_last) {
+                              int rows_here, int rows_per_cta, uint64_t *stage, int *s_last) {
   constexpr int NW = kConsumerWarps + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int t = 0; t < a.T; ++t)
     grid_topk_offer<R, NW>(cand + t * a.cand_cap, rows_here, a.tk.k, t, st, stage, warp, lane,
                            BlockSync{});
-  if (!grid_topk_arrive(st, threadIdx.x, s_last, BlockSync{})) return;
+  if (threadIdx.x == 0) stamp(a, 4);
+  const bool last = grid_topk_arrive(st, threadIdx.x, s_last, BlockSync{});
+  if (threadIdx.x == 0) stamp(a, 5);
+  if (!last) {
+    if (threadIdx.x == 0) stamp(a, 7);
+    return;
+  }
   __shared__ int s_n;
   uint64_t *gather = stage + NW * 64;
+  // CTA b owns rows [b * rows_per_cta, (b + 1) * rows_per_cta) of the shard
+  const int row_offset = a.tk.row_offset;
+  auto list_of = [row_offset, rows_per_cta](uint64_t key) {
+    return (topk_key_id(key) - row_offset) / rows_per_cta;
+  };
   for (int t = 0; t < a.T; ++t)
     grid_topk_select<R, NW>(a.tk.k, t, st, a.tk.val, a.tk.idx, stage, gather, &s_n, warp, lane,
-                            BlockSync{});
-  if (threadIdx.x == 0) *st.arrive = 0u;
+                            BlockSync{}, list_of);
+  if (a.sync.done) {
+    // Remote LM-head shard: val/idx went to GPU 0; publish them, then count the forward.
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned e = *a.sync.seq + 1u;
+      *a.sync.seq = e;
+      st_release_sys(a.sync.done, e);
+    }
+  }
+  if (threadIdx.x == 0) {
+    *st.arrive = 0u;
+    stamp(a, 6);
+    stamp(a, 7);
+  }
 }
 
 template <int TT, int RPW, bool TOPK>
@@ -128,6 +166,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
   const int tile_end = min(tile0 + a.tiles_per_cta, a.num_tiles);
   const int ntiles = tile_end - tile0;
   const int total = ntiles * a.nk;
+  if (threadIdx.x == 0) stamp(a, 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.ns; ++s) {
@@ -140,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
     for (int i = threadIdx.x; i < TT * a.cand_cap; i += blockDim.x) cand[i] = 0ull;
   }
   __syncthreads();
+  if (threadIdx.x == 0) stamp(a, 1);
 
   if (warp == kConsumerWarps) {
     // ------------------------------- producer warp -------------------------------
@@ -173,6 +213,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
     }
     // Activations (and everything written by the previous kernel) are read only after this.
     pdl_wait();
+    if (a.sync.x_ready) {
+      // Remote LM-head shard: GPU 0 stores this forward's activations into our staging buffer
+      // and then bumps x_ready.  On a timeout the (stale) rows are still copied so the kernel
+      // ends promptly; the error word records the failure.
+      if (lane == 0) {
+        wait_flag_reached(a.sync.x_ready, *a.sync.seq + 1u, kXReadyLimitNs, a.err,
+                          kDevPeerTimeout);
+        fence_proxy_async_global();
+      }
+      __syncwarp();
+    }
     for (int it = 0; it < pre; ++it) {
       int tile, k0, bytes, rows;
       stage_geom(it, tile, k0, bytes, rows);
@@ -212,6 +263,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
       const int slot = it % a.ns;
       const int use = it / a.ns;
       if (ok) ok = mbar_wait_bounded(smem_addr(&bars[slot]), use & 1, a.err, kDevTimeoutFull);
+      if (it == 0 && warp == 0) stamp(a, 2);
       const int kci = it % a.nk;
       const int bytes = min(a.kc, a.k_pad - kci * a.kc);
       const uint8_t *sw = stages + static_cast<size_t>(slot) * a.stage_bytes;
@@ -271,18 +323,28 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
     }
   }
   pdl_launch_dependents();
-  if (!TOPK) return;
+  if (!TOPK) {
+    if (a.trace) {
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        stamp(a, 3);
+        stamp(a, 7);
+      }
+    }
+    return;
+  }
 
   // ------------------------------- top-k epilogue -------------------------------
   // The drained stage ring (at least kTopkStageBytes) stages the warps' sorted lists.
   __syncthreads();
+  if (threadIdx.x == 0) stamp(a, 3);
   const int rows_here = min(ntiles * RB, a.N - tile0 * RB);
   const GridTopkState st{a.tk.counter, a.tk.lists};
   uint64_t *stage = reinterpret_cast<uint64_t *>(smem);
   if (a.tk.k > 32)
-    topk_epilogue<2>(a, st, cand, rows_here, stage, &s_last);
+    topk_epilogue<2>(a, st, cand, rows_here, a.tiles_per_cta * RB, stage, &s_last);
   else
-    topk_epilogue<1>(a, st, cand, rows_here, stage, &s_last);
+    topk_epilogue<1>(a, st, cand, rows_here, a.tiles_per_cta * RB, stage, &s_last);
 }
 
 template <int TT, int RPW, bool TOPK>
@@ -397,6 +459,8 @@ cudaError_t launch_gemv(const GemvLaunch &L, const GemvPlan &plan, cudaStream_t 
   a.ep = L.ep;
   a.tk = L.tk;
   a.err = L.err;
+  a.trace = L.trace;
+  a.sync = L.sync;
   switch (plan.tt) {
     case 1: return dispatch_rpw<1>(a, plan, stream, L.pdl, L.topk);
     case 2: return dispatch_rpw<2>(a, plan, stream, L.pdl, L.topk);

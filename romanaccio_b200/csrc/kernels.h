@@ -49,6 +49,14 @@ struct TopK {
   int64_t ldl;
 };
 
+// Cross-device handshake of an LM-head shard on another device than the merging one (GPU 0).
+// All three are counters of forwards that only grow.
+struct ShardSync {
+  unsigned *seq;            // shard device: forwards this shard completed (last CTA bumps it)
+  const unsigned *x_ready;  // shard device: forwards whose int8 activations GPU 0 stored here
+  unsigned *done;           // GPU 0 (peer pointer): forwards whose candidates this shard stored
+};
+
 struct GemvLaunch {
   const int8_t *w;          // [N, ldw] zero-padded up to k_pad
   int64_t ldw;
@@ -61,6 +69,8 @@ struct GemvLaunch {
   int *err;
   int sm_count;
   bool pdl;
+  unsigned long long *trace;  // optional [grid, 8] %globaltimer stamps (diagnostics)
+  ShardSync sync;             // all null: activations are local and ordered by the stream
 };
 
 // Shape plan of one GEMV launch (filled by plan_gemv; the scratch sizes of the top-k path
@@ -190,6 +200,11 @@ cudaError_t launch_moe_swiglu(const float *gu, int I, int pairs, float *h, bool 
 cudaError_t launch_moe_combine(const MoeCombineLaunch &L, cudaStream_t stream);
 
 // Activation quantisation (pack) of x [T, K] fp32 into q [T, ldq] int8 (+ ratio [T]).
+struct PublishPeer {
+  int8_t *q;       // peer's int8 staging buffer
+  unsigned *flag;  // peer's x_ready counter
+};
+
 struct ActQuantLaunch {
   const float *x;
   int64_t ldx;
@@ -203,6 +218,13 @@ struct ActQuantLaunch {
   int64_t ldq;
   float *ratio;             // [T] (dyntok)
   bool pdl;
+  // Optional publication to LM-head shards on other devices: every quantised row is also
+  // stored into each peer's staging buffer (same ldq), then the last CTA bumps *pub_seq and
+  // stores it into every peer's flag.
+  const PublishPeer *peers;  // device array [n_peers]
+  int n_peers;
+  unsigned *pub_seq;         // this device; null: no publication
+  unsigned *pub_arrive;      // this device, zero between launches
 };
 cudaError_t launch_act_quant(const ActQuantLaunch &L, cudaStream_t stream);
 
@@ -236,6 +258,12 @@ struct MergeLaunch {
   int32_t *out_idx;
   int32_t *argmax;
   bool pdl;
+  // Optional: lists s with bit s of remote_mask are stored by other devices; the merge first
+  // waits (bounded) until done[s] reaches *pub_seq, recording kDevPeerTimeout in *err if not.
+  const unsigned *done;
+  uint64_t remote_mask;
+  const unsigned *pub_seq;
+  int *err;
 };
 cudaError_t launch_topk_merge(const MergeLaunch &L, cudaStream_t stream);
 

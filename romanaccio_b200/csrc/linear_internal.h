@@ -1,0 +1,27 @@
+// Internal stages of a linear's top-k forward, used by the multi-device LM head (lmhead.cu):
+// activation quantisation into the linear's int8 staging buffer (optionally also stored into
+// other devices' staging buffers) and the top-k GEMV over that buffer (optionally with the
+// cross-device handshake of a remote shard).  Defined in api.cu.
+#pragma once
+
+#include "../../include/w8a8.h"
+#include "kernels.h"
+
+namespace w8a8 {
+
+w8a8_status linear_quant_input(w8a8_linear *l, const float *x, int64_t ldx, int T, int act_mode,
+                               const PublishPeer *peers, int n_peers, unsigned *pub_seq,
+                               unsigned *pub_arrive, cudaStream_t s);
+
+w8a8_status linear_topk_quantized(w8a8_linear *l, int T, int act_mode, int out_mode, int k,
+                                  int row_offset, float *topk_val, int32_t *topk_idx,
+                                  float *logits, int64_t ldl, const ShardSync &sync, bool pdl,
+                                  cudaStream_t s);
+
+// The int8 staging buffer ([tokens, ld] bytes) and its row stride; stable once reserved.
+int8_t *linear_staging(w8a8_linear *l);
+int linear_staging_ld(const w8a8_linear *l);
+w8a8_status linear_reserve_tokens(w8a8_linear *l, int T);
+int *linear_error_word(w8a8_linear *l);
+
+}  // namespace w8a8

@@ -4,11 +4,25 @@
 // src/eswin_runtime/src/llm/transformer_session.cpp:538-614, and run_dual_die,
 // src/LFM3/lfm3_v2.cpp:1311-1332, which runs one host thread per die and concatenates the two
 // halves of the logits before Sampler::sample scans the full vocabulary).  Here every shard
-// keeps only its top-k (logit, vocab id) pairs on chip, stores them into a gather buffer on the
-// first device with peer stores over NVLink, and one merge kernel on that device produces the
-// global top-k and argmax.  The host issues everything asynchronously: the shards' streams are
-// forked from and joined back to the caller's stream with events, so a whole forward is a DAG
-// that a CUDA graph can capture.
+// keeps only its top-k (logit, vocab id) pairs on chip and device 0 merges the n lists.
+//
+// Device 0 drives a forward; shards on other devices ("remote" shards) synchronise with it
+// through counters in device memory instead of cross-device stream events:
+//   * the remote shards' GEMVs are launched first, each on its own stream of its own device; a
+//     remote GEMV streams its first weight stages at once (weights do not depend on h) and its
+//     producer waits (bounded) until its x_ready counter reaches the forward's number;
+//   * device 0 quantises h once (static in_step, the broadcast of fused_emb_norm_broadcast_t1,
+//     lfm3_v2.cpp:810-831) and stores the int8 rows into every shard's staging buffer over
+//     NVLink, then bumps every x_ready counter (system-scope release);
+//   * each remote shard's last CTA stores its sorted top-k into device 0's gather buffer (peer
+//     stores), then bumps its done counter on device 0;
+//   * device 0 runs its own shard(s), then the merge kernel, which waits (bounded) for every
+//     done counter before merging.
+// A forward is therefore a handful of asynchronous launches with no host or cross-device
+// stream dependency; the shards on device 0 follow the caller's stream.  Shards that share
+// device 0 need no counters (stream order), and a head whose shards all live on device 0 can be
+// captured in a CUDA graph; one with remote shards cannot (the remote launches are outside the
+// captured stream), and forwards of one head must be issued on one stream, one at a time.
 #include "../../include/w8a8.h"
 
 #include <cuda_runtime.h>
@@ -19,6 +33,7 @@
 #include <vector>
 
 #include "kernels.h"
+#include "linear_internal.h"
 
 struct w8a8_lmhead {
   int n = 0, K = 0, V = 0, max_T = 0, k_max = 0;
@@ -27,10 +42,14 @@ struct w8a8_lmhead {
   std::vector<int> dev;                 // device of each shard
   std::vector<int> lo;                  // first vocab id of each shard
   std::vector<w8a8_linear *> shards;
-  std::vector<cudaStream_t> streams;    // shards 1..n-1 (shard 0 runs on the caller's stream)
-  std::vector<cudaEvent_t> done;        // shards 1..n-1
-  cudaEvent_t h_ready = nullptr;        // on device 0
-  float *cand_val = nullptr;            // device 0: [n][max_T * k_max]
+  std::vector<char> remote;             // shard on another device than shard 0
+  std::vector<cudaStream_t> streams;    // per shard (remote shards only; else null)
+  std::vector<unsigned *> counters;     // per shard s >= 1, on its device: [0] seq, [1] x_ready
+  uint64_t remote_mask = 0;
+  // device 0
+  unsigned *ctr0 = nullptr;             // [0] forwards published, [1] arrival, [2 + s] done[s]
+  w8a8::PublishPeer *peers = nullptr;   // [n - 1]: shards 1..n-1 staging buffers and x_ready
+  float *cand_val = nullptr;            // [n][max_T * k_max]
   int32_t *cand_idx = nullptr;
 };
 
@@ -64,20 +83,41 @@ w8a8_status invalid(const char *msg) {
 void lmhead_free(w8a8_lmhead *lm) {
   if (!lm) return;
   for (w8a8_linear *l : lm->shards) w8a8_linear_destroy(l);
-  for (size_t i = 0; i < lm->streams.size(); ++i) {
-    if (lm->streams[i]) {
-      DeviceScope d(lm->dev[i + 1]);
-      cudaStreamDestroy(lm->streams[i]);
-      if (lm->done[i]) cudaEventDestroy(lm->done[i]);
-    }
+  for (size_t s = 0; s < lm->streams.size(); ++s) {
+    if (!lm->streams[s]) continue;
+    DeviceScope d(lm->dev[s]);
+    cudaStreamDestroy(lm->streams[s]);
+  }
+  for (size_t s = 0; s < lm->counters.size(); ++s) {
+    if (!lm->counters[s]) continue;
+    DeviceScope d(lm->dev[s]);
+    cudaFree(lm->counters[s]);
   }
   if (!lm->dev.empty()) {
     DeviceScope d(lm->dev[0]);
-    if (lm->h_ready) cudaEventDestroy(lm->h_ready);
+    cudaFree(lm->ctr0);
+    cudaFree(lm->peers);
     cudaFree(lm->cand_val);
     cudaFree(lm->cand_idx);
   }
   delete lm;
+}
+
+// Peer access from device `from` to device `to` (idempotent).
+w8a8_status enable_peer(int from, int to) {
+  int can = 0;
+  cudaDeviceCanAccessPeer(&can, from, to);
+  if (!can) {
+    w8a8::set_last_error("a shard device has no peer access to the first device");
+    return W8A8_ERR_NOT_SUPPORTED;
+  }
+  DeviceScope d(from);
+  const cudaError_t e = cudaDeviceEnablePeerAccess(to, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+    return W8A8_SUCCESS;
+  }
+  return cuda_status(e, "cudaDeviceEnablePeerAccess");
 }
 
 }  // namespace
@@ -106,6 +146,15 @@ w8a8_status w8a8_lmhead_create(w8a8_ctx *const *ctxs, int32_t n, int32_t K, int3
   lm->ctxs.assign(ctxs, ctxs + n);
   for (int s = 0; s < n; ++s) lm->dev.push_back(w8a8_ctx_device(ctxs[s]));
   const int dev0 = lm->dev[0];
+  for (int s = 0; s < n; ++s) {
+    const bool r = lm->dev[s] != dev0;
+    lm->remote.push_back(r ? 1 : 0);
+    if (r) lm->remote_mask |= 1ull << s;
+  }
+  if (lm->remote_mask && max_T > 8) {
+    lmhead_free(lm);
+    return invalid("shards on other devices take at most 8 tokens a forward (max_tokens <= 8)");
+  }
 
   // Shard linears: rows [lo, hi) with their acc_step slice; static input quantisation with
   // in_step (in_thresh = 127 * in_step keeps the descriptor consistent).
@@ -128,53 +177,59 @@ w8a8_status w8a8_lmhead_create(w8a8_ctx *const *ctxs, int32_t n, int32_t K, int3
     d.scale.out_step = 1.0f;
     w8a8_linear *l = nullptr;
     w8a8_status st = w8a8_linear_create(ctxs[s], &d, &l);
+    if (st == W8A8_SUCCESS) {
+      lm->shards.push_back(l);
+      // the staging buffers are written by device 0 and must not move afterwards
+      st = w8a8::linear_reserve_tokens(l, max_T);
+    }
     if (st != W8A8_SUCCESS) {
       lmhead_free(lm);
       return st;
     }
-    lm->shards.push_back(l);
   }
-  // Peer access from every other device to device 0 (activations read, candidates stored).
+  // Peer access both ways between device 0 and every remote shard's device: device 0 stores
+  // activations and counters there, the shard stores candidates and its counter on device 0.
   for (int s = 1; s < n; ++s) {
-    if (lm->dev[s] == dev0) continue;
-    int can = 0;
-    cudaDeviceCanAccessPeer(&can, lm->dev[s], dev0);
-    if (!can) {
+    if (!lm->remote[s]) continue;
+    w8a8_status st = enable_peer(lm->dev[s], dev0);
+    if (st == W8A8_SUCCESS) st = enable_peer(dev0, lm->dev[s]);
+    if (st != W8A8_SUCCESS) {
       lmhead_free(lm);
-      w8a8::set_last_error("a shard device has no peer access to the first device");
-      return W8A8_ERR_NOT_SUPPORTED;
-    }
-    DeviceScope d(lm->dev[s]);
-    cudaError_t e = cudaDeviceEnablePeerAccess(dev0, 0);
-    if (e == cudaErrorPeerAccessAlreadyEnabled) {
-      cudaGetLastError();
-    } else if (e != cudaSuccess) {
-      lmhead_free(lm);
-      return cuda_status(e, "cudaDeviceEnablePeerAccess");
+      return st;
     }
   }
+  lm->streams.assign(n, nullptr);
+  lm->counters.assign(n, nullptr);
+  std::vector<w8a8::PublishPeer> table;
   for (int s = 1; s < n; ++s) {
     DeviceScope d(lm->dev[s]);
-    cudaStream_t st = nullptr;
-    cudaEvent_t ev = nullptr;
-    cudaError_t e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-    lm->streams.push_back(st);
-    lm->done.push_back(ev);
+    cudaError_t e = cudaMalloc(&lm->counters[s], 2 * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(lm->counters[s], 0, 2 * sizeof(unsigned));
+    if (e == cudaSuccess && lm->remote[s])
+      e = cudaStreamCreateWithFlags(&lm->streams[s], cudaStreamNonBlocking);
     if (e != cudaSuccess) {
       lmhead_free(lm);
-      return cuda_status(e, "shard stream / event");
+      return cuda_status(e, "shard counters / stream");
     }
+    table.push_back({w8a8::linear_staging(lm->shards[s]), lm->counters[s] + 1});
   }
   {
     DeviceScope d(dev0);
-    cudaError_t e = cudaEventCreateWithFlags(&lm->h_ready, cudaEventDisableTiming);
     const size_t cells = static_cast<size_t>(n) * max_T * k_max;
-    if (e == cudaSuccess) e = cudaMalloc(&lm->cand_val, cells * sizeof(float));
+    cudaError_t e = cudaMalloc(&lm->cand_val, cells * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&lm->cand_idx, cells * sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&lm->ctr0, (2 + n) * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(lm->ctr0, 0, (2 + n) * sizeof(unsigned));
+    if (e == cudaSuccess && !table.empty()) {
+      e = cudaMalloc(&lm->peers, table.size() * sizeof(w8a8::PublishPeer));
+      if (e == cudaSuccess)
+        e = cudaMemcpy(lm->peers, table.data(), table.size() * sizeof(w8a8::PublishPeer),
+                       cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
       lmhead_free(lm);
-      return cuda_status(e, "LM-head gather buffers");
+      return cuda_status(e, "LM-head gather buffers / counters");
     }
   }
   *out = lm;
@@ -188,39 +243,65 @@ w8a8_status w8a8_lmhead_forward(w8a8_lmhead *lm, const float *h, int32_t T, int3
     return invalid("T or k outside [1, max_tokens] / [1, k_max]");
   cudaStream_t s0 = static_cast<cudaStream_t>(stream);
   const int n = lm->n;
+  const int dev0 = lm->dev[0];
+  if (lm->remote_mask) {
+    DeviceScope d(dev0);
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    w8a8_status st = cuda_status(cudaStreamIsCapturing(s0, &cs), "cudaStreamIsCapturing");
+    if (st != W8A8_SUCCESS) return st;
+    if (cs != cudaStreamCaptureStatusNone) {
+      w8a8::set_last_error("an LM head with shards on other devices cannot be graph-captured");
+      return W8A8_ERR_NOT_SUPPORTED;
+    }
+  }
   // Shard s writes its [T, k] block at cand + s * T * k: the merge reads candidate (t, s, j)
   // at t * k + s * (T * k) + j.
   const int64_t block = static_cast<int64_t>(T) * k;
-  if (n > 1) {
-    DeviceScope d(lm->dev[0]);
-    w8a8_status st = cuda_status(cudaEventRecord(lm->h_ready, s0), "cudaEventRecord");
-    if (st != W8A8_SUCCESS) return st;
-  }
+  // 1. remote shards: launched first, they stream weights while waiting for the activations
   for (int s = 1; s < n; ++s) {
+    if (!lm->remote[s]) continue;
     DeviceScope d(lm->dev[s]);
-    cudaStream_t ss = lm->streams[s - 1];
-    w8a8_status st = cuda_status(cudaStreamWaitEvent(ss, lm->h_ready, 0), "cudaStreamWaitEvent");
-    if (st != W8A8_SUCCESS) return st;
-    st = w8a8_linear_forward_topk(lm->shards[s], h, lm->K, T, W8A8_ACT_STATIC, W8A8_OUT_F32_ACC,
-                                  k, lm->lo[s], lm->cand_val + s * block,
-                                  lm->cand_idx + s * block, nullptr, 0, ss);
-    if (st != W8A8_SUCCESS) return st;
-    st = cuda_status(cudaEventRecord(lm->done[s - 1], ss), "cudaEventRecord");
+    w8a8::ShardSync sync;
+    sync.seq = lm->counters[s];
+    sync.x_ready = lm->counters[s] + 1;
+    sync.done = lm->ctr0 + 2 + s;
+    w8a8_status st = w8a8::linear_topk_quantized(
+        lm->shards[s], T, W8A8_ACT_STATIC, W8A8_OUT_F32_ACC, k, lm->lo[s], lm->cand_val + s * block,
+        lm->cand_idx + s * block, nullptr, 0, sync, false, lm->streams[s]);
     if (st != W8A8_SUCCESS) return st;
   }
-  // Shard 0 on the caller's stream, then the merge after every other shard's event (with one
-  // shard the merge only copies its sorted list and writes the argmax).
-  DeviceScope d(lm->dev[0]);
-  w8a8_status st = w8a8_linear_forward_topk(lm->shards[0], h, lm->K, T, W8A8_ACT_STATIC,
-                                            W8A8_OUT_F32_ACC, k, lm->lo[0], lm->cand_val,
-                                            lm->cand_idx, nullptr, 0, s0);
+  // 2. device 0: quantise h into every shard's staging buffer, then its own shards, then merge
+  DeviceScope d(dev0);
+  w8a8_status st = w8a8::linear_quant_input(lm->shards[0], h, lm->K, T, W8A8_ACT_STATIC,
+                                            lm->peers, n - 1, lm->ctr0, lm->ctr0 + 1, s0);
   if (st != W8A8_SUCCESS) return st;
-  for (int s = 1; s < n; ++s) {
-    st = cuda_status(cudaStreamWaitEvent(s0, lm->done[s - 1], 0), "cudaStreamWaitEvent");
+  for (int s = 0; s < n; ++s) {
+    if (lm->remote[s]) continue;
+    st = w8a8::linear_topk_quantized(lm->shards[s], T, W8A8_ACT_STATIC, W8A8_OUT_F32_ACC, k,
+                                     lm->lo[s], lm->cand_val + s * block, lm->cand_idx + s * block,
+                                     nullptr, 0, w8a8::ShardSync{}, true, s0);
     if (st != W8A8_SUCCESS) return st;
   }
-  return w8a8_topk_merge(lm->ctxs[0], lm->cand_val, lm->cand_idx, T, n, k, block, k, k, val, idx,
-                         argmax, s0);
+  w8a8::MergeLaunch L = {};
+  L.in_val = lm->cand_val;
+  L.in_idx = lm->cand_idx;
+  L.T = T;
+  L.n_lists = n;
+  L.k_in = k;
+  L.k_out = k;
+  L.list_stride = block;
+  L.token_stride = k;
+  L.out_val = val;
+  L.out_idx = idx;
+  L.argmax = argmax;
+  L.pdl = true;
+  if (lm->remote_mask) {
+    L.done = lm->ctr0 + 2;
+    L.remote_mask = lm->remote_mask;
+    L.pub_seq = lm->ctr0;
+    L.err = w8a8::linear_error_word(lm->shards[0]);
+  }
+  return cuda_status(w8a8::launch_topk_merge(L, s0), "LM-head merge launch");
 }
 
 void w8a8_lmhead_destroy(w8a8_lmhead *lm) { lmhead_free(lm); }

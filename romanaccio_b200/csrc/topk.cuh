@@ -13,8 +13,9 @@
 //   * the grid protocol: each CTA writes its sorted top-k list and, separately, the list's head
 //     (its largest key).  The last CTA to arrive takes T0 = the k-th largest head: k distinct
 //     keys are >= T0, so every key of the grid's top-k is >= T0, and only the k lists whose
-//     head reaches T0 can hold such keys.  It walks those lists' prefixes >= T0 (on random
-//     logits about k + a few keys in all; never more than k * k) and selects the top-k of them.
+//     head reaches T0 can hold such keys.  One thread per such list walks its prefix >= T0 (on
+//     random logits about k + a few keys in all; never more than k * k) and the top-k of the
+//     gathered keys is the grid's.
 #pragma once
 
 #include "common.cuh"
@@ -90,11 +91,14 @@ __device__ __forceinline__ uint64_t load_key(const uint64_t *p) {
 // The 32R largest of keys[0..n) (0 past n), sorted descending, in warp 0's `out` (other warps'
 // `out` are unspecified) and in stage[0..32R) for every warp after the call.  Warps 0..NW-1 take
 // part and sync() is a barrier over exactly them; `stage` holds NW * 32R keys of shared memory.
+// Only the first ceil(n / 32R) warps (at most NW) hold a chunk and take part in the tree.
 // kCg: the keys were written by other CTAs of the grid (read through L2).
 template <int R, int NW, bool kCg, typename Sync>
 __device__ void cta_top_keys(const uint64_t *keys, int n, uint64_t *stage, int warp, int lane,
                              Sync sync, uint64_t (&out)[R]) {
   constexpr int L = 32 * R;
+  const int chunks = (n + L - 1) / L;
+  const int act = chunks < 1 ? 1 : (chunks < NW ? chunks : NW);
   uint64_t a[R];
   bool first = true;
 #pragma unroll
@@ -115,11 +119,13 @@ __device__ void cta_top_keys(const uint64_t *keys, int n, uint64_t *stage, int w
       warp_merge_desc<R>(a, b, lane);
     }
   }
+  if (warp < act) {
 #pragma unroll
-  for (int j = 0; j < R; ++j) stage[warp * L + lane + 32 * j] = a[j];
+    for (int j = 0; j < R; ++j) stage[warp * L + lane + 32 * j] = a[j];
+  }
   sync();
-  for (int s = 1; s < NW; s <<= 1) {
-    if ((warp & (2 * s - 1)) == 0 && warp + s < NW) {
+  for (int s = 1; s < act; s <<= 1) {
+    if ((warp & (2 * s - 1)) == 0 && warp + s < act) {
       uint64_t b[R];
 #pragma unroll
       for (int j = 0; j < R; ++j) b[j] = stage[(warp + s) * L + lane + 32 * j];
@@ -166,34 +172,59 @@ __device__ bool grid_topk_arrive(const GridTopkState &st, int tid, int *s_flag, 
 
 // Last CTA: token t's top-k into val/idx[t * k ..].  NW * 32 threads (tid < NW * 32) take part;
 // `stage` holds NW * 32R keys and `gather` kTopkGatherKeys keys of shared memory; s_int is one
-// shared int.  Returns after a sync() over the NW warps.
-template <int R, int NW, typename Sync>
+// shared int.  list_of(key) gives the index of the CTA (list) that owns a key's vocab row.
+// Returns after a sync() over the NW warps.
+template <int R, int NW, typename Sync, typename ListOf>
 __device__ void grid_topk_select(int k, int t, const GridTopkState &st, float *val, int32_t *idx,
                                  uint64_t *stage, uint64_t *gather, int *s_int, int warp, int lane,
-                                 Sync sync) {
+                                 Sync sync, ListOf list_of) {
   const int G = gridDim.x;
   const uint64_t *base = st.keys + t * grid_topk_stride(G, k);
   const uint64_t *heads = base + static_cast<size_t>(G) * k;
   uint64_t v[R];
-  // T0 = the k-th largest head (0 when fewer than k lists are non-empty: every list is walked)
+  // the k largest heads; T0 = the k-th (0 when fewer than k lists are non-empty)
   cta_top_keys<R, NW, true>(heads, G, stage, warp, lane, sync, v);
   const uint64_t t0 = stage[k - 1];
   const int tid = warp * 32 + lane;
   if (tid == 0) *s_int = 0;
   sync();
-  for (int g = tid; g < G; g += NW * 32) {
-    if (__ldcg(reinterpret_cast<const unsigned long long *>(heads) + g) < t0) continue;
-    const unsigned long long *list =
-        reinterpret_cast<const unsigned long long *>(base) + static_cast<size_t>(g) * k;
-    for (int j = 0; j < k; ++j) {
-      const uint64_t key = __ldcg(list + j);
-      if (key == 0ull || key < t0) break;
-      gather[atomicAdd(s_int, 1)] = key;
+  // Thread j < k walks the list headed by the j-th largest head: the head itself, then the
+  // entries after it while they reach T0 (four loads in flight per step).
+  if (tid < k) {
+    const uint64_t head = stage[tid];
+    if (head != 0ull) {
+      gather[atomicAdd(s_int, 1)] = head;
+      const unsigned long long *list =
+          reinterpret_cast<const unsigned long long *>(base) + static_cast<size_t>(list_of(head)) * k;
+      for (int j = 1; j < k; j += 4) {
+        uint64_t e[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) e[u] = j + u < k ? __ldcg(list + j + u) : 0ull;
+        bool more = true;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          more = more && e[u] != 0ull && e[u] >= t0;
+          if (more) gather[atomicAdd(s_int, 1)] = e[u];
+        }
+        if (!more) break;
+      }
     }
   }
   sync();
   const int n = *s_int;
-  cta_top_keys<R, NW, false>(gather, n, stage, warp, lane, sync, v);
+  if (n <= 32 * R) {
+    // the usual case (about k + a few candidates): one warp sorts them
+    if (warp == 0) {
+#pragma unroll
+      for (int j = 0; j < R; ++j) {
+        const int i = lane + 32 * j;
+        v[j] = i < n ? gather[i] : 0ull;
+      }
+      warp_sort_desc<R>(v, lane);
+    }
+  } else {
+    cta_top_keys<R, NW, false>(gather, n, stage, warp, lane, sync, v);
+  }
   if (warp == 0) {
 #pragma unroll
     for (int j = 0; j < R; ++j) {

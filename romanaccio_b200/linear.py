@@ -142,8 +142,9 @@ class W8A8Linear:
         return cls(ctx, p.wq, scale, quant_m=p.quant_m, trunc=p.trunc, acc_step=p.acc_step)
 
     def enable_trace(self, sm_count: int, device) -> torch.Tensor:
-        """Per-CTA timeline [sm_count, 8] (int64 %globaltimer ns) of tensor-core launches."""
-        buf = torch.zeros((sm_count, 8), dtype=torch.int64, device=device)
+        """Per-CTA timeline [2 * sm_count, 8] (int64 %globaltimer ns) of every launch (tensor-core
+        launches fill the first sm_count rows)."""
+        buf = torch.zeros((2 * sm_count, 8), dtype=torch.int64, device=device)
         check(self._lib.w8a8_linear_set_trace(self.handle, buf.data_ptr()), "w8a8_linear_set_trace")
         self._trace = buf
         return buf

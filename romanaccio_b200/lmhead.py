@@ -126,11 +126,14 @@ class MultiDeviceLmHead:
 
     Shard s holds vocab rows shard_range(V, n, s) on the device of ctxs[s]; forward(h) with h
     on ctxs[0]'s device returns (top-k values [T, k], top-k vocab ids [T, k], argmax [T]) there.
-    The shards read h and store their candidates over NVLink; one merge kernel finishes.
+    Device 0 stores the quantised h into every shard's staging buffer over NVLink, the shards
+    store their candidates into device 0, and one merge kernel finishes; shards on other devices
+    synchronise through device-memory counters (no stream events), so a head with such shards is
+    not graph-capturable and takes at most 8 tokens a forward.
     """
 
     def __init__(self, ctxs: list[Context], wq: np.ndarray, acc_step: np.ndarray,
-                 in_step: float, max_tokens: int = 64, k_max: int = 64):
+                 in_step: float, max_tokens: int = 8, k_max: int = 64):
         import ctypes as C
         from ._lib import check
         self._lib = ctxs[0]._lib

@@ -43,7 +43,7 @@ def test_shards_on_one_device(ctx, n, V, K, T, k):
 
 
 def test_graph_capture(ctx):
-    """The whole forward (fork to the shard streams, join, merge) is capturable."""
+    """With every shard on device 0 the whole forward is ordered on one stream: capturable."""
     V, K, T, k, n = 65536, 1536, 1, 40, 4
     wq, w_step = lm_params(V, K, seed=5)
     in_step = 0.02
@@ -77,12 +77,54 @@ def test_shards_on_several_devices():
     ctxs = [rb.Context(d) for d in range(n)]
     # Creating contexts on other devices leaves the caller's current device alone.
     assert torch.cuda.current_device() == before
-    V, K, T, k = 151936, 1536, 2, 40
+    V, K, k = 151936, 1536, 40
     wq, w_step = lm_params(V, K, seed=11)
     in_step = 0.031
     acc_step = (in_step * w_step).astype(np.float32)
     lm = rb.MultiDeviceLmHead(ctxs, wq, acc_step, in_step, max_tokens=8, k_max=64)
-    x = synth.activations(T, K, seed=12).numpy()
-    _check(lm, x, wq, in_step, acc_step, k)
+    # consecutive forwards advance the cross-device counters; token counts vary
+    for i, T in enumerate((2, 1, 8, 3, 1)):
+        x = synth.activations(T, K, seed=12 + i).numpy()
+        _check(lm, x, wq, in_step, acc_step, k if i != 3 else 64)
     for c in ctxs:
         c.check()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 or more GPUs")
+def test_mixed_local_and_remote_shards():
+    """Shards 0 and 1 on device 0 (stream-ordered), shards 2 and 3 on device 1 (counters)."""
+    c0, c1 = rb.Context(0), rb.Context(1)
+    V, K, k = 40000, 1024, 40
+    wq, w_step = lm_params(V, K, seed=21)
+    in_step = 0.027
+    acc_step = (in_step * w_step).astype(np.float32)
+    lm = rb.MultiDeviceLmHead([c0, c0, c1, c1], wq, acc_step, in_step, max_tokens=4, k_max=40)
+    for i in range(3):
+        x = synth.activations(1 + i, K, seed=30 + i).numpy()
+        _check(lm, x, wq, in_step, acc_step, k)
+    c0.check()
+    c1.check()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 or more GPUs")
+def test_remote_shards_refuse_graph_capture():
+    c0, c1 = rb.Context(0), rb.Context(1)
+    V, K, T, k = 8192, 512, 1, 16
+    wq, w_step = lm_params(V, K, seed=3)
+    acc_step = (0.02 * w_step).astype(np.float32)
+    lm = rb.MultiDeviceLmHead([c0, c1], wq, acc_step, 0.02, max_tokens=2, k_max=16)
+    x = torch.from_numpy(synth.activations(T, K, seed=4).numpy()).cuda(0)
+    val = torch.empty((T, k), dtype=torch.float32, device="cuda:0")
+    idx = torch.empty((T, k), dtype=torch.int32, device="cuda:0")
+    g = torch.cuda.CUDAGraph()
+    with pytest.raises(RuntimeError, match="graph-captured"):
+        with torch.cuda.graph(g):
+            lm.forward(x, k, val, idx)
+    del g
+    torch.cuda.synchronize()
+    # the head still works outside capture
+    _check(lm, synth.activations(T, K, seed=5).numpy(), wq, 0.02, acc_step, k)
+    c0.check()
+    c1.check()
+    with pytest.raises(RuntimeError, match="max_tokens"):
+        rb.MultiDeviceLmHead([c0, c1], wq, acc_step, 0.02, max_tokens=9, k_max=16)
