@@ -130,6 +130,7 @@ SIGNATURES = {
     "w8a8_lmhead_forward": (C.c_int, [_P, _P, _I32, _I32, _P, _P, _P, _P]),
     "w8a8_lmhead_destroy": (None, [_P]),
     "w8a8_lmhead_shards": (_I32, [_P]),
+    "w8a8_lmhead_set_trace": (C.c_int, [_P, _P, C.POINTER(_P)]),
     "w8a8_moe_create": (C.c_int, [_P, C.POINTER(MoeDesc), C.POINTER(_P)]),
     "w8a8_moe_destroy": (None, [_P]),
     "w8a8_moe_route": (C.c_int, [_P, _P, _I64, _I32, _P, _P, _P]),

@@ -29,6 +29,7 @@ struct ActArgs {
   const PublishPeer *peers;
   int n_peers;
   unsigned *pub_seq, *pub_arrive;
+  unsigned long long *trace;
 };
 
 // Publication of the quantised rows to other devices: every CTA's stores are fenced at system
@@ -42,7 +43,9 @@ __device__ void publish_arrive(const ActArgs &a) {
     const unsigned e = *a.pub_seq + 1u;
     *a.pub_seq = e;
     *a.pub_arrive = 0u;
-    for (int p = 0; p < a.n_peers; ++p) st_release_sys(a.peers[p].flag, e);
+    // (the fence above makes these relaxed stores a release of every CTA's rows)
+    for (int p = 0; p < a.n_peers; ++p) st_relaxed_sys(a.peers[p].flag, e);
+    if (a.trace) a.trace[1] = global_timer_ns();
   }
 }
 
@@ -53,6 +56,7 @@ template <bool DYN, bool SMOOTH, bool VEC>
 __global__ void __launch_bounds__(kActThreads) act_quant_kernel(const ActArgs a) {
   pdl_launch_dependents();
   pdl_wait();
+  if (a.trace && blockIdx.x == 0 && threadIdx.x == 0) a.trace[0] = global_timer_ns();
   const int t = blockIdx.x;
   const float *x = a.x + t * a.ldx;
   int8_t *q = a.q + t * a.ldq;
@@ -178,6 +182,7 @@ struct MergeArgs {
   uint64_t remote_mask;
   const unsigned *pub_seq;
   int *err;
+  unsigned long long *trace;
 };
 
 constexpr int kMergeWarps = 8;
@@ -189,6 +194,8 @@ __global__ void __launch_bounds__(kMergeWarps * 32) topk_merge_kernel(const Merg
   uint64_t *stage = keys + a.P;  // kMergeWarps * 64 keys
   pdl_launch_dependents();
   pdl_wait();
+  const bool tr = a.trace && blockIdx.x == 0 && threadIdx.x == 0;
+  if (tr) a.trace[2] = global_timer_ns();
   if (a.done) {
     // lists stored by other devices: wait until each has reached this forward's count
     const unsigned e = *a.pub_seq;
@@ -196,6 +203,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) topk_merge_kernel(const Merg
       if ((a.remote_mask >> s) & 1ull) wait_flag_reached(a.done + s, e, kWaitLimitNs, a.err, kDevPeerTimeout);
     __syncthreads();
   }
+  if (tr) a.trace[3] = global_timer_ns();
   const int t = blockIdx.x;
   const int n = a.n_lists * a.k_in;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -205,33 +213,26 @@ __global__ void __launch_bounds__(kMergeWarps * 32) topk_merge_kernel(const Merg
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   auto sync = [] { __syncthreads(); };
-  uint64_t v[2];
-  if (a.k_out > 32) {
-    cta_top_keys<2, kMergeWarps, false>(keys, n, stage, warp, lane, sync, v);
-  } else {
-    uint64_t v1[1];
-    cta_top_keys<1, kMergeWarps, false>(keys, n, stage, warp, lane, sync, v1);
-    v[0] = v1[0];
-    v[1] = 0ull;
-  }
+  if (a.k_out > 32)
+    cta_top_keys<2, kMergeWarps>(keys, n, false, stage, warp, lane, sync);
+  else
+    cta_top_keys<1, kMergeWarps>(keys, n, false, stage, warp, lane, sync);
   if (warp == 0) {
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int e = lane + 32 * j;
-      if (e < a.k_out) {
-        a.out_val[t * a.k_out + e] = topk_key_value(v[j]);
-        a.out_idx[t * a.k_out + e] = topk_key_id(v[j]);
-      }
+    for (int e = lane; e < a.k_out; e += 32) {
+      a.out_val[t * a.k_out + e] = topk_key_value(stage[e]);
+      a.out_idx[t * a.k_out + e] = topk_key_id(stage[e]);
     }
-    if (a.argmax && lane == 0) a.argmax[t] = topk_key_id(v[0]);
+    if (a.argmax && lane == 0) a.argmax[t] = topk_key_id(stage[0]);
   }
+  if (tr) a.trace[4] = global_timer_ns();
 }
 
 }  // namespace
 
 cudaError_t launch_act_quant(const ActQuantLaunch &L, cudaStream_t st) {
   ActArgs a{L.x,     L.ldx,   L.K,       L.k_fill,  L.inv_smooth, L.inv_step,  L.safe_thresh,
-            L.q,     L.ldq,   L.ratio,   L.peers,   L.n_peers,    L.pub_seq,   L.pub_arrive};
+            L.q,     L.ldq,   L.ratio,   L.peers,   L.n_peers,    L.pub_seq,   L.pub_arrive,
+            L.trace};
   const bool vec = (L.K % 4 == 0) && (L.ldx % 4 == 0) && (L.ldq % 4 == 0) &&
                    (reinterpret_cast<uintptr_t>(L.x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(L.q) % 4 == 0) &&
@@ -263,7 +264,7 @@ cudaError_t launch_topk_merge(const MergeLaunch &L, cudaStream_t st) {
   const int P = (L.n_lists * L.k_in + 1) & ~1;
   MergeArgs a{L.in_val,  L.in_idx,  L.n_lists, L.k_in,        L.k_out,   P,
               L.list_stride, L.token_stride, L.out_val, L.out_idx, L.argmax,
-              L.done,    L.remote_mask, L.pub_seq, L.err};
+              L.done,    L.remote_mask, L.pub_seq, L.err,     L.trace};
   const size_t smem = (static_cast<size_t>(P) + kMergeWarps * 64) * 8;
   return launch_ex(topk_merge_kernel, dim3(L.T), dim3(kMergeWarps * 32), smem, st, L.pdl, a);
 }

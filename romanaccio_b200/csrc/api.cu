@@ -293,7 +293,7 @@ namespace w8a8 {
 
 w8a8_status linear_quant_input(w8a8_linear *l, const float *x, int64_t ldx, int T, int act_mode,
                                const PublishPeer *peers, int n_peers, unsigned *pub_seq,
-                               unsigned *pub_arrive, cudaStream_t s) {
+                               unsigned *pub_arrive, cudaStream_t s, unsigned long long *trace) {
   ActQuantLaunch A = {};
   A.x = x;
   A.ldx = ldx;
@@ -312,20 +312,33 @@ w8a8_status linear_quant_input(w8a8_linear *l, const float *x, int64_t ldx, int 
   A.n_peers = n_peers;
   A.pub_seq = pub_seq;
   A.pub_arrive = pub_arrive;
+  A.trace = trace;
   W8A8_CUDA(launch_act_quant(A, s));
   return W8A8_SUCCESS;
+}
+
+bool linear_can_fuse(const w8a8_linear *l, int T, int act_mode, FusedQuant *fq) {
+  const int tg = std::min(T, 8);
+  const int tt = tg <= 1 ? 1 : tg <= 2 ? 2 : tg <= 4 ? 4 : 8;
+  if (act_mode != W8A8_ACT_STATIC || tt * l->k_pad > kFusedXMaxBytes) return false;
+  *fq = FusedQuant{};
+  fq->K = l->K;
+  fq->inv_smooth = l->inv_smooth;
+  fq->inv_step = l->inv_step;
+  return true;
 }
 
 w8a8_status linear_topk_quantized(w8a8_linear *l, int T, int act_mode, int out_mode, int k,
                                   int row_offset, float *topk_val, int32_t *topk_idx,
                                   float *logits, int64_t ldl, const ShardSync &sync, bool pdl,
-                                  cudaStream_t s) {
-  if (sync.seq && T > 8)
-    return fail(W8A8_ERR_INVALID_ARG, "a shard on another device takes at most 8 tokens a forward");
+                                  cudaStream_t s, const FusedQuant *fq) {
+  if ((sync.seq || (fq && fq->pub_seq)) && T > 8)
+    return fail(W8A8_ERR_INVALID_ARG, "a multi-device LM head takes at most 8 tokens a forward");
+  const bool fused = fq && fq->x;
   for (int t0 = 0; t0 < T; t0 += 8) {
     const int tg = std::min(8, T - t0);
     GemvPlan plan;
-    if (!plan_gemv(tg, l->N, l->k_pad, true, k, l->ctx->sm_count, &plan))
+    if (!plan_gemv(tg, l->N, l->k_pad, true, k, l->ctx->sm_count, &plan, fused))
       return fail(W8A8_ERR_NOT_SUPPORTED, "no top-k plan for T=%d N=%d K=%d k=%d", tg, l->N, l->K, k);
     if (static_cast<size_t>(tg) * plan.grid * (k + 1) > l->lists_keys)
       return fail(W8A8_ERR_NOT_SUPPORTED, "top-k scratch too small");
@@ -352,6 +365,10 @@ w8a8_status linear_topk_quantized(w8a8_linear *l, int T, int act_mode, int out_m
     L.pdl = pdl;
     L.trace = plan.grid <= 2 * l->ctx->sm_count ? l->tc_trace : nullptr;
     L.sync = sync;
+    if (fused) {
+      L.fq = *fq;
+      L.fq.x = fq->x + static_cast<size_t>(t0) * fq->ldx;
+    }
     W8A8_CUDA(launch_gemv(L, plan, s));
   }
   return W8A8_SUCCESS;
@@ -687,6 +704,14 @@ w8a8_status w8a8_linear_forward_topk(w8a8_linear *l, const float *x, int64_t ldx
   st = ensure_tokens(l, T);
   if (st != W8A8_SUCCESS) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  w8a8::FusedQuant fq;
+  if (w8a8::linear_can_fuse(l, T, act_mode, &fq)) {
+    // static quantisation runs in the GEMV prologue: one launch per 8 tokens
+    fq.x = x;
+    fq.ldx = ldx;
+    return w8a8::linear_topk_quantized(l, T, act_mode, out_mode, k, row_offset, topk_val,
+                                       topk_idx, logits, ldl, w8a8::ShardSync{}, true, s, &fq);
+  }
   st = w8a8::linear_quant_input(l, x, ldx, T, act_mode, nullptr, 0, nullptr, nullptr, s);
   if (st != W8A8_SUCCESS) return st;
   return w8a8::linear_topk_quantized(l, T, act_mode, out_mode, k, row_offset, topk_val, topk_idx,

@@ -90,6 +90,10 @@ __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ void st_relaxed_sys(unsigned *p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Orders this thread's earlier generic-proxy accesses (an acquire included) before its later
 // bulk copies, which read global memory through the async proxy.
 __device__ __forceinline__ void fence_proxy_async_global() {

@@ -48,6 +48,8 @@ struct GemvArgs {
   int *err;
   unsigned long long *trace;
   ShardSync sync;
+  FusedQuant fq;
+  uint32_t xres_off;  // fused quantisation: resident [TT][k_pad] int8 slab
 };
 
 // A shard on another device than GPU 0 waits at most this long for GPU 0 to store its
@@ -103,6 +105,98 @@ struct BlockSync {
   __device__ void operator()() const { __syncthreads(); }
 };
 
+// Barrier over the consumer warps only (the producer warp keeps streaming).
+__device__ __forceinline__ void consumer_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+}
+
+// Fused prologue: the T fp32 rows quantised into the resident slab xres ([TT][k_pad]; rows >= T
+// and columns >= K zero) by the consumer threads, with the arithmetic of act_quant_kernel's
+// static path: q = round_clamp(x * (s * inv_step), 127), or x * inv_step without smoothing.
+// The last CTA of a multi-device LM head's shard-0 grid (it owns the fewest tiles, so the time
+// it spends here is least likely to delay the grid) then stores rows [0, T) into every peer's
+// staging buffer and bumps the peers' x_ready counters (one system-scope fence, then relaxed
+// stores: a release).
+template <int TT>
+__device__ void quantise_resident(const GemvArgs &a, int8_t *xres, int tid) {
+  const FusedQuant &f = a.fq;
+  // The publishing CTA fetches its metadata (peer buffers, forward counter) first, so those
+  // reads overlap the activations' instead of following them.
+  __shared__ int8_t *s_peer_q[64];
+  __shared__ unsigned *s_peer_flag[64];
+  __shared__ unsigned s_seq;
+  const bool publisher = blockIdx.x == gridDim.x - 1 && f.pub_seq != nullptr;
+  if (publisher) {
+    if (tid < f.n_peers) {
+      s_peer_q[tid] = f.peers[tid].q;
+      s_peer_flag[tid] = f.peers[tid].flag;
+    }
+    if (tid == 0) s_seq = *f.pub_seq;
+  }
+  const float inv = f.inv_step;
+  const bool vec = (f.K % 4 == 0) && (f.ldx % 4 == 0) &&
+                   (reinterpret_cast<uintptr_t>(f.x) % 16 == 0) &&
+                   (f.inv_smooth == nullptr || reinterpret_cast<uintptr_t>(f.inv_smooth) % 16 == 0);
+  constexpr int NT = kConsumerWarps * 32;
+  for (int t = 0; t < TT; ++t) {
+    int8_t *q = xres + t * a.k_pad;
+    if (t >= a.T) {
+      for (int c = tid * 16; c < a.k_pad; c += NT * 16)
+        *reinterpret_cast<int4 *>(q + c) = make_int4(0, 0, 0, 0);
+      continue;
+    }
+    const float *x = f.x + t * f.ldx;
+    if (vec) {
+      const float4 *x4 = reinterpret_cast<const float4 *>(x);
+      const float4 *s4 = reinterpret_cast<const float4 *>(f.inv_smooth);
+      for (int c = tid; c < f.K / 4; c += NT) {
+        const float4 v = x4[c];
+        char4 o;
+        if (s4) {
+          const float4 sv = s4[c];
+          o.x = static_cast<signed char>(round_clamp(v.x * (sv.x * inv), 127.0f));
+          o.y = static_cast<signed char>(round_clamp(v.y * (sv.y * inv), 127.0f));
+          o.z = static_cast<signed char>(round_clamp(v.z * (sv.z * inv), 127.0f));
+          o.w = static_cast<signed char>(round_clamp(v.w * (sv.w * inv), 127.0f));
+        } else {
+          o.x = static_cast<signed char>(round_clamp(v.x * inv, 127.0f));
+          o.y = static_cast<signed char>(round_clamp(v.y * inv, 127.0f));
+          o.z = static_cast<signed char>(round_clamp(v.z * inv, 127.0f));
+          o.w = static_cast<signed char>(round_clamp(v.w * inv, 127.0f));
+        }
+        reinterpret_cast<char4 *>(q)[c] = o;
+      }
+    } else {
+      for (int c = tid; c < f.K; c += NT) {
+        const float v = f.inv_smooth ? x[c] * (f.inv_smooth[c] * inv) : x[c] * inv;
+        q[c] = static_cast<int8_t>(round_clamp(v, 127.0f));
+      }
+    }
+    for (int c = f.K + tid; c < a.k_pad; c += NT) q[c] = 0;
+  }
+  consumer_bar();
+  if (!publisher) return;
+  if (tid == 0 && f.trace) f.trace[0] = global_timer_ns();
+  const int vecs = a.k_pad / 16;
+  for (int p = 0; p < f.n_peers; ++p) {
+    int8_t *dst = s_peer_q[p];
+    for (int i = tid; i < a.T * vecs; i += NT) {
+      const int t = i / vecs, c = (i - t * vecs) * 16;
+      *reinterpret_cast<int4 *>(dst + t * a.k_pad + c) =
+          *reinterpret_cast<const int4 *>(xres + t * a.k_pad + c);
+    }
+  }
+  __threadfence_system();
+  consumer_bar();
+  if (tid == 0) {
+    __threadfence_system();
+    const unsigned e = s_seq + 1u;
+    *f.pub_seq = e;
+    for (int p = 0; p < f.n_peers; ++p) st_relaxed_sys(s_peer_flag[p], e);
+    if (f.trace) f.trace[1] = global_timer_ns();
+  }
+}
+
 // Shared memory of the top-k epilogue (in the drained stage ring): the warps' staged lists (64
 // keys each), then the last CTA's gathered candidates.
 constexpr uint32_t kTopkStageBytes = ((kConsumerWarps + 1) * 64 + kTopkGatherKeys) * 8;
@@ -139,9 +233,10 @@ __device__ void topk_epilogue(const GemvArgs &a, const GridTopkState &st, const 
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
+      __threadfence_system();
       const unsigned e = *a.sync.seq + 1u;
       *a.sync.seq = e;
-      st_release_sys(a.sync.done, e);
+      st_relaxed_sys(a.sync.done, e);
     }
   }
   if (threadIdx.x == 0) {
@@ -186,6 +281,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
     const uint64_t pol_w = policy_evict_first();
     const uint64_t pol_x = policy_evict_last();
     const int pre = min(a.ns, total);
+    // fused quantisation: the stages carry weights only
+    const int x_rows = a.fq.x ? 0 : a.T;
     auto stage_geom = [&](int it, int &tile, int &k0, int &bytes, int &rows) {
       tile = tile0 + it / a.nk;
       k0 = (it % a.nk) * a.kc;
@@ -203,16 +300,22 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
           bulk_g2s(dst + r * a.kc, src + static_cast<int64_t>(r) * a.ldw, bytes, full, pol_w);
       }
     };
-    for (int it = 0; it < pre; ++it) {
+    auto issue_w = [&](int it) {
       int tile, k0, bytes, rows;
       stage_geom(it, tile, k0, bytes, rows);
       const uint32_t full = smem_addr(&bars[it]);
-      if (lane == 0) mbar_arrive_expect_tx(full, static_cast<uint32_t>((rows + a.T) * bytes));
+      if (lane == 0) mbar_arrive_expect_tx(full, static_cast<uint32_t>((rows + x_rows) * bytes));
       __syncwarp();
       copy_w(smem_addr(stages + static_cast<size_t>(it) * a.stage_bytes), tile, k0, bytes, rows, full);
-    }
+    };
+    // With fused quantisation the consumers read the fp32 activations right after the
+    // dependency wait: only one stage goes ahead of them, so that read does not queue behind
+    // the whole grid's prefetch.
+    const int early = a.fq.x ? min(1, pre) : pre;
+    for (int it = 0; it < early; ++it) issue_w(it);
     // Activations (and everything written by the previous kernel) are read only after this.
     pdl_wait();
+    for (int it = early; it < pre; ++it) issue_w(it);
     if (a.sync.x_ready) {
       // Remote LM-head shard: GPU 0 stores this forward's activations into our staging buffer
       // and then bumps x_ready.  On a timeout the (stale) rows are still copied so the kernel
@@ -229,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
       stage_geom(it, tile, k0, bytes, rows);
       const uint32_t full = smem_addr(&bars[it]);
       const uint32_t dst = smem_addr(stages + static_cast<size_t>(it) * a.stage_bytes) + RB * a.kc;
-      for (int t = lane; t < a.T; t += 32)
+      for (int t = lane; t < x_rows; t += 32)
         bulk_g2s(dst + t * a.kc, a.x + t * a.ldx + k0, bytes, full, pol_x);
     }
     bool ok = true;
@@ -243,16 +346,19 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
       int tile, k0, bytes, rows;
       stage_geom(it, tile, k0, bytes, rows);
       const uint32_t full = smem_addr(&bars[slot]);
-      if (lane == 0) mbar_arrive_expect_tx(full, static_cast<uint32_t>((rows + a.T) * bytes));
+      if (lane == 0) mbar_arrive_expect_tx(full, static_cast<uint32_t>((rows + x_rows) * bytes));
       __syncwarp();
       const uint32_t dst = smem_addr(stages + static_cast<size_t>(slot) * a.stage_bytes);
       copy_w(dst, tile, k0, bytes, rows, full);
-      for (int t = lane; t < a.T; t += 32)
+      for (int t = lane; t < x_rows; t += 32)
         bulk_g2s(dst + RB * a.kc + t * a.kc, a.x + t * a.ldx + k0, bytes, full, pol_x);
     }
   } else {
     // ------------------------------- consumer warps -------------------------------
     pdl_wait();
+    int8_t *xres = reinterpret_cast<int8_t *>(smem + a.xres_off);
+    const bool fused = a.fq.x != nullptr;
+    if (fused) quantise_resident<TT>(a, xres, threadIdx.x);
     int acc[RPW][TT];
 #pragma unroll
     for (int r = 0; r < RPW; ++r)
@@ -267,12 +373,15 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
       const int kci = it % a.nk;
       const int bytes = min(a.kc, a.k_pad - kci * a.kc);
       const uint8_t *sw = stages + static_cast<size_t>(slot) * a.stage_bytes;
-      const uint8_t *sx = sw + RB * a.kc;
+      // activations: the stage's slab (row stride kc) or the resident slab (row stride k_pad)
+      const uint8_t *sx =
+          fused ? reinterpret_cast<const uint8_t *>(xres) + kci * a.kc : sw + RB * a.kc;
+      const int ldsx = fused ? a.k_pad : a.kc;
       if (ok) {
         for (int kk = lane * 16; kk < bytes; kk += 512) {
           int4 xv[TT];
 #pragma unroll
-          for (int t = 0; t < TT; ++t) xv[t] = *reinterpret_cast<const int4 *>(sx + t * a.kc + kk);
+          for (int t = 0; t < TT; ++t) xv[t] = *reinterpret_cast<const int4 *>(sx + t * ldsx + kk);
 #pragma unroll
           for (int r = 0; r < RPW; ++r) {
             const int4 wv =
@@ -382,10 +491,14 @@ size_t pow2_ceil(size_t v) {
 
 }  // namespace
 
-bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan *plan) {
+bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan *plan,
+               bool fused_x) {
   if (T < 1 || T > 8 || N < 1 || k_pad < 16 || (k_pad % 16) != 0 || sm_count < 1) return false;
   GemvPlan p = {};
   p.tt = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
+  if (fused_x && p.tt * k_pad > kFusedXMaxBytes) return false;
+  p.fused_x = fused_x;
+  const size_t xres = fused_x ? static_cast<size_t>(p.tt) * k_pad : 0;
   auto tiles = [&](int rb) { return (N + rb - 1) / rb; };
   const int min_tiles = 2 * sm_count;
   constexpr int kMaxStage = 32768;
@@ -403,17 +516,18 @@ bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan
   }
   p.rb = 8 * p.rpw;
   p.nk = (k_pad + p.kc - 1) / p.kc;
-  const size_t stage = static_cast<size_t>(p.rb + p.tt) * p.kc;
+  const size_t stage = static_cast<size_t>(p.rb + (fused_x ? 0 : p.tt)) * p.kc;
   p.num_tiles = tiles(p.rb);
   const size_t bars = 2 * kMaxStages * 8;
   if (!topk) {
-    const size_t budget = 110 * 1024;
+    const size_t budget = 110 * 1024 - xres;
     p.ns = static_cast<int>(std::min<size_t>(kMaxStages, std::max<size_t>(2, budget / stage)));
     p.grid = std::min(p.num_tiles, 2 * sm_count);
     p.tiles_per_cta = (p.num_tiles + p.grid - 1) / p.grid;
     p.grid = (p.num_tiles + p.tiles_per_cta - 1) / p.tiles_per_cta;
     p.cand_cap = 0;
-    p.smem = p.ns * stage + bars;
+    p.xres_off = static_cast<uint32_t>(p.ns * stage + bars);
+    p.smem = p.ns * stage + bars + xres;
   } else {
     if (k < 1 || k > 64 || k > N) return false;
     int grid = std::min(p.num_tiles, 2 * sm_count);
@@ -429,9 +543,12 @@ bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan
     p.grid = (p.num_tiles + p.tiles_per_cta - 1) / p.tiles_per_cta;
     p.cand_cap = static_cast<int>(cap);
     const size_t cand_bytes = static_cast<size_t>(p.tt) * cap * 8;
-    const size_t budget = 110 * 1024 > cand_bytes + 2 * stage ? 110 * 1024 - cand_bytes : 2 * stage;
+    const size_t used = cand_bytes + xres;
+    const size_t budget = 110 * 1024 > used + 2 * stage ? 110 * 1024 - used : 2 * stage;
     p.ns = static_cast<int>(std::min<size_t>(kMaxStages, std::max<size_t>(2, budget / stage)));
-    p.smem = std::max<size_t>(p.ns * stage, kTopkStageBytes) + bars + cand_bytes;
+    const size_t ring = std::max<size_t>(p.ns * stage, kTopkStageBytes);
+    p.xres_off = static_cast<uint32_t>(ring + bars + cand_bytes);
+    p.smem = ring + bars + cand_bytes + xres;
   }
   if (p.smem > kMaxDynSmem) return false;
   *plan = p;
@@ -453,7 +570,7 @@ cudaError_t launch_gemv(const GemvLaunch &L, const GemvPlan &plan, cudaStream_t 
   a.num_tiles = plan.num_tiles;
   a.tiles_per_cta = plan.tiles_per_cta;
   a.cand_cap = plan.cand_cap;
-  a.stage_bytes = static_cast<uint32_t>((plan.rb + plan.tt) * plan.kc);
+  a.stage_bytes = static_cast<uint32_t>((plan.rb + (plan.fused_x ? 0 : plan.tt)) * plan.kc);
   a.ring_bytes = static_cast<uint32_t>(plan.ns) * a.stage_bytes;
   if (L.topk) a.ring_bytes = std::max(a.ring_bytes, kTopkStageBytes);
   a.ep = L.ep;
@@ -461,6 +578,9 @@ cudaError_t launch_gemv(const GemvLaunch &L, const GemvPlan &plan, cudaStream_t 
   a.err = L.err;
   a.trace = L.trace;
   a.sync = L.sync;
+  a.fq = L.fq;
+  a.xres_off = plan.xres_off;
+  if ((L.fq.x != nullptr) != plan.fused_x) return cudaErrorInvalidValue;
   switch (plan.tt) {
     case 1: return dispatch_rpw<1>(a, plan, stream, L.pdl, L.topk);
     case 2: return dispatch_rpw<2>(a, plan, stream, L.pdl, L.topk);

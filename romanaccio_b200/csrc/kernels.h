@@ -49,12 +49,37 @@ struct TopK {
   int64_t ldl;
 };
 
+// A destination of the int8 activation rows on another device (multi-device LM head).
+struct PublishPeer {
+  int8_t *q;       // peer's int8 staging buffer
+  unsigned *flag;  // peer's x_ready counter
+};
+
 // Cross-device handshake of an LM-head shard on another device than the merging one (GPU 0).
 // All three are counters of forwards that only grow.
 struct ShardSync {
   unsigned *seq;            // shard device: forwards this shard completed (last CTA bumps it)
   const unsigned *x_ready;  // shard device: forwards whose int8 activations GPU 0 stored here
   unsigned *done;           // GPU 0 (peer pointer): forwards whose candidates this shard stored
+};
+
+// Activation quantisation fused into a GEMV's prologue: every CTA quantises the fp32 rows into
+// a resident shared-memory slab itself (the arithmetic of launch_act_quant), so no separate
+// quantisation kernel precedes the GEMV.  Optionally one CTA also stores the int8 rows into other
+// devices' staging buffers and bumps their x_ready counters (the multi-device LM head; the
+// grid's last CTA does it).
+// Static (per-tensor in_step) quantisation only: a per-token dyntok ratio would have to be
+// agreed on by every CTA before its epilogue.
+struct FusedQuant {
+  const float *x;              // [T, ldx] fp32; null: the GEMV reads int8 rows (GemvLaunch::x)
+  int64_t ldx;
+  int K;
+  const float *inv_smooth;     // [K] or null
+  float inv_step;
+  const PublishPeer *peers;    // device array [n_peers]
+  int n_peers;
+  unsigned *pub_seq;           // null: no publication
+  unsigned long long *trace;   // optional: [0] publishing CTA quantised, [1] counters stored
 };
 
 struct GemvLaunch {
@@ -71,6 +96,7 @@ struct GemvLaunch {
   bool pdl;
   unsigned long long *trace;  // optional [grid, 8] %globaltimer stamps (diagnostics)
   ShardSync sync;             // all null: activations are local and ordered by the stream
+  FusedQuant fq;              // fq.x null: int8 activations from x
 };
 
 // Shape plan of one GEMV launch (filled by plan_gemv; the scratch sizes of the top-k path
@@ -87,9 +113,15 @@ struct GemvPlan {
   int grid;
   int cand_cap;    // top-k: power-of-two candidate slots per token per CTA
   size_t smem;     // dynamic shared memory bytes
+  bool fused_x;    // activations quantised in the prologue into a resident slab
+  uint32_t xres_off;  // offset of that slab ([tt][k_pad] int8) in dynamic shared memory
 };
 
-bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan *plan);
+// Largest resident activation slab (tt * k_pad bytes) of a fused-quantisation plan.
+constexpr int kFusedXMaxBytes = 16 * 1024;
+
+bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan *plan,
+               bool fused_x = false);
 cudaError_t launch_gemv(const GemvLaunch &L, const GemvPlan &plan, cudaStream_t stream);
 
 // Tensor-core (tcgen05 kind::i8) contraction for larger token counts.
@@ -200,11 +232,6 @@ cudaError_t launch_moe_swiglu(const float *gu, int I, int pairs, float *h, bool 
 cudaError_t launch_moe_combine(const MoeCombineLaunch &L, cudaStream_t stream);
 
 // Activation quantisation (pack) of x [T, K] fp32 into q [T, ldq] int8 (+ ratio [T]).
-struct PublishPeer {
-  int8_t *q;       // peer's int8 staging buffer
-  unsigned *flag;  // peer's x_ready counter
-};
-
 struct ActQuantLaunch {
   const float *x;
   int64_t ldx;
@@ -225,6 +252,7 @@ struct ActQuantLaunch {
   int n_peers;
   unsigned *pub_seq;         // this device; null: no publication
   unsigned *pub_arrive;      // this device, zero between launches
+  unsigned long long *trace; // optional: [0] entry of CTA 0, [1] peers' flags stored
 };
 cudaError_t launch_act_quant(const ActQuantLaunch &L, cudaStream_t stream);
 
@@ -264,6 +292,7 @@ struct MergeLaunch {
   uint64_t remote_mask;
   const unsigned *pub_seq;
   int *err;
+  unsigned long long *trace;  // optional: [2] CTA 0 past its stream wait, [3] flags seen, [4] end
 };
 cudaError_t launch_topk_merge(const MergeLaunch &L, cudaStream_t stream);
 

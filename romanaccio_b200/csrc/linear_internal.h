@@ -11,12 +11,19 @@ namespace w8a8 {
 
 w8a8_status linear_quant_input(w8a8_linear *l, const float *x, int64_t ldx, int T, int act_mode,
                                const PublishPeer *peers, int n_peers, unsigned *pub_seq,
-                               unsigned *pub_arrive, cudaStream_t s);
+                               unsigned *pub_arrive, cudaStream_t s,
+                               unsigned long long *trace = nullptr);
 
+// fq (or null): fp32 activations quantised in the GEMV's prologue (linear_can_fuse must hold)
+// instead of reading the staging buffer; with fq->pub_seq, the last CTA also publishes the rows.
 w8a8_status linear_topk_quantized(w8a8_linear *l, int T, int act_mode, int out_mode, int k,
                                   int row_offset, float *topk_val, int32_t *topk_idx,
                                   float *logits, int64_t ldl, const ShardSync &sync, bool pdl,
-                                  cudaStream_t s);
+                                  cudaStream_t s, const FusedQuant *fq = nullptr);
+
+// Whether T tokens of this linear can be quantised in the GEMV prologue (static activation
+// quantisation and a small enough resident slab); fills the linear's static parameters.
+bool linear_can_fuse(const w8a8_linear *l, int T, int act_mode, FusedQuant *fq);
 
 // The int8 staging buffer ([tokens, ld] bytes) and its row stride; stable once reserved.
 int8_t *linear_staging(w8a8_linear *l);

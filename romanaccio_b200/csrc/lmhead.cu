@@ -51,6 +51,7 @@ struct w8a8_lmhead {
   w8a8::PublishPeer *peers = nullptr;   // [n - 1]: shards 1..n-1 staging buffers and x_ready
   float *cand_val = nullptr;            // [n][max_T * k_max]
   int32_t *cand_idx = nullptr;
+  unsigned long long *trace = nullptr;  // optional diagnostics timeline (device 0)
 };
 
 namespace {
@@ -270,16 +271,31 @@ w8a8_status w8a8_lmhead_forward(w8a8_lmhead *lm, const float *h, int32_t T, int3
         lm->cand_idx + s * block, nullptr, 0, sync, false, lm->streams[s]);
     if (st != W8A8_SUCCESS) return st;
   }
-  // 2. device 0: quantise h into every shard's staging buffer, then its own shards, then merge
+  // 2. device 0: quantise h into every shard's staging buffer, then its own shards, then merge.
+  // Shard 0's GEMV quantises h in its prologue and its last CTA publishes the rows (one launch);
+  // when the rows do not fit that, a quantisation kernel publishes them first.
   DeviceScope d(dev0);
-  w8a8_status st = w8a8::linear_quant_input(lm->shards[0], h, lm->K, T, W8A8_ACT_STATIC,
-                                            lm->peers, n - 1, lm->ctr0, lm->ctr0 + 1, s0);
-  if (st != W8A8_SUCCESS) return st;
+  w8a8::FusedQuant fq;
+  const bool fused = w8a8::linear_can_fuse(lm->shards[0], T, W8A8_ACT_STATIC, &fq);
+  w8a8_status st = W8A8_SUCCESS;
+  if (fused) {
+    fq.x = h;
+    fq.ldx = lm->K;
+    fq.peers = lm->peers;
+    fq.n_peers = n - 1;
+    fq.pub_seq = n > 1 ? lm->ctr0 : nullptr;
+    fq.trace = lm->trace;
+  } else {
+    st = w8a8::linear_quant_input(lm->shards[0], h, lm->K, T, W8A8_ACT_STATIC, lm->peers, n - 1,
+                                  lm->ctr0, lm->ctr0 + 1, s0, lm->trace);
+    if (st != W8A8_SUCCESS) return st;
+  }
   for (int s = 0; s < n; ++s) {
     if (lm->remote[s]) continue;
     st = w8a8::linear_topk_quantized(lm->shards[s], T, W8A8_ACT_STATIC, W8A8_OUT_F32_ACC, k,
                                      lm->lo[s], lm->cand_val + s * block, lm->cand_idx + s * block,
-                                     nullptr, 0, w8a8::ShardSync{}, true, s0);
+                                     nullptr, 0, w8a8::ShardSync{}, true, s0,
+                                     s == 0 && fused ? &fq : nullptr);
     if (st != W8A8_SUCCESS) return st;
   }
   w8a8::MergeLaunch L = {};
@@ -301,11 +317,23 @@ w8a8_status w8a8_lmhead_forward(w8a8_lmhead *lm, const float *h, int32_t T, int3
     L.pub_seq = lm->ctr0;
     L.err = w8a8::linear_error_word(lm->shards[0]);
   }
+  L.trace = lm->trace;
   return cuda_status(w8a8::launch_topk_merge(L, s0), "LM-head merge launch");
 }
 
 void w8a8_lmhead_destroy(w8a8_lmhead *lm) { lmhead_free(lm); }
 
 int32_t w8a8_lmhead_shards(const w8a8_lmhead *lm) { return lm ? lm->n : 0; }
+
+w8a8_status w8a8_lmhead_set_trace(w8a8_lmhead *lm, unsigned long long *head_trace,
+                                  unsigned long long *const *shard_traces) {
+  if (!lm) return invalid("lmhead is NULL");
+  lm->trace = head_trace;
+  for (int s = 0; s < lm->n; ++s) {
+    w8a8_status st = w8a8_linear_set_trace(lm->shards[s], shard_traces ? shard_traces[s] : nullptr);
+    if (st != W8A8_SUCCESS) return st;
+  }
+  return W8A8_SUCCESS;
+}
 
 }  // extern "C"

@@ -82,20 +82,15 @@ __device__ __forceinline__ void warp_merge_desc(uint64_t (&a)[R], const uint64_t
   for (int d = 16 * R; d > 0; d >>= 1) warp_bitonic_stage<R>(a, lane, 64 * R, d);
 }
 
-template <bool kCg>
-__device__ __forceinline__ uint64_t load_key(const uint64_t *p) {
-  if (kCg) return __ldcg(reinterpret_cast<const unsigned long long *>(p));
-  return *p;
-}
-
-// The 32R largest of keys[0..n) (0 past n), sorted descending, in warp 0's `out` (other warps'
-// `out` are unspecified) and in stage[0..32R) for every warp after the call.  Warps 0..NW-1 take
-// part and sync() is a barrier over exactly them; `stage` holds NW * 32R keys of shared memory.
-// Only the first ceil(n / 32R) warps (at most NW) hold a chunk and take part in the tree.
-// kCg: the keys were written by other CTAs of the grid (read through L2).
-template <int R, int NW, bool kCg, typename Sync>
-__device__ void cta_top_keys(const uint64_t *keys, int n, uint64_t *stage, int warp, int lane,
-                             Sync sync, uint64_t (&out)[R]) {
+// The 32R largest of keys[0..n) (0 past n), sorted descending, into stage[0..32R), visible to
+// every warp when the call returns.  Warps 0..NW-1 take part and sync() is a barrier over
+// exactly them; `stage` holds NW * 32R keys of shared memory.  Only the first ceil(n / 32R)
+// warps (at most NW) hold a chunk and take part in the tree.  cg: the keys were written by
+// other CTAs of the grid (read through L2).  Not inlined: the per-CTA lists and the last CTA's
+// selection run the same code, so the selection finds it in the SM's instruction cache.
+template <int R, int NW, typename Sync>
+__device__ __noinline__ void cta_top_keys(const uint64_t *keys, int n, bool cg, uint64_t *stage,
+                                          int warp, int lane, Sync sync) {
   constexpr int L = 32 * R;
   const int chunks = (n + L - 1) / L;
   const int act = chunks < 1 ? 1 : (chunks < NW ? chunks : NW);
@@ -108,7 +103,9 @@ __device__ void cta_top_keys(const uint64_t *keys, int n, uint64_t *stage, int w
 #pragma unroll
     for (int j = 0; j < R; ++j) {
       const int i = c + lane + 32 * j;
-      b[j] = i < n ? load_key<kCg>(keys + i) : 0ull;
+      b[j] = i >= n ? 0ull
+             : cg   ? __ldcg(reinterpret_cast<const unsigned long long *>(keys) + i)
+                    : keys[i];
     }
     warp_sort_desc<R>(b, lane);
     if (first) {
@@ -135,8 +132,6 @@ __device__ void cta_top_keys(const uint64_t *keys, int n, uint64_t *stage, int w
     }
     sync();
   }
-#pragma unroll
-  for (int j = 0; j < R; ++j) out[j] = a[j];
 }
 
 // This CTA's share of token t's grid top-k: its sorted top k of cand[0..n) (0 past n) and the
@@ -144,15 +139,12 @@ __device__ void cta_top_keys(const uint64_t *keys, int n, uint64_t *stage, int w
 template <int R, int NW, typename Sync>
 __device__ void grid_topk_offer(const uint64_t *cand, int n, int k, int t, const GridTopkState &st,
                                 uint64_t *stage, int warp, int lane, Sync sync) {
-  uint64_t v[R];
-  cta_top_keys<R, NW, false>(cand, n, stage, warp, lane, sync, v);
+  cta_top_keys<R, NW>(cand, n, false, stage, warp, lane, sync);
   if (warp == 0) {
     uint64_t *base = st.keys + t * grid_topk_stride(gridDim.x, k);
     uint64_t *list = base + static_cast<size_t>(blockIdx.x) * k;
-#pragma unroll
-    for (int j = 0; j < R; ++j)
-      if (lane + 32 * j < k) list[lane + 32 * j] = v[j];
-    if (lane == 0) base[static_cast<size_t>(gridDim.x) * k + blockIdx.x] = v[0];
+    for (int e = lane; e < k; e += 32) list[e] = stage[e];
+    if (lane == 0) base[static_cast<size_t>(gridDim.x) * k + blockIdx.x] = stage[0];
   }
   sync();
 }
@@ -181,9 +173,8 @@ __device__ void grid_topk_select(int k, int t, const GridTopkState &st, float *v
   const int G = gridDim.x;
   const uint64_t *base = st.keys + t * grid_topk_stride(G, k);
   const uint64_t *heads = base + static_cast<size_t>(G) * k;
-  uint64_t v[R];
   // the k largest heads; T0 = the k-th (0 when fewer than k lists are non-empty)
-  cta_top_keys<R, NW, true>(heads, G, stage, warp, lane, sync, v);
+  cta_top_keys<R, NW>(heads, G, true, stage, warp, lane, sync);
   const uint64_t t0 = stage[k - 1];
   const int tid = warp * 32 + lane;
   if (tid == 0) *s_int = 0;
@@ -211,28 +202,12 @@ __device__ void grid_topk_select(int k, int t, const GridTopkState &st, float *v
     }
   }
   sync();
-  const int n = *s_int;
-  if (n <= 32 * R) {
-    // the usual case (about k + a few candidates): one warp sorts them
-    if (warp == 0) {
-#pragma unroll
-      for (int j = 0; j < R; ++j) {
-        const int i = lane + 32 * j;
-        v[j] = i < n ? gather[i] : 0ull;
-      }
-      warp_sort_desc<R>(v, lane);
-    }
-  } else {
-    cta_top_keys<R, NW, false>(gather, n, stage, warp, lane, sync, v);
-  }
+  // the usual case is about k + a few candidates: one chunk, no tree
+  cta_top_keys<R, NW>(gather, *s_int, false, stage, warp, lane, sync);
   if (warp == 0) {
-#pragma unroll
-    for (int j = 0; j < R; ++j) {
-      const int e = lane + 32 * j;
-      if (e < k) {
-        val[t * k + e] = topk_key_value(v[j]);
-        idx[t * k + e] = topk_key_id(v[j]);
-      }
+    for (int e = lane; e < k; e += 32) {
+      val[t * k + e] = topk_key_value(stage[e]);
+      idx[t * k + e] = topk_key_id(stage[e]);
     }
   }
   sync();

@@ -167,6 +167,19 @@ class MultiDeviceLmHead:
                                                   _stream(stream)), "w8a8_lmhead_forward")
         return v, i, a
 
+    def enable_trace(self) -> tuple[torch.Tensor, list[torch.Tensor]]:
+        """Diagnostics: device-0 forward timeline [8] and each shard's per-CTA timeline
+        [2 * sm_count, 8] (int64 %globaltimer ns, w8a8_lmhead_set_trace)."""
+        import ctypes as C
+        head = torch.zeros((8,), dtype=torch.int64, device=f"cuda:{self.device}")
+        shards = [torch.zeros((2 * c.sm_count, 8), dtype=torch.int64, device=f"cuda:{c.device}")
+                  for c in self.ctxs]
+        arr = (C.c_void_p * len(shards))(*[t.data_ptr() for t in shards])
+        self._check(self._lib.w8a8_lmhead_set_trace(self.handle, head.data_ptr(), arr),
+                    "w8a8_lmhead_set_trace")
+        self._trace = (head, shards)
+        return head, shards
+
     def close(self) -> None:
         if getattr(self, "handle", None):
             self._lib.w8a8_lmhead_destroy(self.handle)
