@@ -262,8 +262,9 @@ w8a8_status w8a8_lmhead_forward(w8a8_lmhead *lmhead, const float *h_dev, int32_t
 void        w8a8_lmhead_destroy(w8a8_lmhead *lmhead);
 int32_t     w8a8_lmhead_shards(const w8a8_lmhead *lmhead);
 /* Diagnostics (no reference counterpart): head_trace_dev (device 0, 8 uint64, or NULL) receives
- * %globaltimer stamps of a forward: [0] quantisation entry, [1] every shard's activations
- * stored, [2] merge past its stream wait, [3] every remote shard's candidates seen, [4] merge
+ * %globaltimer stamps of a forward with several shards: [0] activations quantised (by the
+ * publishing CTA, or entry of the quantisation kernel when shard 0 cannot fuse it), [1] every
+ * shard's activations stored, [2] merge past its stream wait, [3] every remote shard's candidates seen, [4] merge
  * end; shard_traces[s] (device of shard s, 2 x sm_count x 8 uint64, or NULL; the array itself
  * may be NULL) is attached to shard s's linear as by w8a8_linear_set_trace. */
 w8a8_status w8a8_lmhead_set_trace(w8a8_lmhead *lmhead, unsigned long long *head_trace_dev,

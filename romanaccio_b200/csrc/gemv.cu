@@ -110,6 +110,19 @@ __device__ __forceinline__ void consumer_bar() {
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
 }
 
+// True in the CTA that publishes the activations to other devices (quantise_resident).
+__device__ __forceinline__ bool is_publisher(const GemvArgs &a) {
+  return a.fq.x != nullptr && a.fq.pub_seq != nullptr && blockIdx.x == gridDim.x - 1;
+}
+
+// Producer side of the publisher CTA: no weight copy of this CTA is in flight while its
+// consumers fence the peer stores at system scope (the fence would wait for them too), so the
+// producer waits here until the publication is done.  The publisher owns the grid's last,
+// shortest tile range.
+__device__ __forceinline__ void publish_gate() {
+  asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory");
+}
+
 // Fused prologue: the T fp32 rows quantised into the resident slab xres ([TT][k_pad]; rows >= T
 // and columns >= K zero) by the consumer threads, with the arithmetic of act_quant_kernel's
 // static path: q = round_clamp(x * (s * inv_step), 127), or x * inv_step without smoothing.
@@ -125,7 +138,7 @@ __device__ void quantise_resident(const GemvArgs &a, int8_t *xres, int tid) {
   __shared__ int8_t *s_peer_q[64];
   __shared__ unsigned *s_peer_flag[64];
   __shared__ unsigned s_seq;
-  const bool publisher = blockIdx.x == gridDim.x - 1 && f.pub_seq != nullptr;
+  const bool publisher = is_publisher(a);
   if (publisher) {
     if (tid < f.n_peers) {
       s_peer_q[tid] = f.peers[tid].q;
@@ -195,6 +208,8 @@ __device__ void quantise_resident(const GemvArgs &a, int8_t *xres, int tid) {
     for (int p = 0; p < f.n_peers; ++p) st_relaxed_sys(s_peer_flag[p], e);
     if (f.trace) f.trace[1] = global_timer_ns();
   }
+  // releases the producer warp, which held this CTA's weight copies back (publish_gate)
+  asm volatile("bar.arrive 2, %0;" ::"n"(kThreads) : "memory");
 }
 
 // Shared memory of the top-k epilogue (in the drained stage ring): the warps' staged lists (64
@@ -311,10 +326,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
     // With fused quantisation the consumers read the fp32 activations right after the
     // dependency wait: only one stage goes ahead of them, so that read does not queue behind
     // the whole grid's prefetch.
-    const int early = a.fq.x ? min(1, pre) : pre;
+    const bool publisher = is_publisher(a);
+    const int early = publisher ? 0 : a.fq.x ? min(1, pre) : pre;
     for (int it = 0; it < early; ++it) issue_w(it);
     // Activations (and everything written by the previous kernel) are read only after this.
     pdl_wait();
+    if (publisher) publish_gate();
     for (int it = early; it < pre; ++it) issue_w(it);
     if (a.sync.x_ready) {
       // Remote LM-head shard: GPU 0 stores this forward's activations into our staging buffer

@@ -50,6 +50,32 @@ def test_shard_topk_matches_oracle(ctx, V, K, T, k):
         assert idx[t, 0].item() == O.argmax(lg[t]) + off
 
 
+@pytest.mark.parametrize("T,k", [(1, 64), (3, 40)])
+def test_top_keys_concentrated_in_one_cta(ctx, T, k):
+    """The whole top-k inside one CTA's rows, with exact ties: one per-CTA list holds every
+    winner, so the final selection walks that list far past its head (and breaks the ties by
+    the lowest vocab id)."""
+    V, K = 151936, 1536
+    wq, w_step = lm_params(V, K, seed=77)
+    in_step = 0.031
+    x = synth.activations(T, K, seed=78).numpy()
+    q = O.pack_static(x, in_step, None)
+    # rows 5000..5099: 127 * sign(q[0]) -> the largest accumulators for token 0; pairs of equal rows
+    hot = np.arange(5000, 5100)
+    sign = np.where(q[0] >= 0, 127, -127).astype(np.int8)
+    wq[hot] = sign
+    wq[hot[1::2], :8] = 0  # every other row slightly smaller; duplicates below tie exactly
+    w_step[hot] = 1e-3
+    acc_step = (in_step * w_step).astype(np.float32)
+    shard = rb.LmHeadShard(ctx, wq, acc_step, in_step, row_offset=0)
+    val, idx = shard.forward(torch.from_numpy(x).cuda(), k)
+    lg = oracle_logits(x, wq, in_step, acc_step)
+    wv, wi = O.topk(lg, k)
+    assert np.isin(wi[0], hot).all()
+    assert np.array_equal(idx.cpu().numpy(), wi)
+    assert np.array_equal(val.cpu().numpy(), wv)
+
+
 def test_saturated_int8_logits_tie_rule(ctx):
     """LFM3's INT8 LM head requantises logits to int8 (static out_step), so the largest logits
     saturate at +127 and tie; the lowest vocab id must win (FINDINGS.md:2476-2498 case)."""
