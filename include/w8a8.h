@@ -392,7 +392,7 @@ w8a8_status w8a8_chain_set_trace(w8a8_chain *chain, unsigned long long *trace_de
  * x_dev: fp32 [T, ldx].  in_step: static input step (q = RNE(clamp(x * (1 / in_step), +-127))).
  * Outputs topk_val_dev fp32 [T, k], topk_idx_dev int32 [T, k] (ids = row_offset + n), sorted
  * (value desc, id asc).  Limits: T <= 8, T * round_up(K, 16) <= 128 KiB, and
- * T * (CTAs of the launch, at most two per SM) * k <= 163840 candidate keys; larger requests
+ * T * (CTAs of the launch, at most two per SM) * (k + 1) <= 163840 candidate keys; larger requests
  * return W8A8_ERR_INVALID_ARG with the reason in w8a8_last_error().
  *
  * The first call on a device resolves the scratch array's device address (with that device
@@ -404,6 +404,47 @@ w8a8_status w8a8_lmhead_topk_noalloc(const int8_t *w_dev, int64_t ldw, int32_t K
                                      const float *acc_step_dev, float in_step, const float *x_dev,
                                      int64_t ldx, int32_t T, int32_t k, int32_t row_offset,
                                      float *topk_val_dev, int32_t *topk_idx_dev, void *stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Token sampler over the merged LM-head candidates: Sampler::sample (sampler.cpp:83-179) with
+ * its SamplerParams (sampler.hpp:10-19) and history (Sampler::accept / reset), run on the host
+ * over the k (logit, vocab id) pairs that w8a8_lmhead_forward / w8a8_topk_merge leave, instead
+ * of over the full vocabulary: repetition penalty over the history window, loop breaking,
+ * greedy argmax or temperature, top-k, softmax, min-p, top-p and the draw from std::mt19937
+ * (seed 0 = a random seed, as the reference).  The float steps use the host's libm and the
+ * same order of operations, so a sampler given the same seed returns the reference's token.
+ *
+ * cand_val / cand_id: host arrays of n_cand pairs that are the n_cand largest raw logits of the
+ * vocabulary in (logit desc, id asc) order (the merge's output).  The result is the reference's
+ * whenever the candidates decide it; when they cannot (top_k = 0 or >= vocab with
+ * n_cand < vocab, too few candidates left above the smallest one after the penalties, or a
+ * repeat_penalty below 1 with history tokens outside the candidates) the call returns
+ * W8A8_ERR_NOT_SUPPORTED and consumes no random number, so the caller can retry with more
+ * candidates.  Ties among the top_k kept logits are ordered by id here, while the reference's
+ * std::partial_sort leaves their order unspecified: the drawn token can differ only then.
+ * Host only: no device memory, no CUDA call.
+ * ------------------------------------------------------------------------------------- */
+typedef struct {
+    float    temperature;                 /* <= 0: greedy */
+    int32_t  top_k;                       /* 0 disables */
+    float    top_p;                       /* 1 disables */
+    float    min_p;                       /* 0 disables */
+    float    repeat_penalty;              /* 1 disables */
+    int32_t  repeat_window;
+    int32_t  max_consecutive_duplicates;  /* <= 0 disables */
+    uint32_t seed;                        /* 0: random seed */
+} w8a8_sampler_params;
+
+typedef struct w8a8_sampler w8a8_sampler;
+
+/* NULL params: the reference defaults (0.7, 40, 0.9, 0.05, 1.15, 64, 2, seed 0). */
+w8a8_status w8a8_sampler_create(const w8a8_sampler_params *params, w8a8_sampler **out_sampler);
+void        w8a8_sampler_destroy(w8a8_sampler *sampler);
+w8a8_status w8a8_sampler_accept(w8a8_sampler *sampler, int32_t token_id);
+w8a8_status w8a8_sampler_reset(w8a8_sampler *sampler);
+w8a8_status w8a8_sampler_sample(w8a8_sampler *sampler, const float *cand_val,
+                                const int32_t *cand_id, int32_t n_cand, int32_t vocab_size,
+                                int32_t *token_out);
 
 #ifdef __cplusplus
 } /* extern "C" */

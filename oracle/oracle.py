@@ -44,6 +44,8 @@ _REF_SIGS = {
     "ref_unpack_int8": (C.c_int, [_P, C.c_int, C.c_int, _F, _P, _P, _P]),
     "ref_unpack_int16": (C.c_int, [_P, C.c_int, C.c_int, _F, _P, _P]),
     "ref_sampler_greedy": (C.c_int32, [_P, C.c_size_t]),
+    "ref_sampler_run": (C.c_int, [_F, C.c_int, _F, _F, _F, C.c_int, C.c_int, C.c_uint, _P,
+                                  C.c_int, _P, C.c_int, C.c_size_t, _P]),
     "ref_moe_route": (C.c_int, [_P, C.c_int, C.c_int, _P, _P, C.c_int, C.c_int, C.c_int, _F, _P, _P]),
 }
 
@@ -266,6 +268,20 @@ def ref_unpack_i16(yq: np.ndarray, out_step: float, out_step_chan: np.ndarray | 
 def ref_greedy(logits_row: np.ndarray) -> int:
     lg = np.array(logits_row, dtype=np.float32, copy=True)
     return int(ref().ref_sampler_greedy(_p(lg), lg.shape[0]))
+
+
+def ref_sampler_run(params: dict, history, logits: np.ndarray) -> np.ndarray:
+    """The reference Sampler (sampler.cpp:83-179) over S steps of full logits [S, V]: accepts
+    `history`, then samples each step and accepts the sampled token."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    S, V = lg.shape
+    h = np.ascontiguousarray(np.asarray(history, dtype=np.int32))
+    out = np.empty(S, np.int32)
+    assert ref().ref_sampler_run(
+        params["temperature"], params["top_k"], params["top_p"], params["min_p"],
+        params["repeat_penalty"], params["repeat_window"], params["max_consecutive_duplicates"],
+        params["seed"], _p(h), h.shape[0], _p(lg), S, V, _p(out)) == 0
+    return out
 
 
 def ref_moe_route(hidden: np.ndarray, gate_w: np.ndarray, k: int, bias: np.ndarray | None = None,

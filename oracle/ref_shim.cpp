@@ -8,7 +8,8 @@
 //   src/LFM3/lfm3_v2.cpp   pack_npu_input_int8 (:892-940), pack_npu_input_int8_dyntok
 //                          (:1050-1141), unpack_npu_output_int8 (:971-1008), _int16 (:1011-1046),
 //                          _int8_dyntok (:1143-1183), round_clamp_f32 (:248-257)
-//   src/eswin_runtime/src/nlp/sampler.cpp   Sampler::sample greedy path (:93-103)
+//   src/eswin_runtime/src/nlp/sampler.cpp   Sampler::sample (greedy path :93-103; the whole
+//                                            sampler, :28-179, for the candidate sampler)
 //   src/eswin_runtime/src/llm/moe_router.cpp MoERouter::route (:211-260)
 //
 // lfm3_v2.cpp is a program: its main() is renamed so this shim can include it as a
@@ -103,6 +104,31 @@ int32_t ref_sampler_greedy(float *logits, size_t vocab) {
     p.seed = 1;
     eswin::Sampler s(p);
     return s.sample(logits, vocab);
+}
+
+// A reference Sampler with the given parameters: accepts `history`, then for each of S steps
+// samples a copy of logits[s] (the sampler modifies its input) and accepts the sampled token.
+int ref_sampler_run(float temperature, int top_k, float top_p, float min_p, float penalty,
+                    int window, int max_dup, unsigned seed, const int32_t *history, int n_hist,
+                    const float *logits, int S, size_t vocab, int32_t *out) {
+    eswin::SamplerParams p;
+    p.temperature = temperature;
+    p.top_k = top_k;
+    p.top_p = top_p;
+    p.min_p = min_p;
+    p.repeat_penalty = penalty;
+    p.repeat_window = window;
+    p.max_consecutive_duplicates = max_dup;
+    p.seed = seed;
+    eswin::Sampler s(p);
+    for (int i = 0; i < n_hist; ++i) s.accept(history[i]);
+    std::vector<float> row(vocab);
+    for (int st = 0; st < S; ++st) {
+        std::memcpy(row.data(), logits + static_cast<size_t>(st) * vocab, sizeof(float) * vocab);
+        out[st] = s.sample(row.data(), vocab);
+        s.accept(out[st]);
+    }
+    return 0;
 }
 
 // MoERouter::route over T tokens (softmax scoring, greedy top-k): ids [T, k], weights [T, k].

@@ -8,6 +8,7 @@ from ._lib import (ACT_DYNTOK, ACT_STATIC, DTYPE_FP16, DTYPE_INT8, DTYPE_INT16, 
                    W8A8Error)
 from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
 from .lmhead import LmHeadShard, MultiDeviceLmHead, VocabShardedLmHead, shard_range
+from .sampler import CandidateSampler, SamplingConfig
 
 __all__ = [
     "ACT_DYNTOK", "ACT_STATIC", "DTYPE_FP16", "DTYPE_INT8", "DTYPE_INT16", "OUT_ACC_I32",
@@ -15,5 +16,5 @@ __all__ = [
     "W8A8Error", "Context",
     "SubgraphScaleInfo", "W8A8Linear", "topk_merge", "LmHeadShard", "MultiDeviceLmHead",
     "VocabShardedLmHead",
-    "shard_range",
+    "shard_range", "CandidateSampler", "SamplingConfig",
 ]

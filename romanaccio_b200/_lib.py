@@ -85,6 +85,20 @@ class MoeDesc(C.Structure):
     ]
 
 
+class SamplerParams(C.Structure):
+    """w8a8_sampler_params (mirrors eswin::SamplerParams, sampler.hpp:10-19)."""
+    _fields_ = [
+        ("temperature", C.c_float),
+        ("top_k", C.c_int32),
+        ("top_p", C.c_float),
+        ("min_p", C.c_float),
+        ("repeat_penalty", C.c_float),
+        ("repeat_window", C.c_int32),
+        ("max_consecutive_duplicates", C.c_int32),
+        ("seed", C.c_uint32),
+    ]
+
+
 class ChainStep(C.Structure):
     _fields_ = [
         ("linear", C.c_void_p),
@@ -143,6 +157,11 @@ SIGNATURES = {
     "w8a8_chain_barriers": (_I32, [_P]),
     "w8a8_chain_grid": (_I32, [_P]),
     "w8a8_chain_set_trace": (C.c_int, [_P, _P]),
+    "w8a8_sampler_create": (C.c_int, [C.POINTER(SamplerParams), C.POINTER(_P)]),
+    "w8a8_sampler_destroy": (None, [_P]),
+    "w8a8_sampler_accept": (C.c_int, [_P, _I32]),
+    "w8a8_sampler_reset": (C.c_int, [_P]),
+    "w8a8_sampler_sample": (C.c_int, [_P, _P, _P, _I32, _I32, _P]),
     "w8a8_lmhead_topk_noalloc": (
         C.c_int, [_P, _I64, _I32, _I32, _P, C.c_float, _P, _I64, _I32, _I32, _I32, _P, _P, _P]),
 }
