@@ -406,6 +406,34 @@ w8a8_status w8a8_lmhead_topk_noalloc(const int8_t *w_dev, int64_t ldw, int32_t K
                                      float *topk_val_dev, int32_t *topk_idx_dev, void *stream);
 
 /* ---------------------------------------------------------------------------------------
+ * The steps on either side of each linear of the reference's decode loop, on the GPU with the
+ * reference's float order (sums of squares in its four interleaved chains, then its tail; IEEE
+ * sqrt and division; products left to right), bit-identical to it.  One token row per CTA;
+ * every pointer is device memory; C <= 12288.
+ *
+ * w8a8_rmsnorm_pack_dyntok replaces fused_rms_norm_pack_dyntok_t1 (lfm3_v2.cpp:652-700) for T
+ * rows: inv_rms = 1 / sqrt(sum_sq / C + eps); u = h * inv_rms * smooth[c];
+ * ratio[t] = max(max|u|, 1e-8) / max(in_thresh, 1e-8); q = round_clamp(u * (127 / amax), 127),
+ * and (u_out non-NULL) u_out = h * inv_rms * norm[c].  q / ratio feed w8a8_linear_forward_q in
+ * W8A8_ACT_DYNTOK mode.
+ *
+ * w8a8_post_op_ffn_pack replaces fused_post_op_residual_ffn_pack_mlp_t1 (lfm3_v2.cpp:702-765):
+ * h_mid = h + op_out * inv_rms(op_out) * post_norm[c]; q = round_clamp(h_mid * inv_rms(h_mid)
+ * * ffn_scaled[c], 127) (ffn_scaled folds the FFN norm weight, the smoothing and 1 / in_step:
+ * a static-mode input for the MLP's first linear).  h_mid may alias h.
+ * ------------------------------------------------------------------------------------- */
+w8a8_status w8a8_rmsnorm_pack_dyntok(w8a8_ctx *ctx, const float *h_dev, int64_t ldh, int32_t T,
+                                     int32_t C, const float *norm_dev, const float *smooth_dev,
+                                     float in_thresh, float eps, int8_t *q_dev, int64_t ldq,
+                                     float *ratio_dev, float *u_out_dev, int64_t ldu,
+                                     void *stream);
+w8a8_status w8a8_post_op_ffn_pack(w8a8_ctx *ctx, const float *op_out_dev, int64_t ldo,
+                                  const float *post_norm_dev, const float *h_dev, int64_t ldh,
+                                  int32_t T, int32_t C, const float *ffn_scaled_dev, float eps,
+                                  float *h_mid_dev, int64_t ldm, int8_t *q_dev, int64_t ldq,
+                                  void *stream);
+
+/* ---------------------------------------------------------------------------------------
  * Token sampler over the merged LM-head candidates: Sampler::sample (sampler.cpp:83-179) with
  * its SamplerParams (sampler.hpp:10-19) and history (Sampler::accept / reset), run on the host
  * over the k (logit, vocab id) pairs that w8a8_lmhead_forward / w8a8_topk_merge leave, instead

@@ -32,6 +32,10 @@ _ORACLE_SIGS = {
     "orc_argmax": (C.c_int32, [_P, _I32]),
     "orc_moe_route": (None, [_P, _I64, _I32, _I32, _P, _P, _I32, _I32, _I32, _F, _P, _P]),
     "orc_moe_combine": (None, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P]),
+    "orc_rmsnorm_pack_dyntok": (None, [_P, _I64, _I32, _I32, _P, _P, _F, _F, _P, _I64, _P, _P,
+                                       _I64]),
+    "orc_post_op_ffn_pack": (None, [_P, _I64, _P, _P, _I64, _I32, _I32, _P, _F, _P, _I64, _P,
+                                    _I64]),
     "orc_num_threads": (C.c_int, []),
     "orc_set_threads": (None, [C.c_int]),
     "orc_linear_dyntok_omp": (None, [_P, _I32, _I32, _I32, _P, _P, _F, _P, _I32, _P, _P, _P, _P]),
@@ -44,6 +48,8 @@ _REF_SIGS = {
     "ref_unpack_int8": (C.c_int, [_P, C.c_int, C.c_int, _F, _P, _P, _P]),
     "ref_unpack_int16": (C.c_int, [_P, C.c_int, C.c_int, _F, _P, _P]),
     "ref_sampler_greedy": (C.c_int32, [_P, C.c_size_t]),
+    "ref_rmsnorm_pack_dyntok": (C.c_int, [_P, C.c_int, _P, _P, _F, _F, _P, _P, _P]),
+    "ref_post_op_ffn_pack": (C.c_int, [_P, _P, _P, _P, _P, _P, C.c_int, _F]),
     "ref_sampler_run": (C.c_int, [_F, C.c_int, _F, _F, _F, C.c_int, C.c_int, C.c_uint, _P,
                                   C.c_int, _P, C.c_int, C.c_size_t, _P]),
     "ref_moe_route": (C.c_int, [_P, C.c_int, C.c_int, _P, _P, C.c_int, C.c_int, C.c_int, _F, _P, _P]),
@@ -204,6 +210,56 @@ def moe_combine(yq: np.ndarray, idx: np.ndarray, w: np.ndarray, out_step_chan: n
     out = np.empty((T, H), np.float32)
     lib().orc_moe_combine(_p(y), T, k, slots, n_routed, H, _p(ix), _p(ww), _p(osc), _p(out))
     return out
+
+
+def rmsnorm_pack_dyntok(h: np.ndarray, norm: np.ndarray, smooth: np.ndarray, in_thresh: float,
+                        eps: float = 1e-5):
+    """fused_rms_norm_pack_dyntok_t1 per row of h [T, C] -> (q [T, C], ratio [T], u_out [T, C])."""
+    hh = _c(h, np.float32)
+    T, Cn = hh.shape
+    q = np.empty((T, Cn), np.int8)
+    ratio = np.empty(T, np.float32)
+    u = np.empty((T, Cn), np.float32)
+    lib().orc_rmsnorm_pack_dyntok(_p(hh), Cn, T, Cn, _p(_c(norm, np.float32)),
+                                  _p(_c(smooth, np.float32)), float(in_thresh), float(eps), _p(q),
+                                  Cn, _p(ratio), _p(u), Cn)
+    return q, ratio, u
+
+
+def post_op_ffn_pack(op_out: np.ndarray, post_norm: np.ndarray, h: np.ndarray,
+                     ffn_scaled: np.ndarray, eps: float = 1e-5):
+    """fused_post_op_residual_ffn_pack_mlp_t1 per row -> (h_mid [T, C], q [T, C])."""
+    o = _c(op_out, np.float32)
+    hh = _c(h, np.float32)
+    T, Cn = o.shape
+    m = np.empty((T, Cn), np.float32)
+    q = np.empty((T, Cn), np.int8)
+    lib().orc_post_op_ffn_pack(_p(o), Cn, _p(_c(post_norm, np.float32)), _p(hh), Cn, T, Cn,
+                               _p(_c(ffn_scaled, np.float32)), float(eps), _p(m), Cn, _p(q), Cn)
+    return m, q
+
+
+def ref_rmsnorm_pack_dyntok(h_row, norm, smooth, in_thresh: float, eps: float = 1e-5):
+    hh = _c(h_row, np.float32)
+    Cn = hh.shape[0]
+    q = np.empty(Cn, np.int8)
+    ratio = np.empty(1, np.float32)
+    u = np.empty(Cn, np.float32)
+    assert ref().ref_rmsnorm_pack_dyntok(_p(hh), Cn, _p(_c(norm, np.float32)),
+                                         _p(_c(smooth, np.float32)), float(in_thresh), float(eps),
+                                         _p(q), _p(ratio), _p(u)) == 0
+    return q, ratio[0], u
+
+
+def ref_post_op_ffn_pack(op_row, post_norm, h_row, ffn_scaled, eps: float = 1e-5):
+    o = _c(op_row, np.float32)
+    Cn = o.shape[0]
+    m = np.empty(Cn, np.float32)
+    q = np.empty(Cn, np.int8)
+    assert ref().ref_post_op_ffn_pack(_p(o), _p(_c(post_norm, np.float32)), _p(_c(h_row, np.float32)),
+                                      _p(m), _p(_c(ffn_scaled, np.float32)), _p(q), Cn,
+                                      float(eps)) == 0
+    return m, q
 
 
 def linear(x: np.ndarray, wq: np.ndarray, quant_m: np.ndarray, trunc: int, out_step_chan: np.ndarray,

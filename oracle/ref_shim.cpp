@@ -131,6 +131,21 @@ int ref_sampler_run(float temperature, int top_k, float top_p, float min_p, floa
     return 0;
 }
 
+// fused_rms_norm_pack_dyntok_t1 (T = 1 row): q [C], ratio [1], u_out [C] or NULL.
+int ref_rmsnorm_pack_dyntok(const float *h, int C, const float *norm, const float *smooth,
+                            float in_thresh, float eps, int8_t *q, float *ratio, float *u_out) {
+    if (C > 4096) return -1;  // the reference's u_smooth buffer
+    fused_rms_norm_pack_dyntok_t1(h, norm, smooth, q, C, in_thresh, ratio, u_out, eps);
+    return 0;
+}
+
+// fused_post_op_residual_ffn_pack_mlp_t1 (T = 1 row): h_mid [C], q [C].
+int ref_post_op_ffn_pack(const float *op_out, const float *post_norm, const float *h, float *h_mid,
+                         const float *ffn_scaled, int8_t *q, int C, float eps) {
+    fused_post_op_residual_ffn_pack_mlp_t1(op_out, post_norm, h, h_mid, ffn_scaled, q, C, eps);
+    return 0;
+}
+
 // MoERouter::route over T tokens (softmax scoring, greedy top-k): ids [T, k], weights [T, k].
 int ref_moe_route(const float *hidden, int T, int H, const float *gate_w, const float *bias, int E,
                   int k, int norm_topk, float scaling, int32_t *idx, float *w) {

@@ -20,6 +20,8 @@
  *                     ties; top-k ordered value desc, then id asc)
  *   orc_moe_route     src/eswin_runtime/src/llm/moe_router.cpp:92-130, 211-260 (MoERouter::route)
  *   orc_moe_combine   src/LFM2.5-8B-A1B/lfm2_moe.cpp:2300-2318 (weighted expert combine)
+ *   orc_rmsnorm_pack_dyntok  src/LFM3/lfm3_v2.cpp:652-700 fused_rms_norm_pack_dyntok_t1
+ *   orc_post_op_ffn_pack     src/LFM3/lfm3_v2.cpp:702-765 fused_post_op_residual_ffn_pack_mlp_t1
  *
  * Compile without fast-math and with -ffp-contract=off so every float step rounds like the
  * reference's scalar C++.
@@ -272,5 +274,65 @@ void orc_moe_combine(const int32_t *yq, int32_t T, int32_t k, int32_t slots, int
             }
             out[(int64_t)t * H + c] = acc;
         }
+    }
+}
+
+/* Sum of squares in the reference's order (lfm3_v2.cpp:659-667): four interleaved partial sums
+ * over the multiple-of-4 prefix, combined as (s0 + s1) + (s2 + s3), then the tail one by one. */
+static float orc_sum_sq4(const float *v, int32_t C) {
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    int32_t c = 0;
+    for (; c + 3 < C; c += 4) {
+        s0 += v[c] * v[c];
+        s1 += v[c + 1] * v[c + 1];
+        s2 += v[c + 2] * v[c + 2];
+        s3 += v[c + 3] * v[c + 3];
+    }
+    float sum = (s0 + s1) + (s2 + s3);
+    for (; c < C; ++c) sum += v[c] * v[c];
+    return sum;
+}
+
+/* fused_rms_norm_pack_dyntok_t1 (lfm3_v2.cpp:657-700), row by row of [T, C]:
+ * inv_rms = 1 / sqrt(sum_sq / C + eps); u = h * inv_rms * smooth; amax = max(max|u|, 1e-8);
+ * ratio = amax / max(in_thresh, 1e-8); q = round_clamp(u * (127 / amax), 127);
+ * u_out (when given) = h * inv_rms * norm. */
+void orc_rmsnorm_pack_dyntok(const float *h, int64_t ldh, int32_t T, int32_t C, const float *norm,
+                             const float *smooth, float in_thresh, float eps, int8_t *q,
+                             int64_t ldq, float *ratio, float *u_out, int64_t ldu) {
+    for (int32_t t = 0; t < T; ++t) {
+        const float *hr = h + (int64_t)t * ldh;
+        const float inv_rms = 1.0f / sqrtf(orc_sum_sq4(hr, C) / (float)C + eps);
+        float amax = 0.0f;
+        for (int32_t i = 0; i < C; ++i) {
+            if (u_out) u_out[(int64_t)t * ldu + i] = hr[i] * inv_rms * norm[i];
+            const float a = fabsf(hr[i] * inv_rms * smooth[i]);
+            if (a > amax) amax = a;
+        }
+        amax = amax < 1e-8f ? 1e-8f : amax;
+        ratio[t] = amax / (in_thresh < 1e-8f ? 1e-8f : in_thresh);
+        const float inv_step = 127.0f / amax;
+        for (int32_t i = 0; i < C; ++i)
+            q[(int64_t)t * ldq + i] = (int8_t)orc_round_clamp(hr[i] * inv_rms * smooth[i] * inv_step,
+                                                              127.0f);
+    }
+}
+
+/* fused_post_op_residual_ffn_pack_mlp_t1 (lfm3_v2.cpp:702-765), row by row:
+ * inv_rms_op = 1 / sqrt(sum_sq(op_out) / C + eps); h_mid = h + op_out * inv_rms_op * post_norm;
+ * inv_rms_ffn = 1 / sqrt(sum_sq(h_mid) / C + eps); q = round_clamp(h_mid * inv_rms_ffn * ffn_scaled,
+ * 127) (ffn_scaled carries the norm weight, the smoothing and 1 / in_step). */
+void orc_post_op_ffn_pack(const float *op_out, int64_t ldo, const float *post_norm, const float *h,
+                          int64_t ldh, int32_t T, int32_t C, const float *ffn_scaled, float eps,
+                          float *h_mid, int64_t ldm, int8_t *q, int64_t ldq) {
+    for (int32_t t = 0; t < T; ++t) {
+        const float *o = op_out + (int64_t)t * ldo;
+        const float *hr = h + (int64_t)t * ldh;
+        float *m = h_mid + (int64_t)t * ldm;
+        const float inv_op = 1.0f / sqrtf(orc_sum_sq4(o, C) / (float)C + eps);
+        for (int32_t i = 0; i < C; ++i) m[i] = hr[i] + o[i] * inv_op * post_norm[i];
+        const float inv_ffn = 1.0f / sqrtf(orc_sum_sq4(m, C) / (float)C + eps);
+        for (int32_t i = 0; i < C; ++i)
+            q[(int64_t)t * ldq + i] = (int8_t)orc_round_clamp(m[i] * inv_ffn * ffn_scaled[i], 127.0f);
     }
 }

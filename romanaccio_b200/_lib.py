@@ -157,6 +157,10 @@ SIGNATURES = {
     "w8a8_chain_barriers": (_I32, [_P]),
     "w8a8_chain_grid": (_I32, [_P]),
     "w8a8_chain_set_trace": (C.c_int, [_P, _P]),
+    "w8a8_rmsnorm_pack_dyntok": (C.c_int, [_P, _P, _I64, _I32, _I32, _P, _P, C.c_float,
+                                         C.c_float, _P, _I64, _P, _P, _I64, _P]),
+    "w8a8_post_op_ffn_pack": (C.c_int, [_P, _P, _I64, _P, _P, _I64, _I32, _I32, _P, C.c_float,
+                                        _P, _I64, _P, _I64, _P]),
     "w8a8_sampler_create": (C.c_int, [C.POINTER(SamplerParams), C.POINTER(_P)]),
     "w8a8_sampler_destroy": (None, [_P]),
     "w8a8_sampler_accept": (C.c_int, [_P, _I32]),

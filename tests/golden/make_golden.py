@@ -183,6 +183,28 @@ def make_moe_route(path: Path) -> None:
     print(f"{path.name}: ids {idx_raw[0].tolist()}")
 
 
+def make_norm_pack(path: Path) -> None:
+    """fused_rms_norm_pack_dyntok_t1 and fused_post_op_residual_ffn_pack_mlp_t1 run by the
+    reference on seeded rows (a multiple-of-4 width and one with a 3-element tail)."""
+    rng = np.random.default_rng(41)
+    out = {}
+    for tag, C in (("c1536", 1536), ("c579", 579)):
+        h = (rng.standard_normal(C) * 4).astype(np.float32)
+        norm = (rng.standard_normal(C) * 0.3 + 1).astype(np.float32)
+        smooth = (rng.random(C) * 2 + 0.05).astype(np.float32)
+        op = (rng.standard_normal(C) * 6).astype(np.float32)
+        post = (rng.standard_normal(C) * 0.2 + 1).astype(np.float32)
+        ffn = (rng.random(C) * 25).astype(np.float32)
+        q, ratio, u = O.ref_rmsnorm_pack_dyntok(h, norm, smooth, 7.5)
+        m, q2 = O.ref_post_op_ffn_pack(op, post, h, ffn)
+        out.update({f"{tag}_h": h, f"{tag}_norm": norm, f"{tag}_smooth": smooth,
+                    f"{tag}_op": op, f"{tag}_post": post, f"{tag}_ffn": ffn, f"{tag}_q": q,
+                    f"{tag}_ratio": np.float32(ratio), f"{tag}_u": u, f"{tag}_hmid": m,
+                    f"{tag}_q2": q2})
+    np.savez_compressed(path, in_thresh=np.float32(7.5), **out)
+    print(f"{path.name}: ratio {out['c1536_ratio']}")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -193,6 +215,9 @@ def main() -> None:
     if args.only == "moe":
         make_moe_route(HERE / "moe_route.npz")
         return
+    if args.only == "norm":
+        make_norm_pack(HERE / "norm_pack.npz")
+        return
     builder = import_builder(ref)
     make_quant_linear(builder, 136, 160, 22, 11, HERE / "quant_linear_n136_k160_t22.npz")
     make_quant_linear(builder, 520, 96, 23, 12, HERE / "quant_linear_n520_k96_t23.npz")
@@ -201,6 +226,7 @@ def main() -> None:
     make_requant_kat(HERE / "requant_kat.npz")
     make_sampler_kat(HERE / "sampler_kat.npz")
     make_moe_route(HERE / "moe_route.npz")
+    make_norm_pack(HERE / "norm_pack.npz")
 
 
 if __name__ == "__main__":
