@@ -205,6 +205,33 @@ def make_norm_pack(path: Path) -> None:
     print(f"{path.name}: ratio {out['c1536_ratio']}")
 
 
+def make_nvdla_tiles(builder, path: Path) -> None:
+    """The reference's NVDLA weight tiling (tile_int8_slice / tile_int16_slice) of seeded slices,
+    with the row-major quantised weights computed from the same formula, for the package
+    reader's un-tiling."""
+    rng = np.random.default_rng(51)
+    out = {}
+    for tag, (m, k) in (("a", (512, 96)), ("b", (16, 200)), ("c", (24, 96))):
+        w = rng.standard_normal((m, k)) * 0.05
+        tiled, step = builder.tile_int8_slice(w)
+        w64 = w.astype(np.float64)
+        st = np.maximum(np.max(np.abs(w64), axis=1, keepdims=True), 1e-12) / 127.0
+        q = np.clip(np.round(w64 / st), -127, 127).astype(np.int8)
+        out[f"i8_{tag}_tiled"] = np.frombuffer(tiled, np.int8)
+        out[f"i8_{tag}_q"] = q
+        out[f"i8_{tag}_step"] = step
+    for tag, (m, k) in (("a", (16, 100)), ("b", (8, 48))):
+        w = rng.standard_normal((m, k)) * 0.05
+        tiled, step = builder.tile_int16_slice(w)
+        w64 = w.astype(np.float64)
+        st = np.maximum(np.max(np.abs(w64), axis=1, keepdims=True), 1e-12) / 32767.0
+        q = np.clip(np.round(w64 / st), -32767, 32767).astype(np.int16)
+        out[f"i16_{tag}_tiled"] = np.frombuffer(tiled, np.int16)
+        out[f"i16_{tag}_q"] = q
+    np.savez_compressed(path, **out)
+    print(f"{path.name}: {len(out)} arrays")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -218,6 +245,9 @@ def main() -> None:
     if args.only == "norm":
         make_norm_pack(HERE / "norm_pack.npz")
         return
+    if args.only == "tiles":
+        make_nvdla_tiles(import_builder(ref), HERE / "nvdla_tiles.npz")
+        return
     builder = import_builder(ref)
     make_quant_linear(builder, 136, 160, 22, 11, HERE / "quant_linear_n136_k160_t22.npz")
     make_quant_linear(builder, 520, 96, 23, 12, HERE / "quant_linear_n520_k96_t23.npz")
@@ -227,6 +257,7 @@ def main() -> None:
     make_sampler_kat(HERE / "sampler_kat.npz")
     make_moe_route(HERE / "moe_route.npz")
     make_norm_pack(HERE / "norm_pack.npz")
+    make_nvdla_tiles(builder, HERE / "nvdla_tiles.npz")
 
 
 if __name__ == "__main__":
