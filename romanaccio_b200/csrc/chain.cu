@@ -30,6 +30,9 @@ constexpr int kCW = 8;              // consumer warps
 constexpr int kCT = kCW * 32;       // consumer threads
 constexpr int kThreads = kCT + 32;  // + producer warp
 constexpr int kMaxStages = 8;
+// activation float4 loads in flight per thread in quantise_input (more registers at TT = 1)
+template <int TT>
+__host__ __device__ constexpr int quant_batch() { return TT == 1 ? 6 : 4; }
 
 struct ChainArgs {
   const ChainOp *ops;
@@ -103,15 +106,14 @@ __device__ void quantise_input(const ChainOp &op, int T, int8_t *xq, int kpad_ma
   const int warp = tid >> 5, lane = tid & 31;
   const bool vec = op.vec_x;
   float inv_r[TT];
-  if (op.act_mode == kActDyntok && op.amax_src) {
-    // every thread derives the inverse steps itself: no barrier before the x pass
+  // amax already reduced by the producing step: every thread derives the inverse steps itself
+  // (no barrier before the x pass).  The loads are issued here; the divisions wait until the
+  // first activation loads of the token are in flight (see `lazy` below), so the two L2 round
+  // trips overlap.
+  const bool lazy = op.act_mode == kActDyntok && op.amax_src != nullptr;
+  if (lazy) {
 #pragma unroll
-    for (int t = 0; t < TT; ++t) {
-      float m = t < T ? __ldcg(op.amax_src + t) : 1.0f;
-      m = (m < 1e-8f) ? 1e-8f : m;
-      inv_r[t] = 127.0f / m;
-      if (tid == t && t < T) s_ratio[t] = m / op.safe_thresh;
-    }
+    for (int t = 0; t < TT; ++t) inv_r[t] = t < T ? __ldcg(op.amax_src + t) : 1.0f;
   } else if (op.act_mode == kActDyntok) {
     float amax[TT];
 #pragma unroll
@@ -174,35 +176,51 @@ __device__ void quantise_input(const ChainOp &op, int T, int8_t *xq, int kpad_ma
 #pragma unroll
     for (int t = 0; t < TT; ++t) inv_r[t] = op.inv_step;
   }
+  // the reference's amax floor, ratio and inverse step from a reduced amax
+  auto derive = [&](int t, float m) {
+    m = (m < 1e-8f) ? 1e-8f : m;
+    if (tid == t) s_ratio[t] = m / op.safe_thresh;
+    return 127.0f / m;
+  };
 #pragma unroll
   for (int t = 0; t < TT; ++t) {
     if (t >= T) break;
-    const float inv = inv_r[t];
+    float inv = inv_r[t];
+    bool pending = lazy;
     const float *xr = op.x + t * op.ldx;
     int8_t *q = xq + t * kpad_max;
     if (vec) {
-      // 4 independent 16-byte loads in flight per thread before any use
+      // QB independent 16-byte loads (and their smoothing factors) in flight per thread before
+      // any use: K = 8960 takes two batches of L2 round trips instead of three
       const int n4 = op.K / 4;
       const bool smooth = op.inv_smooth != nullptr;
       const float4 *x4 = reinterpret_cast<const float4 *>(xr);
       const float4 *s4 = reinterpret_cast<const float4 *>(op.inv_smooth);
-      for (int c0 = tid; c0 < n4; c0 += 4 * kCT) {
-        float4 v[4], sv[4];
+      constexpr int QB = quant_batch<TT>();
+      for (int c0 = tid; c0 < n4; c0 += QB * kCT) {
+        float4 v[QB], sv[QB];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < QB; ++u) {
           const int c = c0 + u * kCT;
           v[u] = c < n4 ? __ldcg(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-          sv[u] = c0 == tid ? s_pre[u]
-                            : ((smooth && c < n4) ? s4[c] : make_float4(0.f, 0.f, 0.f, 0.f));
+          sv[u] = (c0 == tid && u < 4)
+                      ? s_pre[u & 3]
+                      : ((smooth && c < n4) ? s4[c] : make_float4(0.f, 0.f, 0.f, 0.f));
+        }
+        if (pending) {
+          inv = derive(t, inv_r[t]);
+          pending = false;
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < QB; ++u) {
           const int c = c0 + u * kCT;
           if (c < n4) reinterpret_cast<char4 *>(q)[c] = quant4(v[u], sv[u], smooth, inv);
         }
       }
+      if (pending) inv = derive(t, inv_r[t]);  // (this thread had no column)
       for (int c = (op.K & ~3) + tid; c < op.k_pad; c += kCT) q[c] = 0;
     } else {
+      if (pending) inv = derive(t, inv_r[t]);
       for (int c = tid; c < op.k_pad; c += kCT) {
         int8_t v = 0;
         if (c < op.K) {
