@@ -205,6 +205,26 @@ def make_norm_pack(path: Path) -> None:
     print(f"{path.name}: ratio {out['c1536_ratio']}")
 
 
+def make_sampler_seq(path: Path) -> None:
+    """Token sequences drawn by the reference Sampler (full logits, seeded) for the candidate
+    sampler's parity without the reference built."""
+    rng = np.random.default_rng(61)
+    V, S = 2000, 16
+    logits = (rng.standard_normal((S, V)) * 3).astype(np.float32)
+    history = np.argsort(-logits[0])[:10].astype(np.int32)
+    cfgs = {"default": dict(temperature=0.7, top_k=40, top_p=0.9, min_p=0.05, repeat_penalty=1.15,
+                            repeat_window=64, max_consecutive_duplicates=2, seed=1234),
+            "greedy": dict(temperature=0.0, top_k=40, top_p=0.9, min_p=0.05, repeat_penalty=1.3,
+                           repeat_window=8, max_consecutive_duplicates=2, seed=1)}
+    out = {"logits": logits, "history": history}
+    for name, c in cfgs.items():
+        out[f"{name}_tokens"] = O.ref_sampler_run(c, history, logits)
+        for key, val in c.items():
+            out[f"{name}_{key}"] = np.asarray(val)
+    np.savez_compressed(path, **out)
+    print(f"{path.name}: default {out['default_tokens'][:6].tolist()}")
+
+
 def make_nvdla_tiles(builder, path: Path) -> None:
     """The reference's NVDLA weight tiling (tile_int8_slice / tile_int16_slice) of seeded slices,
     with the row-major quantised weights computed from the same formula, for the package
@@ -245,6 +265,9 @@ def main() -> None:
     if args.only == "norm":
         make_norm_pack(HERE / "norm_pack.npz")
         return
+    if args.only == "sampler":
+        make_sampler_seq(HERE / "sampler_seq.npz")
+        return
     if args.only == "tiles":
         make_nvdla_tiles(import_builder(ref), HERE / "nvdla_tiles.npz")
         return
@@ -258,6 +281,7 @@ def main() -> None:
     make_moe_route(HERE / "moe_route.npz")
     make_norm_pack(HERE / "norm_pack.npz")
     make_nvdla_tiles(builder, HERE / "nvdla_tiles.npz")
+    make_sampler_seq(HERE / "sampler_seq.npz")
 
 
 if __name__ == "__main__":

@@ -111,6 +111,19 @@ def test_undecided_draws_nothing():
     assert np.array_equal(np.array(got, np.int32), want)
 
 
+@pytest.mark.parametrize("name", ["default", "greedy"])
+def test_candidates_match_reference_fixture(name):
+    """Token sequences the reference drew (tests/golden/sampler_seq.npz), reproduced from the
+    64 largest logits of each step."""
+    from pathlib import Path
+    g = np.load(Path(__file__).resolve().parent / "golden" / "sampler_seq.npz")
+    keys = ("temperature", "top_k", "top_p", "min_p", "repeat_penalty", "repeat_window",
+            "max_consecutive_duplicates", "seed")
+    cfg = SamplingConfig(**{k: g[f"{name}_{k}"].item() for k in keys})
+    got = run_ours(cfg, g["history"].tolist(), g["logits"], n_cand=64)
+    assert np.array_equal(got, g[f"{name}_tokens"])
+
+
 def test_greedy_without_reference():
     """Greedy decoding is the lowest id among the largest candidates, and the loop breaker
     blocks a token repeated max_consecutive_duplicates times."""
