@@ -14,8 +14,9 @@
 // per step: wait at a grid barrier when the step reads an earlier step's output, quantise the
 // step's fp32 input into shared memory (dyntok amax / static step, the reference's
 // pack_npu_input_int8[_dyntok] arithmetic), run dp4a over the landed slabs, and apply the
-// requant / unpack epilogue (or keep LM-head logits on chip for the grid top-k of topk.cuh).  The grid barrier is a per-step arrival counter (release: fence + atomic
-// add; acquire: ld.acquire spin, bounded by 2 s of %globaltimer).
+// requant / unpack epilogue (or keep LM-head logits on chip for the grid top-k of topk.cuh).
+// The grid barrier is a per-step arrival counter (release: fence + atomic add; acquire:
+// ld.acquire spin, bounded by 2 s of %globaltimer).
 #include "common.cuh"
 #include "kernels.h"
 #include "topk.cuh"
