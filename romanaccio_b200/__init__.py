@@ -8,6 +8,8 @@ from ._lib import (ACT_DYNTOK, ACT_STATIC, DTYPE_FP16, DTYPE_INT8, DTYPE_INT16, 
                    W8A8Error)
 from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
 from .lmhead import LmHeadShard, MultiDeviceLmHead, VocabShardedLmHead, shard_range
+from .norm import post_op_ffn_pack, rmsnorm_pack_dyntok
+from .package import load_quant_scales, read_weight_region, untile_int8, untile_int16
 from .sampler import CandidateSampler, SamplingConfig
 
 __all__ = [
@@ -16,5 +18,6 @@ __all__ = [
     "W8A8Error", "Context",
     "SubgraphScaleInfo", "W8A8Linear", "topk_merge", "LmHeadShard", "MultiDeviceLmHead",
     "VocabShardedLmHead",
-    "shard_range", "CandidateSampler", "SamplingConfig",
+    "shard_range", "CandidateSampler", "SamplingConfig", "rmsnorm_pack_dyntok",
+    "post_op_ffn_pack", "load_quant_scales", "read_weight_region", "untile_int8", "untile_int16",
 ]
