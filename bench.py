@@ -622,6 +622,44 @@ def run_prefill(args) -> None:
 
 
 # ---------------------------------------------------------------------------- LM-head latency
+def lmhead_cpu_baseline(wq: np.ndarray, acc_step: np.ndarray, in_step: float, h: np.ndarray,
+                        k: int, seconds: float) -> dict:
+    """The LM head on the host cores: the C restatement (OpenMP over every core this process may
+    use) of the static input quantisation, the int8 GEMV over the whole vocabulary and the
+    top-k, timed over repeated tokens for about `seconds` (the reference's own host LM head,
+    TransformerSession's fp32 fallback GEMV + Sampler::sample over V, is the same loop shape)."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    import ctypes as C
+    lib = O.lib()
+    cores = len(os.sched_getaffinity(0))
+    lib.orc_set_threads(cores)
+    T, K = h.shape
+    V = wq.shape[0]
+    x = np.ascontiguousarray(h, dtype=np.float32)
+    w = np.ascontiguousarray(wq)
+    st = np.ascontiguousarray(acc_step, dtype=np.float32)
+    logits = np.empty((T, V), np.float32)
+    q = np.empty((T, K), np.int8)
+    val = np.empty((T, k), np.float32)
+    idx = np.empty((T, k), np.int32)
+
+    def run():
+        lib.orc_lmhead_topk_omp(x.ctypes.data, T, K, V, w.ctypes.data, C.c_float(in_step),
+                                st.ctypes.data, k, logits.ctypes.data, q.ctypes.data,
+                                val.ctypes.data, idx.ctypes.data)
+
+    run()
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n < 3:
+        run()
+        n += 1
+    us = (time.perf_counter() - t0) / n * 1e6
+    return {"value": us, "unit": "us", "cores": cores, "kind": "port",
+            "sample": f"{n} LM-head steps ({T} token(s), {K}x{V} int8 + top-{k}), C restatement, "
+                      "OpenMP", "ids": idx[:, 0].tolist()}
+
+
 LMHEAD_METRIC = ("LM-head latency per decode step (hidden state in HBM -> top-40 ids and argmax "
                  "on the host), vocab-sharded over n GPUs of one process")
 
@@ -722,6 +760,11 @@ def run_lmhead(args) -> None:
                 "d2h_bytes_per_step": T * 4},
         "gpu_launches": counts[-1] + 2,
     }
+    if not args.no_cpu:
+        cpu = lmhead_cpu_baseline(wq, acc_step, in_step, h.cpu().numpy(), k, args.cpu_seconds)
+        cpu_ids = cpu.pop("ids")
+        cpu["ids_equal_gpu"] = cpu_ids == ids_ref.tolist()
+        line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
 
 
