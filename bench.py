@@ -31,15 +31,14 @@ import torch
 ROOT = Path(__file__).resolve().parent
 METRIC = "decode tok/s & HBM GB/s of W8A8 linear + sharded LM-head argmax, 1/2/4/8 B200"
 WORKLOAD = "qwen2.5-1.5b-shaped W8A8 decode: 28 x {qkv,o,gate_up,down} + LM head 1536x151936 top-40"
-# DRAM bytes (read + write) per launch of the gate_up GEMV at T=1 from one ncu capture
-# (profiles/gemv_w8a8_gate_up_qwen15b_t1.md): 27.666688 MB read + 0 B written.
+# DRAM bytes (read + write) per launch of the gate_up GEMV at T=1, from one ncu capture of
+# that launch: 27.666688 MB read + 0 B written.
 GEMV_TRAFFIC_BYTES = 27666688
-# DRAM bytes per algorithmic byte of the chain kernel from one ncu capture of a 4-layer,
-# 1024-vocab chain (profiles/chain_kernel_qwen15b_4layer.md): 189.84 MB read / 188.7 MB.
+# DRAM bytes per algorithmic byte of the chain kernel, from one ncu capture of a 4-layer,
+# 1024-vocab chain: 189.84 MB read / 188.7 MB algorithmic.
 CHAIN_TRAFFIC_RATIO = 1.006
-# DRAM bytes (read + write) of one launch of the M=2048, K=N=8192 tensor-core GEMM from one ncu
-# capture (profiles/gemm_w8a8_tc_prefill_2048x8192x8192.md): 84.005632 MB read + 6.348032 MB
-# written.
+# DRAM bytes (read + write) of one launch of the M=2048, K=N=8192 tensor-core GEMM, from one ncu
+# capture of that launch: 84.005632 MB read + 6.348032 MB written.
 PREFILL_GEMM_TRAFFIC_BYTES = 90353664
 
 
@@ -324,7 +323,7 @@ def run_ours(args) -> None:
     if stack.chain is not None:
         # dominant (only) kernel of the step: the persistent chain kernel; one launch moves the
         # whole step's algorithmic bytes (world == 1: linears + LM head)
-        chain_bytes = sb.linear + (sb.lm_head if world == 1 else 0)
+        chain_bytes = sb.linear + (sb.lm_head if stack.chain_lm else 0)
         for _ in range(3):
             stack.chain.forward()
         torch.cuda.synchronize()

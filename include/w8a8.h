@@ -395,8 +395,11 @@ w8a8_status w8a8_chain_set_trace(w8a8_chain *chain, unsigned long long *trace_de
  * T * (CTAs of the launch, at most two per SM) * (k + 1) <= 163840 candidate keys; larger requests
  * return W8A8_ERR_INVALID_ARG with the reason in w8a8_last_error().
  *
- * The first call on a device resolves the scratch array's device address (with that device
- * current); make that first call before any stream capture.  Every call on a device shares the
+ * The first call on a device is a set-up call: it resolves the scratch array's device address
+ * (with that device current) and, under CUDA's default lazy module loading, makes the driver
+ * load the library's kernels on that device, which allocates device memory inside the driver.
+ * Make that first call (a warm-up call) before any stream capture and outside any context where
+ * allocating is not allowed; later calls allocate nothing.  Every call on a device shares the
  * array and it keeps the last call's contents: calls whose executions overlap on the GPU race
  * and corrupt each other's results, so order them on one stream.  A bounded in-kernel wait that
  * runs out is not reported by this entry point (it has no context). */

@@ -31,9 +31,10 @@ constexpr int kCW = 8;              // consumer warps
 constexpr int kCT = kCW * 32;       // consumer threads
 constexpr int kThreads = kCT + 32;  // + producer warp
 constexpr int kMaxStages = 8;
-// activation float4 loads in flight per thread in quantise_input (more registers at TT = 1)
+// activation float4 loads in flight per thread in quantise_input (more registers at TT = 1,
+// fewer at TT = 8, whose accumulators and activation vectors leave less room)
 template <int TT>
-__host__ __device__ constexpr int quant_batch() { return TT == 1 ? 6 : 4; }
+__host__ __device__ constexpr int quant_batch() { return TT == 1 ? 6 : TT == 8 ? 3 : 4; }
 
 struct ChainArgs {
   const ChainOp *ops;
@@ -404,10 +405,12 @@ __device__ void consume_dispatch(const ChainOp &op, const ChainArgs &a, int tb, 
                                  const uint8_t *ring, const int8_t *xq, uint64_t *bars,
                                  const float *s_ratio, uint64_t *cand, int *s_amax,
                                  const EpiSmem &ep, int tid, bool &ok, unsigned long long *tr) {
+  // (the planner never gives TT = 8 more than 2 rows per warp: 4 x 8 accumulators spill)
+  constexpr int kRpwMax = TT >= 8 ? 2 : 4;
   switch (op.rpw) {
     case 1: consume_tiles<TT, 1, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, ep, tid, ok, tr); break;
     case 2: consume_tiles<TT, 2, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, ep, tid, ok, tr); break;
-    default: consume_tiles<TT, 4, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, ep, tid, ok, tr); break;
+    default: consume_tiles<TT, kRpwMax, TOPK>(op, a, tb, te, it, ring, xq, bars, s_ratio, cand, s_amax, ep, tid, ok, tr); break;
   }
 }
 
@@ -677,7 +680,7 @@ bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, Chain
       // whole-row tiles: a tile is one contiguous rb x k_pad block (one bulk copy per stage)
       op.rpw = 1;
       for (int r : {4, 2})
-        if (8 * r * op.k_pad <= kMaxStage && tiles(8 * r) >= min_tiles) {
+        if ((r < 4 || p.tt < 8) && 8 * r * op.k_pad <= kMaxStage && tiles(8 * r) >= min_tiles) {
           op.rpw = r;
           break;
         }

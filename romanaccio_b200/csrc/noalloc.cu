@@ -14,6 +14,12 @@
 // calls whose executions overlap on the GPU (different streams, or different host threads
 // without ordering) race and corrupt each other's results; the arrival counter, which must
 // start at zero, is cleared on the call's stream before each launch.
+//
+// The first call on a device is a set-up call: it resolves the array's device address and,
+// under CUDA's default lazy module loading, makes the driver load this library's kernels on that
+// device, which allocates device memory inside the driver.  Make it (a warm-up call) before any
+// stream capture and outside any context where allocating is not allowed; later calls allocate
+// nothing.
 #include "../../include/w8a8.h"
 #include "kernels.h"
 
@@ -135,7 +141,10 @@ extern "C" w8a8_status w8a8_lmhead_topk_noalloc(const int8_t *w_dev, int64_t ldw
   uint64_t *lists = reinterpret_cast<uint64_t *>(slot.scratch + kXqBytes + kMiscBytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-  if (cudaMemsetAsync(counter, 0, sizeof(unsigned), s) != cudaSuccess)
+  // the arrival counter must start at zero; the error word (which no call reads back) is
+  // cleared with it so a bounded wait that ran out in an earlier call leaves nothing behind
+  static_assert(128 + sizeof(int) <= kMiscBytes, "the error word lies inside the cleared range");
+  if (cudaMemsetAsync(counter, 0, 64 + sizeof(int), s) != cudaSuccess)
     return reject(W8A8_ERR_CUDA, "clearing the arrival counter failed");
 
   ActQuantLaunch A = {};

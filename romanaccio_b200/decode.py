@@ -19,7 +19,8 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from ._lib import ACT_STATIC, DTYPE_INT8, OUT_F32, OUT_F32_ACC, TC_MIN_TOKENS
+from ._lib import (ACT_STATIC, DTYPE_INT8, ERR_NOT_SUPPORTED, OUT_F32, OUT_F32_ACC,
+                   TC_MIN_TOKENS, W8A8Error)
 from .chain import ChainStepSpec, DecodeChain
 from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
 from .lmhead import (LmHeadShard, candidate_buffers, exchange_candidates, shard_range,
@@ -111,11 +112,25 @@ class DecodeStack:
         self.graph = None
         # the persistent chain kernel covers decode batches of up to 8 tokens; larger batches run
         # each linear as act_quant + tensor-core GEMM
-        self.chain = self._build_chain() if use_chain and self.T <= 8 else None
+        self.chain_lm = False  # the chain's last step is the (unsharded) LM head
+        self.chain = None
+        if use_chain and self.T <= 8:
+            if self.world == 1:
+                try:
+                    self.chain = self._build_chain(with_lm=True)
+                    self.chain_lm = True
+                except W8A8Error as e:
+                    # the LM head's per-CTA logit keys for T tokens do not fit the kernel's
+                    # shared memory next to the linears' staging: the head runs as its own
+                    # top-k GEMV after the chain
+                    if e.status != ERR_NOT_SUPPORTED:
+                        raise
+            if self.chain is None:
+                self.chain = self._build_chain(with_lm=False)
 
-    def _build_chain(self) -> DecodeChain:
-        """The whole linear stack (+ the LM head when it is not sharded) as one persistent
-        kernel: same buffers and the same data dependences as run_linears / run_lm_head."""
+    def _build_chain(self, with_lm: bool) -> DecodeChain:
+        """The whole linear stack (+ the LM head when with_lm) as one persistent kernel: same
+        buffers and the same data dependences as run_linears / run_lm_head."""
         qkv, o, gu, down = self.outs
         x = self.x
         steps = []
@@ -125,7 +140,7 @@ class DecodeStack:
             steps.append(ChainStepSpec(row[2], o, gu))
             steps.append(ChainStepSpec(row[3], gu[:, :self.shape.ffn], down))
             x = down
-        if self.world == 1:
+        if with_lm:
             steps.append(ChainStepSpec(self.lm.linear, down, None, act_mode=ACT_STATIC,
                                        out_mode=OUT_F32_ACC, topk_k=self.k,
                                        row_offset=self.lo, topk_val=self.top_val,
@@ -138,7 +153,7 @@ class DecodeStack:
         # LM head: act_quant + top-k GEMV per group of 8 tokens (+ merge when sharded)
         lm = 1 + (T_all + 7) // 8 + (1 if self.world > 1 else 0)
         if self.chain is not None:
-            return 1 + (0 if self.world == 1 else lm)
+            return 1 + (0 if self.chain_lm else lm)
         # each linear: act_quant + one tensor-core GEMM, or a GEMV per group of 8 tokens
         contraction = 1 if self.T >= TC_MIN_TOKENS else (self.T + 7) // 8
         return self.layers * 4 * (1 + contraction) + lm
@@ -191,8 +206,10 @@ class DecodeStack:
         """The part of the step that needs no collective (everything when world == 1)."""
         if self.chain is not None:
             self.chain.forward()
-            if self.world == 1:
+            if self.chain_lm:
                 self.ids.copy_(self.top_idx[:, 0])
+            elif self.world == 1:
+                self.run_lm_head()
             return
         self.run_linears()
         if self.world == 1:

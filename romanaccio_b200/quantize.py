@@ -12,8 +12,9 @@ romanaccio's package builder step by step:
                          out_step_chan = in_s*w_step*2^trunc/QuantM)
   TRUNCS                 src/LFM3/build_lfm3_int8_pkg.py:49-54
 
-The same torch operations are used in the same order as the reference builder, so on CPU the
-parameters come out bit-identical (pinned by tests/test_quantize_golden.py).
+Every float operation is the builder's, applied in the builder's order (the grouping into
+helpers below is this module's own), so on CPU the parameters come out bit-identical to the
+reference builder's (pinned by tests/test_oracle_golden.py against fixtures it produced).
 """
 from __future__ import annotations
 
@@ -85,52 +86,70 @@ class LinearParams:
         return (self.in_step * self.w_step).astype(np.float32)
 
 
+def _calibration_range(x_smooth: torch.Tensor) -> tuple[float, float, torch.Tensor]:
+    """Static input range of the smoothed calibration tokens, each token quantised dyntok-style.
+
+    Returns (in_thresh = the largest per-token max |x|, in_step = in_thresh / 127, the tokens'
+    int8 codes as float64)."""
+    tok_absmax = x_smooth.abs().amax(dim=-1, keepdim=True).clamp(min=1e-8)
+    in_thresh = float(tok_absmax.max().item())
+    codes = torch.clamp(torch.round(x_smooth * (127.0 / tok_absmax)), -127.0, 127.0)
+    return in_thresh, in_thresh / 127.0, codes.double()
+
+
+def _row_codes(w_smooth: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row symmetric int8 codes of the float64 smoothed weights (round-half-even) and the
+    row steps max|w| / 127.  Exactly rounded elementwise float64 ops only, so any device gives
+    the builder's numpy bytes; rows are independent, so the builder's 512-row slices change
+    nothing."""
+    row_step = w_smooth.abs().amax(dim=1).clamp(min=1e-12) / 127.0
+    codes = torch.clamp(torch.round(w_smooth / row_step.unsqueeze(1)), -127.0, 127.0)
+    return codes, row_step
+
+
+def _output_steps(x_codes: torch.Tensor, w_codes: torch.Tensor, row_step: torch.Tensor,
+                  in_step: float, row_norm: torch.Tensor) -> np.ndarray:
+    """Per-output-channel output step: 1.15x the channel's largest calibration output, floored
+    at 1.15x the 80th percentile of (largest output / weight-row L2 norm) times that norm,
+    over 127."""
+    peak_out = F.linear(x_codes, w_codes).abs().amax(dim=0) * (in_step * row_step)
+    ratio_q80 = torch.quantile(peak_out / row_norm, 0.80)
+    bound = torch.maximum(peak_out * 1.15, ratio_q80 * row_norm * 1.15)
+    return (bound / 127.0).cpu().numpy()
+
+
+def _quantm(in_step: float, row_step: torch.Tensor, out_step: np.ndarray,
+            trunc: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """QuantM[n] = clip(RNE(in_step * w_step[n] / out_step[n] * 2^trunc), 1, 32767) and the
+    fp32 out_step_chan[n] = in_step * w_step[n] * 2^trunc / QuantM[n] the requantised int8
+    outputs are unpacked with."""
+    target = torch.as_tensor(out_step, dtype=torch.float64, device=row_step.device)
+    two_t = float(1 << trunc)
+    qm = torch.clamp(torch.round((in_step * row_step / target) * two_t), 1.0, 32767.0)
+    return qm, ((in_step * row_step * two_t) / qm).to(torch.float32)
+
+
 def build_linear(w: np.ndarray | torch.Tensor, calib_x: torch.Tensor, trunc: int = TRUNC_CONV,
-                 stat: str = "rms", clamp: tuple[float, float] | None = (0.05, 20.0),
-                 slice_rows: int = 512) -> LinearParams:
+                 stat: str = "rms", clamp: tuple[float, float] | None = (0.05, 20.0)
+                 ) -> LinearParams:
     """SmoothQuant + per-row int8 + per-output-channel QuantM for one linear.
 
     w: float [N, K] (output channel rows); calib_x: [M, K] calibration activations.
     """
-    w0 = torch.as_tensor(np.asarray(w) if not isinstance(w, torch.Tensor) else w).float()
+    w32 = torch.as_tensor(np.asarray(w) if not isinstance(w, torch.Tensor) else w).float()
     x = calib_x.float()
-    s_in = smooth_scales(x, w0, stat=stat, clamp=clamp)
-    in_inv_smooth = (1.0 / s_in).float()
-
-    # Static input range measured on the smoothed calibration tokens (dyntok-quantised per token).
-    x_sc = x / s_in
-    amax_tok = x_sc.abs().amax(dim=-1, keepdim=True).clamp(min=1e-8)
-    in_t = float(amax_tok.max().item())
-    in_s = in_t / 127.0
-    x_q = torch.clamp(torch.round(x_sc * (127.0 / amax_tok)), -127.0, 127.0).double()
-
-    # Smoothed weights, per-row step, and the per-channel output bound with an L2-norm floor.
-    w_sc = (w0 * s_in.unsqueeze(0)).double()
-    ws = w_sc.abs().amax(dim=1).clamp(min=1e-12) / 127.0
-    wq_t = torch.clamp(torch.round(w_sc / ws.unsqueeze(1)), -127.0, 127.0)
-    u_c = w_sc.norm(dim=1).clamp(min=1e-8)
-    y_norm_max = (F.linear(x_q, wq_t).abs().amax(dim=0)) * (in_s * ws)
-    qf = torch.quantile(y_norm_max / u_c, 0.80)
-    y_bound_c = torch.maximum(y_norm_max * 1.15, qf * u_c * 1.15)
-    out_s_c = (y_bound_c / 127.0).cpu().numpy()
-
-    # Per-row int8 quantisation + QuantM.  Every operation below is an exactly rounded float64
-    # elementwise op (abs, max, /, *, round-half-even), so torch on any device reproduces the
-    # reference's numpy slice loop bit for bit; rows are independent, so slicing by 512 rows
-    # does not change any value.
-    del slice_rows
-    amax = torch.clamp(w_sc.abs().amax(dim=1, keepdim=True), min=1e-12)
-    step = amax / 127.0
-    wq_t = torch.clamp(torch.round(w_sc / step), -127, 127).to(torch.int8)
-    w_step = step[:, 0]
-    out_s = torch.as_tensor(out_s_c, dtype=torch.float64, device=w_step.device)
-    qm_f = torch.clamp(torch.round((in_s * w_step / out_s) * float(1 << trunc)), 1.0, 32767.0)
-    out_step_chan = ((in_s * w_step * float(1 << trunc)) / qm_f).to(torch.float32)
-    return LinearParams(wq=wq_t.cpu().numpy(), w_step=w_step.cpu().numpy(),
-                        in_inv_smooth=in_inv_smooth.cpu().numpy(),
-                        quant_m=qm_f.to(torch.int16).cpu().numpy(),
-                        out_step_chan=out_step_chan.cpu().numpy(), in_thresh=in_t,
-                        in_step=in_s, trunc=trunc)
+    col_scale = smooth_scales(x, w32, stat=stat, clamp=clamp)
+    in_thresh, in_step, x_codes = _calibration_range(x / col_scale)
+    w_smooth = (w32 * col_scale.unsqueeze(0)).double()
+    w_codes, row_step = _row_codes(w_smooth)
+    out_step = _output_steps(x_codes, w_codes, row_step, in_step,
+                             w_smooth.norm(dim=1).clamp(min=1e-8))
+    qm, out_step_chan = _quantm(in_step, row_step, out_step, trunc)
+    return LinearParams(wq=w_codes.to(torch.int8).cpu().numpy(), w_step=row_step.cpu().numpy(),
+                        in_inv_smooth=(1.0 / col_scale).float().cpu().numpy(),
+                        quant_m=qm.to(torch.int16).cpu().numpy(),
+                        out_step_chan=out_step_chan.cpu().numpy(), in_thresh=in_thresh,
+                        in_step=in_step, trunc=trunc)
 
 
 def split_columns(p: LinearParams, n: int) -> list[LinearParams]:
