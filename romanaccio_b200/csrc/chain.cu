@@ -434,11 +434,14 @@ __device__ void topk_finish(const ChainOp &op, const ChainArgs &a, int tb, int t
   if (!grid_topk_arrive(st, tid, &s_last, sync)) return;
   // CTA g owns the tiles split_range(num_tiles, G, g): tile i belongs to
   // g = ceil((i + 1) * G / num_tiles) - 1
-  const int row_offset = op.tk.row_offset, rb = op.rb, num_tiles = op.num_tiles;
-  const long long G = gridDim.x;
+  // (32-bit arithmetic: tile < num_tiles and (tile + 1) * G < 2^32 for any chain shape, and a
+  // 32-bit division is a short inline sequence where a 64-bit one is a slow-path call)
+  const int row_offset = op.tk.row_offset;
+  const unsigned rb = static_cast<unsigned>(op.rb), num_tiles = static_cast<unsigned>(op.num_tiles);
+  const unsigned G = gridDim.x;
   auto list_of = [row_offset, rb, num_tiles, G](uint64_t key) {
-    const long long tile = (topk_key_id(key) - row_offset) / rb;
-    return static_cast<int>(((tile + 1) * G + num_tiles - 1) / num_tiles - 1);
+    const unsigned tile = static_cast<unsigned>(topk_key_id(key) - row_offset) / rb;
+    return static_cast<int>(((tile + 1u) * G + num_tiles - 1u) / num_tiles - 1u);
   };
   for (int t = 0; t < a.T; ++t)
     grid_topk_select<R, kCW>(k, t, st, op.tk.val, op.tk.idx, stage, gather, &s_n, warp, lane,
