@@ -9,9 +9,17 @@ gate|up fused as shared-input subgraphs) + the 1536x151936 LM head with a fused 
 argmax, vocab-sharded over the N GPUs.  Each GPU decodes its own T tokens (replica of the
 linear stack); the LM head shards its vocab across all N GPUs for all N*T tokens.
 
-Prints one JSON line (rank 0).  `--impl reference` times the reference's CPU path (the C
-restatement of the NPU integer steps around the reference's pack/unpack arithmetic, OpenMP over
-all host cores) on the same workload.
+Prints one JSON line (rank 0).  Besides the headline it carries:
+  parity      the measured step (same input) against the oracle's 28-layer step: final hidden
+              state bit for bit, top-40 ids and values and the argmax identical (at N > 1 rank 0
+              checks its tokens' merged candidates against the whole-vocabulary head);
+  per_config  (N = 1) one record per BASELINE configuration with its own CUDA-event time,
+              roofline fraction and oracle parity flag: SmolLM-135M T=1, Qwen2.5-1.5B T=8 and
+              T=32, the prefill GEMM sweep, the DeepSeek-V2-Lite MoE layer at T=1/64 with its
+              102400-row head, Gemma-12B-class T=1 with its 262144-row head;
+  lmhead_us   the LM-head tail's cost per step (step minus the same linear stack alone).
+`--impl reference` times the reference's CPU path (the C restatement of the NPU integer steps
+around the reference's pack/unpack arithmetic, OpenMP over all host cores) on the same workload.
 """
 from __future__ import annotations
 
@@ -132,39 +140,49 @@ def cpu_model(T: int, layers: int, seed: int = 0):
     return params, (wq, (in_step * step[:, 0].numpy()).astype(np.float32), in_step)
 
 
-def cpu_step_fn(params, lm, T: int, shape):
-    """Returns a closure running one decode step through the OpenMP oracle baseline."""
-    sys.path.insert(0, str(ROOT))
-    from oracle import oracle as O
-    lib = O.lib()
-    import ctypes as C
-    # every host core this process may run on (launchers such as torchrun export
-    # OMP_NUM_THREADS=1 to their workers)
-    lib.orc_set_threads(len(os.sched_getaffinity(0)))
+class OracleDecode:
+    """One decode step of a linear stack + LM head through the oracle's OpenMP C restatement
+    (the same arithmetic as the CUDA path): dyntok pack -> int32 GEMM -> QuantM requant ->
+    unpack per linear, each linear reading the previous one's output (o the q slice of qkv, down
+    the gate slice of gate_up), then the static-input LM head with its top-k.  Used as the
+    checker of the GPU step and, timed, as the CPU baseline."""
 
-    def p(a):
-        return a.ctypes.data
+    def __init__(self, params, lm, T: int, shape, k: int = 40):
+        sys.path.insert(0, str(ROOT))
+        from oracle import oracle as O
+        import ctypes as C
+        self.C = C
+        self.lib = O.lib()
+        # every host core this process may run on (launchers such as torchrun export
+        # OMP_NUM_THREADS=1 to their workers)
+        self.lib.orc_set_threads(len(os.sched_getaffinity(0)))
+        self.cores = int(self.lib.orc_num_threads())
+        self.T, self.shape, self.k = T, shape, k
+        self.bufs = {name: np.empty((T, N), np.float32) for (name, K, N, _) in shape.subgraphs()}
+        self.qbuf = np.empty((T, max(kk for (_, kk, _, _) in shape.subgraphs())), np.int8)
+        self.ratio = np.empty((T,), np.float32)
+        self.wq_lm, self.acc_step_lm, self.in_step_lm = lm
+        V = self.wq_lm.shape[0]
+        self.logits = np.empty((T, V), np.float32)
+        self.val = np.empty((T, k), np.float32)
+        self.idx = np.empty((T, k), np.int32)
+        self.qlm = np.empty((T, shape.hidden), np.int8)
+        self.prepared = []
+        for name, prm in params:
+            self.prepared.append((name, prm.wq.shape[1], prm.wq.shape[0], np.ascontiguousarray(prm.wq),
+                                  np.ascontiguousarray(prm.in_inv_smooth, np.float32), prm.in_thresh,
+                                  np.ascontiguousarray(prm.quant_m), prm.trunc,
+                                  np.ascontiguousarray(prm.out_step_chan, np.float32)))
 
-    x0 = np.random.default_rng(0).standard_normal((T, shape.hidden)).astype(np.float32)
-    bufs = {name: np.empty((T, N), np.float32) for (name, K, N, _) in shape.subgraphs()}
-    qbuf = np.empty((T, max(k for (_, k, _, _) in shape.subgraphs())), np.int8)
-    ratio = np.empty((T,), np.float32)
-    wq_lm, acc_step_lm, in_step_lm = lm
-    V = wq_lm.shape[0]
-    logits = np.empty((T, V), np.float32)
-    val = np.empty((T, 40), np.float32)
-    idx = np.empty((T, 40), np.int32)
-    qlm = np.empty((T, shape.hidden), np.int8)
-    prepared = []
-    for name, prm in params:
-        prepared.append((name, prm.wq.shape[1], prm.wq.shape[0], np.ascontiguousarray(prm.wq),
-                         np.ascontiguousarray(prm.in_inv_smooth, np.float32), prm.in_thresh,
-                         np.ascontiguousarray(prm.quant_m), prm.trunc,
-                         np.ascontiguousarray(prm.out_step_chan, np.float32)))
+    def run(self, x0: np.ndarray):
+        """Returns (final hidden state [T, hidden], top-k values [T, k], top-k ids [T, k])."""
+        C, lib, shape, bufs = self.C, self.lib, self.shape, self.bufs
 
-    def run():
-        x = x0
-        for (name, K, N, wq, inv, thr, qm, tr, osc) in prepared:
+        def p(a):
+            return a.ctypes.data
+
+        x = np.ascontiguousarray(x0, dtype=np.float32)
+        for (name, K, N, wq, inv, thr, qm, tr, osc) in self.prepared:
             if name == "o":
                 x = np.ascontiguousarray(bufs["qkv"][:, :shape.q])
             elif name == "down":
@@ -172,15 +190,61 @@ def cpu_step_fn(params, lm, T: int, shape):
             elif name == "gate_up":
                 x = bufs["o"]
             y = bufs[name]
-            lib.orc_linear_dyntok_omp(p(x), T, K, N, p(wq), p(inv), C.c_float(thr), p(qm), tr,
-                                      p(osc), p(y), p(qbuf), p(ratio))
+            lib.orc_linear_dyntok_omp(p(x), self.T, K, N, p(wq), p(inv), C.c_float(thr), p(qm),
+                                      tr, p(osc), p(y), p(self.qbuf), p(self.ratio))
             x = bufs["down"] if name == "down" else x
-        lib.orc_lmhead_topk_omp(p(bufs["down"]), T, shape.hidden, V, p(wq_lm),
-                                C.c_float(in_step_lm), p(acc_step_lm), 40, p(logits), p(qlm),
-                                p(val), p(idx))
-        return idx[:, 0].copy()
+        V = self.wq_lm.shape[0]
+        lib.orc_lmhead_topk_omp(p(bufs["down"]), self.T, shape.hidden, V, p(self.wq_lm),
+                                C.c_float(self.in_step_lm), p(self.acc_step_lm), self.k,
+                                p(self.logits), p(self.qlm), p(self.val), p(self.idx))
+        return bufs["down"].copy(), self.val.copy(), self.idx.copy()
 
-    return run, int(lib.orc_num_threads())
+
+def decode_step_on(stack, x_host: np.ndarray) -> None:
+    """One GPU step on x_host (every rank of a sharded head takes part)."""
+    stack.x.copy_(torch.from_numpy(x_host[:stack.T]))
+    stack.step()
+    torch.cuda.synchronize()
+
+
+def decode_parity(stack, x_host: np.ndarray, lm=None) -> dict:
+    """Checks the stack's last step (run on x_host by decode_step_on) against the oracle's step
+    on the same input: the final hidden state (bit for bit), the top-k ids and values
+    (identical) and the argmax.  lm: the full-vocabulary LM head (wq, acc_step, in_step) when the
+    stack holds one shard of it."""
+    import time as _t
+    T = stack.T
+    h = stack.outs[3].cpu().numpy()
+    val, idx = stack.top_val.cpu().numpy(), stack.top_idx.cpu().numpy()
+    ids = stack.ids.cpu().numpy()
+    if lm is None:
+        lm = (stack.lm_host[0], stack.lm_host[1], stack.lm_in_step)
+    t0 = _t.perf_counter()
+    orc = OracleDecode(stack.params_host, lm, T, stack.shape, k=stack.k)
+    h_ref, val_ref, idx_ref = orc.run(x_host[:T])
+    out = {
+        "oracle": "C restatement of the reference path (OpenMP), same weights and input",
+        "layers": stack.layers, "tokens": T, "vocab": int(lm[0].shape[0]), "k": stack.k,
+        "hidden_equal": bool(np.array_equal(h, h_ref)),
+        "topk_ids_equal": bool(np.array_equal(idx, idx_ref)),
+        "topk_values_equal": bool(np.array_equal(val, val_ref)),
+        "argmax_equal": bool(np.array_equal(ids, idx_ref[:, 0])),
+        "oracle_s": round(_t.perf_counter() - t0, 2),
+    }
+    out["parity"] = (out["hidden_equal"] and out["topk_ids_equal"] and out["topk_values_equal"]
+                     and out["argmax_equal"])
+    return out
+
+
+def cpu_step_fn(params, lm, T: int, shape):
+    """Returns a closure running one decode step through the OpenMP oracle baseline."""
+    orc = OracleDecode(params, lm, T, shape)
+    x0 = np.random.default_rng(0).standard_normal((T, shape.hidden)).astype(np.float32)
+
+    def run():
+        return orc.run(x0)[2][:, 0]
+
+    return run, orc.cores
 
 
 def run_reference(args) -> None:
@@ -213,6 +277,207 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------- per-config records
+def time_steps(step, steps: int, warmup: int, flush: torch.Tensor | None = None) -> float:
+    """Mean device time (CUDA events on the current stream) of `steps` calls of step(), after
+    `warmup` untimed ones; with flush, a buffer larger than L2 is rewritten before every step,
+    outside the events."""
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.add_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        step()
+        b.record(stream)
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / steps
+
+
+def decode_record(name: str, stack, x_host: np.ndarray, steps: int, warmup: int, peak: float,
+                  flush: torch.Tensor | None, note: str) -> dict:
+    """Timed decode steps (graph replays) of one stack + the oracle check of the same step."""
+    stack.x.copy_(torch.from_numpy(x_host[:stack.T]))
+    stack.step()
+    torch.cuda.synchronize()
+    try:
+        stack.capture()
+    except RuntimeError:
+        stack.graph = None
+    ms = time_steps(stack.step, steps, warmup, flush)
+    sb = stack.step_bytes()
+    nbytes = sb.linear + sb.lm_head
+    rec = {"workload": name, "tokens_per_step": stack.T, "layers": stack.layers,
+           "vocab": stack.V, "steps": steps, "ms_per_step": round(ms, 4),
+           "tok_s": round(stack.T / (ms / 1e3), 1),
+           "kernel": ("persistent chain (linears" + (" + LM head" if stack.chain_lm else "")
+                      + "), 1 launch" if stack.chain is not None
+                      else "act_quant + tcgen05 GEMM per linear"),
+           "roofline": {"bound": "hbm", "algorithmic_bytes": nbytes,
+                        "achieved_gbs": round(nbytes / (ms / 1e3) / 1e9, 1), "peak_gbs": peak,
+                        "frac": round(nbytes / (ms / 1e3) / 1e9 / peak, 4)},
+           "l2": note}
+    decode_step_on(stack, x_host)
+    par = decode_parity(stack, x_host)
+    rec["parity"] = par.pop("parity")
+    rec["parity_detail"] = par
+    stack.release()
+    return rec
+
+
+def moe_record(ctx, dev, steps: int, warmup: int, peak: float, flush: torch.Tensor) -> dict:
+    """Config 3: one DeepSeek-V2-Lite-shaped W8A8 MoE decode layer (hidden 2048, 64 routed + 2
+    shared experts of 1408, top-6) at T = 1 and 64, and its 2048 x 102400 LM head (top-40),
+    on one GPU; oracle-checked routing, expert stages and combine."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    from romanaccio_b200 import LmHeadShard, synth
+    from romanaccio_b200.moe import MoELayer, make_moe_params
+    H, I, E, S, k = 2048, 1408, 64, 2, 6
+    p = make_moe_params(H=H, I=I, E=E, S=S, k=k, seed=3, device=dev)
+    layer = MoELayer(ctx, p, max_tokens=64)
+    expert_bytes = 2 * I * H + H * I
+    out = {"workload": "deepseek-v2-lite-shaped W8A8 MoE layer: hidden 2048, 64 routed + 2 "
+                       "shared experts (gate|up 2048x2816, down 1408x2048), top-6",
+           "l2": "256 MB rewritten before every timed step (a layer's active experts fit in L2)"}
+    ok_all = True
+    for T in (1, 64):
+        x = synth.activations(T, H, seed=100 + T)
+        xd = x.to(dev)
+        y = torch.empty((T, H), dtype=torch.float32, device=dev)
+        ms = time_steps(lambda: layer.forward(xd, out=y), steps, warmup, flush)
+        v = {kk: t.cpu().numpy() for kk, t in layer.views(T).items()}
+        active = len(set(v["idx"].reshape(-1).tolist())) + S
+        nbytes = active * expert_bytes + T * H * 4 * 2
+        # oracle: routing ids identical, weights within float rounding of the logit sum order,
+        # every expert stage bit-exact on a sample of (token, slot) pairs, combine bit-exact
+        xh = x.numpy()
+        idx, w = O.moe_route(xh, p.gate_w, k)
+        ids_ok = bool(np.array_equal(v["idx"], idx))
+        w_ok = bool(np.allclose(v["w"], w, rtol=1e-4, atol=0))
+        slots = k + S
+        rng = np.random.default_rng(T)
+        pairs = range(T * slots) if T * slots <= 16 else sorted(rng.choice(T * slots, 16, replace=False).tolist())
+        stage_ok = True
+        for pi in pairs:
+            t, j = divmod(pi, slots)
+            e = int(v["idx"][t, j]) if j < k else E + (j - k)
+            gu, dn = p.gu[e], p.dn[e]
+            q, r = O.pack_dyntok(xh[t:t + 1], gu.in_thresh, gu.in_inv_smooth)
+            yq = O.requant(O.gemm_i32(q, gu.wq), gu.quant_m, gu.trunc, 127)
+            stage_ok &= bool(np.array_equal(v["gate_up"][pi:pi + 1], O.unpack(yq, 0.0, gu.out_step_chan, r)))
+            q2 = O.pack_static(v["act"][pi:pi + 1], dn.in_step, dn.in_inv_smooth)
+            want = O.requant(O.gemm_i32(q2, dn.wq), dn.quant_m, dn.trunc, 127)
+            stage_ok &= bool(np.array_equal(v["down_q"][pi:pi + 1].astype(np.int32), want))
+        osc = np.stack([q.out_step_chan for q in p.dn])
+        comb = O.moe_combine(v["down_q"].astype(np.int32), v["idx"], v["w"], osc, E, slots)
+        comb_ok = bool(np.array_equal(layer.forward(xd).cpu().numpy(), comb))
+        par = ids_ok and w_ok and stage_ok and comb_ok
+        ok_all &= par
+        out[f"T{T}"] = {"ms_per_layer": round(ms, 4), "tok_s_per_layer": round(T / (ms / 1e3), 1),
+                        "active_experts": active,
+                        "roofline": {"bound": "hbm", "algorithmic_bytes": nbytes,
+                                     "achieved_gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                                     "peak_gbs": peak,
+                                     "frac": round(nbytes / (ms / 1e3) / 1e9 / peak, 4)},
+                        "parity": par,
+                        "parity_detail": {"expert_ids_equal": ids_ok, "weights_rel_1e-4": w_ok,
+                                          "sampled_pairs": len(pairs), "stages_bit_exact": stage_ok,
+                                          "combine_bit_exact": comb_ok}}
+    layer.close()
+    # the 2048 x 102400 LM head with the fused top-40 (one shard at N = 1)
+    K, V = synth.DEEPSEEK_V2_LITE_LMHEAD
+    from romanaccio_b200.decode import _lm_rows
+    wq, w_step = _lm_rows(K, 0, V, 31, dev)
+    in_step = float(synth.activations(64, K, 37).abs().max()) / 127.0
+    acc_step = (in_step * w_step).astype(np.float32)
+    shard = LmHeadShard(ctx, wq, acc_step, in_step, row_offset=0)
+    h = synth.activations(1, K, seed=41)
+    hd = h.to(dev)
+    val = torch.empty((1, 40), dtype=torch.float32, device=dev)
+    idx = torch.empty((1, 40), dtype=torch.int32, device=dev)
+    ms = time_steps(lambda: shard.forward(hd, 40, val=val, idx=idx), steps, warmup, flush)
+    lg = O.dequant_acc(O.gemm_i32(O.pack_static(h.numpy(), in_step), wq), acc_step)
+    wv, wi = O.topk(lg, 40)
+    lm_ok = bool(np.array_equal(idx.cpu().numpy(), wi) and np.array_equal(val.cpu().numpy(), wv))
+    ok_all &= lm_ok
+    nbytes = V * K + K * 4 + V * 4 + 40 * 8
+    out["lm_head_2048x102400"] = {"ms": round(ms, 4),
+                                  "roofline": {"bound": "hbm", "algorithmic_bytes": nbytes,
+                                               "achieved_gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                                               "peak_gbs": peak,
+                                               "frac": round(nbytes / (ms / 1e3) / 1e9 / peak, 4)},
+                                  "parity": lm_ok}
+    out["parity"] = ok_all
+    return out
+
+
+def per_config_records(ctx, dev, headline, args, peak: float) -> dict:
+    """Untimed against the headline: one record per BASELINE configuration (decode configs 0, 1
+    at T = 8 and 32, 3 and 4, the prefill sweep of config 2), each with its own CUDA-event time,
+    roofline fraction and oracle parity flag."""
+    from romanaccio_b200 import synth
+    from romanaccio_b200.decode import DecodeStack
+    steps, warmup = args.config_steps, 3
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    rng = np.random.default_rng(7)
+    recs = {}
+
+    def guarded(key, fn):
+        t0 = time.perf_counter()
+        try:
+            recs[key] = fn()
+        except Exception as e:  # a failing configuration is reported, not hidden
+            recs[key] = {"error": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}",
+                         "parity": False}
+        recs[key]["wall_s"] = round(time.perf_counter() - t0, 1)
+        torch.cuda.empty_cache()
+
+    def c0():
+        sh = synth.SMOLLM_135M
+        st = DecodeStack(ctx, sh, 1, seed=0, stat="max", clamp=None)
+        x = synth.activations(1, sh.hidden, seed=11).numpy()
+        r = decode_record("smollm-135m-shaped W8A8 decode T=1 (30 layers, LM head 576x49152, "
+                          "smoothing sqrt(max|X|/max|W|), no clamp)", st, x, steps, warmup, peak,
+                          flush, "model 134 MB: 256 MB rewritten before every timed step")
+        del st
+        return r
+
+    def c1(T):
+        def f():
+            st = DecodeStack(ctx, synth.QWEN25_15B, T, seed=0, share_from=headline)
+            x = rng.standard_normal((T, synth.QWEN25_15B.hidden)).astype(np.float32)
+            r = decode_record(f"qwen2.5-1.5b-shaped W8A8 decode T={T}", st, x, steps, warmup,
+                              peak, None, "weights streamed every step: 1.54 GB > L2")
+            del st
+            return r
+        return f
+
+    def c4():
+        sh = synth.GEMMA_12B
+        st = DecodeStack(ctx, sh, 1, seed=0)
+        x = synth.activations(1, sh.hidden, seed=13).numpy()
+        r = decode_record("gemma-12b-class W8A8 decode T=1 (48 layers, LM head 3840x262144)",
+                          st, x, steps, warmup, peak, None,
+                          "weights streamed every step: 11.8 GB > L2")
+        del st
+        return r
+
+    guarded("c0_smollm_t1", c0)
+    guarded("c1_qwen_t8", c1(8))
+    guarded("c1_qwen_t32", c1(32))
+    guarded("c2_prefill_sweep", lambda: prefill_record(ctx, dev, steps, warmup, flush))
+    guarded("c3_moe_v2lite", lambda: moe_record(ctx, dev, steps, warmup, peak, flush))
+    guarded("c4_gemma_t1", c4)
+    recs["all_parity"] = all(r.get("parity", False) for k, r in recs.items() if isinstance(r, dict))
+    return recs
+
+
 # ---------------------------------------------------------------------------- GPU path
 def run_ours(args) -> None:
     world = env_int("WORLD_SIZE", 1)
@@ -226,18 +491,18 @@ def run_ours(args) -> None:
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     sys.path.insert(0, str(ROOT))
     from romanaccio_b200 import Context, synth
-    from romanaccio_b200.decode import DecodeStack
+    from romanaccio_b200.decode import DecodeStack, _lm_rows
 
     T = args.batch
     shape = synth.QWEN25_15B
     ctx = Context(local)
     stack = DecodeStack(ctx, shape, T, rank=rank, world=world, group=group, seed=0,
                         layers=args.layers, use_chain=not args.per_linear)
-    x_host = torch.from_numpy(
-        np.random.default_rng(rank).standard_normal((T, shape.hidden)).astype(np.float32)).pin_memory()
+    x_np = np.random.default_rng(rank).standard_normal((T, shape.hidden)).astype(np.float32)
+    x_host = torch.from_numpy(x_np).pin_memory()
     ids_host = torch.empty((T,), dtype=torch.int32).pin_memory()
     stack.x.copy_(x_host)
     stack.step()  # eager warm-up (configures every kernel instantiation)
@@ -279,11 +544,42 @@ def run_ours(args) -> None:
     e1.record(stream)
     barrier()
     ms_e2e = e0.elapsed_time(e1) / args.steps
-    times = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
+
+    # the LM-head tail's cost per step: the step against the same linear stack alone (a chain
+    # without the head, or the per-linear launches), both as CUDA graphs
+    reps = 10
+    if stack.chain is not None:
+        lin_only = stack.chain if not stack.chain_lm else stack._build_chain(with_lm=False)
+        run_lin = lin_only.forward
+    else:
+        run_lin = stack.run_linears
+    run_lin()
+    torch.cuda.synchronize()
+    g_lin = torch.cuda.CUDAGraph()
+    s_cap = torch.cuda.Stream(device=dev)
+    s_cap.wait_stream(stream)
+    with torch.cuda.stream(s_cap):
+        run_lin()
+    stream.wait_stream(s_cap)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g_lin):
+        run_lin()
+    for _ in range(3):
+        g_lin.replay()
+    torch.cuda.synchronize()
+    l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0.record(stream)
+    for _ in range(reps):
+        g_lin.replay()
+    l1.record(stream)
+    torch.cuda.synchronize()
+    ms_lin = l0.elapsed_time(l1) / reps
+    del g_lin
+    times = torch.tensor([ms, ms_e2e, ms_lin], dtype=torch.float64, device=dev)
     if world > 1:
         import torch.distributed as dist
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    ms, ms_e2e = times.tolist()
+    ms, ms_e2e, ms_lin = times.tolist()
 
     # dominant kernel: the gate_up GEMV (59 % of the linear weight bytes), int8 input in HBM,
     # one launch per layer over the 28 distinct weight matrices (770 MB > L2), in a graph.
@@ -304,7 +600,6 @@ def run_ours(args) -> None:
             lin.submit(q_in, OUT_F32, dyntok_ratios=ratio, out=y_out)
     for _ in range(3):
         g.replay()
-    reps = 10
     torch.cuda.synchronize()
     r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     r0.record(stream)
@@ -321,8 +616,8 @@ def run_ours(args) -> None:
                  "launch_us": gemv_s * 1e6, "algorithmic_bytes": sb.gemv_launch,
                  "traffic": GEMV_TRAFFIC_BYTES}
     if stack.chain is not None:
-        # dominant (only) kernel of the step: the persistent chain kernel; one launch moves the
-        # whole step's algorithmic bytes (world == 1: linears + LM head)
+        # dominant kernel of the step: the persistent chain kernel; one launch moves the step's
+        # algorithmic bytes (linears, plus the LM head when it runs inside the chain)
         chain_bytes = sb.linear + (sb.lm_head if stack.chain_lm else 0)
         for _ in range(3):
             stack.chain.forward()
@@ -342,6 +637,19 @@ def run_ours(args) -> None:
         roof_bytes, roof_s, roof_traffic = sb.gemv_launch, gemv_s, GEMV_TRAFFIC_BYTES
     achieved = roof_bytes / roof_s / 1e9
 
+    # oracle parity of the measured step (rank 0: its own tokens against the oracle's step with
+    # the whole vocabulary; every rank holds the same linear weights)
+    parity = None
+    if not args.no_parity:
+        decode_step_on(stack, x_np)
+    if rank == 0 and not args.no_parity:
+        lm_full = None
+        if world > 1:
+            wq_f, w_step_f = _lm_rows(shape.hidden, 0, stack.V, 17, dev)
+            lm_full = (wq_f, (stack.lm_in_step * w_step_f).astype(np.float32), stack.lm_in_step)
+        parity = decode_parity(stack, x_np, lm=lm_full)
+    barrier()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         run_cpu, cores = cpu_step_fn(stack.params_host, (stack.lm_host[0], stack.lm_host[1],
@@ -357,6 +665,10 @@ def run_ours(args) -> None:
         cpu = {"value": T / dt, "unit": "tok/s", "cores": cores, "kind": "port",
                "sample": f"{n} full decode steps of the same workload (28 layers + LM head), "
                          "C restatement of the reference path, OpenMP"}
+
+    per_config = None
+    if rank == 0 and world == 1 and not args.no_per_config:
+        per_config = per_config_records(ctx, dev, stack, args, peak)
 
     step_bytes = sb.linear + sb.lm_head
     value = world * T / (ms / 1e3)
@@ -375,6 +687,8 @@ def run_ours(args) -> None:
                        "kernel": "per-linear GEMV launches" if args.per_linear else
                                  "persistent decode-chain kernel (1 cooperative launch per step)"},
             "hbm_gbs_step": step_bytes / (ms / 1e3) / 1e9,
+            "lmhead_us": round((ms - ms_lin) * 1e3, 2),
+            "linears_ms": round(ms_lin, 4),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": roof_traffic,
                          "kernel": roof_kernel, "peak_kind": peak_kind,
@@ -385,8 +699,12 @@ def run_ours(args) -> None:
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
         }
+        if parity is not None:
+            line["parity"] = parity
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if per_config is not None:
+            line["per_config"] = per_config
         print(json.dumps(line), flush=True)
     stack.release()
     if world > 1:
@@ -457,6 +775,46 @@ def run_prefill_reference(args) -> None:
         "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def prefill_record(ctx, dev, steps: int, warmup: int, flush: torch.Tensor) -> dict:
+    """Config 2: the 12 prefill linears, each a fused W8A8 forward (dyntok act quant kernel +
+    tcgen05 GEMM with the requant epilogue) on a cold L2, timed per shape; every shape checked
+    against the oracle on 16 seeded token rows (rows are independent: per-token ratio, per-row
+    requant), int8 outputs bit for bit."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    from romanaccio_b200 import OUT_QUANT, PATH_TENSOR, W8A8Linear, synth
+    stream = torch.cuda.current_stream()
+    per, ok_all, tot_ms = {}, True, 0.0
+    for i, (M, K, N) in enumerate(PREFILL_SHAPES):
+        prm = synth.make_linear(K, N, seed=i, device=dev)
+        lin = W8A8Linear.from_params(ctx, prm)
+        lin.set_path(PATH_TENSOR)
+        x = synth.activations(M, K, seed=100 + i, device=dev)
+        y = torch.empty((M, N), dtype=torch.int8, device=dev)
+        ms = time_steps(lambda: lin.forward(x, OUT_QUANT, dyntok=True, out=y), steps, warmup, flush)
+        rows = np.sort(np.random.default_rng(i).choice(M, 16, replace=False))
+        xr = x[torch.as_tensor(rows, device=dev)].cpu().numpy()
+        q, r = O.pack_dyntok(xr, prm.in_thresh, prm.in_inv_smooth)
+        want = O.requant(O.gemm_i32(q, prm.wq), prm.quant_m, prm.trunc, 127)
+        got = y[torch.as_tensor(rows, device=dev)].cpu().numpy().astype(np.int32)
+        ok = bool(np.array_equal(got, want))
+        ok_all &= ok
+        tot_ms += ms
+        per[f"{M}x{K}x{N}"] = {"us": round(ms * 1e3, 2),
+                               "tops": round(2 * M * N * K / (ms / 1e3) / 1e12, 1),
+                               "parity_16_rows": ok}
+        lin.close()
+        del x, y
+    ops = prefill_ops(PREFILL_SHAPES)
+    big = per["2048x8192x8192"]
+    return {"workload": PREFILL_WORKLOAD, "steps": steps, "ms_per_sweep": round(tot_ms, 4),
+            "tops": round(ops / (tot_ms / 1e3) / 1e12, 1), "per_shape": per,
+            "roofline": {"bound": "tensor (M >= 512), hbm (M = 128)",
+                         "largest_gemm_tops": big["tops"], "nominal_int8_tops": 4500.0,
+                         "frac_of_nominal": round(big["tops"] / 4500.0, 4)},
+            "l2": "256 MB rewritten before every timed forward", "parity": ok_all}
 
 
 def run_prefill(args) -> None:
@@ -782,6 +1140,12 @@ def main() -> None:
                     help="decode: the headline decode step; prefill: the int8 GEMM sweep; "
                          "lmhead: sharded LM-head latency over 1, 2, 4, 8 GPUs of one process")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the oracle check of the measured step")
+    ap.add_argument("--no-per-config", action="store_true",
+                    help="skip the per-configuration records (configs 0, 1 at T=8/32, 2, 3, 4)")
+    ap.add_argument("--config-steps", type=int, default=10,
+                    help="timed steps of each per-configuration record")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     if args.warmup < 3:

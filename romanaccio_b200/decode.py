@@ -56,9 +56,17 @@ def _lm_rows(K: int, lo: int, hi: int, seed: int, device) -> tuple[np.ndarray, n
 
 
 class DecodeStack:
+    """stat / clamp select the SmoothQuant statistic of every linear (quantize.smooth_scales):
+    the reference builder's rms with the [0.05, 20] clamp by default, or max |x| with no clamp
+    (the SmolLM-shaped workload).  share_from: another stack of the same shape, seed, layers,
+    smoothing and sharding whose linears and LM-head shard this one uses instead of building its
+    own (a second token count over the same weights)."""
+
     def __init__(self, ctx: Context, shape: DecodeShape, T: int, rank: int = 0, world: int = 1,
                  group=None, seed: int = 0, layers: int | None = None, k: int = 40,
-                 lm_vocab: int | None = None, use_chain: bool = True):
+                 lm_vocab: int | None = None, use_chain: bool = True, stat: str = "rms",
+                 clamp: tuple[float, float] | None = (0.05, 20.0),
+                 share_from: "DecodeStack | None" = None):
         self.ctx = ctx
         self.shape = shape
         self.T = int(T)
@@ -69,7 +77,20 @@ class DecodeStack:
         self.dev = dev
         self.subgraphs = shape.subgraphs()
         self.linears: list[list[W8A8Linear]] = []
-        self.params_host = []  # kept for the CPU baseline
+        self.params_host = []  # kept for the CPU baseline and the oracle check
+        if share_from is not None:
+            src = share_from
+            if (src.shape != shape or src.layers != self.layers or src.world != self.world
+                    or src.rank != self.rank or src.ctx is not ctx):
+                raise ValueError("share_from must be a stack of the same shape, layers, "
+                                 "sharding and context")
+            self.linears, self.params_host = src.linears, src.params_host
+            self.V, self.lo, self.hi = src.V, src.lo, src.hi
+            self.lm_in_step, self.lm_host, self.lm = src.lm_in_step, src.lm_host, src.lm
+            self._shared = src  # keeps the owner alive
+            self._buffers()
+            self._plan_chain(use_chain)
+            return
         for layer in range(self.layers):
             row = []
             for j, (name, K, N, trunc) in enumerate(self.subgraphs):
@@ -77,7 +98,7 @@ class DecodeStack:
                 g = torch.Generator(device=dev).manual_seed(s)
                 w = torch.randn((N, K), generator=g, device=dev, dtype=torch.float32) * 0.02
                 calib = activations(64, K, s + 1, device=dev)
-                p = build_linear(w, calib, trunc=trunc)
+                p = build_linear(w, calib, trunc=trunc, stat=stat, clamp=clamp)
                 del w, calib
                 scale = SubgraphScaleInfo(in_dtype=DTYPE_INT8, out_dtype=DTYPE_INT8,
                                           in_thresh=p.in_thresh, in_step=p.in_step,
@@ -99,7 +120,12 @@ class DecodeStack:
         acc_step = (self.lm_in_step * w_step).astype(np.float32)
         self.lm_host = (wq, acc_step)
         self.lm = LmHeadShard(ctx, wq, acc_step, self.lm_in_step, row_offset=self.lo)
-        # persistent device buffers
+        self._buffers()
+        self._plan_chain(use_chain)
+
+    def _buffers(self) -> None:
+        """Persistent device buffers of one step."""
+        dev, K = self.dev, self.shape.hidden
         T_all = self.T * self.world
         self.x = torch.zeros((self.T, K), dtype=torch.float32, device=dev)
         self.outs = [torch.empty((self.T, N), dtype=torch.float32, device=dev)
@@ -110,6 +136,8 @@ class DecodeStack:
         self.top_val = torch.empty((self.T, self.k), dtype=torch.float32, device=dev)
         self.top_idx = torch.empty((self.T, self.k), dtype=torch.int32, device=dev)
         self.graph = None
+
+    def _plan_chain(self, use_chain: bool) -> None:
         # the persistent chain kernel covers decode batches of up to 8 tokens; larger batches run
         # each linear as act_quant + tensor-core GEMM
         self.chain_lm = False  # the chain's last step is the (unsharded) LM head
