@@ -354,3 +354,62 @@ def ref_moe_route(hidden: np.ndarray, gate_w: np.ndarray, k: int, bias: np.ndarr
     if rc != 0:
         raise RuntimeError(f"ref_moe_route failed ({rc})")
     return idx, w
+
+
+class DecodeOracle:
+    """One decode step of a linear stack + LM head through the oracle's OpenMP C restatement
+    (src/LFM3/lfm3_v2.cpp pack / unpack, cmac.py:300-383 GEMM, attribute_int8_error.py:104-122
+    requant; the same arithmetic as the CUDA path): dyntok pack -> int32 GEMM -> QuantM requant ->
+    unpack per linear, each linear reading the previous one's output (o the q slice of qkv, down
+    the gate slice of gate_up), then the static-input LM head with its top-k.  Used as the
+    checker of the GPU step and, timed, as the CPU baseline."""
+
+    def __init__(self, params, lm, T: int, shape, k: int = 40):
+        import os
+        self.C = C
+        self.lib = lib()
+        # every host core this process may run on (launchers such as torchrun export
+        # OMP_NUM_THREADS=1 to their workers)
+        self.lib.orc_set_threads(len(os.sched_getaffinity(0)))
+        self.cores = int(self.lib.orc_num_threads())
+        self.T, self.shape, self.k = T, shape, k
+        self.bufs = {name: np.empty((T, N), np.float32) for (name, K, N, _) in shape.subgraphs()}
+        self.qbuf = np.empty((T, max(kk for (_, kk, _, _) in shape.subgraphs())), np.int8)
+        self.ratio = np.empty((T,), np.float32)
+        self.wq_lm, self.acc_step_lm, self.in_step_lm = lm
+        V = self.wq_lm.shape[0]
+        self.logits = np.empty((T, V), np.float32)
+        self.val = np.empty((T, k), np.float32)
+        self.idx = np.empty((T, k), np.int32)
+        self.qlm = np.empty((T, shape.hidden), np.int8)
+        self.prepared = []
+        for name, prm in params:
+            self.prepared.append((name, prm.wq.shape[1], prm.wq.shape[0], np.ascontiguousarray(prm.wq),
+                                  np.ascontiguousarray(prm.in_inv_smooth, np.float32), prm.in_thresh,
+                                  np.ascontiguousarray(prm.quant_m), prm.trunc,
+                                  np.ascontiguousarray(prm.out_step_chan, np.float32)))
+
+    def run(self, x0: np.ndarray):
+        """Returns (final hidden state [T, hidden], top-k values [T, k], top-k ids [T, k])."""
+        C, lib, shape, bufs = self.C, self.lib, self.shape, self.bufs
+
+        def p(a):
+            return a.ctypes.data
+
+        x = np.ascontiguousarray(x0, dtype=np.float32)
+        for (name, K, N, wq, inv, thr, qm, tr, osc) in self.prepared:
+            if name == "o":
+                x = np.ascontiguousarray(bufs["qkv"][:, :shape.q])
+            elif name == "down":
+                x = np.ascontiguousarray(bufs["gate_up"][:, :shape.ffn])
+            elif name == "gate_up":
+                x = bufs["o"]
+            y = bufs[name]
+            lib.orc_linear_dyntok_omp(p(x), self.T, K, N, p(wq), p(inv), C.c_float(thr), p(qm),
+                                      tr, p(osc), p(y), p(self.qbuf), p(self.ratio))
+            x = bufs["down"] if name == "down" else x
+        V = self.wq_lm.shape[0]
+        lib.orc_lmhead_topk_omp(p(bufs["down"]), self.T, shape.hidden, V, p(self.wq_lm),
+                                C.c_float(self.in_step_lm), p(self.acc_step_lm), self.k,
+                                p(self.logits), p(self.qlm), p(self.val), p(self.idx))
+        return bufs["down"].copy(), self.val.copy(), self.idx.copy()

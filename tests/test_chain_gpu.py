@@ -109,3 +109,63 @@ def test_independent_steps_need_no_barrier(ctx):
         *_, y = O.linear(x.numpy(), p.wq, p.quant_m, p.trunc, p.out_step_chan, p.in_inv_smooth,
                          in_thresh=p.in_thresh)
         assert np.array_equal(v.cpu().numpy(), y)
+
+
+# ---------------------------------------------------------------------------------------
+# The benchmarked configurations end to end against the oracle's whole decode step.
+_STACKS = {}
+
+
+def _qwen_stack(ctx):
+    if "qwen" not in _STACKS:
+        _STACKS["qwen"] = DecodeStack(ctx, synth.QWEN25_15B, 1, seed=0)
+    return _STACKS["qwen"]
+
+
+def _oracle_step(st, x):
+    from oracle.oracle import DecodeOracle
+    wq, acc_step = st.lm_host
+    orc = DecodeOracle(st.params_host, (wq, acc_step, st.lm_in_step), st.T, st.shape, k=st.k)
+    return orc.run(x)
+
+
+def _check_step(st, x):
+    st.x.copy_(torch.from_numpy(x).to(st.dev))
+    st.run_device()
+    torch.cuda.synchronize()
+    h, val, idx = _oracle_step(st, x)
+    assert np.array_equal(st.outs[3].cpu().numpy(), h), "final hidden state differs"
+    assert np.array_equal(st.top_idx.cpu().numpy(), idx), "top-k ids differ"
+    assert np.array_equal(st.top_val.cpu().numpy(), val), "top-k values differ"
+    assert np.array_equal(st.ids.cpu().numpy(), idx[:, 0]), "argmax differs"
+
+
+@pytest.mark.parametrize("T", [1, 8, 32])
+def test_qwen_28_layer_step_matches_oracle(ctx, T):
+    """Config 1 as benchmarked: all 28 layers and the 151936-row LM head with its top-40, T = 1
+    and 8 through the persistent chain, T = 32 through the tensor-core linears, against the
+    oracle's 28-layer step on the same input."""
+    base = _qwen_stack(ctx)
+    st = base if T == 1 else DecodeStack(ctx, synth.QWEN25_15B, T, seed=0, share_from=base)
+    assert st.layers == 28 and st.V == 151936
+    if T <= 8:
+        assert st.chain is not None
+    else:
+        assert st.chain is None
+    _check_step(st, synth.activations(T, 1536, seed=40 + T).numpy())
+    ctx.check()
+
+
+def test_gemma_48_layer_step_matches_oracle(ctx):
+    """Config 4: 48 Gemma-12B-class layers and the 262144-row LM head, T = 1."""
+    st = DecodeStack(ctx, synth.GEMMA_12B, 1, seed=0)
+    _check_step(st, synth.activations(1, 3840, seed=44).numpy())
+    ctx.check()
+
+
+def test_smollm_30_layer_step_matches_oracle(ctx):
+    """Config 0: 30 SmolLM-135M-shaped layers (smoothing from max |x|, no clamp) and the
+    49152-row LM head, T = 1."""
+    st = DecodeStack(ctx, synth.SMOLLM_135M, 1, seed=0, stat="max", clamp=None)
+    _check_step(st, synth.activations(1, 576, seed=45).numpy())
+    ctx.check()

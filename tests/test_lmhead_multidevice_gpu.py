@@ -128,3 +128,34 @@ def test_remote_shards_refuse_graph_capture():
     c1.check()
     with pytest.raises(RuntimeError, match="max_tokens"):
         rb.MultiDeviceLmHead([c0, c1], wq, acc_step, 0.02, max_tokens=9, k_max=16)
+
+
+_BIG = {}
+
+
+def _device_head(V: int, K: int, seed: int):
+    """Seeded int8 rows generated on the GPU (a 1 GB head would take minutes in numpy)."""
+    key = (V, K, seed)
+    if key not in _BIG:
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        wq = torch.randint(-127, 128, (V, K), generator=g, device="cuda", dtype=torch.int32)
+        w_step = torch.rand((V,), generator=g, device="cuda", dtype=torch.float64) * 0.02 / 127 + 1e-5
+        _BIG.clear()
+        _BIG[key] = (wq.to(torch.int8).cpu().numpy(), w_step.cpu().numpy())
+    return _BIG[key]
+
+
+@pytest.mark.parametrize("V,K,n", [
+    (102400, 2048, 2), (102400, 2048, 4), (102400, 2048, 8),
+    (262144, 3840, 2), (262144, 3840, 4), (262144, 3840, 8),
+])
+def test_config_heads_sharded_on_one_device(ctx, V, K, n):
+    """The DeepSeek-V2-Lite (102400 x 2048) and Gemma-12B-class (262144 x 3840) LM heads in 2, 4
+    and 8 contiguous vocab shards, merged: the oracle's top-40 over the whole vocabulary."""
+    wq, w_step = _device_head(V, K, seed=V)
+    in_step = 0.027
+    acc_step = (in_step * w_step).astype(np.float32)
+    lm = rb.MultiDeviceLmHead([ctx] * n, wq, acc_step, in_step, max_tokens=8, k_max=64)
+    assert lm.shards == n
+    _check(lm, synth.activations(1, K, seed=n).numpy(), wq, in_step, acc_step, 40)
+    ctx.check()
