@@ -333,6 +333,52 @@ w8a8_status w8a8_moe_views(const w8a8_moe *moe, const int32_t **idx_dev, const f
                            const void **down_q_dev);
 
 /* ---------------------------------------------------------------------------------------
+ * One rank of a vocab-sharded LM head over processes: one process per GPU, each holding the
+ * contiguous vocab rows [rank * V / world, (rank + 1) * V / world) (the reference's contiguous
+ * die split, dual_die_splitter.py:95-141, transformer_session.cpp:588-596, for any world <= 64).
+ * Replaces the dual-die LM-head merge of TransformerSession::forward_lm_head_dual_die
+ * (transformer_session.cpp:538-614) and run_dual_die (lfm3_v2.cpp:1311-1332), where each die's
+ * worker computes its half of the logits and the host concatenates them before Sampler::sample:
+ * here every rank's GEMV keeps only the top-k (logit, vocab id) pairs of every rank's tokens,
+ * stores each token's pairs into the token owner's device memory, and each rank merges its own
+ * tokens' lists.  The exchange is done by this library: peer stores into CUDA-IPC-mapped device
+ * memory with counters that only grow, each device-side wait bounded (1 to 2 s, then
+ * W8A8_ERR_PEER_TIMEOUT through w8a8_ctx_check) -- no NCCL call and no host round trip, so a
+ * forward (three launches on `stream`) can be captured in a CUDA graph.
+ *
+ * Set-up: every rank calls w8a8_lmhead_rank_create, then w8a8_lmhead_rank_export (64 bytes),
+ * the caller exchanges the handles between the processes by any means (they are plain bytes),
+ * and every rank calls w8a8_lmhead_rank_connect with all world handles in rank order.  Ranks
+ * driven by one process (one per device) connect with w8a8_lmhead_rank_connect_local instead.
+ * Forward: every rank calls w8a8_lmhead_rank_forward for the same sequence of forwards, with the
+ * same T on every rank (world * max_tokens <= 64), on one stream per rank; the calls of
+ * different ranks may be issued in any order and need not overlap in time beyond the bounded
+ * waits.  h_dev: this rank's T hidden states fp32 [T, K]; outputs this rank's tokens' merged
+ * top-k (value desc, id asc) [T, k] and argmax [T] (may be NULL).
+ * ------------------------------------------------------------------------------------- */
+#define W8A8_LMHEAD_RANK_HANDLE_BYTES 64
+typedef struct w8a8_lmhead_rank w8a8_lmhead_rank;
+
+/* shard_weights: int8 rows of THIS rank's shard [hi - lo, ld] (host or device memory),
+ * shard_acc_step fp32 [hi - lo] (logit = float(acc) * acc_step); static input step in_step. */
+w8a8_status w8a8_lmhead_rank_create(w8a8_ctx *ctx, int32_t rank, int32_t world, int32_t K,
+                                    int32_t V, const int8_t *shard_weights, int64_t ld,
+                                    const float *shard_acc_step, float in_step, int32_t max_tokens,
+                                    int32_t k_max, w8a8_lmhead_rank **out_rank);
+/* Writes W8A8_LMHEAD_RANK_HANDLE_BYTES bytes naming this rank's exchange memory. */
+w8a8_status w8a8_lmhead_rank_export(const w8a8_lmhead_rank *rank, void *handle_out);
+/* handles: world * W8A8_LMHEAD_RANK_HANDLE_BYTES bytes, rank p's at offset p * 64. */
+w8a8_status w8a8_lmhead_rank_connect(w8a8_lmhead_rank *rank, const void *handles);
+/* All world ranks of one process (ranks[p] = rank p), connected to each other directly. */
+w8a8_status w8a8_lmhead_rank_connect_local(w8a8_lmhead_rank *const *ranks, int32_t world);
+w8a8_status w8a8_lmhead_rank_forward(w8a8_lmhead_rank *rank, const float *h_dev, int32_t T,
+                                     int32_t k, float *topk_val_dev, int32_t *topk_idx_dev,
+                                     int32_t *argmax_dev, void *stream);
+void        w8a8_lmhead_rank_destroy(w8a8_lmhead_rank *rank);
+/* Number of vocab rows of this rank's shard; *lo / *hi (may be NULL) its first / end vocab id. */
+int32_t     w8a8_lmhead_rank_shard_range(const w8a8_lmhead_rank *rank, int32_t *lo, int32_t *hi);
+
+/* ---------------------------------------------------------------------------------------
  * Decode chain: a fixed sequence of linears, optionally ending with an LM-head top-k step, run
  * by ONE persistent cooperative kernel launch per forward.  Replaces the per-linear
  * pack -> submit_task -> unpack round trips of the reference's decode loop

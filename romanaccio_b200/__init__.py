@@ -7,7 +7,8 @@ from ._lib import (ACT_DYNTOK, ACT_STATIC, DTYPE_FP16, DTYPE_INT8, DTYPE_INT16, 
                    OUT_F32, OUT_F32_ACC, OUT_QUANT, PATH_AUTO, PATH_GEMV, PATH_TENSOR, TOPK_MAX,
                    W8A8Error)
 from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
-from .lmhead import LmHeadShard, MultiDeviceLmHead, VocabShardedLmHead, shard_range
+from .lmhead import (LmHeadShard, MultiDeviceLmHead, RankLmHead, VocabShardedLmHead,
+                     shard_range)
 from .norm import post_op_ffn_pack, rmsnorm_pack_dyntok
 from .package import load_quant_scales, read_weight_region, untile_int8, untile_int16
 from .sampler import CandidateSampler, SamplingConfig
@@ -17,6 +18,7 @@ __all__ = [
     "OUT_F32", "OUT_F32_ACC", "OUT_QUANT", "PATH_AUTO", "PATH_GEMV", "PATH_TENSOR", "TOPK_MAX",
     "W8A8Error", "Context",
     "SubgraphScaleInfo", "W8A8Linear", "topk_merge", "LmHeadShard", "MultiDeviceLmHead",
+    "RankLmHead",
     "VocabShardedLmHead",
     "shard_range", "CandidateSampler", "SamplingConfig", "rmsnorm_pack_dyntok",
     "post_op_ffn_pack", "load_quant_scales", "read_weight_region", "untile_int8", "untile_int16",

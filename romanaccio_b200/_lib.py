@@ -145,6 +145,14 @@ SIGNATURES = {
     "w8a8_lmhead_destroy": (None, [_P]),
     "w8a8_lmhead_shards": (_I32, [_P]),
     "w8a8_lmhead_set_trace": (C.c_int, [_P, _P, C.POINTER(_P)]),
+    "w8a8_lmhead_rank_create": (C.c_int, [_P, _I32, _I32, _I32, _I32, _P, _I64, _P, C.c_float,
+                                          _I32, _I32, C.POINTER(_P)]),
+    "w8a8_lmhead_rank_export": (C.c_int, [_P, _P]),
+    "w8a8_lmhead_rank_connect": (C.c_int, [_P, _P]),
+    "w8a8_lmhead_rank_connect_local": (C.c_int, [C.POINTER(_P), _I32]),
+    "w8a8_lmhead_rank_forward": (C.c_int, [_P, _P, _I32, _I32, _P, _P, _P, _P]),
+    "w8a8_lmhead_rank_destroy": (None, [_P]),
+    "w8a8_lmhead_rank_shard_range": (_I32, [_P, C.POINTER(_I32), C.POINTER(_I32)]),
     "w8a8_moe_create": (C.c_int, [_P, C.POINTER(MoeDesc), C.POINTER(_P)]),
     "w8a8_moe_destroy": (None, [_P]),
     "w8a8_moe_route": (C.c_int, [_P, _P, _I64, _I32, _P, _P, _P]),

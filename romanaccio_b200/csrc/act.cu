@@ -30,6 +30,7 @@ struct ActArgs {
   int n_peers;
   unsigned *pub_seq, *pub_arrive;
   unsigned long long *trace;
+  int pub_row0;
 };
 
 // Publication of the quantised rows to other devices: every CTA's stores are fenced at system
@@ -117,19 +118,19 @@ __global__ void __launch_bounds__(kActThreads) act_quant_kernel(const ActArgs a)
       }
       q4[c] = o;
       for (int p = 0; p < a.n_peers; ++p)
-        reinterpret_cast<char4 *>(a.peers[p].q + t * a.ldq)[c] = o;
+        reinterpret_cast<char4 *>(a.peers[p].q + (a.pub_row0 + t) * a.ldq)[c] = o;
     }
   } else {
     for (int c = threadIdx.x; c < a.K; c += kActThreads) {
       const float v = SMOOTH ? x[c] * (a.s[c] * inv) : x[c] * inv;
       const int8_t o = static_cast<int8_t>(round_clamp(v, 127.0f));
       q[c] = o;
-      for (int p = 0; p < a.n_peers; ++p) a.peers[p].q[t * a.ldq + c] = o;
+      for (int p = 0; p < a.n_peers; ++p) a.peers[p].q[(a.pub_row0 + t) * a.ldq + c] = o;
     }
   }
   for (int c = a.K + threadIdx.x; c < a.k_fill; c += kActThreads) {
     q[c] = 0;
-    for (int p = 0; p < a.n_peers; ++p) a.peers[p].q[t * a.ldq + c] = 0;
+    for (int p = 0; p < a.n_peers; ++p) a.peers[p].q[(a.pub_row0 + t) * a.ldq + c] = 0;
   }
   if (a.pub_seq) publish_arrive(a);
 }
@@ -232,7 +233,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) topk_merge_kernel(const Merg
 cudaError_t launch_act_quant(const ActQuantLaunch &L, cudaStream_t st) {
   ActArgs a{L.x,     L.ldx,   L.K,       L.k_fill,  L.inv_smooth, L.inv_step,  L.safe_thresh,
             L.q,     L.ldq,   L.ratio,   L.peers,   L.n_peers,    L.pub_seq,   L.pub_arrive,
-            L.trace};
+            L.trace, L.pub_row0};
   const bool vec = (L.K % 4 == 0) && (L.ldx % 4 == 0) && (L.ldq % 4 == 0) &&
                    (reinterpret_cast<uintptr_t>(L.x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(L.q) % 4 == 0) &&

@@ -293,7 +293,8 @@ namespace w8a8 {
 
 w8a8_status linear_quant_input(w8a8_linear *l, const float *x, int64_t ldx, int T, int act_mode,
                                const PublishPeer *peers, int n_peers, unsigned *pub_seq,
-                               unsigned *pub_arrive, cudaStream_t s, unsigned long long *trace) {
+                               unsigned *pub_arrive, cudaStream_t s, unsigned long long *trace,
+                               int8_t *q_rows, int pub_row0) {
   ActQuantLaunch A = {};
   A.x = x;
   A.ldx = ldx;
@@ -304,10 +305,11 @@ w8a8_status linear_quant_input(w8a8_linear *l, const float *x, int64_t ldx, int 
   A.act_mode = act_mode;
   A.inv_step = l->inv_step;
   A.safe_thresh = l->safe_thresh;
-  A.q = l->xq;
+  A.q = q_rows ? q_rows : l->xq;
   A.ldq = l->k_pad;
   A.ratio = l->ratio;
   A.pdl = true;
+  A.pub_row0 = pub_row0;
   A.peers = peers;
   A.n_peers = n_peers;
   A.pub_seq = pub_seq;
@@ -331,8 +333,9 @@ bool linear_can_fuse(const w8a8_linear *l, int T, int act_mode, FusedQuant *fq) 
 w8a8_status linear_topk_quantized(w8a8_linear *l, int T, int act_mode, int out_mode, int k,
                                   int row_offset, float *topk_val, int32_t *topk_idx,
                                   float *logits, int64_t ldl, const ShardSync &sync, bool pdl,
-                                  cudaStream_t s, const FusedQuant *fq) {
-  if ((sync.seq || (fq && fq->pub_seq)) && T > 8)
+                                  cudaStream_t s, const FusedQuant *fq, const int8_t *x_rows,
+                                  const TopkRoute *route) {
+  if (((sync.seq && sync.n_ready == 0) || (fq && fq->pub_seq)) && T > 8)
     return fail(W8A8_ERR_INVALID_ARG, "a multi-device LM head takes at most 8 tokens a forward");
   const bool fused = fq && fq->x;
   for (int t0 = 0; t0 < T; t0 += 8) {
@@ -345,7 +348,7 @@ w8a8_status linear_topk_quantized(w8a8_linear *l, int T, int act_mode, int out_m
     GemvLaunch L = {};
     L.w = l->w;
     L.ldw = l->k_pad;
-    L.x = l->xq + static_cast<size_t>(t0) * l->k_pad;
+    L.x = (x_rows ? x_rows : l->xq) + static_cast<size_t>(t0) * l->k_pad;
     L.ldx = l->k_pad;
     L.T = tg;
     L.N = l->N;
@@ -365,6 +368,15 @@ w8a8_status linear_topk_quantized(w8a8_linear *l, int T, int act_mode, int out_m
     L.pdl = pdl;
     L.trace = plan.grid <= 2 * l->ctx->sm_count ? l->tc_trace : nullptr;
     L.sync = sync;
+    L.sync.hold = t0 + 8 < T ? 1 : 0;  // only the forward's last token group counts it
+    if (route) {
+      L.tk.val_dst = route->val_dst;
+      L.tk.idx_dst = route->idx_dst;
+      L.tk.dst_tokens = route->tokens;
+      L.tk.tok0 = t0;
+      L.tk.dst_row0 = route->row0;
+      L.tk.dst_ld = route->ld;
+    }
     if (fused) {
       L.fq = *fq;
       L.fq.x = fq->x + static_cast<size_t>(t0) * fq->ldx;

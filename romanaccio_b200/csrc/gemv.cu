@@ -240,18 +240,30 @@ __device__ void topk_epilogue(const GemvArgs &a, const GridTopkState &st, const 
   auto list_of = [row_offset, rows_per_cta](uint64_t key) {
     return (topk_key_id(key) - row_offset) / rows_per_cta;
   };
-  for (int t = 0; t < a.T; ++t)
-    grid_topk_select<R, NW>(a.tk.k, t, st, a.tk.val, a.tk.idx, stage, gather, &s_n, warp, lane,
-                            BlockSync{}, list_of);
-  if (a.sync.done) {
-    // Remote LM-head shard: val/idx went to GPU 0; publish them, then count the forward.
+  for (int t = 0; t < a.T; ++t) {
+    float *vr = a.tk.val + t * a.tk.k;
+    int32_t *ir = a.tk.idx + t * a.tk.k;
+    if (a.tk.val_dst) {
+      // the token's owner gathers it: row (g % dst_tokens) of owner g / dst_tokens
+      const int g = a.tk.tok0 + t;
+      const int64_t off = a.tk.dst_row0 + static_cast<int64_t>(g % a.tk.dst_tokens) * a.tk.dst_ld;
+      vr = a.tk.val_dst[g / a.tk.dst_tokens] + off;
+      ir = a.tk.idx_dst[g / a.tk.dst_tokens] + off;
+    }
+    grid_topk_select<R, NW>(a.tk.k, t, st, vr, ir, stage, gather, &s_n, warp, lane, BlockSync{},
+                            list_of);
+  }
+  if ((a.sync.done || a.sync.done_peers) && !a.sync.hold) {
+    // LM-head shard storing into other devices: publish the rows, then count the forward
+    // (system-scope fence, then relaxed counter stores = a release of the rows).
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
       __threadfence_system();
       const unsigned e = *a.sync.seq + 1u;
       *a.sync.seq = e;
-      st_relaxed_sys(a.sync.done, e);
+      if (a.sync.done) st_relaxed_sys(a.sync.done, e);
+      for (int p = 0; p < a.sync.n_done; ++p) st_relaxed_sys(a.sync.done_peers[p], e);
     }
   }
   if (threadIdx.x == 0) {
@@ -338,8 +350,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
       // and then bumps x_ready.  On a timeout the (stale) rows are still copied so the kernel
       // ends promptly; the error word records the failure.
       if (lane == 0) {
-        wait_flag_reached(a.sync.x_ready, *a.sync.seq + 1u, kXReadyLimitNs, a.err,
-                          kDevPeerTimeout);
+        const unsigned target = *a.sync.seq + 1u;
+        const int nr = a.sync.n_ready > 0 ? a.sync.n_ready : 1;
+        for (int p = 0; p < nr; ++p)
+          if (!wait_flag_reached(a.sync.x_ready + p, target, kXReadyLimitNs, a.err,
+                                 kDevPeerTimeout))
+            break;  // (one wait that ran out is enough: the rest would only add their limits)
         fence_proxy_async_global();
       }
       __syncwarp();

@@ -47,6 +47,14 @@ struct TopK {
   int32_t *idx;             // [T, k]
   float *logits;            // optional [T, ldl]
   int64_t ldl;
+  // Optional per-token destinations of the selected (val, idx) rows (an LM-head rank storing
+  // each token's candidates into the token owner's gather buffer): token t of the launch (global
+  // token tok0 + t) goes to val_dst[g / dst_tokens] + dst_row0 + (g % dst_tokens) * dst_ld.
+  float *const *val_dst;    // device array [n owners] (null: val / idx above)
+  int32_t *const *idx_dst;
+  int dst_tokens;
+  int tok0;
+  int64_t dst_row0, dst_ld;
 };
 
 // A destination of the int8 activation rows on another device (multi-device LM head).
@@ -61,6 +69,13 @@ struct ShardSync {
   unsigned *seq;            // shard device: forwards this shard completed (last CTA bumps it)
   const unsigned *x_ready;  // shard device: forwards whose int8 activations GPU 0 stored here
   unsigned *done;           // GPU 0 (peer pointer): forwards whose candidates this shard stored
+  // Multi-process head: x_ready holds n_ready counters (one per source rank, all must reach the
+  // forward's number) and the candidates' completion is stored into every done_peers[p].  With
+  // publish == 0 (a token group before the last of a forward) neither seq nor done is bumped.
+  int n_ready;              // 0 or 1: the single counter above
+  unsigned *const *done_peers;  // device array [n_done] (peer pointers) or null
+  int n_done;
+  int hold;                 // 1: do not bump seq / done (not the forward's last token group)
 };
 
 // Activation quantisation fused into a GEMV's prologue: every CTA quantises the fp32 rows into
@@ -253,6 +268,7 @@ struct ActQuantLaunch {
   unsigned *pub_seq;         // this device; null: no publication
   unsigned *pub_arrive;      // this device, zero between launches
   unsigned long long *trace; // optional: [0] entry of CTA 0, [1] peers' flags stored
+  int pub_row0;              // row t is stored at row pub_row0 + t of every peer's buffer
 };
 cudaError_t launch_act_quant(const ActQuantLaunch &L, cudaStream_t stream);
 

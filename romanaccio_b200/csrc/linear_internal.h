@@ -9,17 +9,32 @@
 
 namespace w8a8 {
 
+// q_rows (or null): where the quantised rows go instead of the linear's staging buffer;
+// pub_row0: the row of the peers' buffers that row 0 is stored at.
 w8a8_status linear_quant_input(w8a8_linear *l, const float *x, int64_t ldx, int T, int act_mode,
                                const PublishPeer *peers, int n_peers, unsigned *pub_seq,
                                unsigned *pub_arrive, cudaStream_t s,
-                               unsigned long long *trace = nullptr);
+                               unsigned long long *trace = nullptr, int8_t *q_rows = nullptr,
+                               int pub_row0 = 0);
+
+// Where each token's selected rows go when they are not [T, k] at topk_val / topk_idx: token t
+// (of the forward) to val_dst[t / tokens] + row0 + (t % tokens) * ld (device pointer tables).
+struct TopkRoute {
+  float *const *val_dst;
+  int32_t *const *idx_dst;
+  int tokens;
+  int64_t row0, ld;
+};
 
 // fq (or null): fp32 activations quantised in the GEMV's prologue (linear_can_fuse must hold)
 // instead of reading the staging buffer; with fq->pub_seq, the last CTA also publishes the rows.
+// x_rows (or null): int8 rows [T, staging ld] to read instead of the linear's staging buffer.
 w8a8_status linear_topk_quantized(w8a8_linear *l, int T, int act_mode, int out_mode, int k,
                                   int row_offset, float *topk_val, int32_t *topk_idx,
                                   float *logits, int64_t ldl, const ShardSync &sync, bool pdl,
-                                  cudaStream_t s, const FusedQuant *fq = nullptr);
+                                  cudaStream_t s, const FusedQuant *fq = nullptr,
+                                  const int8_t *x_rows = nullptr,
+                                  const TopkRoute *route = nullptr);
 
 // Whether T tokens of this linear can be quantised in the GEMV prologue (static activation
 // quantisation and a small enough resident slab); fills the linear's static parameters.

@@ -262,7 +262,7 @@ w8a8_status w8a8_lmhead_forward(w8a8_lmhead *lm, const float *h, int32_t T, int3
   for (int s = 1; s < n; ++s) {
     if (!lm->remote[s]) continue;
     DeviceScope d(lm->dev[s]);
-    w8a8::ShardSync sync;
+    w8a8::ShardSync sync = {};
     sync.seq = lm->counters[s];
     sync.x_ready = lm->counters[s] + 1;
     sync.done = lm->ctr0 + 2 + s;
@@ -334,6 +334,292 @@ w8a8_status w8a8_lmhead_set_trace(w8a8_lmhead *lm, unsigned long long *head_trac
     if (st != W8A8_SUCCESS) return st;
   }
   return W8A8_SUCCESS;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// One rank of a vocab-sharded LM head over processes (w8a8_lmhead_rank_*): one process per GPU,
+// the exchange done by this library with peer stores into CUDA-IPC-mapped device memory and
+// counters in device memory, so a rank's whole forward is three stream-ordered launches that a
+// CUDA graph can hold (no NCCL call, no host round trip, no cross-process stream event).
+//
+// Every rank exports one arena of its device memory:
+//   x_ready[64]  counters: x_ready[p] = forwards whose int8 rows rank p stored here
+//   done[64]     counters: done[s] = forwards whose candidates shard s stored here
+//   staging      int8 [world * max_T][k_pad]: rank p's rows of a T-token forward at p * T
+//   gather       fp32 / int32 [world lists][max_T][k_max]: list s = shard s's candidates for
+//                this rank's tokens
+// A forward of rank r (T tokens of its own, the same T on every rank):
+//   1. the activation quantisation (static in_step, as the reference's broadcast of the final
+//      hidden state to both dies, lfm3_v2.cpp:810-831) stores r's rows into every rank's staging
+//      at rows [r * T, (r + 1) * T) and then bumps x_ready[r] on every rank (system-scope fence +
+//      relaxed stores);
+//   2. r's shard GEMV streams its weights at once, waits (bounded) until every x_ready has
+//      reached the forward's number, runs the fused top-k over all world * T tokens, and its last
+//      CTA stores token t's candidates into the gather buffer of t's owner (list r), then bumps
+//      done[r] there;
+//   3. the merge waits (bounded) for every other shard's done counter and merges the world lists
+//      of r's own tokens (value desc, id asc).
+// Hazards across forwards need no extra wait: a rank re-publishes rows only after its merge saw
+// every shard finish (so every shard's GEMV has read the staging), and a shard stores candidates
+// of the next forward only after every rank published that forward's rows (so every merge of
+// the previous one has run).  Counters only grow; every rank must run the same forwards.
+struct w8a8_lmhead_rank {
+  w8a8_ctx *ctx = nullptr;
+  int rank = 0, world = 1, K = 0, V = 0, max_T = 0, k_max = 0, k_pad = 0, lo = 0, hi = 0;
+  float in_step = 0.0f;
+  w8a8_linear *shard = nullptr;
+  unsigned char *arena = nullptr;
+  size_t off_staging = 0, off_val = 0, off_idx = 0, arena_bytes = 0;
+  std::vector<unsigned char *> base;   // every rank's arena as seen from this process
+  std::vector<char> opened;            // base[p] came from cudaIpcOpenMemHandle
+  bool connected = false;
+  unsigned *local = nullptr;           // [0] forwards published, [1] publication arrival, [2] shard seq
+  w8a8::PublishPeer *peers = nullptr;  // [world] staging + x_ready[rank] of every rank
+  float **val_dst = nullptr;           // [world] list `rank` of every rank's gather
+  int32_t **idx_dst = nullptr;
+  unsigned **done_dst = nullptr;       // [world] done[rank] of every rank
+};
+
+namespace {
+
+constexpr int kRankMax = 64;
+constexpr size_t kCounterBytes = 2 * kRankMax * sizeof(unsigned);
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+void rank_free(w8a8_lmhead_rank *x) {
+  if (!x) return;
+  DeviceScope d(w8a8_ctx_device(x->ctx));
+  for (size_t p = 0; p < x->base.size(); ++p)
+    if (x->opened[p] && x->base[p]) cudaIpcCloseMemHandle(x->base[p]);
+  w8a8_linear_destroy(x->shard);
+  cudaFree(x->arena);
+  cudaFree(x->local);
+  cudaFree(x->peers);
+  cudaFree(x->val_dst);
+  cudaFree(x->idx_dst);
+  cudaFree(x->done_dst);
+  delete x;
+}
+
+// Device pointer tables of every rank's arena (base[p] for every p filled in).
+w8a8_status rank_tables(w8a8_lmhead_rank *x) {
+  const int W = x->world;
+  std::vector<w8a8::PublishPeer> peers(W);
+  std::vector<float *> val(W);
+  std::vector<int32_t *> idx(W);
+  std::vector<unsigned *> done(W);
+  const size_t list = static_cast<size_t>(x->rank) * x->max_T * x->k_max;
+  for (int p = 0; p < W; ++p) {
+    unsigned char *b = x->base[p];
+    unsigned *ctr = reinterpret_cast<unsigned *>(b);
+    peers[p].q = reinterpret_cast<int8_t *>(b + x->off_staging);
+    peers[p].flag = ctr + x->rank;                      // x_ready[rank] on rank p
+    done[p] = ctr + kRankMax + x->rank;                 // done[rank] on rank p
+    val[p] = reinterpret_cast<float *>(b + x->off_val) + list;
+    idx[p] = reinterpret_cast<int32_t *>(b + x->off_idx) + list;
+  }
+  cudaError_t e = cudaMemcpy(x->peers, peers.data(), W * sizeof(peers[0]), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(x->val_dst, val.data(), W * sizeof(float *), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(x->idx_dst, idx.data(), W * sizeof(int32_t *), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(x->done_dst, done.data(), W * sizeof(unsigned *), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  return cuda_status(e, "LM-head rank pointer tables");
+}
+
+}  // namespace
+
+extern "C" {
+
+w8a8_status w8a8_lmhead_rank_create(w8a8_ctx *ctx, int32_t rank, int32_t world, int32_t K,
+                                    int32_t V, const int8_t *shard_weights, int64_t ld,
+                                    const float *shard_acc_step, float in_step, int32_t max_T,
+                                    int32_t k_max, w8a8_lmhead_rank **out) {
+  if (!out) return invalid("out_rank is NULL");
+  *out = nullptr;
+  if (!ctx || !shard_weights || !shard_acc_step)
+    return invalid("ctx, shard_weights or shard_acc_step is NULL");
+  if (world < 1 || world > kRankMax || rank < 0 || rank >= world || K < 1 || V < world ||
+      ld < K || max_T < 1 || world * max_T > 64 || k_max < 1 || k_max > W8A8_TOPK_MAX ||
+      k_max > V / world)
+    return invalid("bad LM-head rank shape (rank, world <= 64, K, V, ld, max_tokens with "
+                   "world * max_tokens <= 64, or k_max)");
+  w8a8_lmhead_rank *x = new (std::nothrow) w8a8_lmhead_rank();
+  if (!x) return W8A8_ERR_NO_MEMORY;
+  x->ctx = ctx;
+  x->rank = rank;
+  x->world = world;
+  x->K = K;
+  x->V = V;
+  x->max_T = max_T;
+  x->k_max = k_max;
+  x->in_step = in_step;
+  x->k_pad = (K + 15) / 16 * 16;
+  x->lo = static_cast<int>((static_cast<int64_t>(rank) * V) / world);
+  x->hi = static_cast<int>((static_cast<int64_t>(rank + 1) * V) / world);
+  w8a8_linear_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.K = K;
+  d.N = x->hi - x->lo;
+  d.weights = shard_weights;
+  d.weights_ld = ld;
+  d.acc_step = shard_acc_step;
+  d.scale.out_dtype = W8A8_DTYPE_INT8;
+  d.scale.in_step = in_step;
+  d.scale.in_thresh = in_step * 127.0f;
+  d.scale.out_step = 1.0f;
+  w8a8_status st = w8a8_linear_create(ctx, &d, &x->shard);
+  if (st != W8A8_SUCCESS) {
+    rank_free(x);
+    return st;
+  }
+  DeviceScope ds(w8a8_ctx_device(ctx));
+  x->off_staging = align256(kCounterBytes);
+  x->off_val = x->off_staging + align256(static_cast<size_t>(world) * max_T * x->k_pad);
+  const size_t cells = static_cast<size_t>(world) * max_T * k_max;
+  x->off_idx = x->off_val + align256(cells * sizeof(float));
+  x->arena_bytes = x->off_idx + align256(cells * sizeof(int32_t));
+  cudaError_t e = cudaMalloc(&x->arena, x->arena_bytes);
+  if (e == cudaSuccess) e = cudaMemset(x->arena, 0, x->arena_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&x->local, 4 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(x->local, 0, 4 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMalloc(&x->peers, world * sizeof(w8a8::PublishPeer));
+  if (e == cudaSuccess) e = cudaMalloc(&x->val_dst, world * sizeof(float *));
+  if (e == cudaSuccess) e = cudaMalloc(&x->idx_dst, world * sizeof(int32_t *));
+  if (e == cudaSuccess) e = cudaMalloc(&x->done_dst, world * sizeof(unsigned *));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    rank_free(x);
+    return cuda_status(e, "LM-head rank arena");
+  }
+  x->base.assign(world, nullptr);
+  x->opened.assign(world, 0);
+  x->base[rank] = x->arena;
+  *out = x;
+  return W8A8_SUCCESS;
+}
+
+w8a8_status w8a8_lmhead_rank_export(const w8a8_lmhead_rank *x, void *handle_out) {
+  if (!x || !handle_out) return invalid("rank or handle_out is NULL");
+  DeviceScope d(w8a8_ctx_device(x->ctx));
+  cudaIpcMemHandle_t h;
+  w8a8_status st = cuda_status(cudaIpcGetMemHandle(&h, x->arena), "cudaIpcGetMemHandle");
+  if (st != W8A8_SUCCESS) return st;
+  static_assert(sizeof(h) == W8A8_LMHEAD_RANK_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle_out, &h, sizeof(h));
+  return W8A8_SUCCESS;
+}
+
+w8a8_status w8a8_lmhead_rank_connect(w8a8_lmhead_rank *x, const void *handles) {
+  if (!x || !handles) return invalid("rank or handles is NULL");
+  if (x->connected) return invalid("rank is already connected");
+  DeviceScope d(w8a8_ctx_device(x->ctx));
+  const unsigned char *hb = static_cast<const unsigned char *>(handles);
+  for (int p = 0; p < x->world; ++p) {
+    if (p == x->rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, hb + static_cast<size_t>(p) * W8A8_LMHEAD_RANK_HANDLE_BYTES, sizeof(h));
+    void *ptr = nullptr;
+    w8a8_status st = cuda_status(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess),
+                                 "cudaIpcOpenMemHandle");
+    if (st != W8A8_SUCCESS) return st;
+    x->base[p] = static_cast<unsigned char *>(ptr);
+    x->opened[p] = 1;
+  }
+  w8a8_status st = rank_tables(x);
+  if (st == W8A8_SUCCESS) x->connected = true;
+  return st;
+}
+
+w8a8_status w8a8_lmhead_rank_connect_local(w8a8_lmhead_rank *const *ranks, int32_t world) {
+  if (!ranks || world < 1) return invalid("ranks is NULL or world < 1");
+  for (int p = 0; p < world; ++p)
+    if (!ranks[p] || ranks[p]->world != world || ranks[p]->rank != p || ranks[p]->connected)
+      return invalid("ranks[p] must be rank p of the same world and not yet connected");
+  for (int r = 0; r < world; ++r) {
+    for (int p = 0; p < world; ++p) {
+      const int dr = w8a8_ctx_device(ranks[r]->ctx), dp = w8a8_ctx_device(ranks[p]->ctx);
+      if (dr != dp) {
+        w8a8_status st = enable_peer(dr, dp);
+        if (st != W8A8_SUCCESS) return st;
+      }
+      ranks[r]->base[p] = ranks[p]->arena;
+    }
+  }
+  for (int r = 0; r < world; ++r) {
+    DeviceScope d(w8a8_ctx_device(ranks[r]->ctx));
+    w8a8_status st = rank_tables(ranks[r]);
+    if (st != W8A8_SUCCESS) return st;
+    ranks[r]->connected = true;
+  }
+  return W8A8_SUCCESS;
+}
+
+w8a8_status w8a8_lmhead_rank_forward(w8a8_lmhead_rank *x, const float *h, int32_t T, int32_t k,
+                                     float *val, int32_t *idx, int32_t *argmax, void *stream) {
+  if (!x || !h || !val || !idx) return invalid("rank, h, val or idx is NULL");
+  if (!x->connected) return invalid("rank is not connected (w8a8_lmhead_rank_connect)");
+  if (T < 1 || T > x->max_T || k < 1 || k > x->k_max)
+    return invalid("T or k outside [1, max_tokens] / [1, k_max]");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceScope d(w8a8_ctx_device(x->ctx));
+  const int W = x->world;
+  int8_t *staging = reinterpret_cast<int8_t *>(x->arena + x->off_staging);
+  unsigned *ctr = reinterpret_cast<unsigned *>(x->arena);
+  // 1. this rank's rows into every rank's staging, then x_ready[rank] everywhere
+  w8a8_status st = w8a8::linear_quant_input(
+      x->shard, h, x->K, T, W8A8_ACT_STATIC, x->peers, W, x->local, x->local + 1, s, nullptr,
+      staging + static_cast<size_t>(x->rank) * T * x->k_pad, x->rank * T);
+  if (st != W8A8_SUCCESS) return st;
+  // 2. the shard's top-k over every rank's tokens, each token's list to its owner
+  w8a8::ShardSync sync = {};
+  sync.seq = x->local + 2;
+  sync.x_ready = ctr;
+  sync.n_ready = W;
+  sync.done_peers = x->done_dst;
+  sync.n_done = W;
+  w8a8::TopkRoute route = {x->val_dst, x->idx_dst, T, 0, x->k_max};
+  float *own_val = reinterpret_cast<float *>(x->arena + x->off_val);
+  int32_t *own_idx = reinterpret_cast<int32_t *>(x->arena + x->off_idx);
+  st = w8a8::linear_topk_quantized(x->shard, W * T, W8A8_ACT_STATIC, W8A8_OUT_F32_ACC, k, x->lo,
+                                   own_val, own_idx, nullptr, 0, sync, true, s, nullptr, staging,
+                                   &route);
+  if (st != W8A8_SUCCESS) return st;
+  // 3. merge the world lists of this rank's tokens once every other shard has stored them
+  w8a8::MergeLaunch L = {};
+  L.in_val = own_val;
+  L.in_idx = own_idx;
+  L.T = T;
+  L.n_lists = W;
+  L.k_in = k;
+  L.k_out = k;
+  L.list_stride = static_cast<int64_t>(x->max_T) * x->k_max;
+  L.token_stride = x->k_max;
+  L.out_val = val;
+  L.out_idx = idx;
+  L.argmax = argmax;
+  L.pdl = true;
+  uint64_t mask = 0;
+  for (int p = 0; p < W; ++p)
+    if (p != x->rank) mask |= 1ull << p;
+  if (mask) {
+    L.done = ctr + kRankMax;
+    L.remote_mask = mask;
+    L.pub_seq = x->local;
+    L.err = w8a8::linear_error_word(x->shard);
+  }
+  return cuda_status(w8a8::launch_topk_merge(L, s), "LM-head rank merge launch");
+}
+
+void w8a8_lmhead_rank_destroy(w8a8_lmhead_rank *x) { rank_free(x); }
+
+int32_t w8a8_lmhead_rank_shard_range(const w8a8_lmhead_rank *x, int32_t *lo, int32_t *hi) {
+  if (!x) return 0;
+  if (lo) *lo = x->lo;
+  if (hi) *hi = x->hi;
+  return x->hi - x->lo;
 }
 
 }  // extern "C"

@@ -162,12 +162,13 @@ __device__ bool grid_topk_arrive(const GridTopkState &st, int tid, int *s_flag, 
   return last;
 }
 
-// Last CTA: token t's top-k into val/idx[t * k ..].  NW * 32 threads (tid < NW * 32) take part;
+// Last CTA: token t's top-k into val_row[0 .. k) / idx_row[0 .. k) (the token's output rows).
+// NW * 32 threads (tid < NW * 32) take part;
 // `stage` holds NW * 32R keys and `gather` kTopkGatherKeys keys of shared memory; s_int is one
 // shared int.  list_of(key) gives the index of the CTA (list) that owns a key's vocab row.
 // Returns after a sync() over the NW warps.
 template <int R, int NW, typename Sync, typename ListOf>
-__device__ void grid_topk_select(int k, int t, const GridTopkState &st, float *val, int32_t *idx,
+__device__ void grid_topk_select(int k, int t, const GridTopkState &st, float *val_row, int32_t *idx_row,
                                  uint64_t *stage, uint64_t *gather, int *s_int, int warp, int lane,
                                  Sync sync, ListOf list_of) {
   const int G = gridDim.x;
@@ -206,8 +207,8 @@ __device__ void grid_topk_select(int k, int t, const GridTopkState &st, float *v
   cta_top_keys<R, NW>(gather, *s_int, false, stage, warp, lane, sync);
   if (warp == 0) {
     for (int e = lane; e < k; e += 32) {
-      val[t * k + e] = topk_key_value(stage[e]);
-      idx[t * k + e] = topk_key_id(stage[e]);
+      val_row[e] = topk_key_value(stage[e]);
+      idx_row[e] = topk_key_id(stage[e]);
     }
   }
   sync();

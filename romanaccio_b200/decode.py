@@ -7,10 +7,12 @@ of that path: each linear consumes the previous linear's output (o takes the q s
 down takes the gate slice of gate_up), so the chain has real data dependences.
 
 Multi-GPU (one process per GPU): every rank runs its own T tokens through a full replica of the
-linear stack, the final hidden states are all-gathered (the reference broadcasts the final
-hidden state into both dies' buffers, lfm3_v2.cpp:810-831), every rank runs its contiguous
-vocab shard of the LM head over all ranks' tokens, and only the per-shard top-k (value, id)
-pairs are all-gathered and merged.
+linear stack; each rank's int8-quantised final hidden states go to every rank (the reference
+broadcasts the final hidden state into both dies' buffers, lfm3_v2.cpp:810-831), every rank runs
+its contiguous vocab shard of the LM head over all ranks' tokens, and only each token's top-k
+(value, id) pairs go back to the token's owner, which merges them.  That exchange is done by the
+library (RankLmHead: peer stores into CUDA-IPC-mapped memory, device counters), so the whole step
+is one CUDA graph on every rank with no collective call.
 """
 from __future__ import annotations
 
@@ -22,9 +24,8 @@ import torch
 from ._lib import (ACT_STATIC, DTYPE_INT8, ERR_NOT_SUPPORTED, OUT_F32, OUT_F32_ACC,
                    TC_MIN_TOKENS, W8A8Error)
 from .chain import ChainStepSpec, DecodeChain
-from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
-from .lmhead import (LmHeadShard, candidate_buffers, exchange_candidates, shard_range,
-                     token_candidates)
+from .linear import Context, SubgraphScaleInfo, W8A8Linear
+from .lmhead import LmHeadShard, RankLmHead, shard_range
 from .quantize import build_linear
 from .synth import DecodeShape, activations, outlier_channels
 
@@ -87,6 +88,9 @@ class DecodeStack:
             self.linears, self.params_host = src.linears, src.params_host
             self.V, self.lo, self.hi = src.V, src.lo, src.hi
             self.lm_in_step, self.lm_host, self.lm = src.lm_in_step, src.lm_host, src.lm
+            self.rank_head = src.rank_head
+            if self.rank_head is not None and self.T * self.world > 64:
+                raise ValueError("a vocab-sharded head takes world * T <= 64 tokens a forward")
             self._shared = src  # keeps the owner alive
             self._buffers()
             self._plan_chain(use_chain)
@@ -119,19 +123,29 @@ class DecodeStack:
         self.lm_in_step = float(calib.abs().amax().item()) / 127.0
         acc_step = (self.lm_in_step * w_step).astype(np.float32)
         self.lm_host = (wq, acc_step)
-        self.lm = LmHeadShard(ctx, wq, acc_step, self.lm_in_step, row_offset=self.lo)
+        self.lm, self.rank_head = None, None
+        if self.world == 1:
+            self.lm = LmHeadShard(ctx, wq, acc_step, self.lm_in_step, row_offset=self.lo)
+        else:
+            # this rank's vocab shard; the library exchanges activations and candidates with the
+            # other ranks (peer stores into CUDA-IPC-mapped memory).  The 64-byte handles are
+            # exchanged once here, over the process group (set-up plumbing only).
+            import torch.distributed as dist
+            self.rank_head = RankLmHead(ctx, self.rank, self.world, wq, acc_step,
+                                        self.lm_in_step, V, max_tokens=max(self.T, 8) if
+                                        self.world * 8 <= 64 else self.T, k_max=self.k)
+            handles = [None] * self.world
+            dist.all_gather_object(handles, self.rank_head.export(), group=self.group)
+            self.rank_head.connect(handles)
         self._buffers()
         self._plan_chain(use_chain)
 
     def _buffers(self) -> None:
         """Persistent device buffers of one step."""
         dev, K = self.dev, self.shape.hidden
-        T_all = self.T * self.world
         self.x = torch.zeros((self.T, K), dtype=torch.float32, device=dev)
         self.outs = [torch.empty((self.T, N), dtype=torch.float32, device=dev)
                      for (_, _, N, _) in self.subgraphs]
-        self.h_all = torch.empty((T_all, K), dtype=torch.float32, device=dev)
-        self.cand, self.cand_all = candidate_buffers(T_all, self.k, self.world, dev)
         self.ids = torch.empty((self.T,), dtype=torch.int32, device=dev)
         self.top_val = torch.empty((self.T, self.k), dtype=torch.float32, device=dev)
         self.top_idx = torch.empty((self.T, self.k), dtype=torch.int32, device=dev)
@@ -178,10 +192,11 @@ class DecodeStack:
     def launches_per_step(self) -> int:
         """Kernels of this library launched per step."""
         T_all = self.T * self.world
-        # LM head: act_quant + top-k GEMV per group of 8 tokens (+ merge when sharded)
-        lm = 1 + (T_all + 7) // 8 + (1 if self.world > 1 else 0)
+        # LM head: act_quant + top-k GEMV per group of 8 tokens (+ merge when sharded, + the
+        # argmax copy when not)
+        lm = 1 + (T_all + 7) // 8 + 1
         if self.chain is not None:
-            return 1 + (0 if self.chain_lm else lm)
+            return 1 + (1 if self.chain_lm else lm)
         # each linear: act_quant + one tensor-core GEMM, or a GEMV per group of 8 tokens
         contraction = 1 if self.T >= TC_MIN_TOKENS else (self.T + 7) // 8
         return self.layers * 4 * (1 + contraction) + lm
@@ -219,33 +234,24 @@ class DecodeStack:
             self.lm.forward(h, self.k, OUT_F32_ACC, val=self.top_val, idx=self.top_idx)
             self.ids.copy_(self.top_idx[:, 0])
             return
-        import torch.distributed as dist
-        dist.all_gather_into_tensor(self.h_all, h, group=self.group)
-        self.lm.forward(self.h_all, self.k, OUT_F32_ACC, val=self.cand[0].view(torch.float32),
-                        idx=self.cand[1])
-        exchange_candidates(self.cand, self.cand_all, self.group)
-        vals, ids = token_candidates(self.cand_all, self.world, self.rank * self.T, self.T)
-        v, i, a = topk_merge(self.ctx, vals, ids, self.k)
-        self.top_val.copy_(v)
-        self.top_idx.copy_(i)
-        self.ids.copy_(a)
+        # this rank's shard over every rank's tokens; each token's candidates go to its owner,
+        # which merges them (all inside the library, on this stream)
+        self.rank_head.forward(h, self.k, val=self.top_val, idx=self.top_idx, argmax=self.ids)
 
     def run_device(self) -> None:
-        """The part of the step that needs no collective (everything when world == 1)."""
+        """One whole step on the device (the sharded head's exchange included)."""
         if self.chain is not None:
             self.chain.forward()
             if self.chain_lm:
                 self.ids.copy_(self.top_idx[:, 0])
-            elif self.world == 1:
+            else:
                 self.run_lm_head()
             return
         self.run_linears()
-        if self.world == 1:
-            self.run_lm_head()
+        self.run_lm_head()
 
     def capture(self) -> None:
-        """Captures the device part of the step in a CUDA graph (the LM head + exchange stays
-        eager for world > 1: the NCCL calls are not captured)."""
+        """Captures the whole step in a CUDA graph."""
         s = torch.cuda.Stream(device=self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(s):
@@ -262,8 +268,6 @@ class DecodeStack:
             self.graph.replay()
         else:
             self.run_device()
-        if self.world > 1:
-            self.run_lm_head()
 
     def step_host(self, x_host: torch.Tensor, ids_host: torch.Tensor) -> None:
         """End-to-end step through the public API: pinned host activations in, sampled ids out."""

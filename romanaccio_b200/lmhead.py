@@ -190,3 +190,85 @@ class MultiDeviceLmHead:
             self.close()
         except Exception:
             pass
+
+
+RANK_HANDLE_BYTES = 64
+
+
+class RankLmHead:
+    """One rank's part of an LM head vocab-sharded over processes (w8a8_lmhead_rank_*): this
+    rank's contiguous vocab rows; the exchange of activations and candidates between the ranks is
+    done by the library (peer stores into CUDA-IPC-mapped device memory, device counters), so
+    forward() is three launches on one stream and can be captured in a CUDA graph.
+
+    Set-up: create on every rank, exchange export() bytes (connect(handles) with the list of all
+    ranks' handles in rank order), or connect_local(heads) for ranks driven by one process.
+    """
+
+    def __init__(self, ctx: Context, rank: int, world: int, wq_rows: np.ndarray,
+                 acc_step_rows: np.ndarray, in_step: float, V: int, max_tokens: int = 8,
+                 k_max: int = 64):
+        import ctypes as C
+        from ._lib import check
+        self._lib = ctx._lib
+        self._check = check
+        self.ctx, self.rank, self.world, self.V = ctx, int(rank), int(world), int(V)
+        w = np.ascontiguousarray(wq_rows, dtype=np.int8)
+        st = np.ascontiguousarray(acc_step_rows, dtype=np.float32)
+        self.K = int(w.shape[1])
+        lo, hi = shard_range(V, world, rank)
+        if w.shape[0] != hi - lo or st.shape[0] != hi - lo:
+            raise ValueError(f"rank {rank} of {world} holds vocab rows [{lo}, {hi})")
+        h = C.c_void_p()
+        check(self._lib.w8a8_lmhead_rank_create(ctx.handle, self.rank, self.world, self.K,
+                                                self.V, w.ctypes.data, self.K, st.ctypes.data,
+                                                float(in_step), int(max_tokens), int(k_max),
+                                                C.byref(h)), "w8a8_lmhead_rank_create")
+        self.handle = h
+        self.lo, self.hi = lo, hi
+
+    def export(self) -> bytes:
+        import ctypes as C
+        buf = (C.c_ubyte * RANK_HANDLE_BYTES)()
+        self._check(self._lib.w8a8_lmhead_rank_export(self.handle, buf), "w8a8_lmhead_rank_export")
+        return bytes(buf)
+
+    def connect(self, handles: list[bytes]) -> None:
+        if len(handles) != self.world or any(len(b) != RANK_HANDLE_BYTES for b in handles):
+            raise ValueError("one 64-byte handle per rank, in rank order")
+        blob = b"".join(handles)
+        self._check(self._lib.w8a8_lmhead_rank_connect(self.handle, blob),
+                    "w8a8_lmhead_rank_connect")
+
+    @staticmethod
+    def connect_local(heads: list["RankLmHead"]) -> None:
+        import ctypes as C
+        arr = (C.c_void_p * len(heads))(*[x.handle.value for x in heads])
+        heads[0]._check(heads[0]._lib.w8a8_lmhead_rank_connect_local(arr, len(heads)),
+                        "w8a8_lmhead_rank_connect_local")
+
+    def forward(self, h: torch.Tensor, k: int, val=None, idx=None, argmax=None, stream=None):
+        from .linear import _stream
+        T = h.shape[0]
+        dev = h.device
+        v = val if val is not None else torch.empty((T, k), dtype=torch.float32, device=dev)
+        i = idx if idx is not None else torch.empty((T, k), dtype=torch.int32, device=dev)
+        a = argmax if argmax is not None else torch.empty((T,), dtype=torch.int32, device=dev)
+        if h.dtype != torch.float32 or not h.is_contiguous() or h.shape[1] != self.K:
+            raise ValueError("h must be a contiguous fp32 [T, K] tensor")
+        self._check(self._lib.w8a8_lmhead_rank_forward(self.handle, h.data_ptr(), T, int(k),
+                                                       v.data_ptr(), i.data_ptr(), a.data_ptr(),
+                                                       _stream(stream)), "w8a8_lmhead_rank_forward")
+        return v, i, a
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self._lib.w8a8_lmhead_rank_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
