@@ -359,6 +359,74 @@ def moe_record(ctx, dev, steps: int, warmup: int, peak: float, flush: torch.Tens
     return out
 
 
+def moe_ep_record(ctx, dev, rank: int, world: int, steps: int, warmup: int, peak: float) -> dict:
+    """Config 3 at N > 1: the DeepSeek-V2-Lite-shaped MoE layer expert-parallel over the `world`
+    ranks (experts e % world == rank, the library's peer-store exchange of the partial combines,
+    ordered sum), T = 1 and 64 tokens (the same tokens on every rank), device time max over
+    ranks; rank 0 checks the output against the oracle's expert-parallel combine of every rank's
+    requantised expert outputs (gathered after the timing, for the check only)."""
+    import torch.distributed as dist
+    sys.path.insert(0, str(ROOT))
+    from romanaccio_b200 import synth
+    from romanaccio_b200.moe import ExpertParallelMoE, MoELayer, make_moe_params
+    H, I, E, S, k = 2048, 1408, 64, 2, 6
+    p = make_moe_params(H=H, I=I, E=E, S=S, k=k, seed=3, device=dev)
+    layer = MoELayer(ctx, p, max_tokens=64)
+    ep = ExpertParallelMoE(layer, rank, world)
+    handles = [None] * world
+    dist.all_gather_object(handles, ep.export())
+    ep.connect(handles)
+    expert_bytes = 2 * I * H + H * I
+    out = {"workload": "deepseek-v2-lite-shaped W8A8 MoE layer, expert-parallel over "
+                       f"{world} GPUs (experts e % {world} == rank, partials exchanged by peer "
+                       "stores and summed in rank order)"}
+    ok_all = True
+    for T in (1, 64):
+        x = synth.activations(T, H, seed=100 + T)
+        xd = x.to(dev)
+        y = torch.empty((T, H), dtype=torch.float32, device=dev)
+        dist.barrier()
+        ms = time_steps(lambda: ep.forward(xd, out=y), steps, warmup)
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        ep.forward(xd, out=y)
+        torch.cuda.synchronize()
+        v = {kk: tt.cpu().numpy() for kk, tt in layer.views(T).items()}
+        parts = [None] * world
+        dist.all_gather_object(parts, {"down_q": v["down_q"], "idx": v["idx"]})
+        rec = {"ms_per_layer": round(ms, 4)}
+        if rank == 0:
+            from oracle import oracle as O
+            slots = k + S
+            yq = np.zeros_like(v["down_q"]).astype(np.int32)
+            for pi in range(T * slots):
+                tt_, j = divmod(pi, slots)
+                e = int(v["idx"][tt_, j]) if j < k else E + (j - k)
+                yq[pi] = parts[e % world]["down_q"][pi]
+            osc = np.stack([q.out_step_chan for q in p.dn])
+            want = O.moe_combine_ep(yq, v["idx"], v["w"], osc, E, slots, world)
+            idx_ref, _ = O.moe_route(x.numpy(), p.gate_w, k)
+            par = bool(np.array_equal(y.cpu().numpy(), want) and np.array_equal(v["idx"], idx_ref)
+                       and all(np.array_equal(q["idx"], v["idx"]) for q in parts))
+            ok_all &= par
+            active = len(set(v["idx"].reshape(-1).tolist())) + S
+            nbytes = active * expert_bytes
+            rec.update({"tok_s_per_layer": round(T / (ms / 1e3), 1), "active_experts": active,
+                        "roofline": {"bound": "hbm", "algorithmic_bytes": nbytes,
+                                     "note": "weights of the active experts over all ranks",
+                                     "achieved_gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                                     "peak_gbs": peak * world,
+                                     "frac": round(nbytes / (ms / 1e3) / 1e9 / (peak * world), 4)},
+                        "parity": par})
+        out[f"T{T}"] = rec
+        dist.barrier()
+    ep.close()
+    layer.close()
+    out["parity"] = ok_all
+    return out
+
+
 def per_config_records(ctx, dev, headline, args, peak: float) -> dict:
     """Untimed against the headline: one record per BASELINE configuration (decode configs 0, 1
     at T = 8 and 32, 3 and 4, the prefill sweep of config 2), each with its own CUDA-event time,
@@ -611,6 +679,10 @@ def run_ours(args) -> None:
     per_config = None
     if rank == 0 and world == 1 and not args.no_per_config:
         per_config = per_config_records(ctx, dev, stack, args, peak)
+    if world > 1 and not args.no_per_config:
+        # every rank takes part in the expert-parallel layer; rank 0 reports it
+        rec = moe_ep_record(ctx, dev, rank, world, args.config_steps, 3, peak)
+        per_config = {"c3_moe_v2lite_ep": rec, "all_parity": rec["parity"]}
 
     step_bytes = sb.linear + sb.lm_head
     value = world * T / (ms / 1e3)

@@ -379,6 +379,33 @@ void        w8a8_lmhead_rank_destroy(w8a8_lmhead_rank *rank);
 int32_t     w8a8_lmhead_rank_shard_range(const w8a8_lmhead_rank *rank, int32_t *lo, int32_t *hi);
 
 /* ---------------------------------------------------------------------------------------
+ * Expert parallelism of a MoE layer over processes (one process per GPU, every rank holding the
+ * same hidden states): rank r computes the experts e with e % world == r (shared expert s counts
+ * as e = n_routed + s) for every token, combines its own slots in slot order into a partial
+ * [T, H], and the library exchanges the partials -- peer stores into CUDA-IPC-mapped device
+ * memory, device counters with bounded waits, no NCCL call -- and sums them in rank order, so
+ * every rank gets the same [T, H] output.  With world = 2 this is the reference's even / odd
+ * split of the selected experts over its two dies and its die-by-die sum
+ * (src/LFM2.5-8B-A1B/lfm2_moe.cpp:2190-2432; MoERouter's per-die grouping, moe_router.hpp:100-130).
+ * Set-up as for w8a8_lmhead_rank_*: create, export (64 bytes), exchange, connect (or
+ * connect_local for ranks of one process).  While the ep object lives, w8a8_moe_forward of
+ * its layer computes only this rank's partial.  Forwards of every rank: the same sequence, the
+ * same T, on one stream per rank; graph-capturable.
+ * ------------------------------------------------------------------------------------- */
+#define W8A8_MOE_EP_HANDLE_BYTES 64
+typedef struct w8a8_moe_ep w8a8_moe_ep;
+
+w8a8_status w8a8_moe_ep_create(w8a8_moe *moe, int32_t rank, int32_t world, int32_t max_tokens,
+                               w8a8_moe_ep **out_ep);
+w8a8_status w8a8_moe_ep_export(const w8a8_moe_ep *ep, void *handle_out);
+w8a8_status w8a8_moe_ep_connect(w8a8_moe_ep *ep, const void *handles);
+w8a8_status w8a8_moe_ep_connect_local(w8a8_moe_ep *const *eps, int32_t world);
+/* hidden_dev fp32 [T, ldh] (the same on every rank) -> out_dev fp32 [T, ldo]. */
+w8a8_status w8a8_moe_ep_forward(w8a8_moe_ep *ep, const float *hidden_dev, int64_t ldh, int32_t T,
+                                float *out_dev, int64_t ldo, void *stream);
+void        w8a8_moe_ep_destroy(w8a8_moe_ep *ep);
+
+/* ---------------------------------------------------------------------------------------
  * Decode chain: a fixed sequence of linears, optionally ending with an LM-head top-k step, run
  * by ONE persistent cooperative kernel launch per forward.  Replaces the per-linear
  * pack -> submit_task -> unpack round trips of the reference's decode loop

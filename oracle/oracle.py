@@ -212,6 +212,33 @@ def moe_combine(yq: np.ndarray, idx: np.ndarray, w: np.ndarray, out_step_chan: n
     return out
 
 
+def moe_combine_ep(yq: np.ndarray, idx: np.ndarray, w: np.ndarray, out_step_chan: np.ndarray,
+                   n_routed: int, slots: int, world: int) -> np.ndarray:
+    """The expert-parallel combine: rank r sums, in slot order from 0.0f, the slots whose
+    expert e has e % world == r (shared expert s is e = n_routed + s), each term
+    float(yq) * (w * out_step_chan[e]) in fp32 as moe_combine; the layer output is the ranks'
+    partials added in rank order from 0.0f (the reference's per-die sums added die after die,
+    src/LFM2.5-8B-A1B/lfm2_moe.cpp:2190-2432, for world = 2)."""
+    y = np.asarray(yq).astype(np.float32)
+    ix = np.asarray(idx, np.int32)
+    ww = np.asarray(w, np.float32)
+    osc = np.asarray(out_step_chan, np.float32)
+    T, k = ix.shape
+    H = y.shape[1]
+    out = np.zeros((T, H), np.float32)
+    for r in range(world):
+        part = np.zeros((T, H), np.float32)
+        for t in range(T):
+            for j in range(slots):
+                e = int(ix[t, j]) if j < k else n_routed + (j - k)
+                if e % world != r:
+                    continue
+                wj = ww[t, j] if j < k else np.float32(1.0)
+                part[t] = part[t] + y[t * slots + j] * (np.float32(wj) * osc[e])
+        out = out + part
+    return out
+
+
 def rmsnorm_pack_dyntok(h: np.ndarray, norm: np.ndarray, smooth: np.ndarray, in_thresh: float,
                         eps: float = 1e-5):
     """fused_rms_norm_pack_dyntok_t1 per row of h [T, C] -> (q [T, C], ratio [T], u_out [T, C])."""

@@ -157,6 +157,12 @@ SIGNATURES = {
     "w8a8_moe_destroy": (None, [_P]),
     "w8a8_moe_route": (C.c_int, [_P, _P, _I64, _I32, _P, _P, _P]),
     "w8a8_moe_forward": (C.c_int, [_P, _P, _I64, _I32, _P, _I64, _P]),
+    "w8a8_moe_ep_create": (C.c_int, [_P, _I32, _I32, _I32, C.POINTER(_P)]),
+    "w8a8_moe_ep_export": (C.c_int, [_P, _P]),
+    "w8a8_moe_ep_connect": (C.c_int, [_P, _P]),
+    "w8a8_moe_ep_connect_local": (C.c_int, [C.POINTER(_P), _I32]),
+    "w8a8_moe_ep_forward": (C.c_int, [_P, _P, _I64, _I32, _P, _I64, _P]),
+    "w8a8_moe_ep_destroy": (None, [_P]),
     "w8a8_moe_views": (C.c_int, [_P, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(_P),
                                  C.POINTER(_P)]),
     "w8a8_chain_create": (C.c_int, [_P, C.POINTER(ChainStep), _I32, _I32, C.POINTER(_P)]),

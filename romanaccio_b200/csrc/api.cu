@@ -397,6 +397,8 @@ w8a8_status linear_reserve_tokens(w8a8_linear *l, int T) {
 
 int *linear_error_word(w8a8_linear *l) { return l->ctx->d_err; }
 
+int *ctx_error_word(w8a8_ctx *ctx) { return ctx->d_err; }
+
 }  // namespace w8a8
 
 

@@ -184,6 +184,9 @@ struct MoePairs {
   int T, k, slots, n_routed;
   const int32_t *routed_idx;  // [T, k]
   const float *routed_w;      // [T, k]
+  // Expert parallelism: only experts e with e % own_world == own_rank are computed and combined
+  // here (own_world <= 1: every expert).
+  int own_rank, own_world;
 };
 
 struct MoeRouteLaunch {
@@ -243,8 +246,26 @@ cudaError_t launch_moe_route(const MoeRouteLaunch &L, cudaStream_t stream);
 cudaError_t launch_moe_act_quant(const MoeActLaunch &L, bool dyn, cudaStream_t stream);
 cudaError_t launch_moe_gemv(const MoeGemvLaunch &L, cudaStream_t stream);
 cudaError_t launch_moe_swiglu(const float *gu, int I, int pairs, float *h, bool pdl,
-                              cudaStream_t stream);
+                              cudaStream_t stream, const MoePairs &P);
 cudaError_t launch_moe_combine(const MoeCombineLaunch &L, cudaStream_t stream);
+
+// Expert-parallel exchange of the per-rank partial combines [T, H] (w8a8_moe_ep_*).
+struct MoeEpLaunch {
+  const float *partial;       // this rank's [T, H] partial
+  float *const *dst;          // device array [world]: every rank's gather base
+  unsigned *const *done;      // device array [world]: done[rank] on every rank
+  int rank, world, T, H, max_T;
+  unsigned *pub_seq;          // this rank: partials published (the last CTA bumps it)
+  unsigned *pub_arrive;       // this rank: CTA arrivals (zero between launches)
+  const float *gather;        // this rank's gather base [2][world][max_T][H]
+  const unsigned *done_here;  // this rank's done[world]
+  float *out;                 // [T, ldo]
+  int64_t ldo;
+  int *err;
+  bool pdl;
+};
+cudaError_t launch_moe_ep_publish(const MoeEpLaunch &L, cudaStream_t stream);
+cudaError_t launch_moe_ep_sum(const MoeEpLaunch &L, cudaStream_t stream);
 
 // Activation quantisation (pack) of x [T, K] fp32 into q [T, ldq] int8 (+ ratio [T]).
 struct ActQuantLaunch {

@@ -45,5 +45,7 @@ int8_t *linear_staging(w8a8_linear *l);
 int linear_staging_ld(const w8a8_linear *l);
 w8a8_status linear_reserve_tokens(w8a8_linear *l, int T);
 int *linear_error_word(w8a8_linear *l);
+// The context's device error word (what w8a8_ctx_check reads).
+int *ctx_error_word(w8a8_ctx *ctx);
 
 }  // namespace w8a8

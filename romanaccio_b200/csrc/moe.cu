@@ -96,6 +96,11 @@ __device__ __forceinline__ int pair_expert(const MoePairs &P, int p) {
   return j < P.k ? P.routed_idx[t * P.k + j] : P.n_routed + (j - P.k);
 }
 
+// Whether this rank computes expert e (expert parallelism: e % world == rank).
+__device__ __forceinline__ bool expert_owned(const MoePairs &P, int e) {
+  return P.own_world <= 1 || e % P.own_world == P.own_rank;
+}
+
 // One CTA per pair: x = src[token or pair row], smoothed by the pair's expert vector.
 template <bool DYN>
 __global__ void __launch_bounds__(kMoeThreads) moe_act_quant_kernel(const MoeActLaunch L) {
@@ -103,6 +108,7 @@ __global__ void __launch_bounds__(kMoeThreads) moe_act_quant_kernel(const MoeAct
   pdl_wait();
   const int p = blockIdx.x;
   const int e = pair_expert(L.pairs, p);
+  if (!expert_owned(L.pairs, e)) return;  // another rank's expert
   const int row = L.per_pair_rows ? p : p / L.pairs.slots;
   const float *x = L.src + static_cast<int64_t>(row) * L.ld;
   const float *s = L.inv_smooth + static_cast<int64_t>(e) * L.K;
@@ -139,6 +145,7 @@ __global__ void __launch_bounds__(kMoeThreads) moe_gemv_kernel(const MoeGemvLaun
   pdl_wait();
   const int p = blockIdx.y;
   const int e = pair_expert(L.pairs, p);
+  if (!expert_owned(L.pairs, e)) return;  // another rank's expert
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int chunks = L.k_pad >> 4;  // 16-byte chunks per row
   const int8_t *xq = L.q + static_cast<int64_t>(p) * L.ldq;
@@ -195,13 +202,14 @@ __global__ void __launch_bounds__(kMoeThreads) moe_gemv_kernel(const MoeGemvLaun
 
 // h[p, i] = silu(gu[p, i]) * gu[p, I + i], silu(g) = g / (1 + exp(-g)).
 __global__ void __launch_bounds__(kMoeThreads) moe_swiglu_kernel(const float *gu, int I, int pairs,
-                                                                 float *h) {
+                                                                 float *h, const MoePairs P) {
   pdl_launch_dependents();
   pdl_wait();
   const int64_t total = static_cast<int64_t>(pairs) * I;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(kMoeThreads) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * kMoeThreads) {
     const int64_t p = i / I, c = i % I;
+    if (!expert_owned(P, pair_expert(P, static_cast<int>(p)))) continue;
     const float g = gu[p * 2 * I + c];
     const float u = gu[p * 2 * I + I + c];
     h[i] = (g / (1.0f + expf(-g))) * u;
@@ -219,6 +227,7 @@ __global__ void __launch_bounds__(kMoeThreads) moe_combine_kernel(const MoeCombi
     for (int j = 0; j < L.pairs.slots; ++j) {
       const int p = t * L.pairs.slots + j;
       const int e = pair_expert(L.pairs, p);
+      if (!expert_owned(L.pairs, e)) continue;  // summed by its owner
       const float w = j < L.pairs.k ? L.pairs.routed_w[t * L.pairs.k + j] : 1.0f;
       const int64_t o = static_cast<int64_t>(p) * L.H + c;
       const float v = L.in_i16 ? static_cast<float>(static_cast<const int16_t *>(L.yq)[o])
@@ -229,7 +238,70 @@ __global__ void __launch_bounds__(kMoeThreads) moe_combine_kernel(const MoeCombi
   }
 }
 
+// Expert-parallel exchange, step 1: this rank's partial [T, H] into buffer (e & 1), list `rank`,
+// of every rank's gather (peer stores; e = this forward's number), then the last CTA to arrive
+// counts the forward and stores it into done[rank] on every rank (system-scope fence + relaxed
+// stores: a release of the rows).
+__global__ void __launch_bounds__(kMoeThreads) moe_ep_publish_kernel(const MoeEpLaunch L) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ unsigned s_e;
+  __shared__ int s_last;
+  if (threadIdx.x == 0) s_e = *L.pub_seq + 1u;
+  __syncthreads();
+  const unsigned e = s_e;
+  const int t = blockIdx.y;
+  const int c = blockIdx.x * kMoeThreads + threadIdx.x;
+  if (c < L.H) {
+    const float v = L.partial[static_cast<int64_t>(t) * L.H + c];
+    const int64_t off =
+        ((static_cast<int64_t>(e & 1u) * L.world + L.rank) * L.max_T + t) * L.H + c;
+    for (int p = 0; p < L.world; ++p) L.dst[p][off] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(L.pub_arrive, 1u) == gridDim.x * gridDim.y - 1;
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    __threadfence_system();
+    *L.pub_seq = e;
+    *L.pub_arrive = 0u;
+    for (int p = 0; p < L.world; ++p) st_relaxed_sys(L.done[p], e);
+  }
+}
+
+// Step 2: once every other rank's partial of this forward has arrived (bounded waits), the
+// layer output out[t, c] = sum over ranks in rank order (from 0.0f) of the partials -- the
+// reference's per-die partial sums added die after die (lfm2_moe.cpp:2432).
+__global__ void __launch_bounds__(kMoeThreads) moe_ep_sum_kernel(const MoeEpLaunch L) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const unsigned e = *L.pub_seq;  // bumped by this rank's publication (stream order)
+  if (threadIdx.x < 32) {
+    for (int p = threadIdx.x; p < L.world; p += 32)
+      if (p != L.rank) wait_flag_reached(L.done_here + p, e, kWaitLimitNs, L.err, kDevPeerTimeout);
+  }
+  __syncthreads();
+  const int t = blockIdx.y;
+  const int c = blockIdx.x * kMoeThreads + threadIdx.x;
+  if (c >= L.H) return;
+  const float *g = L.gather + static_cast<int64_t>(e & 1u) * L.world * L.max_T * L.H;
+  float acc = 0.0f;
+  for (int p = 0; p < L.world; ++p) acc += g[(static_cast<int64_t>(p) * L.max_T + t) * L.H + c];
+  L.out[static_cast<int64_t>(t) * L.ldo + c] = acc;
+}
+
 }  // namespace
+
+cudaError_t launch_moe_ep_publish(const MoeEpLaunch &L, cudaStream_t st) {
+  const int bx = (L.H + kMoeThreads - 1) / kMoeThreads;
+  return launch_ex(moe_ep_publish_kernel, dim3(bx, L.T), dim3(kMoeThreads), 0, st, L.pdl, L);
+}
+
+cudaError_t launch_moe_ep_sum(const MoeEpLaunch &L, cudaStream_t st) {
+  const int bx = (L.H + kMoeThreads - 1) / kMoeThreads;
+  return launch_ex(moe_ep_sum_kernel, dim3(bx, L.T), dim3(kMoeThreads), 0, st, L.pdl, L);
+}
 
 cudaError_t launch_moe_route(const MoeRouteLaunch &L, cudaStream_t st) {
   const size_t smem = static_cast<size_t>(L.H + 2 * L.E) * sizeof(float);
@@ -260,12 +332,12 @@ cudaError_t launch_moe_gemv(const MoeGemvLaunch &L, cudaStream_t st) {
 }
 
 cudaError_t launch_moe_swiglu(const float *gu, int I, int pairs, float *h, bool pdl,
-                              cudaStream_t st) {
+                              cudaStream_t st, const MoePairs &P) {
   const int64_t total = static_cast<int64_t>(pairs) * I;
   int blocks = static_cast<int>((total + kMoeThreads - 1) / kMoeThreads);
   if (blocks > 4096) blocks = 4096;
   return launch_ex(moe_swiglu_kernel, dim3(blocks), dim3(kMoeThreads), 0, st, pdl, gu, I, pairs,
-                   h);
+                   h, P);
 }
 
 cudaError_t launch_moe_combine(const MoeCombineLaunch &L, cudaStream_t st) {

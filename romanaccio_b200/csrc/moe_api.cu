@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "kernels.h"
+#include "linear_internal.h"
 
 using namespace w8a8;
 
@@ -21,6 +22,7 @@ struct w8a8_moe {
   float scaling = 1.0f;
   int gu_trunc = 0, dn_trunc = 0, dn_i16 = 0;
   int ldh = 0, ldi = 0;  // round_up(H, 16), round_up(I, 16)
+  int own_rank = 0, own_world = 1;  // expert parallelism: experts e % own_world == own_rank
   // device tables
   float *gate_w = nullptr, *gate_b = nullptr;
   int8_t *gu_w = nullptr;          // [E+S, 2I, ldh]
@@ -106,6 +108,8 @@ MoePairs pairs_of(const w8a8_moe *m, int T) {
   P.n_routed = m->E;
   P.routed_idx = m->idx;
   P.routed_w = m->w;
+  P.own_rank = m->own_rank;
+  P.own_world = m->own_world;
   return P;
 }
 
@@ -264,7 +268,7 @@ w8a8_status w8a8_moe_forward(w8a8_moe *m, const float *hidden, int64_t ldh, int3
   s = cuda_status(launch_moe_gemv(G, st), "moe gate_up GEMV");
   if (s != W8A8_SUCCESS) return s;
 
-  s = cuda_status(launch_moe_swiglu(m->gu, m->I, n_pairs, m->h, true, st), "moe swiglu");
+  s = cuda_status(launch_moe_swiglu(m->gu, m->I, n_pairs, m->h, true, st, P), "moe swiglu");
   if (s != W8A8_SUCCESS) return s;
 
   MoeActLaunch B = {};
@@ -326,3 +330,203 @@ w8a8_status w8a8_moe_views(const w8a8_moe *m, const int32_t **idx, const float *
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Expert parallelism over processes (w8a8_moe_ep_*): rank r computes the experts e with
+// e % world == r for every token (the hidden states are the same on every rank), combines its
+// own slots in slot order into a partial [T, H], and the library exchanges the partials (peer
+// stores into CUDA-IPC-mapped memory, double-buffered by the forward's parity, device counters)
+// and sums them in rank order on every rank.  With world = 2 that is the reference's even / odd
+// split of the selected experts over its two dies and its die-by-die sum
+// (src/LFM2.5-8B-A1B/lfm2_moe.cpp:2190-2432: mlp_out of die 0, mlp_out_d1 of die 1, added after).
+// A rank publishes forward f + 1's partial only after its sum of forward f saw every rank's
+// forward-f partial, so a rank is at most one forward ahead of any other: two buffers suffice.
+struct w8a8_moe_ep {
+  w8a8_moe *moe = nullptr;
+  int rank = 0, world = 1, max_T = 0;
+  unsigned char *arena = nullptr;  // [0] done[64], then gather [2][world][max_T][H] fp32
+  size_t off_gather = 0, bytes = 0;
+  std::vector<unsigned char *> base;
+  std::vector<char> opened;
+  bool connected = false;
+  float *partial = nullptr;        // [max_T, H]
+  unsigned *local = nullptr;       // [0] forwards published, [1] publication arrivals
+  float **dst = nullptr;           // [world] gather base of every rank
+  unsigned **done = nullptr;       // [world] done[rank] of every rank
+};
+
+namespace {
+
+void ep_free(w8a8_moe_ep *x) {
+  if (!x) return;
+  DeviceScope d(x->moe ? x->moe->dev : 0);
+  for (size_t p = 0; p < x->base.size(); ++p)
+    if (x->opened[p] && x->base[p]) cudaIpcCloseMemHandle(x->base[p]);
+  cudaFree(x->arena);
+  cudaFree(x->partial);
+  cudaFree(x->local);
+  cudaFree(x->dst);
+  cudaFree(x->done);
+  if (x->moe) {
+    x->moe->own_rank = 0;
+    x->moe->own_world = 1;
+  }
+  delete x;
+}
+
+w8a8_status ep_tables(w8a8_moe_ep *x) {
+  std::vector<float *> dst(x->world);
+  std::vector<unsigned *> done(x->world);
+  for (int p = 0; p < x->world; ++p) {
+    dst[p] = reinterpret_cast<float *>(x->base[p] + x->off_gather);
+    done[p] = reinterpret_cast<unsigned *>(x->base[p]) + x->rank;
+  }
+  cudaError_t e = cudaMemcpy(x->dst, dst.data(), x->world * sizeof(float *), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(x->done, done.data(), x->world * sizeof(unsigned *), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  return cuda_status(e, "expert-parallel pointer tables");
+}
+
+}  // namespace
+
+extern "C" {
+
+w8a8_status w8a8_moe_ep_create(w8a8_moe *moe, int32_t rank, int32_t world, int32_t max_T,
+                               w8a8_moe_ep **out) {
+  if (!out) return invalid("out_ep is NULL");
+  *out = nullptr;
+  if (!moe) return invalid("moe is NULL");
+  if (world < 1 || world > 64 || rank < 0 || rank >= world || max_T < 1 || max_T > moe->max_T)
+    return invalid("bad expert-parallel shape (rank, world <= 64, max_tokens <= the layer's)");
+  w8a8_moe_ep *x = new (std::nothrow) w8a8_moe_ep();
+  if (!x) return W8A8_ERR_NO_MEMORY;
+  x->moe = moe;
+  x->rank = rank;
+  x->world = world;
+  x->max_T = max_T;
+  DeviceScope d(moe->dev);
+  x->off_gather = 256;
+  x->bytes = x->off_gather + 2ull * world * max_T * moe->H * sizeof(float);
+  cudaError_t e = cudaMalloc(&x->arena, x->bytes);
+  if (e == cudaSuccess) e = cudaMemset(x->arena, 0, x->bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&x->partial, static_cast<size_t>(max_T) * moe->H * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&x->local, 2 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(x->local, 0, 2 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMalloc(&x->dst, world * sizeof(float *));
+  if (e == cudaSuccess) e = cudaMalloc(&x->done, world * sizeof(unsigned *));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    ep_free(x);
+    return cuda_status(e, "expert-parallel arena");
+  }
+  x->base.assign(world, nullptr);
+  x->opened.assign(world, 0);
+  x->base[rank] = x->arena;
+  moe->own_rank = rank;
+  moe->own_world = world;
+  *out = x;
+  return W8A8_SUCCESS;
+}
+
+w8a8_status w8a8_moe_ep_export(const w8a8_moe_ep *x, void *handle_out) {
+  if (!x || !handle_out) return invalid("ep or handle_out is NULL");
+  DeviceScope d(x->moe->dev);
+  cudaIpcMemHandle_t h;
+  w8a8_status st = cuda_status(cudaIpcGetMemHandle(&h, x->arena), "cudaIpcGetMemHandle");
+  if (st != W8A8_SUCCESS) return st;
+  static_assert(sizeof(h) == W8A8_MOE_EP_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle_out, &h, sizeof(h));
+  return W8A8_SUCCESS;
+}
+
+w8a8_status w8a8_moe_ep_connect(w8a8_moe_ep *x, const void *handles) {
+  if (!x || !handles) return invalid("ep or handles is NULL");
+  if (x->connected) return invalid("ep is already connected");
+  DeviceScope d(x->moe->dev);
+  const unsigned char *hb = static_cast<const unsigned char *>(handles);
+  for (int p = 0; p < x->world; ++p) {
+    if (p == x->rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, hb + static_cast<size_t>(p) * W8A8_MOE_EP_HANDLE_BYTES, sizeof(h));
+    void *ptr = nullptr;
+    w8a8_status st = cuda_status(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess),
+                                 "cudaIpcOpenMemHandle");
+    if (st != W8A8_SUCCESS) return st;
+    x->base[p] = static_cast<unsigned char *>(ptr);
+    x->opened[p] = 1;
+  }
+  w8a8_status st = ep_tables(x);
+  if (st == W8A8_SUCCESS) x->connected = true;
+  return st;
+}
+
+w8a8_status w8a8_moe_ep_connect_local(w8a8_moe_ep *const *eps, int32_t world) {
+  if (!eps || world < 1) return invalid("eps is NULL or world < 1");
+  for (int p = 0; p < world; ++p)
+    if (!eps[p] || eps[p]->world != world || eps[p]->rank != p || eps[p]->connected)
+      return invalid("eps[p] must be rank p of the same world and not yet connected");
+  for (int r = 0; r < world; ++r) {
+    for (int p = 0; p < world; ++p) {
+      const int dr = eps[r]->moe->dev, dp = eps[p]->moe->dev;
+      if (dr != dp) {
+        int can = 0;
+        cudaDeviceCanAccessPeer(&can, dr, dp);
+        if (!can) {
+          set_last_error("no peer access between the ranks' devices");
+          return W8A8_ERR_NOT_SUPPORTED;
+        }
+        DeviceScope d(dr);
+        const cudaError_t e = cudaDeviceEnablePeerAccess(dp, 0);
+        if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+        else if (e != cudaSuccess) return cuda_status(e, "cudaDeviceEnablePeerAccess");
+      }
+      eps[r]->base[p] = eps[p]->arena;
+    }
+  }
+  for (int r = 0; r < world; ++r) {
+    DeviceScope d(eps[r]->moe->dev);
+    w8a8_status st = ep_tables(eps[r]);
+    if (st != W8A8_SUCCESS) return st;
+    eps[r]->connected = true;
+  }
+  return W8A8_SUCCESS;
+}
+
+w8a8_status w8a8_moe_ep_forward(w8a8_moe_ep *x, const float *hidden, int64_t ldh, int32_t T,
+                                float *out, int64_t ldo, void *stream) {
+  if (!x || !hidden || !out) return invalid("ep, hidden or out is NULL");
+  if (!x->connected) return invalid("ep is not connected (w8a8_moe_ep_connect)");
+  if (T < 1 || T > x->max_T) return invalid("T outside [1, max_tokens]");
+  if (ldo < x->moe->H) return invalid("ldo below hidden");
+  // this rank's experts and its partial combine
+  w8a8_status s = w8a8_moe_forward(x->moe, hidden, ldh, T, x->partial, x->moe->H, stream);
+  if (s != W8A8_SUCCESS) return s;
+  DeviceScope d(x->moe->dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MoeEpLaunch L = {};
+  L.partial = x->partial;
+  L.dst = x->dst;
+  L.done = x->done;
+  L.rank = x->rank;
+  L.world = x->world;
+  L.T = T;
+  L.H = x->moe->H;
+  L.max_T = x->max_T;
+  L.pub_seq = x->local;
+  L.pub_arrive = x->local + 1;
+  L.gather = reinterpret_cast<const float *>(x->arena + x->off_gather);
+  L.done_here = reinterpret_cast<const unsigned *>(x->arena);
+  L.out = out;
+  L.ldo = ldo;
+  L.err = w8a8::ctx_error_word(x->moe->ctx);
+  L.pdl = true;
+  s = cuda_status(launch_moe_ep_publish(L, st), "expert-parallel publication");
+  if (s != W8A8_SUCCESS) return s;
+  return cuda_status(launch_moe_ep_sum(L, st), "expert-parallel sum");
+}
+
+void w8a8_moe_ep_destroy(w8a8_moe_ep *x) { ep_free(x); }
+
+}  // extern "C"
+

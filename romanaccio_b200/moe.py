@@ -166,3 +166,65 @@ class MoELayer:
             self.close()
         except Exception:
             pass
+
+
+EP_HANDLE_BYTES = 64
+
+
+class ExpertParallelMoE:
+    """Expert parallelism of one MoE layer over processes (w8a8_moe_ep_*): this rank computes
+    the experts e with e % world == rank for every token and the library exchanges and sums the
+    ranks' partial combines in rank order (peer stores into CUDA-IPC-mapped memory), so forward()
+    returns the whole layer's output on every rank.  The layer's own forward() computes only
+    this rank's partial while this object lives.
+
+    Set-up: create on every rank, exchange export() bytes and connect(handles in rank order), or
+    connect_local(eps) for ranks of one process (one per GPU).
+    """
+
+    def __init__(self, layer: MoELayer, rank: int, world: int, max_tokens: int | None = None):
+        self.layer = layer
+        self._lib = layer._lib
+        self.rank, self.world = int(rank), int(world)
+        self.max_tokens = int(max_tokens or layer.max_tokens)
+        h = C.c_void_p()
+        check(self._lib.w8a8_moe_ep_create(layer.handle, self.rank, self.world,
+                                           self.max_tokens, C.byref(h)), "w8a8_moe_ep_create")
+        self.handle = h
+
+    def export(self) -> bytes:
+        buf = (C.c_ubyte * EP_HANDLE_BYTES)()
+        check(self._lib.w8a8_moe_ep_export(self.handle, buf), "w8a8_moe_ep_export")
+        return bytes(buf)
+
+    def connect(self, handles: list[bytes]) -> None:
+        if len(handles) != self.world or any(len(b) != EP_HANDLE_BYTES for b in handles):
+            raise ValueError("one 64-byte handle per rank, in rank order")
+        check(self._lib.w8a8_moe_ep_connect(self.handle, b"".join(handles)), "w8a8_moe_ep_connect")
+
+    @staticmethod
+    def connect_local(eps: list["ExpertParallelMoE"]) -> None:
+        arr = (C.c_void_p * len(eps))(*[x.handle.value for x in eps])
+        check(eps[0]._lib.w8a8_moe_ep_connect_local(arr, len(eps)), "w8a8_moe_ep_connect_local")
+
+    def forward(self, hidden: torch.Tensor, out: torch.Tensor | None = None,
+                stream=None) -> torch.Tensor:
+        T = hidden.shape[0]
+        y = out if out is not None else torch.empty((T, self.layer.p.hidden), dtype=torch.float32,
+                                                    device=hidden.device)
+        check(self._lib.w8a8_moe_ep_forward(self.handle, hidden.data_ptr(), hidden.stride(0), T,
+                                            y.data_ptr(), y.stride(0), _stream(stream)),
+              "w8a8_moe_ep_forward")
+        return y
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self._lib.w8a8_moe_ep_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
