@@ -189,14 +189,85 @@ def cpu_step_fn(params, lm, T: int, shape):
     return run, orc.cores
 
 
+def cpu_model_name() -> str:
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def reference_cpp_available() -> bool:
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    return O.ref_available()
+
+
+def reference_cpp_baseline(params, lm, T: int, shape, seconds: float) -> dict | None:
+    """The decode step through the reference's own C++ where it has CPU code (oracle.ReferenceDecode:
+    its pack / unpack per linear, TransformerSession's host fp32 LM head, Sampler::sample
+    greedy; the NPU GEMM + requant in between is the C restatement), timed for about `seconds`
+    on every host core this process may use.  None when the reference C++ is not built."""
+    if T != 1 or not reference_cpp_available():
+        return None
+    from oracle.oracle import ReferenceDecode
+    wq, acc_step, in_step = lm
+    w_f32 = (wq.astype(np.float32) * (acc_step / np.float32(in_step))[:, None]).astype(np.float32)
+    rd = ReferenceDecode(params, w_f32, T, shape)
+    del w_f32
+    x0 = np.random.default_rng(0).standard_normal((T, shape.hidden)).astype(np.float32)
+    rd.run(x0)
+    for key in rd.seconds:
+        rd.seconds[key] = 0.0
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n < 2:
+        rd.run(x0)
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    out = {"value": T / dt, "unit": "tok/s", "cores": rd.cores, "kind": "reference",
+           "cpu_model": cpu_model_name(),
+           "sample": f"{n} full decode steps: the reference's pack_npu_input_int8_dyntok / "
+                     "unpack_npu_output_int8_dyntok around each linear's int8 GEMM + QuantM "
+                     "requant (the NPU step: C restatement, OpenMP), TransformerSession's host "
+                     "fp32 LM head over 151936 rows and Sampler::sample (greedy), compiled from "
+                     "the reference sources",
+           "ms_per_step_by_piece": {k: round(v / n * 1e3, 3) for k, v in rd.seconds.items()}}
+    rd.close()
+    return out
+
+
 def run_reference(args) -> None:
     rank = env_int("RANK", 0)
     if rank != 0:
         return
     from romanaccio_b200 import synth
     T = args.batch
-    params, lm = cpu_model(T, synth.QWEN25_15B.layers)
-    run, cores = cpu_step_fn(params, lm, T, synth.QWEN25_15B)
+    shape = synth.QWEN25_15B
+    params, lm = cpu_model(T, shape.layers)
+    if T == 1 and reference_cpp_available():
+        # the reference's own C++ where it has CPU code for the path (see ReferenceDecode)
+        from oracle.oracle import ReferenceDecode
+        wq, acc_step, in_step = lm
+        w_f32 = (wq.astype(np.float32) * (acc_step / np.float32(in_step))[:, None]).astype(np.float32)
+        rd = ReferenceDecode(params, w_f32, T, shape)
+        del w_f32
+        x0 = np.random.default_rng(0).standard_normal((T, shape.hidden)).astype(np.float32)
+
+        def run():
+            return rd.run(x0)
+
+        cores, kind = rd.cores, "reference"
+        sample = (f"{args.steps} full decode steps: the reference's pack / unpack around each "
+                  "linear's int8 GEMM + requant (NPU step: C restatement, OpenMP), "
+                  "TransformerSession's host fp32 LM head and Sampler::sample, compiled from the "
+                  "reference sources")
+    else:
+        run, cores = cpu_step_fn(params, lm, T, shape)
+        kind = "port"
+        sample = (f"{args.steps} full decode steps (all 28 layers + LM head), C restatement of "
+                  "the reference path, OpenMP")
     for _ in range(args.warmup):
         run()
     t0 = time.perf_counter()
@@ -211,9 +282,8 @@ def run_reference(args) -> None:
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": WORKLOAD, "batch_per_gpu": T, "layers": synth.QWEN25_15B.layers,
                    "vocab": synth.QWEN25_15B.vocab, "parallelism": "host cores (OpenMP)"},
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} full decode steps (all 28 layers + LM head), "
-                                   "C restatement of the reference path, OpenMP"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": kind,
+                         "cpu_model": cpu_model_name(), "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -673,8 +743,14 @@ def run_ours(args) -> None:
                 break
         dt = (time.perf_counter() - t0) / n
         cpu = {"value": T / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+               "cpu_model": cpu_model_name(),
                "sample": f"{n} full decode steps of the same workload (28 layers + LM head), "
                          "C restatement of the reference path, OpenMP"}
+        ref_cpp = reference_cpp_baseline(stack.params_host, (stack.lm_host[0], stack.lm_host[1],
+                                                             stack.lm_in_step), T, shape,
+                                         args.cpu_seconds)
+        if ref_cpp is not None:
+            cpu["reference_cpp"] = ref_cpp
 
     per_config = None
     if rank == 0 and world == 1 and not args.no_per_config:

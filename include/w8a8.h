@@ -259,6 +259,11 @@ w8a8_status w8a8_lmhead_create(w8a8_ctx *const *ctxs, int32_t n_shards, int32_t 
 w8a8_status w8a8_lmhead_forward(w8a8_lmhead *lmhead, const float *h_dev, int32_t T, int32_t k,
                                 float *topk_val_dev, int32_t *topk_idx_dev, int32_t *argmax_dev,
                                 void *stream);
+/* Fuses the LM head's input RMSNorm (fused_emb_norm_broadcast_t1, lfm3_v2.cpp:810-831; the
+ * arithmetic of w8a8_emb_norm_pack, emb_norm_scaled_dev on the device of ctxs[0]) into the
+ * forward's quantisation: h is then the un-normalised final hidden state.  NULL turns it off. */
+w8a8_status w8a8_lmhead_set_input_norm(w8a8_lmhead *lmhead, const float *emb_norm_scaled_dev,
+                                       float eps);
 void        w8a8_lmhead_destroy(w8a8_lmhead *lmhead);
 int32_t     w8a8_lmhead_shards(const w8a8_lmhead *lmhead);
 /* Diagnostics (no reference counterpart): head_trace_dev (device 0, 8 uint64, or NULL) receives
@@ -375,6 +380,10 @@ w8a8_status w8a8_lmhead_rank_forward(w8a8_lmhead_rank *rank, const float *h_dev,
                                      int32_t k, float *topk_val_dev, int32_t *topk_idx_dev,
                                      int32_t *argmax_dev, void *stream);
 void        w8a8_lmhead_rank_destroy(w8a8_lmhead_rank *rank);
+/* Fuses the LM head's input RMSNorm (w8a8_emb_norm_pack's arithmetic) into the forward's
+ * quantisation step: h is then the un-normalised final hidden state.  NULL turns it off. */
+w8a8_status w8a8_lmhead_rank_set_input_norm(w8a8_lmhead_rank *rank,
+                                            const float *emb_norm_scaled_dev, float eps);
 /* Number of vocab rows of this rank's shard; *lo / *hi (may be NULL) its first / end vocab id. */
 int32_t     w8a8_lmhead_rank_shard_range(const w8a8_lmhead_rank *rank, int32_t *lo, int32_t *hi);
 
@@ -503,6 +512,13 @@ w8a8_status w8a8_rmsnorm_pack_dyntok(w8a8_ctx *ctx, const float *h_dev, int64_t 
                                      float in_thresh, float eps, int8_t *q_dev, int64_t ldq,
                                      float *ratio_dev, float *u_out_dev, int64_t ldu,
                                      void *stream);
+/* w8a8_emb_norm_pack replaces fused_emb_norm_broadcast_t1 (lfm3_v2.cpp:810-831), the LM head's
+ * input step: q[t, c] = round_clamp(h * inv_rms * emb_norm_scaled[c], 127) with inv_rms from the
+ * reference's ordered sum of squares and emb_norm_scaled[c] = norm_weight[c] * (1 / in_step)
+ * (lfm3_v2.cpp:3906-3912): a static-mode int8 input of the LM head.  C <= 12288. */
+w8a8_status w8a8_emb_norm_pack(w8a8_ctx *ctx, const float *h_dev, int64_t ldh, int32_t T,
+                               int32_t C, const float *emb_norm_scaled_dev, float eps,
+                               int8_t *q_dev, int64_t ldq, void *stream);
 w8a8_status w8a8_post_op_ffn_pack(w8a8_ctx *ctx, const float *op_out_dev, int64_t ldo,
                                   const float *post_norm_dev, const float *h_dev, int64_t ldh,
                                   int32_t T, int32_t C, const float *ffn_scaled_dev, float eps,

@@ -100,3 +100,18 @@ void orc_lmhead_topk_omp(const float *x, int32_t T, int32_t K, int32_t V, const 
         }
     }
 }
+
+/* The NPU step of one linear alone (it has no CPU code in the reference): int8 GEMM of the packed
+ * rows q [T, K] with w [N, K] and the QuantM requant to int8, yq [T, N] (row-major).  Timed between
+ * the reference's own pack_npu_input_int8_dyntok and unpack_npu_output_int8_dyntok in bench.py's
+ * reference-C++ baseline. */
+void orc_gemm_requant_omp(const int8_t *q, int32_t T, int32_t K, int32_t N, const int8_t *w,
+                          const int16_t *quant_m, int32_t trunc, int8_t *yq) {
+#pragma omp parallel for schedule(static)
+    for (int32_t n = 0; n < N; ++n) {
+        const int8_t *wr = w + (int64_t)n * K;
+        for (int32_t t = 0; t < T; ++t)
+            yq[(int64_t)t * N + n] =
+                (int8_t)orc_requant_one(dot_i8(q + (int64_t)t * K, wr, K), quant_m[n], trunc, 127);
+    }
+}

@@ -36,10 +36,12 @@ _ORACLE_SIGS = {
                                        _I64]),
     "orc_post_op_ffn_pack": (None, [_P, _I64, _P, _P, _I64, _I32, _I32, _P, _F, _P, _I64, _P,
                                     _I64]),
+    "orc_emb_norm_pack": (None, [_P, _I64, _I32, _I32, _P, _F, _P, _I64]),
     "orc_num_threads": (C.c_int, []),
     "orc_set_threads": (None, [C.c_int]),
     "orc_linear_dyntok_omp": (None, [_P, _I32, _I32, _I32, _P, _P, _F, _P, _I32, _P, _P, _P, _P]),
     "orc_lmhead_topk_omp": (None, [_P, _I32, _I32, _I32, _P, _F, _P, _I32, _P, _P, _P, _P]),
+    "orc_gemm_requant_omp": (None, [_P, _I32, _I32, _I32, _P, _P, _I32, _P]),
 }
 _REF_SIGS = {
     "ref_round_clamp_f32": (C.c_int32, [_F, _F]),
@@ -50,6 +52,10 @@ _REF_SIGS = {
     "ref_sampler_greedy": (C.c_int32, [_P, C.c_size_t]),
     "ref_rmsnorm_pack_dyntok": (C.c_int, [_P, C.c_int, _P, _P, _F, _F, _P, _P, _P]),
     "ref_post_op_ffn_pack": (C.c_int, [_P, _P, _P, _P, _P, _P, C.c_int, _F]),
+    "ref_emb_norm_pack": (C.c_int, [_P, C.c_int, _P, _F, _P]),
+    "ref_session_create": (_P, [C.c_int, C.c_int, _P]),
+    "ref_session_lm_head": (C.c_int, [_P, _P, _P]),
+    "ref_session_destroy": (None, [_P]),
     "ref_sampler_run": (C.c_int, [_F, C.c_int, _F, _F, _F, C.c_int, C.c_int, C.c_uint, _P,
                                   C.c_int, _P, C.c_int, C.c_size_t, _P]),
     "ref_moe_route": (C.c_int, [_P, C.c_int, C.c_int, _P, _P, C.c_int, C.c_int, C.c_int, _F, _P, _P]),
@@ -253,6 +259,27 @@ def rmsnorm_pack_dyntok(h: np.ndarray, norm: np.ndarray, smooth: np.ndarray, in_
     return q, ratio, u
 
 
+def emb_norm_pack(h: np.ndarray, emb_norm_scaled: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """fused_emb_norm_broadcast_t1 per row of h [T, C] -> q [T, C] int8."""
+    hh = _c(h, np.float32)
+    T, Cn = hh.shape
+    q = np.empty((T, Cn), np.int8)
+    lib().orc_emb_norm_pack(_p(hh), Cn, T, Cn, _p(_c(emb_norm_scaled, np.float32)), float(eps),
+                            _p(q), Cn)
+    return q
+
+
+def ref_emb_norm_pack(h_row: np.ndarray, emb_norm_scaled: np.ndarray, eps: float = 1e-5):
+    """The reference's fused_emb_norm_broadcast_t1 on one row (compiled from its source)."""
+    hh = _c(h_row, np.float32)
+    q = np.empty(hh.shape[0], np.int8)
+    rc = ref().ref_emb_norm_pack(_p(hh), hh.shape[0], _p(_c(emb_norm_scaled, np.float32)),
+                                 float(eps), _p(q))
+    if rc != 0:
+        raise RuntimeError(f"ref_emb_norm_pack returned {rc}")
+    return q
+
+
 def post_op_ffn_pack(op_out: np.ndarray, post_norm: np.ndarray, h: np.ndarray,
                      ffn_scaled: np.ndarray, eps: float = 1e-5):
     """fused_post_op_residual_ffn_pack_mlp_t1 per row -> (h_mid [T, C], q [T, C])."""
@@ -440,3 +467,82 @@ class DecodeOracle:
                                 C.c_float(self.in_step_lm), p(self.acc_step_lm), self.k,
                                 p(self.logits), p(self.qlm), p(self.val), p(self.idx))
         return bufs["down"].copy(), self.val.copy(), self.idx.copy()
+
+
+class ReferenceDecode:
+    """One decode step through the reference's own C++ wherever the reference has CPU code for it
+    (TIMED BASELINE ONLY, compiled from its sources into _ref/libref.so): per linear its
+    pack_npu_input_int8_dyntok (src/LFM3/lfm3_v2.cpp:1050-1141, OpenMP), the NPU's int8 GEMM and
+    QuantM requant (no CPU code in the reference: the C restatement, OpenMP) and its
+    unpack_npu_output_int8_dyntok (:1143-1183); then TransformerSession's host LM head
+    (transformer_session.cpp:597-612, fp32 rows, OpenMP) and Sampler::sample (sampler.cpp:83-179,
+    greedy) over the whole vocabulary.  params / lm as DecodeOracle; the LM head runs on the fp32
+    rows wq * w_step (what its host fallback holds)."""
+
+    def __init__(self, params, lm_f32_rows: np.ndarray, T: int, shape):
+        import os
+        self.C = C
+        self.lib, self.ref = lib(), ref()
+        self.lib.orc_set_threads(len(os.sched_getaffinity(0)))
+        self.cores = int(self.lib.orc_num_threads())
+        if T != 1:
+            raise ValueError("the reference's host LM head takes one hidden state per call")
+        self.T, self.shape = T, shape
+        self.bufs = {name: np.empty((T, N), np.float32) for (name, K, N, _) in shape.subgraphs()}
+        self.q = np.empty((T, max(kk for (_, kk, _, _) in shape.subgraphs())), np.int8)
+        self.yq = np.empty((T, max(n for (_, _, n, _) in shape.subgraphs())), np.int8)
+        self.ratio = np.empty((T,), np.float32)
+        V, K = lm_f32_rows.shape
+        w = np.ascontiguousarray(lm_f32_rows, np.float32)
+        self.session = self.ref.ref_session_create(K, V, _p(w))
+        self.logits = np.empty(V, np.float32)
+        self.V = V
+        self.prepared = [(name, prm.wq.shape[1], prm.wq.shape[0], np.ascontiguousarray(prm.wq),
+                          np.ascontiguousarray(prm.in_inv_smooth, np.float32), prm.in_thresh,
+                          np.ascontiguousarray(prm.quant_m), prm.trunc,
+                          np.ascontiguousarray(prm.out_step_chan, np.float32))
+                         for name, prm in params]
+        self.seconds = {"pack": 0.0, "gemm_requant": 0.0, "unpack": 0.0, "lm_head": 0.0,
+                        "sampler": 0.0}
+
+    def run(self, x0: np.ndarray) -> int:
+        import time
+        ref, lib, shape, bufs, clk = self.ref, self.lib, self.shape, self.bufs, time.perf_counter
+        x = np.ascontiguousarray(x0, dtype=np.float32)
+        for (name, K, N, wq, inv, thr, qm, tr, osc) in self.prepared:
+            if name == "o":
+                x = np.ascontiguousarray(bufs["qkv"][:, :shape.q])
+            elif name == "down":
+                x = np.ascontiguousarray(bufs["gate_up"][:, :shape.ffn])
+            elif name == "gate_up":
+                x = bufs["o"]
+            t0 = clk()
+            ref.ref_pack_int8_dyntok(_p(x), self.T, K, float(thr), _p(inv), _p(self.q), _p(self.ratio))
+            t1 = clk()
+            lib.orc_gemm_requant_omp(_p(self.q), self.T, K, N, _p(wq), _p(qm), tr, _p(self.yq))
+            t2 = clk()
+            ref.ref_unpack_int8(_p(self.yq), self.T, N, 0.0, _p(osc), _p(self.ratio), _p(bufs[name]))
+            t3 = clk()
+            self.seconds["pack"] += t1 - t0
+            self.seconds["gemm_requant"] += t2 - t1
+            self.seconds["unpack"] += t3 - t2
+            x = bufs["down"] if name == "down" else x
+        t0 = clk()
+        ref.ref_session_lm_head(self.session, _p(bufs["down"]), _p(self.logits))
+        t1 = clk()
+        tok = int(ref.ref_sampler_greedy(_p(self.logits), self.V))
+        self.seconds["sampler"] += clk() - t1
+        self.seconds["lm_head"] += t1 - t0
+        return tok
+
+    def close(self) -> None:
+        if getattr(self, "session", None):
+            self.ref.ref_session_destroy(self.session)
+            self.session = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+

@@ -139,6 +139,13 @@ int ref_rmsnorm_pack_dyntok(const float *h, int C, const float *norm, const floa
     return 0;
 }
 
+// fused_emb_norm_broadcast_t1 (T = 1 row): q [C] (the second die's copy is checked equal).
+int ref_emb_norm_pack(const float *h, int C, const float *emb_norm_scaled, float eps, int8_t *q) {
+    std::vector<int8_t> q1(static_cast<size_t>(C));
+    fused_emb_norm_broadcast_t1(h, emb_norm_scaled, q, q1.data(), C, eps);
+    return std::memcmp(q, q1.data(), static_cast<size_t>(C)) == 0 ? 0 : -2;
+}
+
 // fused_post_op_residual_ffn_pack_mlp_t1 (T = 1 row): h_mid [C], q [C].
 int ref_post_op_ffn_pack(const float *op_out, const float *post_norm, const float *h, float *h_mid,
                          const float *ffn_scaled, int8_t *q, int C, float eps) {

@@ -21,6 +21,7 @@
  *   orc_moe_route     src/eswin_runtime/src/llm/moe_router.cpp:92-130, 211-260 (MoERouter::route)
  *   orc_moe_combine   src/LFM2.5-8B-A1B/lfm2_moe.cpp:2300-2318 (weighted expert combine)
  *   orc_rmsnorm_pack_dyntok  src/LFM3/lfm3_v2.cpp:652-700 fused_rms_norm_pack_dyntok_t1
+ *   orc_emb_norm_pack        src/LFM3/lfm3_v2.cpp:810-831 fused_emb_norm_broadcast_t1
  *   orc_post_op_ffn_pack     src/LFM3/lfm3_v2.cpp:702-765 fused_post_op_residual_ffn_pack_mlp_t1
  *
  * Compile without fast-math and with -ffp-contract=off so every float step rounds like the
@@ -315,6 +316,21 @@ void orc_rmsnorm_pack_dyntok(const float *h, int64_t ldh, int32_t T, int32_t C, 
         for (int32_t i = 0; i < C; ++i)
             q[(int64_t)t * ldq + i] = (int8_t)orc_round_clamp(hr[i] * inv_rms * smooth[i] * inv_step,
                                                               127.0f);
+    }
+}
+
+/* fused_emb_norm_broadcast_t1 (lfm3_v2.cpp:810-831), row by row of [T, C]: the LM head's input
+ * step, inv_rms = 1 / sqrt(sum_sq / C + eps) with the four-chain sum of squares, then
+ * q = round_clamp(h * inv_rms * emb_norm_scaled, 127) (emb_norm_scaled = norm weight * (1 /
+ * in_step), lfm3_v2.cpp:3906-3912). */
+void orc_emb_norm_pack(const float *h, int64_t ldh, int32_t T, int32_t C,
+                       const float *emb_norm_scaled, float eps, int8_t *q, int64_t ldq) {
+    for (int32_t t = 0; t < T; ++t) {
+        const float *hr = h + (int64_t)t * ldh;
+        const float inv_rms = 1.0f / sqrtf(orc_sum_sq4(hr, C) / (float)C + eps);
+        for (int32_t i = 0; i < C; ++i)
+            q[(int64_t)t * ldq + i] =
+                (int8_t)orc_round_clamp(hr[i] * inv_rms * emb_norm_scaled[i], 127.0f);
     }
 }
 

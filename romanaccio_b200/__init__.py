@@ -9,7 +9,7 @@ from ._lib import (ACT_DYNTOK, ACT_STATIC, DTYPE_FP16, DTYPE_INT8, DTYPE_INT16, 
 from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
 from .lmhead import (LmHeadShard, MultiDeviceLmHead, RankLmHead, VocabShardedLmHead,
                      shard_range)
-from .norm import post_op_ffn_pack, rmsnorm_pack_dyntok
+from .norm import emb_norm_pack, emb_norm_scaled, post_op_ffn_pack, rmsnorm_pack_dyntok
 from .package import load_quant_scales, read_weight_region, untile_int8, untile_int16
 from .sampler import CandidateSampler, SamplingConfig
 
@@ -21,5 +21,5 @@ __all__ = [
     "RankLmHead",
     "VocabShardedLmHead",
     "shard_range", "CandidateSampler", "SamplingConfig", "rmsnorm_pack_dyntok",
-    "post_op_ffn_pack", "load_quant_scales", "read_weight_region", "untile_int8", "untile_int16",
+    "post_op_ffn_pack", "emb_norm_pack", "emb_norm_scaled", "load_quant_scales", "read_weight_region", "untile_int8", "untile_int16",
 ]

@@ -31,6 +31,8 @@ struct ActArgs {
   unsigned *pub_seq, *pub_arrive;
   unsigned long long *trace;
   int pub_row0;
+  const float *emb;
+  float eps;
 };
 
 // Publication of the quantised rows to other devices: every CTA's stores are fenced at system
@@ -53,6 +55,48 @@ __device__ void publish_arrive(const ActArgs &a) {
 // One CTA per token row.  DYN: amax_t = max_c |x*s| (NaN ignored as by `if (a > amax)`),
 // amax_t = max(amax_t, 1e-8), ratio_t = amax_t / max(in_thresh, 1e-8), inv = 127 / amax_t.
 // q = round_clamp(x * (s * inv), 127) with the reference's association of the products.
+// fused_emb_norm_broadcast_t1 (src/LFM3/lfm3_v2.cpp:810-831) for one token row per CTA: the
+// row is staged in shared memory, four threads run the reference's four interleaved
+// sum-of-squares chains in order over the multiple-of-4 prefix, thread 0 combines them as
+// (s0 + s1) + (s2 + s3) and adds the tail one by one, inv_rms = 1 / sqrt(sum / C + eps) (IEEE),
+// and q[c] = round_clamp(x[c] * inv_rms * emb[c], 127) with the reference's left-to-right
+// products; the rows go to q and, like act_quant_kernel, to every peer.
+constexpr int kEmbNormMaxK = 12288;  // fp32 row in 48 KB of dynamic shared memory
+
+__global__ void __launch_bounds__(kActThreads) emb_norm_pack_kernel(const ActArgs a) {
+  extern __shared__ float row[];
+  __shared__ float s_part[4], s_inv;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const float *x = a.x + t * a.ldx;
+  for (int c = threadIdx.x; c < a.K; c += kActThreads) row[c] = x[c];
+  __syncthreads();
+  const int K4 = a.K & ~3;
+  if (threadIdx.x < 4) {
+    float sum = 0.0f;
+    for (int c = threadIdx.x; c < K4; c += 4) sum += row[c] * row[c];
+    s_part[threadIdx.x] = sum;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sum = (s_part[0] + s_part[1]) + (s_part[2] + s_part[3]);
+    for (int c = K4; c < a.K; ++c) sum += row[c] * row[c];
+    s_inv = 1.0f / sqrtf(sum / static_cast<float>(a.K) + a.eps);
+  }
+  __syncthreads();
+  const float inv_rms = s_inv;
+  int8_t *q = a.q + t * a.ldq;
+  for (int c = threadIdx.x; c < a.k_fill; c += kActThreads) {
+    const int8_t o = c < a.K ? static_cast<int8_t>(round_clamp(row[c] * inv_rms * a.emb[c], 127.0f))
+                             : static_cast<int8_t>(0);
+    q[c] = o;
+    for (int p = 0; p < a.n_peers; ++p) a.peers[p].q[(a.pub_row0 + t) * a.ldq + c] = o;
+  }
+  if (a.ratio && threadIdx.x == 0) a.ratio[t] = 1.0f;
+  if (a.pub_seq) publish_arrive(a);
+}
+
 template <bool DYN, bool SMOOTH, bool VEC>
 __global__ void __launch_bounds__(kActThreads) act_quant_kernel(const ActArgs a) {
   pdl_launch_dependents();
@@ -233,11 +277,16 @@ __global__ void __launch_bounds__(kMergeWarps * 32) topk_merge_kernel(const Merg
 cudaError_t launch_act_quant(const ActQuantLaunch &L, cudaStream_t st) {
   ActArgs a{L.x,     L.ldx,   L.K,       L.k_fill,  L.inv_smooth, L.inv_step,  L.safe_thresh,
             L.q,     L.ldq,   L.ratio,   L.peers,   L.n_peers,    L.pub_seq,   L.pub_arrive,
-            L.trace, L.pub_row0};
+            L.trace, L.pub_row0, L.emb_norm, L.eps};
   const bool vec = (L.K % 4 == 0) && (L.ldx % 4 == 0) && (L.ldq % 4 == 0) &&
                    (reinterpret_cast<uintptr_t>(L.x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(L.q) % 4 == 0) &&
                    (L.inv_smooth == nullptr || reinterpret_cast<uintptr_t>(L.inv_smooth) % 16 == 0);
+  if (L.emb_norm) {
+    if (L.K > kEmbNormMaxK || L.act_mode != kActStatic) return cudaErrorInvalidValue;
+    return launch_ex(emb_norm_pack_kernel, dim3(L.T), dim3(kActThreads),
+                     static_cast<size_t>(L.K) * sizeof(float), st, L.pdl, a);
+  }
   const bool dyn = L.act_mode == kActDyntok;
   const bool sm = L.inv_smooth != nullptr;
   if (dyn && sm) return act_dispatch_vec<true, true>(a, L.T, vec, st, L.pdl);

@@ -294,7 +294,7 @@ namespace w8a8 {
 w8a8_status linear_quant_input(w8a8_linear *l, const float *x, int64_t ldx, int T, int act_mode,
                                const PublishPeer *peers, int n_peers, unsigned *pub_seq,
                                unsigned *pub_arrive, cudaStream_t s, unsigned long long *trace,
-                               int8_t *q_rows, int pub_row0) {
+                               int8_t *q_rows, int pub_row0, const float *emb_norm, float eps) {
   ActQuantLaunch A = {};
   A.x = x;
   A.ldx = ldx;
@@ -310,6 +310,8 @@ w8a8_status linear_quant_input(w8a8_linear *l, const float *x, int64_t ldx, int 
   A.ratio = l->ratio;
   A.pdl = true;
   A.pub_row0 = pub_row0;
+  A.emb_norm = emb_norm;
+  A.eps = eps;
   A.peers = peers;
   A.n_peers = n_peers;
   A.pub_seq = pub_seq;

@@ -290,6 +290,11 @@ struct ActQuantLaunch {
   unsigned *pub_arrive;      // this device, zero between launches
   unsigned long long *trace; // optional: [0] entry of CTA 0, [1] peers' flags stored
   int pub_row0;              // row t is stored at row pub_row0 + t of every peer's buffer
+  // Optional RMSNorm in front of a static quantisation (the LM head's input step,
+  // fused_emb_norm_broadcast_t1): q = round_clamp(x * inv_rms * emb_norm[c], 127) with inv_rms
+  // from the reference's ordered sum of squares; emb_norm = norm weight / in_step (K <= 12288).
+  const float *emb_norm;
+  float eps;
 };
 cudaError_t launch_act_quant(const ActQuantLaunch &L, cudaStream_t stream);
 

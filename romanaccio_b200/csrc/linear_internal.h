@@ -15,7 +15,8 @@ w8a8_status linear_quant_input(w8a8_linear *l, const float *x, int64_t ldx, int 
                                const PublishPeer *peers, int n_peers, unsigned *pub_seq,
                                unsigned *pub_arrive, cudaStream_t s,
                                unsigned long long *trace = nullptr, int8_t *q_rows = nullptr,
-                               int pub_row0 = 0);
+                               int pub_row0 = 0, const float *emb_norm = nullptr,
+                               float eps = 0.0f);
 
 // Where each token's selected rows go when they are not [T, k] at topk_val / topk_idx: token t
 // (of the forward) to val_dst[t / tokens] + row0 + (t % tokens) * ld (device pointer tables).

@@ -52,6 +52,8 @@ struct w8a8_lmhead {
   float *cand_val = nullptr;            // [n][max_T * k_max]
   int32_t *cand_idx = nullptr;
   unsigned long long *trace = nullptr;  // optional diagnostics timeline (device 0)
+  const float *emb_norm = nullptr;      // optional input RMSNorm (device 0), see set_input_norm
+  float eps = 0.0f;
 };
 
 namespace {
@@ -276,7 +278,8 @@ w8a8_status w8a8_lmhead_forward(w8a8_lmhead *lm, const float *h, int32_t T, int3
   // when the rows do not fit that, a quantisation kernel publishes them first.
   DeviceScope d(dev0);
   w8a8::FusedQuant fq;
-  const bool fused = w8a8::linear_can_fuse(lm->shards[0], T, W8A8_ACT_STATIC, &fq);
+  const bool fused =
+      !lm->emb_norm && w8a8::linear_can_fuse(lm->shards[0], T, W8A8_ACT_STATIC, &fq);
   w8a8_status st = W8A8_SUCCESS;
   if (fused) {
     fq.x = h;
@@ -287,7 +290,8 @@ w8a8_status w8a8_lmhead_forward(w8a8_lmhead *lm, const float *h, int32_t T, int3
     fq.trace = lm->trace;
   } else {
     st = w8a8::linear_quant_input(lm->shards[0], h, lm->K, T, W8A8_ACT_STATIC, lm->peers, n - 1,
-                                  lm->ctr0, lm->ctr0 + 1, s0, lm->trace);
+                                  lm->ctr0, lm->ctr0 + 1, s0, lm->trace, nullptr, 0,
+                                  lm->emb_norm, lm->eps);
     if (st != W8A8_SUCCESS) return st;
   }
   for (int s = 0; s < n; ++s) {
@@ -319,6 +323,14 @@ w8a8_status w8a8_lmhead_forward(w8a8_lmhead *lm, const float *h, int32_t T, int3
   }
   L.trace = lm->trace;
   return cuda_status(w8a8::launch_topk_merge(L, s0), "LM-head merge launch");
+}
+
+w8a8_status w8a8_lmhead_set_input_norm(w8a8_lmhead *lm, const float *emb_norm_scaled, float eps) {
+  if (!lm) return invalid("lmhead is NULL");
+  if (emb_norm_scaled && lm->K > 12288) return invalid("input norm needs K <= 12288");
+  lm->emb_norm = emb_norm_scaled;
+  lm->eps = eps;
+  return W8A8_SUCCESS;
 }
 
 void w8a8_lmhead_destroy(w8a8_lmhead *lm) { lmhead_free(lm); }
@@ -380,6 +392,8 @@ struct w8a8_lmhead_rank {
   float **val_dst = nullptr;           // [world] list `rank` of every rank's gather
   int32_t **idx_dst = nullptr;
   unsigned **done_dst = nullptr;       // [world] done[rank] of every rank
+  const float *emb_norm = nullptr;     // optional input RMSNorm, see set_input_norm
+  float eps = 0.0f;
 };
 
 namespace {
@@ -571,7 +585,7 @@ w8a8_status w8a8_lmhead_rank_forward(w8a8_lmhead_rank *x, const float *h, int32_
   // 1. this rank's rows into every rank's staging, then x_ready[rank] everywhere
   w8a8_status st = w8a8::linear_quant_input(
       x->shard, h, x->K, T, W8A8_ACT_STATIC, x->peers, W, x->local, x->local + 1, s, nullptr,
-      staging + static_cast<size_t>(x->rank) * T * x->k_pad, x->rank * T);
+      staging + static_cast<size_t>(x->rank) * T * x->k_pad, x->rank * T, x->emb_norm, x->eps);
   if (st != W8A8_SUCCESS) return st;
   // 2. the shard's top-k over every rank's tokens, each token's list to its owner
   w8a8::ShardSync sync = {};
@@ -611,6 +625,15 @@ w8a8_status w8a8_lmhead_rank_forward(w8a8_lmhead_rank *x, const float *h, int32_
     L.err = w8a8::linear_error_word(x->shard);
   }
   return cuda_status(w8a8::launch_topk_merge(L, s), "LM-head rank merge launch");
+}
+
+w8a8_status w8a8_lmhead_rank_set_input_norm(w8a8_lmhead_rank *x, const float *emb_norm_scaled,
+                                            float eps) {
+  if (!x) return invalid("rank is NULL");
+  if (emb_norm_scaled && x->K > 12288) return invalid("input norm needs K <= 12288");
+  x->emb_norm = emb_norm_scaled;
+  x->eps = eps;
+  return W8A8_SUCCESS;
 }
 
 void w8a8_lmhead_rank_destroy(w8a8_lmhead_rank *x) { rank_free(x); }

@@ -218,3 +218,36 @@ w8a8_status w8a8_post_op_ffn_pack(w8a8_ctx *ctx, const float *op_out, int64_t ld
 }
 
 }  // extern "C"
+
+extern "C" w8a8_status w8a8_emb_norm_pack(w8a8_ctx *ctx, const float *h_dev, int64_t ldh,
+                                          int32_t T, int32_t C, const float *emb_norm_scaled_dev,
+                                          float eps, int8_t *q_dev, int64_t ldq, void *stream) {
+  if (!ctx || !h_dev || !emb_norm_scaled_dev || !q_dev) {
+    w8a8::set_last_error("ctx, h, emb_norm_scaled or q is NULL");
+    return W8A8_ERR_INVALID_ARG;
+  }
+  if (T < 1 || C < 1 || C > 12288 || ldh < C || ldq < C) {
+    w8a8::set_last_error("T >= 1, 1 <= C <= 12288, ldh >= C and ldq >= C required");
+    return W8A8_ERR_INVALID_ARG;
+  }
+  w8a8::ActQuantLaunch A = {};
+  A.x = h_dev;
+  A.ldx = ldh;
+  A.T = T;
+  A.K = C;
+  A.k_fill = C;
+  A.act_mode = w8a8::kActStatic;
+  A.q = q_dev;
+  A.ldq = ldq;
+  A.emb_norm = emb_norm_scaled_dev;
+  A.eps = eps;
+  const cudaError_t e = w8a8::launch_act_quant(A, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    char buf[256];
+    std::snprintf(buf, sizeof(buf), "emb norm pack launch: %s", cudaGetErrorString(e));
+    w8a8::set_last_error(buf);
+    return W8A8_ERR_CUDA;
+  }
+  return W8A8_SUCCESS;
+}
+

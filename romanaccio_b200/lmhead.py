@@ -155,6 +155,14 @@ class MultiDeviceLmHead:
     def shards(self) -> int:
         return int(self._lib.w8a8_lmhead_shards(self.handle))
 
+    def set_input_norm(self, emb_norm_scaled: torch.Tensor | None, eps: float = 1e-5) -> None:
+        """Fuses the reference's LM-head input RMSNorm (fused_emb_norm_broadcast_t1) into the
+        forward: h is then the un-normalised final hidden state.  None turns it off."""
+        self._norm = emb_norm_scaled  # kept alive: the library holds the device pointer
+        self._check(self._lib.w8a8_lmhead_set_input_norm(
+            self.handle, emb_norm_scaled.data_ptr() if emb_norm_scaled is not None else None,
+            float(eps)), "w8a8_lmhead_set_input_norm")
+
     def forward(self, h: torch.Tensor, k: int, val=None, idx=None, argmax=None, stream=None):
         from .linear import _stream
         T = h.shape[0]
@@ -239,6 +247,14 @@ class RankLmHead:
         blob = b"".join(handles)
         self._check(self._lib.w8a8_lmhead_rank_connect(self.handle, blob),
                     "w8a8_lmhead_rank_connect")
+
+    def set_input_norm(self, emb_norm_scaled: torch.Tensor | None, eps: float = 1e-5) -> None:
+        """Fuses the reference's LM-head input RMSNorm (fused_emb_norm_broadcast_t1) into the
+        forward's quantisation: h is then the un-normalised final hidden state."""
+        self._norm = emb_norm_scaled
+        self._check(self._lib.w8a8_lmhead_rank_set_input_norm(
+            self.handle, emb_norm_scaled.data_ptr() if emb_norm_scaled is not None else None,
+            float(eps)), "w8a8_lmhead_rank_set_input_norm")
 
     @staticmethod
     def connect_local(heads: list["RankLmHead"]) -> None:

@@ -1,7 +1,9 @@
-"""The reference's fused norm + quantisation steps around each linear, on the GPU
-(w8a8_rmsnorm_pack_dyntok, w8a8_post_op_ffn_pack; lfm3_v2.cpp:652-765), bit-identical to it."""
+"""The reference's fused norm + quantisation steps around each linear and in front of the LM
+head, on the GPU (w8a8_rmsnorm_pack_dyntok, w8a8_post_op_ffn_pack, w8a8_emb_norm_pack;
+lfm3_v2.cpp:652-831), bit-identical to it."""
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 from ._lib import check
@@ -42,3 +44,25 @@ def post_op_ffn_pack(ctx: Context, op_out: torch.Tensor, post_norm: torch.Tensor
         h.stride(0), T, C, ffn_scaled.data_ptr(), float(eps), h_mid.data_ptr(), C, q.data_ptr(), C,
         _stream(stream)), "w8a8_post_op_ffn_pack")
     return h_mid, q
+
+
+def emb_norm_scaled(weight: np.ndarray, in_step: float) -> np.ndarray:
+    """The LM head's input-norm table as the reference loader builds it (lfm3_v2.cpp:3906-3912):
+    weight[c] * (1 / in_step), in fp32."""
+    inv_step = np.float32(1.0) / np.float32(in_step)
+    return (np.asarray(weight, np.float32) * inv_step).astype(np.float32)
+
+
+def emb_norm_pack(ctx: Context, h: torch.Tensor, emb_norm_scaled_t: torch.Tensor,
+                  eps: float = 1e-5, stream=None) -> torch.Tensor:
+    """fused_emb_norm_broadcast_t1 per row of h [T, C]: the LM head's static int8 input q [T, C]
+    = round_clamp(h * inv_rms * emb_norm_scaled, 127)."""
+    T, C = h.shape
+    _f32(h, C)
+    _f32(emb_norm_scaled_t, C)
+    q = torch.empty((T, C), dtype=torch.int8, device=h.device)
+    check(ctx._lib.w8a8_emb_norm_pack(ctx.handle, h.data_ptr(), h.stride(0), T, C,
+                                      emb_norm_scaled_t.data_ptr(), float(eps), q.data_ptr(), C,
+                                      _stream(stream)), "w8a8_emb_norm_pack")
+    return q
+

@@ -252,6 +252,23 @@ def make_nvdla_tiles(builder, path: Path) -> None:
     print(f"{path.name}: {len(out)} arrays")
 
 
+def make_emb_norm_pack(path: Path) -> None:
+    """fused_emb_norm_broadcast_t1 (the LM head's input step) run by the reference on seeded
+    final hidden states (widths 1536, 2048, 3840 and one with a 2-element tail), with
+    emb_norm_scaled = weight * (1 / in_step) computed as the reference loader does in fp32."""
+    rng = np.random.default_rng(43)
+    out = {}
+    for tag, C in (("c1536", 1536), ("c2048", 2048), ("c3840", 3840), ("c578", 578)):
+        h = (rng.standard_normal(C) * 3).astype(np.float32)
+        w = (rng.standard_normal(C) * 0.3 + 1).astype(np.float32)
+        in_step = np.float32(0.031)
+        emb = (w * (np.float32(1.0) / in_step)).astype(np.float32)
+        q = O.ref_emb_norm_pack(h, emb)
+        out.update({f"{tag}_h": h, f"{tag}_emb": emb, f"{tag}_q": q})
+    np.savez_compressed(path, eps=np.float32(1e-5), **out)
+    print(f"{path.name}: {len(out) // 3} rows")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -264,6 +281,7 @@ def main() -> None:
         return
     if args.only == "norm":
         make_norm_pack(HERE / "norm_pack.npz")
+        make_emb_norm_pack(HERE / "emb_norm_pack.npz")
         return
     if args.only == "sampler":
         make_sampler_seq(HERE / "sampler_seq.npz")
@@ -280,6 +298,7 @@ def main() -> None:
     make_sampler_kat(HERE / "sampler_kat.npz")
     make_moe_route(HERE / "moe_route.npz")
     make_norm_pack(HERE / "norm_pack.npz")
+    make_emb_norm_pack(HERE / "emb_norm_pack.npz")
     make_nvdla_tiles(builder, HERE / "nvdla_tiles.npz")
     make_sampler_seq(HERE / "sampler_seq.npz")
 

@@ -46,3 +46,25 @@ def test_restatement_matches_reference(C):
         m, q2 = O.post_op_ffn_pack(op[None], post, h[None], ffn)
         rm, rq2 = O.ref_post_op_ffn_pack(op, post, h, ffn)
         assert np.array_equal(m[0], rm) and np.array_equal(q2[0], rq2)
+
+
+EMB_GOLDEN = Path(__file__).resolve().parent / "golden" / "emb_norm_pack.npz"
+
+
+@pytest.mark.parametrize("tag", ["c1536", "c2048", "c3840", "c578"])
+def test_emb_norm_pack_matches_reference_fixture(tag):
+    """The LM head's input step (fused_emb_norm_broadcast_t1) against rows the reference
+    produced."""
+    g = np.load(EMB_GOLDEN)
+    q = O.emb_norm_pack(g[f"{tag}_h"][None], g[f"{tag}_emb"], float(g["eps"]))
+    assert np.array_equal(q[0], g[f"{tag}_q"])
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference C++ not built here")
+@pytest.mark.parametrize("C", [1536, 3840, 577, 64])
+def test_emb_norm_pack_matches_reference_cpp(C):
+    rng = np.random.default_rng(C + 5)
+    for _ in range(4):
+        h = (rng.standard_normal(C) * rng.uniform(0.05, 40)).astype(np.float32)
+        emb = ((rng.standard_normal(C) * 0.4 + 1) * rng.uniform(5, 60)).astype(np.float32)
+        assert np.array_equal(O.emb_norm_pack(h[None], emb)[0], O.ref_emb_norm_pack(h, emb))
