@@ -61,7 +61,8 @@ def emb_norm_pack(ctx: Context, h: torch.Tensor, emb_norm_scaled_t: torch.Tensor
     _f32(h, C)
     _f32(emb_norm_scaled_t, C)
     q = torch.empty((T, C), dtype=torch.int8, device=h.device)
-    check(ctx._lib.w8a8_emb_norm_pack(ctx.handle, h.data_ptr(), h.stride(0), T, C,
+    ldh = h.stride(0) if T > 1 else C  # (a single row may carry any leading stride)
+    check(ctx._lib.w8a8_emb_norm_pack(ctx.handle, h.data_ptr(), ldh, T, C,
                                       emb_norm_scaled_t.data_ptr(), float(eps), q.data_ptr(), C,
                                       _stream(stream)), "w8a8_emb_norm_pack")
     return q

@@ -60,7 +60,7 @@ EMB_GOLDEN = Path(__file__).resolve().parent / "golden" / "emb_norm_pack.npz"
 def test_emb_norm_pack_matches_reference_fixture(ctx, tag):
     """The LM head's input step on the GPU, against rows the reference produced."""
     g = np.load(EMB_GOLDEN)
-    h = torch.from_numpy(g[f"{tag}_h"][None]).cuda()
+    h = torch.from_numpy(np.ascontiguousarray(g[f"{tag}_h"][None])).cuda()
     emb = torch.from_numpy(g[f"{tag}_emb"]).cuda()
     q = rb.emb_norm_pack(ctx, h, emb, float(g["eps"]))
     assert np.array_equal(q.cpu().numpy()[0], g[f"{tag}_q"])
