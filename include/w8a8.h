@@ -415,6 +415,29 @@ w8a8_status w8a8_moe_ep_forward(w8a8_moe_ep *ep, const float *hidden_dev, int64_
 void        w8a8_moe_ep_destroy(w8a8_moe_ep *ep);
 
 /* ---------------------------------------------------------------------------------------
+ * int16 x int16 linear: the w2 stage of the reference's SwiGLU MLP subgraph, whose input is the
+ * int16 product silu(gate) * up and whose weights are int16 per-row codes (tile_int16_slice,
+ * build_lfm3_int8_pkg.py:111-122, written for w2 at :290-306 with trunc 28).  It replaces the
+ * NPU's int16 CMAC + SDP step modelled by attribute_int8_error.py:117-121:
+ *   y_q[t, n] = clip(round(sum_k x[t, k] * w[n, k] * (QuantM[n] / 2^trunc)), +-32767)
+ * (float64 in the reference; the sum is accumulated exactly here, so the result is the same
+ * integer), and optionally the unpack y = float(y_q) * out_step_chan[n]
+ * (unpack_npu_output_int16, lfm3_v2.cpp:1010-1046).  weights int16 [N, ld] (host or device),
+ * quant_m int16 [N], out_step_chan fp32 [N] or NULL.  K * 32767^2 < 2^53.
+ * ------------------------------------------------------------------------------------- */
+typedef struct w8a8_linear16 w8a8_linear16;
+
+w8a8_status w8a8_linear16_create(w8a8_ctx *ctx, int32_t K, int32_t N, const int16_t *weights,
+                                 int64_t ld, const int16_t *quant_m, int32_t trunc,
+                                 const float *out_step_chan, int32_t max_tokens,
+                                 w8a8_linear16 **out_linear16);
+/* x_dev int16 [T, ldx] -> y_dev int16 [T, ldy] (W8A8_OUT_QUANT) or fp32 [T, ldy] (W8A8_OUT_F32). */
+w8a8_status w8a8_linear16_forward(w8a8_linear16 *linear16, const int16_t *x_dev, int64_t ldx,
+                                  int32_t T, int32_t out_mode, void *y_dev, int64_t ldy,
+                                  void *stream);
+void        w8a8_linear16_destroy(w8a8_linear16 *linear16);
+
+/* ---------------------------------------------------------------------------------------
  * Decode chain: a fixed sequence of linears, optionally ending with an LM-head top-k step, run
  * by ONE persistent cooperative kernel launch per forward.  Replaces the per-linear
  * pack -> submit_task -> unpack round trips of the reference's decode loop

@@ -37,6 +37,7 @@ _ORACLE_SIGS = {
     "orc_post_op_ffn_pack": (None, [_P, _I64, _P, _P, _I64, _I32, _I32, _P, _F, _P, _I64, _P,
                                     _I64]),
     "orc_emb_norm_pack": (None, [_P, _I64, _I32, _I32, _P, _F, _P, _I64]),
+    "orc_gemm_i16_requant": (None, [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _I32, _P, _I64]),
     "orc_num_threads": (C.c_int, []),
     "orc_set_threads": (None, [C.c_int]),
     "orc_linear_dyntok_omp": (None, [_P, _I32, _I32, _I32, _P, _P, _F, _P, _I32, _P, _P, _P, _P]),
@@ -257,6 +258,18 @@ def rmsnorm_pack_dyntok(h: np.ndarray, norm: np.ndarray, smooth: np.ndarray, in_
                                   _p(_c(smooth, np.float32)), float(in_thresh), float(eps), _p(q),
                                   Cn, _p(ratio), _p(u), Cn)
     return q, ratio, u
+
+
+def gemm_i16_requant(x: np.ndarray, w: np.ndarray, quant_m: np.ndarray, trunc: int) -> np.ndarray:
+    """The MLP's w2 stage: int16 x [T, K] against int16 codes w [N, K], QuantM requant to int16."""
+    xx = _c(x, np.int16)
+    ww = _c(w, np.int16)
+    T, K = xx.shape
+    N = ww.shape[0]
+    y = np.empty((T, N), np.int16)
+    lib().orc_gemm_i16_requant(_p(xx), K, _p(ww), K, T, K, N, _p(_c(quant_m, np.int16)), int(trunc),
+                               _p(y), N)
+    return y
 
 
 def emb_norm_pack(h: np.ndarray, emb_norm_scaled: np.ndarray, eps: float = 1e-5) -> np.ndarray:

@@ -352,3 +352,23 @@ void orc_post_op_ffn_pack(const float *op_out, int64_t ldo, const float *post_no
             q[(int64_t)t * ldq + i] = (int8_t)orc_round_clamp(m[i] * inv_ffn * ffn_scaled[i], 127.0f);
     }
 }
+
+/* The w2 stage of the SwiGLU MLP (attribute_int8_error.py:117-121, int16 codes of
+ * build_lfm3_int8_pkg.py:111-122 / :290-306): y_q[t, n] = clip(round(sum_k x[t, k] * w[n, k] *
+ * (QuantM[n] / 2^trunc)), +-32767) in float64 as the reference computes it; the sum of int16
+ * products is an integer below 2^53, held exactly.  x [T, ldx] int16, w [N, ldw] int16. */
+void orc_gemm_i16_requant(const int16_t *x, int64_t ldx, const int16_t *w, int64_t ldw, int32_t T,
+                          int32_t K, int32_t N, const int16_t *quant_m, int32_t trunc,
+                          int16_t *y, int64_t ldy) {
+    const double two_t = ldexp(1.0, trunc);
+    for (int32_t t = 0; t < T; ++t)
+        for (int32_t n = 0; n < N; ++n) {
+            int64_t acc = 0;
+            for (int32_t k = 0; k < K; ++k)
+                acc += (int64_t)x[(int64_t)t * ldx + k] * (int64_t)w[(int64_t)n * ldw + k];
+            double v = (double)acc * ((double)quant_m[n] / two_t);
+            v = nearbyint(v); /* round half to even (default rounding mode), like torch.round */
+            v = v < -32767.0 ? -32767.0 : (v > 32767.0 ? 32767.0 : v);
+            y[(int64_t)t * ldy + n] = (int16_t)v;
+        }
+}

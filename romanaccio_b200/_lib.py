@@ -155,6 +155,10 @@ SIGNATURES = {
     "w8a8_lmhead_rank_set_input_norm": (C.c_int, [_P, _P, C.c_float]),
     "w8a8_lmhead_set_input_norm": (C.c_int, [_P, _P, C.c_float]),
     "w8a8_emb_norm_pack": (C.c_int, [_P, _P, _I64, _I32, _I32, _P, C.c_float, _P, _I64, _P]),
+    "w8a8_linear16_create": (C.c_int, [_P, _I32, _I32, _P, _I64, _P, _I32, _P, _I32,
+                                       C.POINTER(_P)]),
+    "w8a8_linear16_forward": (C.c_int, [_P, _P, _I64, _I32, _I32, _P, _I64, _P]),
+    "w8a8_linear16_destroy": (None, [_P]),
     "w8a8_lmhead_rank_shard_range": (_I32, [_P, C.POINTER(_I32), C.POINTER(_I32)]),
     "w8a8_moe_create": (C.c_int, [_P, C.POINTER(MoeDesc), C.POINTER(_P)]),
     "w8a8_moe_destroy": (None, [_P]),

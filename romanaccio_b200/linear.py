@@ -270,3 +270,49 @@ def _check_dev(t: torch.Tensor, dtype: torch.dtype, cols: int | None = None) -> 
         raise ValueError("expected a 2-D row-major tensor")
     if cols is not None and t.shape[1] != cols:
         raise ValueError(f"expected {cols} columns, got {t.shape[1]}")
+
+
+class Linear16:
+    """int16 x int16 linear with the QuantM requant to int16 (w8a8_linear16_*): the w2 stage of
+    the reference's SwiGLU MLP subgraph (int16 product silu(gate) * up in, int16 weight codes,
+    trunc 28), optionally unpacked to fp32 with out_step_chan."""
+
+    def __init__(self, ctx: Context, weights: np.ndarray, quant_m: np.ndarray, trunc: int = 28,
+                 out_step_chan: np.ndarray | None = None, max_tokens: int = 64):
+        import ctypes as C
+        self._lib = ctx._lib
+        self.ctx = ctx
+        w = np.ascontiguousarray(weights, dtype=np.int16)
+        qm = np.ascontiguousarray(quant_m, dtype=np.int16)
+        osc = None if out_step_chan is None else np.ascontiguousarray(out_step_chan, np.float32)
+        self.N, self.K = map(int, w.shape)
+        h = C.c_void_p()
+        check(self._lib.w8a8_linear16_create(ctx.handle, self.K, self.N, w.ctypes.data, self.K,
+                                             qm.ctypes.data, int(trunc),
+                                             osc.ctypes.data if osc is not None else None,
+                                             int(max_tokens), C.byref(h)), "w8a8_linear16_create")
+        self.handle = h
+
+    def forward(self, x: torch.Tensor, out_mode: int = OUT_QUANT, out=None, stream=None):
+        T = x.shape[0]
+        if x.dtype != torch.int16 or x.stride(-1) != 1 or x.shape[1] != self.K:
+            raise ValueError("x must be an int16 [T, K] tensor with unit column stride")
+        dt = torch.float32 if out_mode == OUT_F32 else torch.int16
+        y = out if out is not None else torch.empty((T, self.N), dtype=dt, device=x.device)
+        ldx = x.stride(0) if T > 1 else self.K
+        check(self._lib.w8a8_linear16_forward(self.handle, x.data_ptr(), ldx, T, int(out_mode),
+                                              y.data_ptr(), y.stride(0) if T > 1 else self.N,
+                                              _stream(stream)), "w8a8_linear16_forward")
+        return y
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self._lib.w8a8_linear16_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+

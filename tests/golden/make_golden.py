@@ -23,6 +23,7 @@ Sources of truth, all executed here rather than restated:
 from __future__ import annotations
 
 import argparse
+import json
 import sys
 import types
 from pathlib import Path
@@ -269,6 +270,117 @@ def make_emb_norm_pack(path: Path) -> None:
     print(f"{path.name}: {len(out) // 3} rows")
 
 
+def make_mini_package(builder, out_dir: Path) -> None:
+    """A two-subgraph package in the reference's format (build_lfm3_int8_pkg.py:440-511): the
+    weight regions come from the reference builder's own build_single_conv_region (NVDLA-tiled
+    slices + QuantM at the stand-in template's offsets), quant_scales.json / quant_chan_scales.bin
+    / weights_map.json are written the way its record_scale_entry and package loop write them,
+    and region_offsets.json stands in for the loadable templates the engine reads the offsets
+    from.  expected.npz keeps the builder's own returned values and the slices untiled here, for
+    the ingest test to compare against."""
+    out_dir.mkdir(exist_ok=True)
+    chan_floats, subs, w_map, offs = [], {}, {}, {}
+    blob = bytearray()
+    exp = {}
+    for name, n, k, trunc, seed in (("mini_l00_conv_in", 136, 160, 22, 51),
+                                    ("mini_l00_attn_qkv", 520, 96, 23, 52)):
+        w, x = seeded_inputs(n, k, seed)
+        reg = _Region(n, k)
+        buf, in_t, in_s, inv, osc = builder.build_single_conv_region(
+            w, torch.from_numpy(x), None, trunc, cached_reg=reg)
+        in_off = len(chan_floats)
+        chan_floats.extend(np.asarray(inv, np.float32).tolist())
+        out_off = len(chan_floats)
+        chan_floats.extend(np.asarray(osc, np.float32).tolist())
+        med = float(np.median(osc))
+        subs[name] = {"input_dtype": "int8", "output_dtype": "int8",
+                      "input_threshold": float(in_t), "input_step": float(in_s),
+                      "output_threshold": med * 127.0, "output_step": med,
+                      "in_smooth_offset": in_off, "in_smooth_count": int(k),
+                      "out_step_offset": out_off, "out_step_count": int(n)}
+        w_map[name] = {"layer": 0, "die": 0, "weight_offset": len(blob), "weight_size": len(buf)}
+        offs[name] = {"offsets": list(map(int, reg.offsets)), "N": n, "K": k, "trunc": trunc}
+        blob += buf
+        wq = np.empty((n, k), np.int8)
+        qm = np.empty((n,), np.int16)
+        for sl in range(reg.n_slices):
+            m = reg.slice_rows[sl]
+            wo, qo = reg.offsets[2 * sl], reg.offsets[2 * sl + 1]
+            wq[sl * 512:sl * 512 + m] = untile_int8(buf[wo:wo + m * reg.k_pad], m, k, reg.k_pad)
+            qm[sl * 512:sl * 512 + m] = np.frombuffer(buf[qo:qo + 2 * m], dtype=np.int16)
+        exp.update({f"{name}_wq": wq, f"{name}_qm": qm, f"{name}_inv": np.asarray(inv, np.float32),
+                    f"{name}_osc": np.asarray(osc, np.float32), f"{name}_in_t": np.float64(in_t),
+                    f"{name}_in_s": np.float64(in_s), f"{name}_x": x[:5].copy()})
+    (out_dir / "die0.bin").write_bytes(bytes(blob))
+    np.asarray(chan_floats, dtype=np.float32).tofile(str(out_dir / "quant_chan_scales.bin"))
+    (out_dir / "quant_scales.json").write_text(json.dumps({"subgraphs": subs}, indent=2))
+    (out_dir / "weights_map.json").write_text(json.dumps(w_map, indent=2))
+    (out_dir / "region_offsets.json").write_text(json.dumps(offs, indent=2))
+    np.savez_compressed(out_dir / "expected.npz", **exp)
+    print(f"{out_dir.name}: {len(blob)} weight bytes, {len(chan_floats)} sidecar floats")
+
+
+def make_mlp_w2(path: Path, ref: Path) -> None:
+    """The int16 w2 stage of the SwiGLU MLP as the reference's own engine model computes it:
+    attribute_int8_error.sim_mlp_npu (src/LFM3/attribute_int8_error.py:85-122) runs on seeded
+    weights and tokens, and its last F.linear call (int16 activations m1_q against the int16 codes
+    wq2) and the final clamp (the int16 outputs) are recorded as they happen.  QuantM of w2 is
+    stored beside them (the same formula, :120)."""
+    from torch.overrides import TorchFunctionMode
+    import torch.nn.functional as F
+    sys.path.insert(0, str(ref / "src" / "LFM3"))
+    import attribute_int8_error as A  # noqa: E402
+
+    class Record(TorchFunctionMode):
+        def __init__(self):
+            super().__init__()
+            self.linear, self.clamp = [], []
+
+        def __torch_function__(self, func, types, args=(), kwargs=None):
+            out = func(*args, **(kwargs or {}))
+            if func is F.linear:
+                self.linear.append((args[0].detach().clone(), args[1].detach().clone()))
+            elif func is torch.clamp:
+                self.clamp.append(out.detach().clone())
+            return out
+
+    out = {}
+    for tag, H, I, T, seed in (("a", 64, 96, 4, 61), ("b", 200, 328, 3, 62)):
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn((T, H), generator=g, dtype=torch.float64)
+        w1 = torch.randn((I, H), generator=g, dtype=torch.float64) * 0.08
+        w3 = torch.randn((I, H), generator=g, dtype=torch.float64) * 0.08
+        w2 = torch.randn((H, I), generator=g, dtype=torch.float64) * 0.08
+        c0 = x @ w1.T
+        c1 = x @ w3.T
+        m0 = F.silu(c0)
+        m1 = m0 * c1
+        y = m1 @ w2.T
+        tbl = {"blob_info": {
+            "input": {"int8_step": float(x.abs().max()) / 127.0},
+            "/Conv_output_0": {"int16_step": float(c0.abs().max()) * 1.1 / 32767.0},
+            "/Conv_1_output_0": {"int16_step": float(c1.abs().max()) * 1.1 / 32767.0},
+            "/Sigmoid_output_0": {"int16_step": 1.0 / 32767.0},
+            "/Mul_output_0": {"int16_step": float(m0.abs().max()) * 1.1 / 32767.0},
+            "/Mul_1_output_0": {"int16_step": float(m1.abs().max()) * 1.1 / 32767.0},
+            "output": {"int16_step": float(y.abs().max()) * 1.3 / 32767.0}}}
+        rec = Record()
+        with rec:
+            y_ref = A.sim_mlp_npu(x.float(), w1.float(), w3.float(), w2.float(), tbl, True)
+        m1_q, wq2 = rec.linear[-1]
+        out_q = rec.clamp[-1]
+        m1_s = tbl["blob_info"]["/Mul_1_output_0"]["int16_step"]
+        out_s = tbl["blob_info"]["output"]["int16_step"]
+        ws2 = w2.float().double().abs().amax(dim=1, keepdim=True).clamp(min=1e-12) / 32767.0
+        qm2 = torch.round((m1_s * ws2[:, 0] / out_s) * (1 << 28))
+        assert float(qm2.max()) <= 32767.0 and float(qm2.min()) >= 1.0
+        out.update({f"{tag}_x": m1_q.numpy().astype(np.int16), f"{tag}_w": wq2.numpy().astype(np.int16),
+                    f"{tag}_qm": qm2.numpy().astype(np.int16), f"{tag}_yq": out_q.numpy().astype(np.int16),
+                    f"{tag}_y": y_ref.numpy().astype(np.float32), f"{tag}_out_s": np.float64(out_s)})
+    np.savez_compressed(path, trunc=np.int32(28), **out)
+    print(f"{path.name}: yq range [{out['a_yq'].min()}, {out['a_yq'].max()}]")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -289,6 +401,12 @@ def main() -> None:
     if args.only == "tiles":
         make_nvdla_tiles(import_builder(ref), HERE / "nvdla_tiles.npz")
         return
+    if args.only == "package":
+        make_mini_package(import_builder(ref), HERE / "pkg_mini")
+        return
+    if args.only == "mlp_w2":
+        make_mlp_w2(HERE / "mlp_w2_int16.npz", ref)
+        return
     builder = import_builder(ref)
     make_quant_linear(builder, 136, 160, 22, 11, HERE / "quant_linear_n136_k160_t22.npz")
     make_quant_linear(builder, 520, 96, 23, 12, HERE / "quant_linear_n520_k96_t23.npz")
@@ -300,6 +418,8 @@ def main() -> None:
     make_norm_pack(HERE / "norm_pack.npz")
     make_emb_norm_pack(HERE / "emb_norm_pack.npz")
     make_nvdla_tiles(builder, HERE / "nvdla_tiles.npz")
+    make_mini_package(builder, HERE / "pkg_mini")
+    make_mlp_w2(HERE / "mlp_w2_int16.npz", ref)
     make_sampler_seq(HERE / "sampler_seq.npz")
 
 
