@@ -297,7 +297,7 @@ w8a8_status w8a8_lmhead_set_trace(w8a8_lmhead *lmhead, unsigned long long *head_
 typedef struct {
     int32_t        hidden;            /* H <= 4096 */
     int32_t        inter;             /* I <= 4096, expert intermediate size */
-    int32_t        n_routed;          /* E */
+    int32_t        n_routed;          /* E <= 4096 */
     int32_t        n_shared;          /* S */
     int32_t        top_k;             /* k <= 16 */
     int32_t        norm_topk_prob;    /* 0: raw softmax probabilities (DeepSeek-V2-Lite) */

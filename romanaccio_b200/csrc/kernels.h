@@ -198,6 +198,8 @@ struct MoeRouteLaunch {
   float scaling;
   int32_t *idx;         // [T, k]
   float *w;             // [T, k]
+  float *logits;        // [T, E] scratch
+  int *cnt;             // [T] arrival counters, zero between launches
   bool pdl;
 };
 
@@ -229,6 +231,11 @@ struct MoeGemvLaunch {
   int out_f32, out_i16;     // F32 (unpack) or QUANT int16 / int8
   void *y;                  // [pairs, N]
   bool pdl;
+  // Expert-grouped form (launch_moe_gemv_grouped): the pairs of expert e are
+  // grp_pairs[grp_off[e] .. grp_off[e + 1]) (from launch_moe_group).
+  const int32_t *grp_off;   // [n_experts + 1]
+  const int32_t *grp_pairs; // [pairs]
+  int n_experts;
 };
 
 struct MoeCombineLaunch {
@@ -245,6 +252,11 @@ struct MoeCombineLaunch {
 cudaError_t launch_moe_route(const MoeRouteLaunch &L, cudaStream_t stream);
 cudaError_t launch_moe_act_quant(const MoeActLaunch &L, bool dyn, cudaStream_t stream);
 cudaError_t launch_moe_gemv(const MoeGemvLaunch &L, cudaStream_t stream);
+// Pair lists per expert (this rank's experts only): off [n_experts + 1], pairs [T * slots].
+cudaError_t launch_moe_group(const MoePairs &P, int n_experts, int32_t *off, int32_t *pairs,
+                             bool pdl, cudaStream_t stream);
+// The expert GEMV with each expert's weight rows streamed once per group of its pairs.
+cudaError_t launch_moe_gemv_grouped(const MoeGemvLaunch &L, cudaStream_t stream);
 cudaError_t launch_moe_swiglu(const float *gu, int I, int pairs, float *h, bool pdl,
                               cudaStream_t stream, const MoePairs &P);
 cudaError_t launch_moe_combine(const MoeCombineLaunch &L, cudaStream_t stream);

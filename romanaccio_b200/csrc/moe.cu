@@ -23,6 +23,7 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <algorithm>
 #include <cmath>
 
 namespace w8a8 {
@@ -33,55 +34,106 @@ constexpr int kMoeThreads = 256;
 constexpr int kRowsPerWarp = 8;
 constexpr int kRowsPerCta = kRowsPerWarp * (kMoeThreads / 32);
 
-// One CTA per token.  Warp w computes the logits of experts w, w + 8, ... (lane-strided partial
-// sums reduced across the warp); thread 0 then runs the reference's softmax and top-k serially
-// (at most a few hundred experts).
+// grid (ceil(E / 8), T).  Warp w of CTA (x, t) computes the logit of expert 8x + w for token t
+// (16-byte loads, four partial sums per lane, warp-shuffle total) into logits[t, E]; the last CTA
+// of token t to arrive (counter cnt[t], reset by that CTA) runs the reference's softmax and top-k
+// with its first warp: max, exp and a double-precision sum across the lanes, then k rounds of a
+// warp arg-max by (score desc, index asc) over the untaken experts.
+template <bool VEC>
 __global__ void __launch_bounds__(kMoeThreads) moe_route_kernel(const MoeRouteLaunch L) {
-  extern __shared__ float s_route[];
-  float *h = s_route;                 // [H]
-  float *logit = s_route + L.H;       // [E]
-  float *score = logit + L.E;         // [E]
-  const int t = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  extern __shared__ float s_route[];  // [E] logits, [E] scores (last CTA)
+  __shared__ int s_last;
+  const int t = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  pdl_launch_dependents();
   pdl_wait();
-  for (int i = tid; i < L.H; i += kMoeThreads) h[i] = L.hidden[static_cast<int64_t>(t) * L.ldh + i];
-  __syncthreads();
-  for (int e = warp; e < L.E; e += kMoeThreads / 32) {
-    const float *w = L.gate_w + static_cast<int64_t>(e) * L.H;
-    float acc = 0.0f;
-    for (int i = lane; i < L.H; i += 32) acc += w[i] * h[i];
+  const int e = blockIdx.x * (kMoeThreads / 32) + warp;
+  if (e < L.E) {
+    const float *hr = L.hidden + static_cast<int64_t>(t) * L.ldh;
+    const float *wr = L.gate_w + static_cast<int64_t>(e) * L.H;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (VEC) {
+      const float4 *h4 = reinterpret_cast<const float4 *>(hr);
+      const float4 *w4 = reinterpret_cast<const float4 *>(wr);
+      const int n4 = L.H >> 2;
+#pragma unroll 4
+      for (int i = lane; i < n4; i += 32) {
+        const float4 x = __ldg(h4 + i), w = __ldg(w4 + i);
+        acc[0] += w.x * x.x;
+        acc[1] += w.y * x.y;
+        acc[2] += w.z * x.z;
+        acc[3] += w.w * x.w;
+      }
+    } else {
+      for (int i = lane; i < L.H; i += 32) acc[i & 3] += __ldg(wr + i) * __ldg(hr + i);
+    }
+    float v = (acc[0] + acc[1]) + (acc[2] + acc[3]);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-    if (lane == 0) logit[e] = L.bias ? acc + L.bias[e] : acc;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    if (lane == 0) L.logits[static_cast<int64_t>(t) * L.E + e] = L.bias ? v + L.bias[e] : v;
   }
   __syncthreads();
-  if (tid == 0) {
-    const int E = L.E;
-    float mx = logit[0];
-    for (int e = 1; e < E; ++e)
-      if (logit[e] > mx) mx = logit[e];
-    double sum = 0.0;
-    for (int e = 0; e < E; ++e) {
-      score[e] = expf(logit[e] - mx);
-      sum += score[e];
-    }
-    if (sum > 0.0) {
-      const float inv = static_cast<float>(1.0 / sum);
-      for (int e = 0; e < E; ++e) score[e] *= inv;
-    }
-    // top-k by (score desc, index asc): k passes of a max scan over the untaken experts
-    float wsum = 0.0f;
-    for (int j = 0; j < L.k; ++j) {
-      int best = -1;
-      for (int e = 0; e < E; ++e) {
-        if (score[e] < 0.0f) continue;  // taken (probabilities are >= 0)
-        if (best < 0 || score[e] > score[best]) best = e;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(&L.cnt[t], 1) == static_cast<int>(gridDim.x) - 1;
+  }
+  __syncthreads();
+  if (!s_last || warp != 0) return;
+  if (lane == 0) L.cnt[t] = 0;  // every CTA of token t has arrived
+  __threadfence();
+  const int E = L.E;
+  float *logit = s_route, *score = s_route + E;
+  for (int i = lane; i < E; i += 32) logit[i] = __ldcg(L.logits + static_cast<int64_t>(t) * E + i);
+  __syncwarp();
+  float mx = logit[0];
+  for (int i = lane; i < E; i += 32) mx = logit[i] > mx ? logit[i] : mx;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float other = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+    mx = other > mx ? other : mx;
+  }
+  double sum = 0.0;
+  for (int i = lane; i < E; i += 32) {
+    score[i] = expf(logit[i] - mx);
+    sum += score[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+  const float inv = sum > 0.0 ? static_cast<float>(1.0 / sum) : 1.0f;
+  for (int i = lane; i < E; i += 32) {
+    const float sc = sum > 0.0 ? score[i] * inv : score[i];
+    score[i] = sc >= 0.0f ? sc : 0.0f;  // a NaN score ranks as 0, so every round finds an expert
+  }
+  __syncwarp();
+  float wsum = 0.0f;
+  for (int j = 0; j < L.k; ++j) {
+    int best = -1;
+    float bs = 0.0f;
+    for (int i = lane; i < E; i += 32) {  // ascending i: strict > keeps the lower index on ties
+      const float sc = score[i];
+      if (sc >= 0.0f && (best < 0 || sc > bs)) {
+        best = i;
+        bs = sc;
       }
-      L.idx[t * L.k + j] = best;
-      L.w[t * L.k + j] = score[best];
-      wsum += score[best];
-      score[best] = -1.0f;
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const int ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+      const float os = __shfl_xor_sync(0xFFFFFFFFu, bs, o);
+      if (ob >= 0 && (best < 0 || os > bs || (os == bs && ob < best))) {
+        best = ob;
+        bs = os;
+      }
+    }
+    if (lane == 0) {
+      L.idx[t * L.k + j] = best;
+      L.w[t * L.k + j] = bs;
+      score[best] = -1.0f;  // taken (probabilities are >= 0)
+    }
+    wsum += bs;
+    __syncwarp();
+  }
+  if (lane == 0) {
     if (L.norm_topk && wsum > 0.0f) {
       const float inv = 1.0f / wsum;
       for (int j = 0; j < L.k; ++j) L.w[t * L.k + j] *= inv;
@@ -200,6 +252,133 @@ __global__ void __launch_bounds__(kMoeThreads) moe_gemv_kernel(const MoeGemvLaun
   }
 }
 
+// One CTA: the pairs of every expert this rank owns, as lists (counting sort; the order inside an
+// expert's list does not matter: every pair's outputs are computed independently).
+__global__ void __launch_bounds__(kMoeThreads) moe_group_kernel(const MoePairs P, int n_experts,
+                                                               int32_t *off, int32_t *list) {
+  extern __shared__ int s_cnt[];  // [n_experts] counts, then the scatter cursors
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int e = threadIdx.x; e < n_experts; e += kMoeThreads) s_cnt[e] = 0;
+  __syncthreads();
+  const int n = P.T * P.slots;
+  for (int p = threadIdx.x; p < n; p += kMoeThreads) {
+    const int e = pair_expert(P, p);
+    if (expert_owned(P, e)) atomicAdd(&s_cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e < n_experts; ++e) {
+      off[e] = acc;
+      const int c = s_cnt[e];
+      s_cnt[e] = acc;
+      acc += c;
+    }
+    off[n_experts] = acc;
+  }
+  __syncthreads();
+  for (int p = threadIdx.x; p < n; p += kMoeThreads) {
+    const int e = pair_expert(P, p);
+    if (expert_owned(P, e)) list[atomicAdd(&s_cnt[e], 1)] = p;
+  }
+}
+
+constexpr int kGroupTokens = 8;   // pairs of one expert per CTA
+constexpr int kGroupRows = 4;     // weight rows a warp streams together
+constexpr int kGroupMaxK = 6144;  // widest staged row (kGroupTokens rows = 48 KB)
+
+// Sums v[0..31] over the warp: afterwards lane l holds the total of value l.  Each halving step
+// sends the half that the partner lane keeps (31 shuffles for 32 values).
+__device__ __forceinline__ int warp_sum32(int (&v)[32], int lane) {
+#pragma unroll
+  for (int off = 16, c = 32; off >= 1; off >>= 1, c >>= 1) {
+    const bool hi = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < c / 2; ++i) {
+      const int send = hi ? v[i] : v[i + c / 2];
+      const int keep = hi ? v[i + c / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return v[0];
+}
+
+// grid (ceil(N / 64), n_experts, ceil(T / 8)).  CTA (rb, e, z) takes pairs 8z .. 8z + 7 of expert
+// e's list, stages their int8 rows in shared memory and streams its 64 weight rows once for all
+// of them: each warp owns 8 rows, 4 at a time, each lane its 16-byte chunks of the 4 rows, dp4a
+// against the 8 staged rows; the 32 sums of a pass are reduced together and lane l writes
+// (row l / 8, pair l % 8) through the epilogue of moe_gemv_kernel.
+__global__ void __launch_bounds__(kMoeThreads, 2) moe_gemv_grouped_kernel(const MoeGemvLaunch L) {
+  extern __shared__ __align__(16) int4 s_x[];  // [kGroupTokens][chunks]
+  pdl_launch_dependents();
+  pdl_wait();
+  const int e = blockIdx.y;
+  if (!expert_owned(L.pairs, e)) return;
+  const int beg = L.grp_off[e] + blockIdx.z * kGroupTokens, end = L.grp_off[e + 1];
+  if (beg >= end) return;
+  const int ng = min(kGroupTokens, end - beg);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int chunks = L.k_pad >> 4;
+  for (int i = threadIdx.x; i < kGroupTokens * chunks; i += kMoeThreads) {
+    const int t = i / chunks, c = i % chunks;
+    s_x[i] = t < ng ? *reinterpret_cast<const int4 *>(
+                          L.q + static_cast<int64_t>(L.grp_pairs[beg + t]) * L.ldq + c * 16)
+                    : make_int4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  const int8_t *W = L.w + static_cast<int64_t>(e) * L.N * L.k_pad;
+  const int n0 = blockIdx.x * kRowsPerCta + warp * kRowsPerWarp;
+  // this lane's (row, pair) of the reduced sums
+  const int my_u = lane >> 3, my_t = lane & 7;
+  const int my_p = my_t < ng ? L.grp_pairs[beg + my_t] : 0;
+#pragma unroll 1
+  for (int r = 0; r < kRowsPerWarp; r += kGroupRows) {
+    if (n0 + r >= L.N) break;
+    const int8_t *wr[kGroupRows];
+#pragma unroll
+    for (int u = 0; u < kGroupRows; ++u)  // rows past N re-read row N - 1; their sums are dropped
+      wr[u] = W + static_cast<int64_t>(min(n0 + r + u, L.N - 1)) * L.k_pad;
+    int acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0;
+    for (int ci = lane; ci < chunks; ci += 32) {
+      int4 wv[kGroupRows];
+#pragma unroll
+      for (int u = 0; u < kGroupRows; ++u)
+        wv[u] = __ldg(reinterpret_cast<const int4 *>(wr[u] + ci * 16));
+#pragma unroll
+      for (int t = 0; t < kGroupTokens; ++t) {
+        const int4 xv = s_x[t * chunks + ci];
+#pragma unroll
+        for (int u = 0; u < kGroupRows; ++u) {
+          int s = acc[u * kGroupTokens + t];
+          s = __dp4a(wv[u].x, xv.x, s);
+          s = __dp4a(wv[u].y, xv.y, s);
+          s = __dp4a(wv[u].z, xv.z, s);
+          s = __dp4a(wv[u].w, xv.w, s);
+          acc[u * kGroupTokens + t] = s;
+        }
+      }
+    }
+    const int sum = warp_sum32(acc, lane);
+    const int n = n0 + r + my_u;
+    if (my_t < ng && n < L.N) {
+      const int64_t pe = static_cast<int64_t>(e) * L.N + n;
+      const int yq = requant_quantm(sum, L.quant_m[pe], L.trunc, L.qmax);
+      const int64_t o = static_cast<int64_t>(my_p) * L.N + n;
+      if (L.out_f32) {
+        const float step = L.ratio ? L.ratio[my_p] * L.out_step[pe] : L.out_step[pe];
+        static_cast<float *>(L.y)[o] = static_cast<float>(yq) * step;
+      } else if (L.out_i16) {
+        static_cast<int16_t *>(L.y)[o] = static_cast<int16_t>(yq);
+      } else {
+        static_cast<int8_t *>(L.y)[o] = static_cast<int8_t>(yq);
+      }
+    }
+  }
+}
+
 // h[p, i] = silu(gu[p, i]) * gu[p, I + i], silu(g) = g / (1 + exp(-g)).
 __global__ void __launch_bounds__(kMoeThreads) moe_swiglu_kernel(const float *gu, int I, int pairs,
                                                                  float *h, const MoePairs P) {
@@ -304,14 +483,16 @@ cudaError_t launch_moe_ep_sum(const MoeEpLaunch &L, cudaStream_t st) {
 }
 
 cudaError_t launch_moe_route(const MoeRouteLaunch &L, cudaStream_t st) {
-  const size_t smem = static_cast<size_t>(L.H + 2 * L.E) * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(moe_route_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-  }
-  return launch_ex(moe_route_kernel, dim3(L.T), dim3(kMoeThreads), smem, st, L.pdl, L);
+  if (L.E < 1 || L.H < 1 || L.T < 1 || L.k < 1 || L.k > L.E || !L.logits || !L.cnt)
+    return cudaErrorInvalidValue;
+  const size_t smem = static_cast<size_t>(2 * L.E) * sizeof(float);
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;  // more than 6144 experts
+  const bool vec = L.H % 4 == 0 && L.ldh % 4 == 0 &&
+                   reinterpret_cast<uintptr_t>(L.hidden) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(L.gate_w) % 16 == 0;
+  const dim3 grid((L.E + kMoeThreads / 32 - 1) / (kMoeThreads / 32), L.T);
+  if (vec) return launch_ex(moe_route_kernel<true>, grid, dim3(kMoeThreads), smem, st, L.pdl, L);
+  return launch_ex(moe_route_kernel<false>, grid, dim3(kMoeThreads), smem, st, L.pdl, L);
 }
 
 cudaError_t launch_moe_act_quant(const MoeActLaunch &L, bool dyn, cudaStream_t st) {
@@ -329,6 +510,22 @@ cudaError_t launch_moe_gemv(const MoeGemvLaunch &L, cudaStream_t st) {
   if (chunks <= 32 * 8)
     return launch_ex(moe_gemv_kernel<8>, grid, dim3(kMoeThreads), 0, st, L.pdl, L);
   return cudaErrorInvalidValue;  // K above 4096 is not an expert shape here
+}
+
+cudaError_t launch_moe_group(const MoePairs &P, int n_experts, int32_t *off, int32_t *pairs,
+                             bool pdl, cudaStream_t st) {
+  return launch_ex(moe_group_kernel, dim3(1), dim3(kMoeThreads),
+                   static_cast<size_t>(n_experts) * sizeof(int), st, pdl, P, n_experts, off, pairs);
+}
+
+cudaError_t launch_moe_gemv_grouped(const MoeGemvLaunch &L, cudaStream_t st) {
+  if (L.k_pad <= 0 || L.k_pad % 16 != 0 || L.n_experts <= 0) return cudaErrorInvalidValue;
+  if (L.k_pad > kGroupMaxK) return launch_moe_gemv(L, st);  // rows too wide to stage: per pair
+  // an expert holds at most one pair per token, so ceil(T / 8) CTA layers cover every list
+  const dim3 grid((L.N + kRowsPerCta - 1) / kRowsPerCta, L.n_experts,
+                  (L.pairs.T + kGroupTokens - 1) / kGroupTokens);
+  const size_t smem = static_cast<size_t>(kGroupTokens) * L.k_pad;
+  return launch_ex(moe_gemv_grouped_kernel, grid, dim3(kMoeThreads), smem, st, L.pdl, L);
 }
 
 cudaError_t launch_moe_swiglu(const float *gu, int I, int pairs, float *h, bool pdl,

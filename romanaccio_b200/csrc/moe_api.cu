@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -44,6 +45,10 @@ struct w8a8_moe {
   float *h = nullptr;              // [P, I]
   int8_t *q2 = nullptr;            // [P, ldi]
   void *yq = nullptr;              // [P, H]
+  int32_t *grp_off = nullptr;      // [E+S+1] pairs of each expert (grouped GEMV, T > 1)
+  int32_t *grp_pairs = nullptr;    // [P]
+  float *route_logits = nullptr;   // [max_T, E]
+  int *route_cnt = nullptr;        // [max_T] arrival counters of the routing kernel
 };
 
 namespace {
@@ -95,7 +100,8 @@ void moe_free(w8a8_moe *m) {
   DeviceScope d(m->dev);
   void *ptrs[] = {m->gate_w, m->gate_b, m->gu_w, m->gu_qm, m->gu_os, m->gu_s, m->gu_thr,
                   m->dn_w,   m->dn_qm,  m->dn_os, m->dn_s, m->dn_inv, m->idx, m->w,
-                  m->q1,     m->r1,     m->gu,   m->h,    m->q2,     m->yq};
+                  m->q1,     m->r1,     m->gu,   m->h,    m->q2,     m->yq,
+                  m->grp_off, m->grp_pairs, m->route_logits, m->route_cnt};
   for (void *p : ptrs) cudaFree(p);
   delete m;
 }
@@ -126,10 +132,18 @@ w8a8_status route(w8a8_moe *m, const float *hidden, int64_t ldh, int T, int32_t 
   L.k = m->k;
   L.norm_topk = m->norm_topk;
   L.scaling = m->scaling;
-  L.idx = idx;
-  L.w = w;
+  L.logits = m->route_logits;
+  L.cnt = m->route_cnt;
   L.pdl = false;
-  return cuda_status(launch_moe_route(L, st), "moe route");
+  for (int t0 = 0; t0 < T; t0 += m->max_T) {  // the scratch holds max_tokens rows
+    L.hidden = hidden + static_cast<int64_t>(t0) * ldh;
+    L.T = std::min(T - t0, m->max_T);
+    L.idx = idx + static_cast<int64_t>(t0) * m->k;
+    L.w = w + static_cast<int64_t>(t0) * m->k;
+    const w8a8_status s = cuda_status(launch_moe_route(L, st), "moe route");
+    if (s != W8A8_SUCCESS) return s;
+  }
+  return W8A8_SUCCESS;
 }
 
 }  // namespace
@@ -143,8 +157,8 @@ w8a8_status w8a8_moe_create(w8a8_ctx *ctx, const w8a8_moe_desc *d, w8a8_moe **ou
   if (d->hidden < 1 || d->inter < 1 || d->n_routed < 1 || d->n_shared < 0 || d->top_k < 1 ||
       d->top_k > 16 || d->top_k > d->n_routed || d->max_tokens < 1)
     return invalid("bad MoE shape (hidden, inter, n_routed, n_shared, top_k, max_tokens)");
-  if (round16(d->hidden) > 4096 || round16(d->inter) > 4096)
-    return invalid("hidden and inter must be at most 4096");
+  if (round16(d->hidden) > 4096 || round16(d->inter) > 4096 || d->n_routed > 4096)
+    return invalid("hidden, inter and n_routed must be at most 4096");
   if (!d->gate_w || !d->gu_weights || !d->gu_quant_m || !d->gu_out_step_chan ||
       !d->gu_inv_smooth || !d->gu_in_thresh || !d->dn_weights || !d->dn_quant_m ||
       !d->dn_out_step_chan || !d->dn_inv_smooth || !d->dn_in_step)
@@ -203,6 +217,14 @@ w8a8_status w8a8_moe_create(w8a8_ctx *ctx, const w8a8_moe_desc *d, w8a8_moe **ou
   if (e == cudaSuccess) e = upload(&m->h, static_cast<const float *>(nullptr), P * I);
   if (e == cudaSuccess) e = upload(&m->q2, static_cast<const int8_t *>(nullptr), P * m->ldi);
   if (e == cudaSuccess) e = cudaMalloc(&m->yq, P * H * (m->dn_i16 ? 2 : 1));
+  if (e == cudaSuccess)
+    e = upload(&m->grp_off, static_cast<const int32_t *>(nullptr), X + 1);
+  if (e == cudaSuccess) e = upload(&m->grp_pairs, static_cast<const int32_t *>(nullptr), P);
+  if (e == cudaSuccess)
+    e = upload(&m->route_logits, static_cast<const float *>(nullptr),
+               static_cast<size_t>(m->max_T) * m->E);
+  if (e == cudaSuccess)
+    e = upload(&m->route_cnt, static_cast<const int *>(nullptr), static_cast<size_t>(m->max_T));
   if (e != cudaSuccess) {
     w8a8_status st = cuda_status(e, "MoE upload");
     moe_free(m);
@@ -233,6 +255,15 @@ w8a8_status w8a8_moe_forward(w8a8_moe *m, const float *hidden, int64_t ldh, int3
   if (s != W8A8_SUCCESS) return s;
   const MoePairs P = pairs_of(m, T);
   const int n_pairs = T * m->slots;
+  // T > 1: the pairs are grouped by expert so that each expert's weight rows stream once for all
+  // of its pairs; T = 1 keeps one CTA column per pair (every expert has at most one pair).
+  const bool grouped = T > 1;
+  const int n_experts = m->E + m->S;
+  if (grouped) {
+    s = cuda_status(launch_moe_group(P, n_experts, m->grp_off, m->grp_pairs, true, st),
+                    "moe expert grouping");
+    if (s != W8A8_SUCCESS) return s;
+  }
 
   MoeActLaunch A = {};
   A.pairs = P;
@@ -265,7 +296,11 @@ w8a8_status w8a8_moe_forward(w8a8_moe *m, const float *hidden, int64_t ldh, int3
   G.out_f32 = 1;
   G.y = m->gu;
   G.pdl = true;
-  s = cuda_status(launch_moe_gemv(G, st), "moe gate_up GEMV");
+  G.grp_off = m->grp_off;
+  G.grp_pairs = m->grp_pairs;
+  G.n_experts = n_experts;
+  s = cuda_status(grouped ? launch_moe_gemv_grouped(G, st) : launch_moe_gemv(G, st),
+                  "moe gate_up GEMV");
   if (s != W8A8_SUCCESS) return s;
 
   s = cuda_status(launch_moe_swiglu(m->gu, m->I, n_pairs, m->h, true, st, P), "moe swiglu");
@@ -303,7 +338,11 @@ w8a8_status w8a8_moe_forward(w8a8_moe *m, const float *hidden, int64_t ldh, int3
   D.out_i16 = m->dn_i16;
   D.y = m->yq;
   D.pdl = true;
-  s = cuda_status(launch_moe_gemv(D, st), "moe down GEMV");
+  D.grp_off = m->grp_off;
+  D.grp_pairs = m->grp_pairs;
+  D.n_experts = n_experts;
+  s = cuda_status(grouped ? launch_moe_gemv_grouped(D, st) : launch_moe_gemv(D, st),
+                  "moe down GEMV");
   if (s != W8A8_SUCCESS) return s;
 
   MoeCombineLaunch C = {};
