@@ -125,19 +125,29 @@ def cpu_model(T: int, layers: int, seed: int = 0):
     from romanaccio_b200.quantize import build_linear
     shape = synth.QWEN25_15B
     params = []
+    # the DecodeStack recipe: N(0, 1/K) weights, calibration rows propagated through the stack
+    calib_h = synth.activations(64, shape.hidden, seed * 7919 + 1)
     for layer in range(layers):
+        cal_out = {}
         for j, (name, K, N, trunc) in enumerate(shape.subgraphs()):
             s = seed * 7919 + layer * 16 + j
             g = torch.Generator().manual_seed(s)
-            w = torch.randn((N, K), generator=g) * 0.02
-            params.append((name, build_linear(w, synth.activations(64, K, s + 1), trunc=trunc)))
+            w = torch.randn((N, K), generator=g) / float(K) ** 0.5
+            calib = {"qkv": lambda: calib_h, "o": lambda: cal_out["qkv"][:, :shape.q],
+                     "gate_up": lambda: cal_out["o"],
+                     "down": lambda: cal_out["gate_up"][:, :shape.ffn]}[name]().contiguous()
+            params.append((name, build_linear(w, calib, trunc=trunc)))
+            cal_out[name] = calib @ w.t()
+        calib_h = cal_out["down"]
     K, V = shape.hidden, shape.vocab
     g = torch.Generator().manual_seed(seed + 17)
     w = torch.randn((V, K), generator=g) * 0.02
     step = w.double().abs().amax(dim=1, keepdim=True).clamp(min=1e-12) / 127.0
     wq = torch.clamp(torch.round(w.double() / step), -127, 127).to(torch.int8).numpy()
-    in_step = float(synth.activations(64, K, seed + 23).abs().max()) / 127.0
-    return params, (wq, (in_step * step[:, 0].numpy()).astype(np.float32), in_step)
+    from romanaccio_b200.decode import LM_NORM_EPS, lm_input_norm
+    in_step, emb = lm_input_norm(K, seed, "cpu", calib=calib_h)
+    return params, (wq, (in_step * step[:, 0].numpy()).astype(np.float32), in_step, emb,
+                    LM_NORM_EPS)
 
 
 def decode_step_on(stack, x_host: np.ndarray) -> None:
@@ -150,15 +160,15 @@ def decode_step_on(stack, x_host: np.ndarray) -> None:
 def decode_parity(stack, x_host: np.ndarray, lm=None) -> dict:
     """Checks the stack's last step (run on x_host by decode_step_on) against the oracle's step
     on the same input: the final hidden state (bit for bit), the top-k ids and values
-    (identical) and the argmax.  lm: the full-vocabulary LM head (wq, acc_step, in_step) when the
-    stack holds one shard of it."""
+    (identical) and the argmax.  lm: the full-vocabulary LM head (wq, acc_step, in_step,
+    emb_norm_scaled, eps) when the stack holds one shard of it."""
     import time as _t
     T = stack.T
     h = stack.outs[3].cpu().numpy()
     val, idx = stack.top_val.cpu().numpy(), stack.top_idx.cpu().numpy()
     ids = stack.ids.cpu().numpy()
     if lm is None:
-        lm = (stack.lm_host[0], stack.lm_host[1], stack.lm_in_step)
+        lm = stack.lm_oracle()
     t0 = _t.perf_counter()
     from oracle.oracle import DecodeOracle
     orc = DecodeOracle(stack.params_host, lm, T, stack.shape, k=stack.k)
@@ -167,13 +177,16 @@ def decode_parity(stack, x_host: np.ndarray, lm=None) -> dict:
         "oracle": "C restatement of the reference path (OpenMP), same weights and input",
         "layers": stack.layers, "tokens": T, "vocab": int(lm[0].shape[0]), "k": stack.k,
         "hidden_equal": bool(np.array_equal(h, h_ref)),
+        "hidden_finite": bool(np.isfinite(h_ref).all()),
         "topk_ids_equal": bool(np.array_equal(idx, idx_ref)),
         "topk_values_equal": bool(np.array_equal(val, val_ref)),
         "argmax_equal": bool(np.array_equal(ids, idx_ref[:, 0])),
+        # a non-degenerate head: distinct logit values among token 0's top-k
+        "topk_distinct_values": int(len(np.unique(val_ref[0]))),
         "oracle_s": round(_t.perf_counter() - t0, 2),
     }
-    out["parity"] = (out["hidden_equal"] and out["topk_ids_equal"] and out["topk_values_equal"]
-                     and out["argmax_equal"])
+    out["parity"] = (out["hidden_equal"] and out["hidden_finite"] and out["topk_ids_equal"]
+                     and out["topk_values_equal"] and out["argmax_equal"])
     return out
 
 
@@ -213,7 +226,7 @@ def reference_cpp_baseline(params, lm, T: int, shape, seconds: float) -> dict | 
     if T != 1 or not reference_cpp_available():
         return None
     from oracle.oracle import ReferenceDecode
-    wq, acc_step, in_step = lm
+    wq, acc_step, in_step = lm[:3]
     w_f32 = (wq.astype(np.float32) * (acc_step / np.float32(in_step))[:, None]).astype(np.float32)
     rd = ReferenceDecode(params, w_f32, T, shape)
     del w_f32
@@ -726,14 +739,14 @@ def run_ours(args) -> None:
         lm_full = None
         if world > 1:
             wq_f, w_step_f = _lm_rows(shape.hidden, 0, stack.V, 17, dev)
-            lm_full = (wq_f, (stack.lm_in_step * w_step_f).astype(np.float32), stack.lm_in_step)
+            lm_full = (wq_f, (stack.lm_in_step * w_step_f).astype(np.float32), stack.lm_in_step,
+                       stack.lm_norm[0], stack.lm_norm[1])
         parity = decode_parity(stack, x_np, lm=lm_full)
     barrier()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        run_cpu, cores = cpu_step_fn(stack.params_host, (stack.lm_host[0], stack.lm_host[1],
-                                                         stack.lm_in_step), T, shape)
+        run_cpu, cores = cpu_step_fn(stack.params_host, stack.lm_oracle(), T, shape)
         run_cpu()
         n, t0 = 0, time.perf_counter()
         while True:
@@ -746,8 +759,7 @@ def run_ours(args) -> None:
                "cpu_model": cpu_model_name(),
                "sample": f"{n} full decode steps of the same workload (28 layers + LM head), "
                          "C restatement of the reference path, OpenMP"}
-        ref_cpp = reference_cpp_baseline(stack.params_host, (stack.lm_host[0], stack.lm_host[1],
-                                                             stack.lm_in_step), T, shape,
+        ref_cpp = reference_cpp_baseline(stack.params_host, stack.lm_oracle(), T, shape,
                                          args.cpu_seconds)
         if ref_cpp is not None:
             cpu["reference_cpp"] = ref_cpp

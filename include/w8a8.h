@@ -187,6 +187,13 @@ typedef enum {
 } w8a8_path;
 #define W8A8_TC_MIN_TOKENS 16
 w8a8_status w8a8_linear_set_path(w8a8_linear *linear, int32_t path);
+/* The LM-head shard's input RMSNorm (fused_emb_norm_broadcast_t1, lfm3_v2.cpp:810-831): when
+ * emb_norm_scaled_dev ([K] fp32 = norm weight / in_step, lfm3_v2.cpp:3906-3912) is non-NULL,
+ * w8a8_linear_forward_topk with the STATIC act mode packs each row as
+ * round_clamp(x * inv_rms * emb_norm_scaled[c], 127) with the reference's four interleaved sums
+ * of squares.  K <= 12288.  NULL turns it off.  The pointer must stay valid while set. */
+w8a8_status w8a8_linear_set_input_norm(w8a8_linear *linear, const float *emb_norm_scaled_dev,
+                                       float eps);
 /* Diagnostics (no reference counterpart): attaches a device buffer of 2 x sm_count x 8 uint64
  * that each launch of this linear fills with per-CTA %globaltimer stamps.  Tensor-core launches
  * (grid <= sm_count): entry, setup done, first stage issued, first stage landed, first MMAs
@@ -459,6 +466,13 @@ typedef struct {
     int32_t      row_offset;   /* top-k: vocab id of the linear's row 0 */
     float       *topk_val_dev; /* top-k: [T, k] */
     int32_t     *topk_idx_dev; /* top-k: [T, k] */
+    /* Optional RMSNorm folded into a STATIC pack (the LM head's fused_emb_norm_broadcast_t1,
+     * lfm3_v2.cpp:810-831): when non-NULL, x rows are packed as
+     * round_clamp(x * inv_rms * emb_norm_dev[c], 127), inv_rms = 1 / sqrt(sum / K + norm_eps)
+     * with the reference's four interleaved sums of squares; emb_norm_dev = norm weight / in_step
+     * ([K] fp32, lfm3_v2.cpp:3906-3912).  act_mode must be STATIC. */
+    const float *emb_norm_dev;
+    float        norm_eps;
 } w8a8_chain_step;
 
 typedef struct w8a8_chain w8a8_chain;

@@ -6,8 +6,9 @@
  *   linear:  pack_npu_input_int8_dyntok (src/LFM3/lfm3_v2.cpp:1050-1141)
  *            -> int8 GEMM (cmac.py:300-383) -> QuantM requant (attribute_int8_error.py:104-122)
  *            -> unpack_npu_output_int8_dyntok (src/LFM3/lfm3_v2.cpp:1143-1183)
- *   LM head: static int8 pack -> int8 GEMV -> float(acc) * acc_step -> top-k / argmax
- *            (sampler.cpp:93-121)
+ *   LM head: static int8 pack (or the RMSNorm pack fused_emb_norm_broadcast_t1,
+ *            src/LFM3/lfm3_v2.cpp:810-831) -> int8 GEMV -> float(acc) * acc_step -> top-k /
+ *            argmax (sampler.cpp:93-121)
  */
 #include <math.h>
 #include <stdint.h>
@@ -23,6 +24,8 @@ void orc_pack_dyntok(const float *x, int64_t ldx, int32_t T, int32_t K, float in
                      const float *inv_smooth, int8_t *q, int64_t ldq, float *ratio);
 void orc_pack_static(const float *x, int64_t ldx, int32_t T, int32_t K, float in_step,
                      const float *inv_smooth, int8_t *q, int64_t ldq);
+void orc_emb_norm_pack(const float *h, int64_t ldh, int32_t T, int32_t C,
+                       const float *emb_norm_scaled, float eps, int8_t *q, int64_t ldq);
 
 int orc_num_threads(void) {
 #ifdef _OPENMP
@@ -65,12 +68,31 @@ void orc_linear_dyntok_omp(const float *x, int32_t T, int32_t K, int32_t N, cons
     }
 }
 
+static void lmhead_topk_packed(const int8_t *q, int32_t T, int32_t K, int32_t V,
+                               const int8_t *w, const float *acc_step, int32_t k, float *logits,
+                               float *val, int32_t *idx);
+
 /* LM head over V rows with static input quant; logits = float(acc) * acc_step[v].
  * Writes the top-k (value desc, id asc) of each token into val/idx [T, k]; logits: [T, V]. */
 void orc_lmhead_topk_omp(const float *x, int32_t T, int32_t K, int32_t V, const int8_t *w,
                          float in_step, const float *acc_step, int32_t k, float *logits,
                          int8_t *q, float *val, int32_t *idx) {
     orc_pack_static(x, K, T, K, in_step, NULL, q, K);
+    lmhead_topk_packed(q, T, K, V, w, acc_step, k, logits, val, idx);
+}
+
+/* The same LM head with the final RMSNorm folded into its pack (emb_norm_scaled = norm weight /
+ * in_step, lfm3_v2.cpp:3906-3912). */
+void orc_lmhead_topk_norm_omp(const float *x, int32_t T, int32_t K, int32_t V, const int8_t *w,
+                              const float *emb_norm_scaled, float eps, const float *acc_step,
+                              int32_t k, float *logits, int8_t *q, float *val, int32_t *idx) {
+    orc_emb_norm_pack(x, K, T, K, emb_norm_scaled, eps, q, K);
+    lmhead_topk_packed(q, T, K, V, w, acc_step, k, logits, val, idx);
+}
+
+static void lmhead_topk_packed(const int8_t *q, int32_t T, int32_t K, int32_t V,
+                               const int8_t *w, const float *acc_step, int32_t k, float *logits,
+                               float *val, int32_t *idx) {
 #pragma omp parallel for schedule(static)
     for (int32_t v = 0; v < V; ++v) {
         const int8_t *wr = w + (int64_t)v * K;

@@ -42,6 +42,8 @@ _ORACLE_SIGS = {
     "orc_set_threads": (None, [C.c_int]),
     "orc_linear_dyntok_omp": (None, [_P, _I32, _I32, _I32, _P, _P, _F, _P, _I32, _P, _P, _P, _P]),
     "orc_lmhead_topk_omp": (None, [_P, _I32, _I32, _I32, _P, _F, _P, _I32, _P, _P, _P, _P]),
+    "orc_lmhead_topk_norm_omp": (None, [_P, _I32, _I32, _I32, _P, _P, _F, _P, _I32, _P, _P, _P,
+                                        _P]),
     "orc_gemm_requant_omp": (None, [_P, _I32, _I32, _I32, _P, _P, _I32, _P]),
 }
 _REF_SIGS = {
@@ -428,8 +430,10 @@ class DecodeOracle:
     (src/LFM3/lfm3_v2.cpp pack / unpack, cmac.py:300-383 GEMM, attribute_int8_error.py:104-122
     requant; the same arithmetic as the CUDA path): dyntok pack -> int32 GEMM -> QuantM requant ->
     unpack per linear, each linear reading the previous one's output (o the q slice of qkv, down
-    the gate slice of gate_up), then the static-input LM head with its top-k.  Used as the
-    checker of the GPU step and, timed, as the CPU baseline."""
+    the gate slice of gate_up), then the LM head with its top-k: lm = (wq, acc_step, in_step) for
+    a static pack, or (wq, acc_step, in_step, emb_norm_scaled, eps) for the RMSNorm pack of
+    fused_emb_norm_broadcast_t1 (src/LFM3/lfm3_v2.cpp:810-831).  Used as the checker of the GPU
+    step and, timed, as the CPU baseline."""
 
     def __init__(self, params, lm, T: int, shape, k: int = 40):
         import os
@@ -443,7 +447,8 @@ class DecodeOracle:
         self.bufs = {name: np.empty((T, N), np.float32) for (name, K, N, _) in shape.subgraphs()}
         self.qbuf = np.empty((T, max(kk for (_, kk, _, _) in shape.subgraphs())), np.int8)
         self.ratio = np.empty((T,), np.float32)
-        self.wq_lm, self.acc_step_lm, self.in_step_lm = lm
+        self.wq_lm, self.acc_step_lm, self.in_step_lm = lm[:3]
+        self.emb_lm = (np.ascontiguousarray(lm[3], np.float32), float(lm[4])) if len(lm) > 3 else None
         V = self.wq_lm.shape[0]
         self.logits = np.empty((T, V), np.float32)
         self.val = np.empty((T, k), np.float32)
@@ -476,9 +481,15 @@ class DecodeOracle:
                                       tr, p(osc), p(y), p(self.qbuf), p(self.ratio))
             x = bufs["down"] if name == "down" else x
         V = self.wq_lm.shape[0]
-        lib.orc_lmhead_topk_omp(p(bufs["down"]), self.T, shape.hidden, V, p(self.wq_lm),
-                                C.c_float(self.in_step_lm), p(self.acc_step_lm), self.k,
-                                p(self.logits), p(self.qlm), p(self.val), p(self.idx))
+        if self.emb_lm is not None:
+            lib.orc_lmhead_topk_norm_omp(p(bufs["down"]), self.T, shape.hidden, V, p(self.wq_lm),
+                                         p(self.emb_lm[0]), C.c_float(self.emb_lm[1]),
+                                         p(self.acc_step_lm), self.k, p(self.logits),
+                                         p(self.qlm), p(self.val), p(self.idx))
+        else:
+            lib.orc_lmhead_topk_omp(p(bufs["down"]), self.T, shape.hidden, V, p(self.wq_lm),
+                                    C.c_float(self.in_step_lm), p(self.acc_step_lm), self.k,
+                                    p(self.logits), p(self.qlm), p(self.val), p(self.idx))
         return bufs["down"].copy(), self.val.copy(), self.idx.copy()
 
 

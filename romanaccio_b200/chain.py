@@ -30,6 +30,9 @@ class ChainStepSpec:
     row_offset: int = 0
     topk_val: torch.Tensor | None = None
     topk_idx: torch.Tensor | None = None
+    # RMSNorm folded into the STATIC pack (the LM head's input step): norm weight / in_step [K]
+    emb_norm: torch.Tensor | None = None
+    norm_eps: float = 1e-5
 
 
 class DecodeChain:
@@ -59,6 +62,12 @@ class DecodeChain:
             arr[i].row_offset = int(s.row_offset)
             arr[i].topk_val_dev = s.topk_val.data_ptr() if s.topk_val is not None else None
             arr[i].topk_idx_dev = s.topk_idx.data_ptr() if s.topk_idx is not None else None
+            if s.emb_norm is not None:
+                if (s.emb_norm.dtype != torch.float32 or not s.emb_norm.is_contiguous()
+                        or s.emb_norm.numel() != s.linear.K):
+                    raise ValueError(f"step {i}: emb_norm must be a contiguous fp32 [K] tensor")
+                arr[i].emb_norm_dev = s.emb_norm.data_ptr()
+            arr[i].norm_eps = float(s.norm_eps)
         h = C.c_void_p()
         check(self._lib.w8a8_chain_create(ctx.handle, arr, len(steps), self.T, C.byref(h)),
               "w8a8_chain_create")

@@ -77,6 +77,9 @@ struct w8a8_linear {
   bool has_quant_m = false, has_acc_step = false;
   int trunc = 0, qmax = 127, out_i16 = 0;
   float inv_step = 0.0f, safe_thresh = 1e-8f;
+  // RMSNorm folded into the STATIC pack of the top-k forward (w8a8_linear_set_input_norm)
+  const float *emb_norm = nullptr;
+  float norm_eps = 0.0f;
   // scratch
   int8_t *xq = nullptr;         // [xq_tokens, k_pad]
   int xq_tokens = 0;
@@ -589,6 +592,15 @@ w8a8_status w8a8_linear_set_trace(w8a8_linear *l, unsigned long long *trace_dev)
   return W8A8_SUCCESS;
 }
 
+w8a8_status w8a8_linear_set_input_norm(w8a8_linear *l, const float *emb_norm_scaled, float eps) {
+  if (!l) return fail(W8A8_ERR_INVALID_ARG, "linear is NULL");
+  if (emb_norm_scaled && l->K > 12288) return fail(W8A8_ERR_INVALID_ARG, "input norm needs K <= 12288");
+  if (emb_norm_scaled && !(eps >= 0.0f)) return fail(W8A8_ERR_INVALID_ARG, "eps must be >= 0");
+  l->emb_norm = emb_norm_scaled;
+  l->norm_eps = eps;
+  return W8A8_SUCCESS;
+}
+
 w8a8_status w8a8_linear_set_path(w8a8_linear *l, int32_t path) {
   if (!l) return fail(W8A8_ERR_INVALID_ARG, "linear is NULL");
   if (path != W8A8_PATH_AUTO && path != W8A8_PATH_GEMV && path != W8A8_PATH_TENSOR)
@@ -720,6 +732,13 @@ w8a8_status w8a8_linear_forward_topk(w8a8_linear *l, const float *x, int64_t ldx
   st = ensure_tokens(l, T);
   if (st != W8A8_SUCCESS) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (l->emb_norm && act_mode == W8A8_ACT_STATIC) {
+    st = w8a8::linear_quant_input(l, x, ldx, T, act_mode, nullptr, 0, nullptr, nullptr, s,
+                                  nullptr, nullptr, 0, l->emb_norm, l->norm_eps);
+    if (st != W8A8_SUCCESS) return st;
+    return w8a8::linear_topk_quantized(l, T, act_mode, out_mode, k, row_offset, topk_val,
+                                       topk_idx, logits, ldl, w8a8::ShardSync{}, true, s);
+  }
   w8a8::FusedQuant fq;
   if (w8a8::linear_can_fuse(l, T, act_mode, &fq)) {
     // static quantisation runs in the GEMV prologue: one launch per 8 tokens
@@ -838,6 +857,10 @@ w8a8_status w8a8_chain_create(w8a8_ctx *ctx, const w8a8_chain_step *steps, int32
     } else if (!st.y_dev || st.ldy < l->N) {
       return fail(W8A8_ERR_INVALID_ARG, "step %d: y NULL or ldy < N", s);
     }
+    if (st.emb_norm_dev && st.act_mode != W8A8_ACT_STATIC)
+      return fail(W8A8_ERR_INVALID_ARG, "step %d: emb_norm needs the STATIC act mode", s);
+    if (st.emb_norm_dev && !(st.norm_eps >= 0.0f))
+      return fail(W8A8_ERR_INVALID_ARG, "step %d: norm_eps must be >= 0", s);
     ChainOp &op = ops[s];
     op = ChainOp{};
     op.w = l->w;
@@ -852,6 +875,11 @@ w8a8_status w8a8_chain_create(w8a8_ctx *ctx, const w8a8_chain_step *steps, int32
     op.act_mode = st.act_mode;
     op.inv_step = l->inv_step;
     op.safe_thresh = l->safe_thresh;
+    if (st.emb_norm_dev) {
+      op.act_mode = kActEmbNorm;
+      op.inv_smooth = st.emb_norm_dev;
+      op.norm_eps = st.norm_eps;
+    }
     op.ratio_out = st.ratio_dev;
     op.out_mode = st.out_mode;
     op.quant_m = l->quant_m;

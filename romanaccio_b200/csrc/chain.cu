@@ -34,7 +34,7 @@ constexpr int kMaxStages = 8;
 // activation float4 loads in flight per thread in quantise_input (more registers at TT = 1,
 // fewer at TT = 8, whose accumulators and activation vectors leave less room)
 template <int TT>
-__host__ __device__ constexpr int quant_batch() { return TT == 1 ? 6 : TT == 8 ? 3 : 4; }
+__host__ __device__ constexpr int quant_batch() { return TT == 1 ? 5 : TT == 8 ? 3 : 4; }
 
 struct ChainArgs {
   const ChainOp *ops;
@@ -50,6 +50,7 @@ struct ChainArgs {
   int cand_cap;
   int max_rows;       // most rows one CTA owns in any step (epilogue parameter staging)
   uint32_t ring_bytes;
+  int norm_floats;    // fp32 staging row of a kActEmbNorm step (0: none)
   unsigned long long *trace;  // optional [grid][n_ops][8] %globaltimer stamps
 };
 
@@ -70,13 +71,16 @@ __device__ __forceinline__ void split_range(int total, int parts, int idx, int &
 // ratio / inverse step, exactly as pack_npu_input_int8[_dyntok].
 // When the step that produced x already reduced max_c |x*s| per token (amax_src), x is read
 // once; otherwise (the chain's external input) once for the amax and once to quantise.
-__device__ __forceinline__ char4 quant4(const float4 v, const float4 sv, bool smooth, float inv) {
+__device__ __forceinline__ char4 quant4(const float4 v, const float4 sv, bool smooth, float inv,
+                                        bool emb = false) {
   char4 o;
   if (smooth) {
-    o.x = static_cast<signed char>(round_clamp(v.x * (sv.x * inv), 127.0f));
-    o.y = static_cast<signed char>(round_clamp(v.y * (sv.y * inv), 127.0f));
-    o.z = static_cast<signed char>(round_clamp(v.z * (sv.z * inv), 127.0f));
-    o.w = static_cast<signed char>(round_clamp(v.w * (sv.w * inv), 127.0f));
+    // smoothing: x * (s * inv) == (s * inv) * x; RMSNorm pack (emb): (x * inv_rms) * emb[c]
+    const float4 p = emb ? v : sv, r = emb ? sv : v;
+    o.x = static_cast<signed char>(round_clamp(p.x * inv * r.x, 127.0f));
+    o.y = static_cast<signed char>(round_clamp(p.y * inv * r.y, 127.0f));
+    o.z = static_cast<signed char>(round_clamp(p.z * inv * r.z, 127.0f));
+    o.w = static_cast<signed char>(round_clamp(p.w * inv * r.w, 127.0f));
   } else {
     o.x = static_cast<signed char>(round_clamp(v.x * inv, 127.0f));
     o.y = static_cast<signed char>(round_clamp(v.y * inv, 127.0f));
@@ -101,12 +105,46 @@ __device__ __forceinline__ void preload_smooth(const ChainOp &op, int tid, float
   }
 }
 
+// kActEmbNorm (the LM head's input, fused_emb_norm_broadcast_t1, src/LFM3/lfm3_v2.cpp:810-831):
+// inv_rms per token into s_inv.  The row is staged in shared memory (xs); four threads form the
+// reference's interleaved sums of squares s0..s3 (column c into s_{c mod 4}, in column order) and
+// one thread adds (s0 + s1) + (s2 + s3) and the K mod 4 tail: inv_rms = 1 / sqrt(sum / K + eps).
+// The pack itself is the static one with the product taken as (x * inv_rms) * emb_norm_scaled[c].
+__device__ void emb_norm_inv(const ChainOp &op, int T, float *xs, float *s_inv, int tid) {
+  __shared__ float s_sq[4];
+  const int K = op.K, K4 = K & ~3;
+  for (int t = 0; t < T; ++t) {
+    const float *xr = op.x + t * op.ldx;
+    if (op.vec_x) {
+      const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+      for (int c = tid; c < K / 4; c += kCT) reinterpret_cast<float4 *>(xs)[c] = __ldcg(x4 + c);
+    } else {
+      for (int c = tid; c < K; c += kCT) xs[c] = __ldcg(xr + c);
+    }
+    consumer_sync();
+    if (tid < 4) {
+      float sum = 0.0f;
+#pragma unroll 8
+      for (int c = tid; c < K4; c += 4) sum += xs[c] * xs[c];
+      s_sq[tid] = sum;
+    }
+    __syncwarp();
+    if (tid == 0) {
+      float sum = (s_sq[0] + s_sq[1]) + (s_sq[2] + s_sq[3]);
+      for (int c = K4; c < K; ++c) sum += xs[c] * xs[c];
+      s_inv[t] = 1.0f / sqrtf(sum / static_cast<float>(K) + op.norm_eps);
+    }
+    consumer_sync();  // s_inv[t] visible; xs is restaged for the next token
+  }
+}
+
 template <int TT>
 __device__ void quantise_input(const ChainOp &op, int T, int8_t *xq, int kpad_max, float *s_ratio,
                                float *s_inv, float (*s_part)[TT], int tid,
-                               const float4 (&s_pre)[4]) {
+                               const float4 (&s_pre)[4], float *xs) {
   const int warp = tid >> 5, lane = tid & 31;
   const bool vec = op.vec_x;
+  const bool emb = op.act_mode == kActEmbNorm;
   float inv_r[TT];
   // amax already reduced by the producing step: every thread derives the inverse steps itself
   // (no barrier before the x pass).  The loads are issued here; the divisions wait until the
@@ -175,8 +213,9 @@ __device__ void quantise_input(const ChainOp &op, int T, int8_t *xq, int kpad_ma
     for (int t = 0; t < TT; ++t) inv_r[t] = t < T ? s_inv[t] : 0.0f;
   } else {
     if (tid < T) s_ratio[tid] = 1.0f;
+    if (emb) emb_norm_inv(op, T, xs, s_inv, tid);
 #pragma unroll
-    for (int t = 0; t < TT; ++t) inv_r[t] = op.inv_step;
+    for (int t = 0; t < TT; ++t) inv_r[t] = emb ? (t < T ? s_inv[t] : 0.0f) : op.inv_step;
   }
   // the reference's amax floor, ratio and inverse step from a reduced amax
   auto derive = [&](int t, float m) {
@@ -216,7 +255,7 @@ __device__ void quantise_input(const ChainOp &op, int T, int8_t *xq, int kpad_ma
 #pragma unroll
         for (int u = 0; u < QB; ++u) {
           const int c = c0 + u * kCT;
-          if (c < n4) reinterpret_cast<char4 *>(q)[c] = quant4(v[u], sv[u], smooth, inv);
+          if (c < n4) reinterpret_cast<char4 *>(q)[c] = quant4(v[u], sv[u], smooth, inv, emb);
         }
       }
       if (pending) inv = derive(t, inv_r[t]);  // (this thread had no column)
@@ -227,8 +266,9 @@ __device__ void quantise_input(const ChainOp &op, int T, int8_t *xq, int kpad_ma
         int8_t v = 0;
         if (c < op.K) {
           const float xv = __ldcg(xr + c);
-          v = static_cast<int8_t>(
-              round_clamp(op.inv_smooth ? xv * (op.inv_smooth[c] * inv) : xv * inv, 127.0f));
+          const float y = emb ? xv * inv * op.inv_smooth[c]
+                              : (op.inv_smooth ? xv * (op.inv_smooth[c] * inv) : xv * inv);
+          v = static_cast<int8_t>(round_clamp(y, 127.0f));
         }
         q[c] = v;
       }
@@ -467,6 +507,9 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
       p += 3 * a.max_rows;
     }
   }
+  // (max_rows is a multiple of 4: the staging row starts 16-byte aligned)
+  float *xs = a.norm_floats ? reinterpret_cast<float *>(bars + 2 * kMaxStages) + 6 * a.max_rows
+                            : nullptr;
   __shared__ float s_part[kCW][TT];
   __shared__ float s_ratio[TT];
   __shared__ float s_inv[TT];
@@ -606,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
     if (tr && tid == 0) tr[0] = global_timer_ns();
     if (te > tb || op.topk) {
       // (quantise_input ends with a consumer barrier: the staged parameters are visible)
-      if (te > tb) quantise_input<TT>(op, a.T, xq, a.kpad_max, s_ratio, s_inv, s_part, tid, s_pre);
+      if (te > tb) quantise_input<TT>(op, a.T, xq, a.kpad_max, s_ratio, s_inv, s_part, tid, s_pre, xs);
       else consumer_sync();
       if (tr && tid == 0) tr[1] = global_timer_ns();
       // the CTA owning tile 0 publishes the per-token ratios
@@ -671,6 +714,7 @@ bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, Chain
   size_t stage = 0;
   size_t cand_cap = 0;
   int max_rows = 8;
+  int norm_floats = 0;
   // Stage size target: every stage carries ~24 KB (whole-row tiles of up to 32 rows, or 8-row
   // K chunks of 3 KB per row for long rows), so the fixed-size ring slots stay full.
   constexpr int kMaxStage = 24576;
@@ -698,6 +742,7 @@ bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, Chain
     op.num_tiles = tiles(op.rb);
     stage = std::max(stage, static_cast<size_t>(op.rb) * op.kc);
     kpad_max = std::max(kpad_max, op.k_pad);
+    if (op.act_mode == kActEmbNorm) norm_floats = std::max(norm_floats, (op.K + 3) / 4 * 4);
     const int max_tiles = (op.num_tiles + p.grid - 1) / p.grid;
     max_rows = std::max(max_rows, max_tiles * op.rb);
     if (op.topk) {
@@ -710,9 +755,10 @@ bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, Chain
   p.cand_cap = static_cast<int>(cand_cap);
   p.max_rows = (max_rows + 3) / 4 * 4;
   p.stage_bytes = static_cast<uint32_t>(stage);
+  p.norm_floats = norm_floats;
   const size_t fixed = static_cast<size_t>(p.tt) * p.kpad_max + static_cast<size_t>(p.tt) * cand_cap * 8 +
                       2 * kMaxStages * 8 + 2 * static_cast<size_t>(p.max_rows) * 12 +
-                      kWindow * sizeof(ChainOp);
+                      static_cast<size_t>(norm_floats) * 4 + kWindow * sizeof(ChainOp);
   // the SM's 228 KB split between the co-resident CTAs, less the per-CTA reservation and
   // static shared memory
   const size_t budget = 233472 / cps - 1024 - 2048;
@@ -757,6 +803,7 @@ cudaError_t launch_chain(const ChainOp *ops_dev, int n_ops, int T, const ChainPl
   a.cand_cap = plan.cand_cap;
   a.max_rows = plan.max_rows;
   a.ring_bytes = plan.ring_bytes;
+  a.norm_floats = plan.norm_floats;
   a.trace = trace;
   void (*kern)(ChainArgs) = nullptr;
   switch (plan.tt) {

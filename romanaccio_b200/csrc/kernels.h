@@ -20,7 +20,9 @@ enum DeviceError : int {
 // Output modes (values of w8a8_out_mode).
 enum OutMode : int { kOutAccI32 = 0, kOutQuant = 1, kOutF32 = 2, kOutF32Acc = 3 };
 // Activation modes (values of w8a8_act_mode).
-enum ActMode : int { kActStatic = 0, kActDyntok = 1 };
+enum ActMode : int { kActStatic = 0, kActDyntok = 1,
+                     // chain only: RMSNorm folded into a static pack (fused_emb_norm_broadcast_t1)
+                     kActEmbNorm = 2 };
 
 // Epilogue parameters shared by every contraction kernel.
 struct Epilogue {
@@ -362,9 +364,10 @@ struct alignas(128) ChainOp {
   const float *x;
   int64_t ldx;
   int vec_x;                 // x rows 16-byte aligned, K % 4 == 0
-  const float *inv_smooth;   // [K] or null (16-byte aligned)
+  const float *inv_smooth;   // [K] or null (16-byte aligned); kActEmbNorm: emb_norm_scaled [K]
   int act_mode;
   float inv_step, safe_thresh;
+  float norm_eps;            // kActEmbNorm: the RMSNorm epsilon
   float *ratio_out;          // optional [T]
   // epilogue
   int out_mode;
@@ -388,6 +391,7 @@ struct alignas(128) ChainOp {
 
 struct ChainPlan {
   int tt, grid, kpad_max, cand_cap, max_rows, ns;
+  int norm_floats;  // fp32 staging of one token's input row for kActEmbNorm steps (0: none)
   uint32_t stage_bytes, ring_bytes;
   size_t smem;
 };

@@ -16,6 +16,7 @@ is one CUDA graph on every rank with no collective call.
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 import numpy as np
@@ -30,6 +31,7 @@ from .quantize import build_linear
 from .synth import DecodeShape, activations, outlier_channels
 
 LM_CHUNK = 4096  # LM-head rows are generated in seeded chunks so every sharding agrees
+LM_NORM_EPS = 1e-5  # the final RMSNorm's epsilon (fused_emb_norm_broadcast_t1's default)
 
 
 @dataclass
@@ -54,6 +56,22 @@ def _lm_rows(K: int, lo: int, hi: int, seed: int, device) -> tuple[np.ndarray, n
         wq_parts.append(wq.cpu().numpy())
         step_parts.append(step[:, 0].cpu().numpy())
     return np.concatenate(wq_parts), np.concatenate(step_parts)
+
+
+def lm_input_norm(K: int, seed: int, device,
+                  calib: torch.Tensor | None = None) -> tuple[float, np.ndarray]:
+    """The synthetic final RMSNorm of the LM head's input: (in_step, emb_norm_scaled [K] fp32).
+    Norm weight 1 + N(0, 0.05^2); in_step = max |normalised calibration row| / 127 over the
+    calibration rows (the stack's final calibration hidden states, else 64 synthetic rows);
+    emb_norm_scaled = weight * (1 / in_step) in fp32 (lfm3_v2.cpp:3906-3912)."""
+    g = torch.Generator(device=device).manual_seed(seed * 1_000_003 + 29)
+    norm_w = 1.0 + 0.05 * torch.randn((K,), generator=g, device=device, dtype=torch.float32)
+    if calib is None:
+        calib = activations(64, K, seed + 23, device=device)
+    normed = calib * torch.rsqrt(calib.pow(2).mean(dim=1, keepdim=True) + LM_NORM_EPS) * norm_w
+    in_step = float(normed.abs().amax().item()) / 127.0
+    inv_step = np.float32(1.0) / np.float32(in_step)
+    return in_step, (norm_w.cpu().numpy() * inv_step).astype(np.float32)
 
 
 class DecodeStack:
@@ -88,6 +106,7 @@ class DecodeStack:
             self.linears, self.params_host = src.linears, src.params_host
             self.V, self.lo, self.hi = src.V, src.lo, src.hi
             self.lm_in_step, self.lm_host, self.lm = src.lm_in_step, src.lm_host, src.lm
+            self.lm_norm, self.lm_emb = src.lm_norm, src.lm_emb
             self.rank_head = src.rank_head
             if self.rank_head is not None and self.T * self.world > 64:
                 raise ValueError("a vocab-sharded head takes world * T <= 64 tokens a forward")
@@ -95,14 +114,26 @@ class DecodeStack:
             self._buffers()
             self._plan_chain(use_chain)
             return
+        # Weights N(0, 1/K) (variance preserving: the linears-only stack has no norms between
+        # layers).  Calibration as in post-training quantisation: 64 calibration rows (N(0, 1)
+        # with 1 % outlier channels x20) enter layer 0, and every linear is calibrated on the
+        # fp32 outputs its calibration rows give upstream (o on the q slice of qkv, down on the
+        # gate slice of gate_up), so each linear's output steps match the activations it sees
+        # and the quantised stack tracks the fp32 one over any depth.
+        calib_h = activations(64, shape.hidden, seed * 7919 + 1, device=dev)
         for layer in range(self.layers):
             row = []
+            cal_out = {}
             for j, (name, K, N, trunc) in enumerate(self.subgraphs):
                 s = seed * 7919 + layer * 16 + j
                 g = torch.Generator(device=dev).manual_seed(s)
-                w = torch.randn((N, K), generator=g, device=dev, dtype=torch.float32) * 0.02
-                calib = activations(64, K, s + 1, device=dev)
+                w = torch.randn((N, K), generator=g, device=dev, dtype=torch.float32) / math.sqrt(K)
+                calib = {"qkv": lambda: calib_h,
+                         "o": lambda: cal_out["qkv"][:, :shape.q],
+                         "gate_up": lambda: cal_out["o"],
+                         "down": lambda: cal_out["gate_up"][:, :shape.ffn]}[name]().contiguous()
                 p = build_linear(w, calib, trunc=trunc, stat=stat, clamp=clamp)
+                cal_out[name] = calib @ w.t()
                 del w, calib
                 scale = SubgraphScaleInfo(in_dtype=DTYPE_INT8, out_dtype=DTYPE_INT8,
                                           in_thresh=p.in_thresh, in_step=p.in_step,
@@ -112,20 +143,28 @@ class DecodeStack:
                                       acc_step=p.acc_step))
                 self.params_host.append((name, p))
             self.linears.append(row)
-        # LM head: static int8 input (in_step from a calibration of the final hidden state),
-        # logit = float(acc) * in_step * w_step[v].
+            calib_h = cal_out["down"]
+            del cal_out
+        # LM head: the final RMSNorm folded into a static int8 pack, as the reference's
+        # fused_emb_norm_broadcast_t1 (lfm3_v2.cpp:810-831): q = round_clamp(h * inv_rms *
+        # emb_norm_scaled[c], 127) with emb_norm_scaled = norm weight * (1 / in_step)
+        # (:3906-3912), in_step calibrated on normalised rows; logit = float(acc) * in_step *
+        # w_step[v].  The norm weight is seeded 1 + N(0, 0.05^2).
         K = shape.hidden
         V = shape.vocab if lm_vocab is None else int(lm_vocab)
         self.V = V
         self.lo, self.hi = shard_range(V, self.world, self.rank)
         wq, w_step = _lm_rows(K, self.lo, self.hi, seed + 17, dev)
-        calib = activations(64, K, seed + 23, device=dev)
-        self.lm_in_step = float(calib.abs().amax().item()) / 127.0
+        self.lm_in_step, emb = lm_input_norm(K, seed, dev, calib=calib_h)
+        del calib_h
+        self.lm_norm = (emb, LM_NORM_EPS)
+        self.lm_emb = torch.from_numpy(emb).to(dev)
         acc_step = (self.lm_in_step * w_step).astype(np.float32)
         self.lm_host = (wq, acc_step)
         self.lm, self.rank_head = None, None
         if self.world == 1:
             self.lm = LmHeadShard(ctx, wq, acc_step, self.lm_in_step, row_offset=self.lo)
+            self.lm.set_input_norm(self.lm_emb, LM_NORM_EPS)
         else:
             # this rank's vocab shard; the library exchanges activations and candidates with the
             # other ranks (peer stores into CUDA-IPC-mapped memory).  The 64-byte handles are
@@ -134,6 +173,7 @@ class DecodeStack:
             self.rank_head = RankLmHead(ctx, self.rank, self.world, wq, acc_step,
                                         self.lm_in_step, V, max_tokens=max(self.T, 8) if
                                         self.world * 8 <= 64 else self.T, k_max=self.k)
+            self.rank_head.set_input_norm(self.lm_emb, LM_NORM_EPS)
             handles = [None] * self.world
             dist.all_gather_object(handles, self.rank_head.export(), group=self.group)
             self.rank_head.connect(handles)
@@ -186,7 +226,8 @@ class DecodeStack:
             steps.append(ChainStepSpec(self.lm.linear, down, None, act_mode=ACT_STATIC,
                                        out_mode=OUT_F32_ACC, topk_k=self.k,
                                        row_offset=self.lo, topk_val=self.top_val,
-                                       topk_idx=self.top_idx))
+                                       topk_idx=self.top_idx, emb_norm=self.lm_emb,
+                                       norm_eps=LM_NORM_EPS))
         return DecodeChain(self.ctx, steps, self.T)
 
     def launches_per_step(self) -> int:
@@ -200,6 +241,10 @@ class DecodeStack:
         # each linear: act_quant + one tensor-core GEMM, or a GEMV per group of 8 tokens
         contraction = 1 if self.T >= TC_MIN_TOKENS else (self.T + 7) // 8
         return self.layers * 4 * (1 + contraction) + lm
+
+    def lm_oracle(self) -> tuple:
+        """This rank's LM head for the oracle: (wq, acc_step, in_step, emb_norm_scaled, eps)."""
+        return (self.lm_host[0], self.lm_host[1], self.lm_in_step, self.lm_norm[0], self.lm_norm[1])
 
     # ------------------------------------------------------------------ byte accounting
     def step_bytes(self) -> StepBytes:

@@ -17,7 +17,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from ._lib import DTYPE_INT8, OUT_F32_ACC
+from ._lib import DTYPE_INT8, OUT_F32_ACC, check
 from .linear import Context, SubgraphScaleInfo, W8A8Linear, topk_merge
 
 
@@ -63,6 +63,18 @@ class LmHeadShard:
                                  acc_step=acc_step_rows)
         self.row_offset = int(row_offset)
         self.rows = int(wq_rows.shape[0])
+
+    def set_input_norm(self, emb_norm_scaled: torch.Tensor | None, eps: float = 1e-5) -> None:
+        """Fuses the reference's LM-head input RMSNorm (fused_emb_norm_broadcast_t1) into the
+        static pack of forward(): h is then the un-normalised final hidden state."""
+        if emb_norm_scaled is not None and (emb_norm_scaled.dtype != torch.float32
+                                            or not emb_norm_scaled.is_contiguous()
+                                            or emb_norm_scaled.numel() != self.linear.K):
+            raise ValueError("emb_norm_scaled must be a contiguous fp32 [K] tensor")
+        self._norm = emb_norm_scaled  # kept alive: the library holds the device pointer
+        check(self.linear._lib.w8a8_linear_set_input_norm(
+            self.linear.handle, emb_norm_scaled.data_ptr() if emb_norm_scaled is not None else None,
+            float(eps)), "w8a8_linear_set_input_norm")
 
     def forward(self, h: torch.Tensor, k: int, out_mode: int = OUT_F32_ACC, val=None, idx=None,
                 logits=None, stream=None):

@@ -43,7 +43,7 @@ def test_chain_matches_per_linear_path(ctx, shape, T, layers, vocab):
     # and against the oracle: the final hidden state's LM head
     h = st.outs[3].cpu().numpy()
     wq, acc_step = st.lm_host
-    lg = O.dequant_acc(O.gemm_i32(O.pack_static(h, st.lm_in_step), wq), acc_step)
+    lg = O.dequant_acc(O.gemm_i32(O.emb_norm_pack(h, *st.lm_norm), wq), acc_step)
     wv, wi = O.topk(lg, st.k)
     assert np.array_equal(chain_idx.cpu().numpy(), wi)
     assert np.array_equal(chain_val.cpu().numpy(), wv)
@@ -124,8 +124,7 @@ def _qwen_stack(ctx):
 
 def _oracle_step(st, x):
     from oracle.oracle import DecodeOracle
-    wq, acc_step = st.lm_host
-    orc = DecodeOracle(st.params_host, (wq, acc_step, st.lm_in_step), st.T, st.shape, k=st.k)
+    orc = DecodeOracle(st.params_host, st.lm_oracle(), st.T, st.shape, k=st.k)
     return orc.run(x)
 
 
@@ -134,10 +133,13 @@ def _check_step(st, x):
     st.run_device()
     torch.cuda.synchronize()
     h, val, idx = _oracle_step(st, x)
+    assert np.isfinite(h).all(), "the oracle's final hidden state is not finite"
     assert np.array_equal(st.outs[3].cpu().numpy(), h), "final hidden state differs"
     assert np.array_equal(st.top_idx.cpu().numpy(), idx), "top-k ids differ"
     assert np.array_equal(st.top_val.cpu().numpy(), val), "top-k values differ"
     assert np.array_equal(st.ids.cpu().numpy(), idx[:, 0]), "argmax differs"
+    # the LM head sees a real distribution (its normalised input does not quantise to zeros)
+    assert all(len(np.unique(val[t])) > st.k // 2 for t in range(st.T)), "tied top-k logits"
 
 
 @pytest.mark.parametrize("T", [1, 8, 32])
