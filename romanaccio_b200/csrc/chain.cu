@@ -51,6 +51,7 @@ struct ChainArgs {
   int max_rows;       // most rows one CTA owns in any step (epilogue parameter staging)
   uint32_t ring_bytes;
   int norm_floats;    // fp32 staging row of a kActEmbNorm step (0: none)
+  uint32_t xq_off, cand_off, bars_off, ep_off, norm_off;  // ChainPlan's shared-memory layout
   unsigned long long *trace;  // optional [grid][n_ops][8] %globaltimer stamps
 };
 
@@ -278,6 +279,47 @@ __device__ void quantise_input(const ChainOp &op, int T, int8_t *xq, int kpad_ma
 }
 
 // Per-row epilogue parameters of the CTA's rows of the current step, in shared memory.
+__host__ __device__ constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v >> 1); }
+
+// Sums of NV (a power of two <= 32) per-lane values over the warp.  Each halving step sends the
+// half of the values that the partner lane keeps (offsets 16, 8, ...), then the remaining
+// offsets add whole: lane l ends with the total of value l >> (5 - log2 NV), in
+// NV - 1 + 5 - log2 NV shuffles instead of 5 NV.
+template <int NV>
+__device__ __forceinline__ int warp_sum_multi(int (&v)[NV], int lane) {
+  constexpr int kSteps = ilog2(NV);
+#pragma unroll
+  for (int step = 0; step < kSteps; ++step) {
+    const int off = 16 >> step;
+    const int c = NV >> step;
+    const bool hi = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < c / 2; ++i) {
+      const int send = hi ? v[i] : v[i + c / 2];
+      const int keep = hi ? v[i + c / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, off);
+    }
+  }
+#pragma unroll
+  for (int off = 16 >> kSteps; off > 0; off >>= 1) v[0] += __shfl_xor_sync(0xFFFFFFFFu, v[0], off);
+  return v[0];
+}
+
+// Position in the weight ring: slot = it % ns and phase = (it / ns) & 1 of the ring iteration
+// it, advanced incrementally (no integer division on the per-stage path).
+struct RingPos {
+  int slot = 0;
+  uint32_t phase = 0;
+  bool lapped = false;  // it >= ns: the slot has been filled before
+  __device__ __forceinline__ void advance(int ns) {
+    if (++slot == ns) {
+      slot = 0;
+      phase ^= 1u;
+      lapped = true;
+    }
+  }
+};
+
 struct EpiSmem {
   int *qm;        // QuantM
   float *step;    // out_step_chan / out_step / acc_step
@@ -309,6 +351,7 @@ __device__ __forceinline__ void cp_async_wait_all_but_newest() {
 // parameters costs the current step nothing.  The caller commits the copy group.
 __device__ void stage_epilogue_params(const ChainOp &op, int tb, int te, const EpiSmem &ep,
                                       int tid) {
+  if (op.topk) return;  // the LM-head step reads its per-row parameters from global memory
   const int r0 = tb * op.rb;
   const int rows = te > tb ? min((te - tb) * op.rb, op.N - r0) : 0;
   const float *step = op.out_mode == kOutF32Acc ? op.acc_step : op.out_step;
@@ -343,25 +386,23 @@ __device__ __forceinline__ void fetch_descriptor(ChainOp *window, const ChainOp 
 // Consumes this CTA's tiles [tb, te) of one step.  `it` is the ring iteration counter shared
 // with the producer's issue order.
 template <int TT, int RPW, bool TOPK>
-__device__ void consume_tiles(const ChainOp &op, const ChainArgs &a, int tb, int te, int &it,
+__device__ void consume_tiles(const ChainOp &op, const ChainArgs &a, int tb, int te, RingPos &rp,
                               const uint8_t *ring, const int8_t *xq, uint64_t *bars,
                               const float *s_ratio, uint64_t *cand, int *s_amax,
                               const EpiSmem &ep, int tid, bool &ok, unsigned long long *tr) {
   const int warp = tid >> 5, lane = tid & 31;
-  const int it_first = it;
+  bool first = true;
   constexpr int RB = kCW * RPW;
   const bool dyn = op.act_mode == kActDyntok;
   for (int tile = tb; tile < te; ++tile) {
-    int acc[RPW][TT];
+    int acc[RPW * TT];  // value r * TT + t: row r, token t
 #pragma unroll
-    for (int r = 0; r < RPW; ++r)
-#pragma unroll
-      for (int t = 0; t < TT; ++t) acc[r][t] = 0;
-    for (int kci = 0; kci < op.nk; ++kci, ++it) {
-      const int slot = it % a.ns;
-      const int use = it / a.ns;
-      if (ok) ok = mbar_wait_bounded(smem_addr(&bars[slot]), use & 1, a.err, kDevTimeoutFull);
-      if (tr && it == it_first && tid == 0) tr[6] = global_timer_ns();
+    for (int i = 0; i < RPW * TT; ++i) acc[i] = 0;
+    for (int kci = 0; kci < op.nk; ++kci, rp.advance(a.ns)) {
+      const int slot = rp.slot;
+      if (ok) ok = mbar_wait_bounded(smem_addr(&bars[slot]), rp.phase, a.err, kDevTimeoutFull);
+      if (tr && first && tid == 0) tr[6] = global_timer_ns();
+      first = false;
       const int k0 = kci * op.kc;
       const int bytes = min(op.kc, op.k_pad - k0);
       const uint8_t *sw = ring + static_cast<size_t>(slot) * a.stage_bytes;
@@ -376,12 +417,12 @@ __device__ void consume_tiles(const ChainOp &op, const ChainArgs &a, int tb, int
             const int4 wv = *reinterpret_cast<const int4 *>(sw + (warp * RPW + r) * op.kc + kk);
 #pragma unroll
             for (int t = 0; t < TT; ++t) {
-              int s = acc[r][t];
+              int s = acc[r * TT + t];
               s = __dp4a(wv.x, xv[t].x, s);
               s = __dp4a(wv.y, xv[t].y, s);
               s = __dp4a(wv.z, xv[t].z, s);
               s = __dp4a(wv.w, xv[t].w, s);
-              acc[r][t] = s;
+              acc[r * TT + t] = s;
             }
           }
         }
@@ -389,24 +430,39 @@ __device__ void consume_tiles(const ChainOp &op, const ChainArgs &a, int tb, int
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_addr(&bars[kMaxStages + slot]));
     }
+    // the RPW x TT sums reduced together: lane l ends with value l >> kShift
+    constexpr int kNV = RPW * TT;
+    constexpr int kShift = 5 - ilog2(kNV);
     int mine = 0;
+    if constexpr (kNV <= 4) {
+      mine = warp_sum_multi<kNV>(acc, lane);
+    } else {  // (the halving form's extra live values spill at 96 registers)
 #pragma unroll
-    for (int r = 0; r < RPW; ++r)
-#pragma unroll
-      for (int t = 0; t < TT; ++t) {
-        const int s = warp_sum(acc[r][t]);
-        if (lane == r * TT + t) mine = s;
+      for (int i = 0; i < kNV; ++i) {
+        const int s2 = warp_sum(acc[i]);
+        if (lane == (i << kShift)) mine = s2;
       }
-    if (lane < RPW * TT) {
-      const int r = lane / TT, t = lane % TT;
+    }
+    if ((lane & ((1 << kShift) - 1)) == 0) {
+      const int vi = lane >> kShift;
+      const int r = vi / TT, t = vi % TT;
       const int row = warp * RPW + r;
       const int n = tile * RB + row;
       if (t < a.T && n < op.N && ok) {
-        // per-row parameters staged in shared memory before the step's grid barrier
+        // per-row parameters: staged in shared memory before the step's grid barrier, or for
+        // the LM-head step (hundreds of rows a CTA, streaming-bound) read from global memory
         const int lr = (tile - tb) * RB + row;
-        const int e_qm = ep.qm[lr];
-        const float e_step = ep.step[lr];
-        const float e_smooth = ep.smooth[lr];
+        int e_qm;
+        float e_step, e_smooth;
+        if (TOPK) {
+          e_qm = op.out_mode == kOutF32 ? __ldg(op.quant_m32 + n) : 0;
+          e_step = __ldg((op.out_mode == kOutF32Acc ? op.acc_step : op.out_step) + n);
+          e_smooth = -1.0f;
+        } else {
+          e_qm = ep.qm[lr];
+          e_step = ep.step[lr];
+          e_smooth = ep.smooth[lr];
+        }
         const bool e_amax = e_smooth >= 0.0f;
         const float step = dyn ? s_ratio[t] * e_step : e_step;
         if (op.out_mode == kOutAccI32) {
@@ -441,7 +497,7 @@ __device__ void consume_tiles(const ChainOp &op, const ChainArgs &a, int tb, int
 }
 
 template <int TT, bool TOPK>
-__device__ void consume_dispatch(const ChainOp &op, const ChainArgs &a, int tb, int te, int &it,
+__device__ void consume_dispatch(const ChainOp &op, const ChainArgs &a, int tb, int te, RingPos &it,
                                  const uint8_t *ring, const int8_t *xq, uint64_t *bars,
                                  const float *s_ratio, uint64_t *cand, int *s_amax,
                                  const EpiSmem &ep, int tid, bool &ok, unsigned long long *tr) {
@@ -494,12 +550,12 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   ChainOp *window = reinterpret_cast<ChainOp *>(smem);
   uint8_t *ring = smem + kWindow * sizeof(ChainOp);
-  int8_t *xq = reinterpret_cast<int8_t *>(ring + a.ring_bytes);
-  uint64_t *cand = reinterpret_cast<uint64_t *>(ring + a.ring_bytes + TT * a.kpad_max);
-  uint64_t *bars = cand + TT * a.cand_cap;
+  int8_t *xq = reinterpret_cast<int8_t *>(smem + a.xq_off);
+  uint64_t *cand = reinterpret_cast<uint64_t *>(smem + a.cand_off);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.bars_off);
   EpiSmem ep_buf[2];
   {
-    int *p = reinterpret_cast<int *>(bars + 2 * kMaxStages);
+    int *p = reinterpret_cast<int *>(smem + a.ep_off);
     for (int b = 0; b < 2; ++b) {
       ep_buf[b].qm = p;
       ep_buf[b].step = reinterpret_cast<float *>(p + a.max_rows);
@@ -507,9 +563,7 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
       p += 3 * a.max_rows;
     }
   }
-  // (max_rows is a multiple of 4: the staging row starts 16-byte aligned)
-  float *xs = a.norm_floats ? reinterpret_cast<float *>(bars + 2 * kMaxStages) + 6 * a.max_rows
-                            : nullptr;
+  float *xs = a.norm_floats ? reinterpret_cast<float *>(smem + a.norm_off) : nullptr;
   __shared__ float s_part[kCW][TT];
   __shared__ float s_ratio[TT];
   __shared__ float s_inv[TT];
@@ -534,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
   if (warp == kCW) {
     // ------------------------------- producer warp -------------------------------
     const uint64_t pol = policy_evict_first();
-    int it = 0;
+    RingPos rp;
     bool ok = true;
     for (int s = 0; s < a.n_ops && ok; ++s) {
       // The producer runs ahead of the consumers: fetch the next descriptor into L1 now, and
@@ -553,11 +607,11 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
       if (ptr && lane == 0) ptr[4] = global_timer_ns();
       for (int tile = tb; tile < te && ok; ++tile) {
         const int rows = min(rb, N - tile * rb);
-        for (int kci = 0; kci < nk; ++kci, ++it) {
-          const int slot = it % a.ns;
-          const int use = it / a.ns;
-          if (it >= a.ns) {
-            ok = mbar_wait_bounded(smem_addr(&bars[kMaxStages + slot]), (use - 1) & 1, a.err,
+        for (int kci = 0; kci < nk; ++kci, rp.advance(a.ns)) {
+          const int slot = rp.slot;
+          if (rp.lapped) {
+            // the consumers' release of this slot's previous fill (phase of the lap before)
+            ok = mbar_wait_bounded(smem_addr(&bars[kMaxStages + slot]), rp.phase ^ 1u, a.err,
                                    kDevTimeoutEmpty);
             if (!ok) break;
           }
@@ -588,7 +642,7 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
 
   // ------------------------------- consumer warps -------------------------------
   const int tid = threadIdx.x;
-  int it = 0;
+  RingPos it;
   bool ok = true;
   // descriptors 0 .. kWindow-2 into the window, then step 0's per-row epilogue parameters;
   // every later descriptor is fetched kWindow-1 steps ahead and every later step's
@@ -625,8 +679,6 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
     cp_async_wait_all_but_newest();
     float4 s_pre[4];
     preload_smooth(op, tid, s_pre);
-    if (op.topk)
-      for (int i = tid; i < TT * a.cand_cap; i += kCT) cand[i] = 0ull;
     if (op.barrier_before && s > 0) {
       // Once one grid wait has run out, later ones are skipped so the kernel still ends.
       if (tid == 0 && !s_abort) {
@@ -651,6 +703,12 @@ __global__ void __launch_bounds__(kThreads, 2) chain_kernel(const ChainArgs a) {
       // (quantise_input ends with a consumer barrier: the staged parameters are visible)
       if (te > tb) quantise_input<TT>(op, a.T, xq, a.kpad_max, s_ratio, s_inv, s_part, tid, s_pre, xs);
       else consumer_sync();
+      if (op.topk) {
+        // candidate slots (they may share bytes with the activation rows' tail and the norm
+        // staging row, both dead once the input is quantised)
+        for (int i = tid; i < TT * a.cand_cap; i += kCT) cand[i] = 0ull;
+        consumer_sync();
+      }
       if (tr && tid == 0) tr[1] = global_timer_ns();
       // the CTA owning tile 0 publishes the per-token ratios
       if (tb == 0 && te > 0 && op.ratio_out && tid < a.T && op.act_mode == kActDyntok)
@@ -715,6 +773,7 @@ bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, Chain
   size_t cand_cap = 0;
   int max_rows = 8;
   int norm_floats = 0;
+  int kpad_topk = 0;
   // Stage size target: every stage carries ~24 KB (whole-row tiles of up to 32 rows, or 8-row
   // K chunks of 3 KB per row for long rows), so the fixed-size ring slots stay full.
   constexpr int kMaxStage = 24576;
@@ -744,32 +803,54 @@ bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, Chain
     kpad_max = std::max(kpad_max, op.k_pad);
     if (op.act_mode == kActEmbNorm) norm_floats = std::max(norm_floats, (op.K + 3) / 4 * 4);
     const int max_tiles = (op.num_tiles + p.grid - 1) / p.grid;
-    max_rows = std::max(max_rows, max_tiles * op.rb);
     if (op.topk) {
-      size_t c = 1;
-      while (c < static_cast<size_t>(max_tiles) * op.rb) c <<= 1;
-      cand_cap = c;
+      // candidate slots of the LM-head step (its epilogue parameters are not staged)
+      cand_cap = (static_cast<size_t>(max_tiles) * op.rb + 7) / 8 * 8;
+      kpad_topk = op.k_pad;
+    } else {
+      max_rows = std::max(max_rows, max_tiles * op.rb);
     }
   }
-  p.kpad_max = (kpad_max + 15) / 16 * 16;
+  auto up16 = [](size_t v) { return (v + 15) / 16 * 16; };
+  p.kpad_max = static_cast<int>(up16(kpad_max));
   p.cand_cap = static_cast<int>(cand_cap);
   p.max_rows = (max_rows + 3) / 4 * 4;
   p.stage_bytes = static_cast<uint32_t>(stage);
   p.norm_floats = norm_floats;
-  const size_t fixed = static_cast<size_t>(p.tt) * p.kpad_max + static_cast<size_t>(p.tt) * cand_cap * 8 +
-                      2 * kMaxStages * 8 + 2 * static_cast<size_t>(p.max_rows) * 12 +
-                      static_cast<size_t>(norm_floats) * 4 + kWindow * sizeof(ChainOp);
+  // Layout after the ring, relative to the activation rows: xq [tt][kpad_max]; the LM-head
+  // step's candidates in the rows' tail when one token leaves room after its row (the
+  // candidates are written only once that step's input is quantised), else after xq; the
+  // mbarriers; the two epilogue parameter buffers; the norm staging row, inside xq when it fits
+  // (it is dead before the step writes its quantised rows).
+  const size_t xq_bytes = static_cast<size_t>(p.tt) * p.kpad_max;
+  const size_t cand_bytes = static_cast<size_t>(p.tt) * cand_cap * 8;
+  const bool cand_in_xq = p.tt == 1 && cand_bytes > 0 && up16(kpad_topk) + cand_bytes <= xq_bytes;
+  const bool norm_in_xq = static_cast<size_t>(norm_floats) * 4 <= xq_bytes;
+  const size_t cand_rel = cand_in_xq ? up16(kpad_topk) : xq_bytes;
+  const size_t bars_rel = up16(cand_in_xq ? xq_bytes : xq_bytes + cand_bytes);
+  const size_t ep_rel = bars_rel + 2 * kMaxStages * 8;
+  const size_t norm_rel = norm_in_xq ? 0 : up16(ep_rel + 2 * static_cast<size_t>(p.max_rows) * 12);
+  const size_t tail = norm_in_xq ? ep_rel + 2 * static_cast<size_t>(p.max_rows) * 12
+                                 : norm_rel + static_cast<size_t>(norm_floats) * 4;
+  const size_t window = kWindow * sizeof(ChainOp);
+  const size_t fixed = window + up16(tail);
   // the SM's 228 KB split between the co-resident CTAs, less the per-CTA reservation and
-  // static shared memory
-  const size_t budget = 233472 / cps - 1024 - 2048;
+  // static shared memory (a few hundred bytes)
+  const size_t budget = 233472 / cps - 1024 - 1024;
   if (fixed + 2 * stage > budget) return false;
   p.ns = static_cast<int>(std::min<size_t>(kMaxStages, (budget - fixed) / stage));
   p.ring_bytes = static_cast<uint32_t>(p.ns * stage);
+  const size_t xq_off = window + p.ring_bytes;
+  p.xq_off = static_cast<uint32_t>(xq_off);
+  p.cand_off = static_cast<uint32_t>(xq_off + cand_rel);
+  p.bars_off = static_cast<uint32_t>(xq_off + bars_rel);
+  p.ep_off = static_cast<uint32_t>(xq_off + ep_rel);
+  p.norm_off = static_cast<uint32_t>(xq_off + norm_rel);
   // the top-k step reuses the drained ring for its staged lists and gathered candidates
   bool any_topk = false;
   for (int s = 0; s < n_ops; ++s) any_topk = any_topk || ops[s].topk;
   if (any_topk && p.ring_bytes < (kCW * 64 + kTopkGatherKeys) * 8) return false;
-  p.smem = p.ring_bytes + fixed;
+  p.smem = p.ring_bytes + fixed;  // (fixed includes the window)
   *plan = p;
   return true;
 }
@@ -804,6 +885,11 @@ cudaError_t launch_chain(const ChainOp *ops_dev, int n_ops, int T, const ChainPl
   a.max_rows = plan.max_rows;
   a.ring_bytes = plan.ring_bytes;
   a.norm_floats = plan.norm_floats;
+  a.xq_off = plan.xq_off;
+  a.cand_off = plan.cand_off;
+  a.bars_off = plan.bars_off;
+  a.ep_off = plan.ep_off;
+  a.norm_off = plan.norm_off;
   a.trace = trace;
   void (*kern)(ChainArgs) = nullptr;
   switch (plan.tt) {

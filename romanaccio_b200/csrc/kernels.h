@@ -393,6 +393,10 @@ struct ChainPlan {
   int tt, grid, kpad_max, cand_cap, max_rows, ns;
   int norm_floats;  // fp32 staging of one token's input row for kActEmbNorm steps (0: none)
   uint32_t stage_bytes, ring_bytes;
+  // byte offsets in dynamic shared memory (the descriptor window sits at 0, the ring after it):
+  // activation rows, top-k candidate keys, mbarriers, epilogue parameters, norm staging row.
+  // The candidates and the staging row may lie inside the activation rows' unused bytes.
+  uint32_t xq_off, cand_off, bars_off, ep_off, norm_off;
   size_t smem;
 };
 
