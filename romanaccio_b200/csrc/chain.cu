@@ -31,6 +31,15 @@ constexpr int kCW = 8;              // consumer warps
 constexpr int kCT = kCW * 32;       // consumer threads
 constexpr int kThreads = kCT + 32;  // + producer warp
 constexpr int kMaxStages = 8;
+// Weight stages in flight per CTA.  When a CTA streams little per dependent step (latency-bound
+// chains), two stages of ~24 KB beat a deeper ring: bytes queued in the memory system lengthen
+// every L2 round trip on the step-to-step critical path (the arrival fence, the counter poll, the
+// activation read) more than they add overlap (28-layer Qwen2.5-1.5B-shaped step, ~47 KB per CTA
+// per step: 688 us at two stages against 723 us at four).  Chains streaming more per step keep
+// every stage that fits (48-layer Gemma-12B-shaped step, ~200 KB: 2716 us at four against 2990 us
+// at two).
+constexpr int kLatencyRingStages = 2;
+constexpr size_t kDeepRingBytesPerStep = 96 * 1024;  // weight bytes per CTA per step
 // activation float4 loads in flight per thread in quantise_input (more registers at TT = 1,
 // fewer at TT = 8, whose accumulators and activation vectors leave less room)
 template <int TT>
@@ -838,7 +847,10 @@ bool plan_chain_cps(ChainOp *ops, int n_ops, int T, int sm_count, int cps, Chain
   // static shared memory (a few hundred bytes)
   const size_t budget = 233472 / cps - 1024 - 1024;
   if (fixed + 2 * stage > budget) return false;
-  p.ns = static_cast<int>(std::min<size_t>(kMaxStages, (budget - fixed) / stage));
+  size_t weight_bytes = 0;
+  for (int s = 0; s < n_ops; ++s) weight_bytes += static_cast<size_t>(ops[s].N) * ops[s].k_pad;
+  const bool deep = weight_bytes / (static_cast<size_t>(n_ops) * p.grid) >= kDeepRingBytesPerStep;
+  p.ns = static_cast<int>(std::min<size_t>(deep ? kMaxStages : kLatencyRingStages, (budget - fixed) / stage));
   p.ring_bytes = static_cast<uint32_t>(p.ns * stage);
   const size_t xq_off = window + p.ring_bytes;
   p.xq_off = static_cast<uint32_t>(xq_off);
