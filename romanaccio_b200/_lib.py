@@ -28,7 +28,7 @@ DTYPE_FP16, DTYPE_INT8, DTYPE_INT16 = 0, 1, 2
 ACT_STATIC, ACT_DYNTOK = 0, 1
 OUT_ACC_I32, OUT_QUANT, OUT_F32, OUT_F32_ACC = 0, 1, 2, 3
 TOPK_MAX = 64
-PATH_AUTO, PATH_GEMV, PATH_TENSOR = 0, 1, 2
+PATH_AUTO, PATH_GEMV, PATH_TENSOR, PATH_TENSOR_PAIR = 0, 1, 2, 3
 TC_MIN_TOKENS = 16
 
 

@@ -231,11 +231,11 @@ w8a8_status check_modes(const w8a8_linear *l, int act_mode, int out_mode) {
 w8a8_status run_gemv(w8a8_linear *l, const int8_t *xq, int64_t ldx, int T, int act_mode,
                      const float *ratio, int out_mode, void *y, int64_t ldy, bool pdl,
                      cudaStream_t st) {
-  const bool tensor = l->path == W8A8_PATH_TENSOR ||
+  const bool tensor = l->path == W8A8_PATH_TENSOR || l->path == W8A8_PATH_TENSOR_PAIR ||
                       (l->path == W8A8_PATH_AUTO && T >= W8A8_TC_MIN_TOKENS);
   if (tensor) {
     TcPlan plan;
-    if (!plan_tc(T, l->N, l->k_pad, l->ctx->sm_count, &plan))
+    if (!plan_tc(T, l->N, l->k_pad, l->ctx->sm_count, &plan, l->path == W8A8_PATH_TENSOR_PAIR))
       return fail(W8A8_ERR_NOT_SUPPORTED, "no tensor-core plan for T=%d N=%d K=%d", T, l->N, l->K);
     if (plan.splits > 1) {
       w8a8_status s = ensure_tc_scratch(l, static_cast<size_t>(plan.splits) * T * l->N,
@@ -603,7 +603,8 @@ w8a8_status w8a8_linear_set_input_norm(w8a8_linear *l, const float *emb_norm_sca
 
 w8a8_status w8a8_linear_set_path(w8a8_linear *l, int32_t path) {
   if (!l) return fail(W8A8_ERR_INVALID_ARG, "linear is NULL");
-  if (path != W8A8_PATH_AUTO && path != W8A8_PATH_GEMV && path != W8A8_PATH_TENSOR)
+  if (path != W8A8_PATH_AUTO && path != W8A8_PATH_GEMV && path != W8A8_PATH_TENSOR &&
+      path != W8A8_PATH_TENSOR_PAIR)
     return fail(W8A8_ERR_INVALID_ARG, "path %d is not a w8a8_path", path);
   l->path = path;
   return W8A8_SUCCESS;

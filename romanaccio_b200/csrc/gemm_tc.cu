@@ -26,6 +26,7 @@
 // quarter a warp may access is fixed by its id modulo 4) and every 4th column chunk from (w-2)/4.
 #include <cuda.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <mutex>
@@ -134,6 +135,101 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// ---- CTA pair (cluster of two) helpers ----
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Arrives on an mbarrier of the other CTA of the pair (address from map_to_rank).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+// Bounded wait on a local mbarrier phase completed by arrivals from the other CTA (acquire at
+// cluster scope).
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int *err, int code) {
+  auto try_wait = [&]() {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+  };
+  if (try_wait()) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (try_wait()) return true;
+    if ((i & 511u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+      if (err) atomicExch(err, code);
+      return false;
+    }
+  }
+}
+
+// 2-D tensor copy into this CTA's shared memory whose completion (complete_tx) is signalled on
+// the mbarrier at cluster address `bar`, which may be the other CTA's of the pair (.cta_group::2).
+// A plain per-CTA load: no multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int c0, int c1,
+                                                 uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair_hint(uint32_t dst, const CUtensorMap *map, int c0,
+                                                      int c1, uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// The pair's MMA (issued by the even CTA): A = both CTAs' 128-row weight halves (M = 256),
+// B = both CTAs' token halves (N = BT), D = each CTA's own TMEM (its 128 channels).
+__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on the mbarrier at offset `bar` in both CTAs of the pair once the MMAs issued so far
+// have completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(bar), "h"(static_cast<uint16_t>(3))
+      : "memory");
 }
 
 // Shared-memory matrix descriptor of a K-major tile written by TMA with the 128-byte swizzle:
@@ -292,18 +388,35 @@ __device__ __forceinline__ Unit decode_unit(const TcArgs &a, int u) {
   return r;
 }
 
-// The epilogue warps' loop over this CTA's units.
-template <int MODE>
+// A CTA pair's unit u: 256 channels (this CTA's 128: channel block 2 * (u / tiles_t) + rank)
+// by BT tokens, the whole K.
+__device__ __forceinline__ Unit decode_pair_unit(const TcArgs &a, int u, uint32_t rank) {
+  Unit r;
+  r.split = 0;
+  r.tile = u;
+  r.tb = u % a.tiles_t;
+  r.nb = 2 * (u / a.tiles_t) + static_cast<int>(rank);
+  r.k_begin = 0;
+  r.k_end = a.k_iters;
+  return r;
+}
+
+// The epilogue warps' loop over this CTA's units (PAIR: over its pair's units, handing the
+// accumulator buffer back to the even CTA, which issues the pair's MMAs).
+template <int MODE, bool PAIR>
 __device__ __forceinline__ void epilogue_role(const TcArgs &a, uint32_t tmem, uint32_t tfull0,
                                               uint32_t tempty0, int warp, int lane, int *s_last) {
   const Epilogue &ep = a.ep;
   const int q = warp & 3;
   const int group = (warp - 2) >> 2;  // column group of this warp
   const size_t plane = static_cast<size_t>(a.T) * a.N;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
   bool ok = true;
   int j = 0;
-  for (int u = blockIdx.x; u < a.units; u += gridDim.x, ++j) {
-    const Unit un = decode_unit(a, u);
+  const int u0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int du = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  for (int u = u0; u < a.units; u += du, ++j) {
+    const Unit un = PAIR ? decode_pair_unit(a, u, rank) : decode_unit(a, u);
     const int buf = j & 1, use = j >> 1;
     if (ok) ok = mbar_wait_bounded(tfull0 + 8 * buf, use & 1, a.err, kDevTimeoutFull);
     // tcgen05.ld is warp-collective: the whole warp takes the same branch.
@@ -343,7 +456,12 @@ __device__ __forceinline__ void epilogue_role(const TcArgs &a, uint32_t tmem, ui
     // TMEM buffer free for the next unit's MMAs.
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
+    if (lane == 0) {
+      if (PAIR && rank != 0)
+        mbar_arrive_remote(map_to_rank(tempty0 + 8 * buf, 0));
+      else
+        mbar_arrive(tempty0 + 8 * buf);
+    }
     if (j == 0 && threadIdx.x == 64) stamp(a, 6);
   }
 }
@@ -464,17 +582,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     switch (a.ep.out_mode | rq_int) {
       case kOutAccI32:
       case kOutAccI32 | kRqInt:
-        epilogue_role<kOutAccI32>(a, tmem, tfull0, tempty0, warp, lane, &s_last);
+        epilogue_role<kOutAccI32, false>(a, tmem, tfull0, tempty0, warp, lane, &s_last);
         break;
-      case kOutQuant: epilogue_role<kOutQuant>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+      case kOutQuant: epilogue_role<kOutQuant, false>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
       case kOutQuant | kRqInt:
-        epilogue_role<kOutQuant | kRqInt>(a, tmem, tfull0, tempty0, warp, lane, &s_last);
+        epilogue_role<kOutQuant | kRqInt, false>(a, tmem, tfull0, tempty0, warp, lane, &s_last);
         break;
-      case kOutF32: epilogue_role<kOutF32>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+      case kOutF32: epilogue_role<kOutF32, false>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
       case kOutF32 | kRqInt:
-        epilogue_role<kOutF32 | kRqInt>(a, tmem, tfull0, tempty0, warp, lane, &s_last);
+        epilogue_role<kOutF32 | kRqInt, false>(a, tmem, tfull0, tempty0, warp, lane, &s_last);
         break;
-      default: epilogue_role<kOutF32Acc>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+      default: epilogue_role<kOutF32Acc, false>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
     }
     tc_fence_before();
     __syncwarp();
@@ -490,6 +608,167 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, a.tmem_cols);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) stamp(a, 7);
+}
+
+// The CTA-pair kernel (clusters of two, launched with a cluster dimension of 2).  Each CTA loads
+// its own operand halves into the same shared-memory offsets as its peer, by 2-D tensor copies
+// (weights: the pre-swizzled 16 KB tiles viewed as a [tiles * 128, 128] byte matrix, copied
+// unswizzled) whose completion both CTAs signal on the even CTA's full barrier (.cta_group::2; the
+// even CTA announces both halves' bytes).  The even CTA ("leader") issues the pair's cta_group::2
+// MMAs once a stage's barrier completes; the MMA commits arrive on both CTAs' empty / tfull
+// barriers (tcgen05.commit multicast); both CTAs' epilogue warps hand an accumulator buffer back
+// to the leader's tempty barrier.  Before either CTA deallocates TMEM and exits, the two exchange
+// a final arrival (bye), so no arrival targets a CTA that has exited.  Every wait is bounded.
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_w8a8_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
+                             const __grid_constant__ CUtensorMap tm_w, const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 6];
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_last;
+
+  const uint32_t raw = smem_addr(smem_raw);
+  const uint32_t tiles = (raw + 1023u) & ~1023u;  // (the same offset in both CTAs)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const uint32_t full0 = smem_addr(&bars[0]);
+  const uint32_t empty0 = smem_addr(&bars[kMaxStages]);
+  const uint32_t tfull0 = smem_addr(&bars[2 * kMaxStages]);
+  const uint32_t tempty0 = smem_addr(&bars[2 * kMaxStages + 2]);
+  const uint32_t epi_done = smem_addr(&bars[2 * kMaxStages + 4]);
+  const uint32_t bye = smem_addr(&bars[2 * kMaxStages + 5]);
+  const int u0 = static_cast<int>(blockIdx.x >> 1), du = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    stamp(a, 0);
+    for (int s = 0; s < a.ns; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);
+      mbar_init(tempty0 + 8 * b, 2 * kEpiWarps);
+    }
+    mbar_init(epi_done, kEpiWarps);
+    mbar_init(bye, 1);
+    fence_barrier_init();
+  }
+  // both CTAs' barriers are initialised before either CTA arrives on the other's
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (warp == 1) tmem_alloc_pair(smem_addr(&s_tmem), a.tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  if (threadIdx.x == 0) stamp(a, 1);
+
+  if (warp == 0) {
+    // ------------------------------- TMA producer (both CTAs) -------------------------------
+    if (lane == 0) {
+      prefetch_tensormap(&tm_x);
+      prefetch_tensormap(&tm_w);
+      const uint64_t pol_w = a.w_stream ? policy_evict_first() : policy_evict_last();
+      const uint32_t full_leader = map_to_rank(full0, 0);  // (the even CTA's own address for it)
+      const int tiles_n = (a.N + kBM - 1) / kBM;
+      bool ok = true, dep_done = false;
+      uint32_t g = 0;
+      for (int u = u0; u < a.units && ok; u += du) {
+        const Unit un = decode_pair_unit(a, u, rank);
+        const int nb = un.nb < tiles_n ? un.nb : tiles_n - 1;  // (a missing half: outputs masked)
+        for (int kit = 0; kit < a.k_iters; ++kit, ++g) {
+          const uint32_t s = g % a.ns, use = g / a.ns;
+          if (use > 0) ok = mbar_wait_bounded(empty0 + 8 * s, (use - 1) & 1, a.err, kDevTimeoutEmpty);
+          if (!ok) break;
+          const uint32_t full = full_leader + 8 * s;
+          const uint32_t dst = tiles + s * a.stage_bytes;
+          // the leader announces both CTAs' bytes of the stage; either CTA's copies may complete
+          // first (the transaction count may go below zero until the announcement)
+          if (rank == 0) mbar_arrive_expect_tx(full0 + 8 * s, 2 * a.stage_bytes);
+          tma_load_2d_pair_hint(dst, &tm_w, 0, (nb * a.k_iters + kit) * kBM, full, pol_w);
+          if (!dep_done) {
+            pdl_wait();
+            dep_done = true;
+          }
+          tma_load_2d_pair(dst + kTileWBytes, &tm_x, kit * kBK,
+                           un.tb * a.BT + static_cast<int>(rank) * (a.BT / 2), full);
+          if (g == 0) stamp(a, 2);
+        }
+      }
+      // Every MMA reading this CTA's stages has completed (the leader's commits on the empty
+      // barriers) before the CTA may exit.
+      const uint32_t first = g > static_cast<uint32_t>(a.ns) ? g - a.ns : 0u;
+      for (uint32_t i = first; i < g && ok; ++i)
+        ok = mbar_wait_bounded(empty0 + 8 * (i % a.ns), (i / a.ns) & 1, a.err, kDevTimeoutEmpty);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ------------------------------- MMA issuer (even CTA) -------------------------------
+      bool ok = true;
+      uint32_t g = 0;
+      int j = 0;
+      for (int u = u0; u < a.units; u += du, ++j) {
+        const int buf = j & 1, use = j >> 1;
+        if (ok && use > 0)
+          ok = mbar_wait_cluster(tempty0 + 8 * buf, (use - 1) & 1, a.err, kDevTimeoutEmpty);
+        tc_fence_after();
+        const uint32_t d = tmem + buf * a.buf_stride;
+        for (int kit = 0; kit < a.k_iters && ok; ++kit, ++g) {
+          const uint32_t s = g % a.ns, su = g / a.ns;
+          ok = mbar_wait_cluster(full0 + 8 * s, su & 1, a.err, kDevTimeoutFull);
+          if (!ok) break;
+          if (g == 0) stamp(a, 3);
+          tc_fence_after();
+          const uint32_t base = tiles + s * a.stage_bytes;
+          const uint64_t adesc = smem_desc_sw128(base);
+          const uint64_t bdesc = smem_desc_sw128(base + kTileWBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / kMmaK; ++kk)
+            mma_i8_pair(d, adesc + 2 * kk, bdesc + 2 * kk, a.idesc, (kit > 0 || kk > 0) ? 1u : 0u);
+          mma_commit_pair(empty0 + 8 * s);
+        }
+        // always released (also after a timeout) so that the epilogue warps do not wait twice
+        mma_commit_pair(tfull0 + 8 * buf);
+        if (j == 0) stamp(a, 4);
+        if (!ok) break;
+      }
+    }
+  } else {
+    // ------------------------------- epilogue (both CTAs) -------------------------------
+    pdl_wait();
+    const int rq_int = (a.ep.trunc >= 15 && a.ep.trunc <= 31) ? kRqInt : 0;
+    switch (a.ep.out_mode | rq_int) {
+      case kOutAccI32:
+      case kOutAccI32 | kRqInt:
+        epilogue_role<kOutAccI32, true>(a, tmem, tfull0, tempty0, warp, lane, &s_last);
+        break;
+      case kOutQuant: epilogue_role<kOutQuant, true>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+      case kOutQuant | kRqInt:
+        epilogue_role<kOutQuant | kRqInt, true>(a, tmem, tfull0, tempty0, warp, lane, &s_last);
+        break;
+      case kOutF32: epilogue_role<kOutF32, true>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+      case kOutF32 | kRqInt:
+        epilogue_role<kOutF32 | kRqInt, true>(a, tmem, tfull0, tempty0, warp, lane, &s_last);
+        break;
+      default: epilogue_role<kOutF32Acc, true>(a, tmem, tfull0, tempty0, warp, lane, &s_last); break;
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(epi_done);
+  }
+
+  __syncwarp();
+  if (warp == 1) {
+    bool ok = mbar_wait_bounded(epi_done, 0, a.err, kDevTimeoutFull);
+    if (lane == 0) {
+      mbar_arrive_remote(map_to_rank(bye, rank ^ 1u));
+      if (ok) mbar_wait_cluster(bye, 0, a.err, kDevPeerTimeout);
+    }
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, a.tmem_cols);
   }
   __syncthreads();
   if (threadIdx.x == 0) stamp(a, 7);
@@ -531,6 +810,20 @@ bool encode_i8_rows(CUtensorMap *map, const int8_t *base, int64_t rows, int64_t 
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The tile-ordered weights as a [rows, 128] byte matrix read in 128 x 128 boxes without swizzle
+// (each box is one 16 KB tile, already in its shared-memory image).
+bool encode_w_tiles(CUtensorMap *map, const int8_t *tiles, int64_t rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kBK), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kBK)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(kBM)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(tiles), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // One CTA per 128 x 128-byte tile: 16-byte chunk c of row r goes to chunk c ^ (r % 8) of the
 // row, the pattern TMA writes for CU_TENSOR_MAP_SWIZZLE_128B into a 1024-byte aligned tile.
 __global__ void tile_weights_kernel(const int8_t *__restrict__ w, int64_t ldw, int N, int k_pad,
@@ -550,7 +843,7 @@ __global__ void tile_weights_kernel(const int8_t *__restrict__ w, int64_t ldw, i
 
 }  // namespace
 
-bool plan_tc(int T, int N, int k_pad, int sm_count, TcPlan *p) {
+bool plan_tc(int T, int N, int k_pad, int sm_count, TcPlan *p, bool force_pair) {
   if (T < 1 || N < 1 || k_pad < 16 || sm_count < 1) return false;
   TcPlan r = {};
   r.tiles_t = (T + kMaxBT - 1) / kMaxBT;
@@ -558,6 +851,28 @@ bool plan_tc(int T, int N, int k_pad, int sm_count, TcPlan *p) {
   r.BT = (per + 15) / 16 * 16;
   r.tiles_n = (N + kBM - 1) / kBM;
   r.k_iters = (k_pad + kBK - 1) / kBK;
+  const size_t budget = kMaxDynSmem - 1024 - 1024;  // alignment slack + static barriers
+  // CTA pairs when the 256-channel tiles alone fill the SMs (no split-K) and K is long enough
+  // for the pipeline: half the tokens per CTA, token tiles a multiple of 32.
+  const int pair_units = ((r.tiles_n + 1) / 2) * r.tiles_t;
+  if (force_pair || (T >= 256 && r.k_iters >= 8 && 2 * pair_units >= sm_count)) {
+    r.pair = 1;
+    r.BT = (per + 31) / 32 * 32;
+    r.splits = 1;
+    r.ips = r.k_iters;
+    r.units = pair_units;
+    r.grid = 2 * (pair_units < sm_count / 2 ? pair_units : sm_count / 2);
+    r.stage_bytes = kTileWBytes + static_cast<uint32_t>(r.BT / 2) * kBK;
+    int ns = static_cast<int>(budget / r.stage_bytes);
+    if (ns > kMaxStages) ns = kMaxStages;
+    r.ns = ns;
+    r.smem = static_cast<size_t>(ns) * r.stage_bytes + 1024;
+    uint32_t cols = 32;
+    while (cols < static_cast<uint32_t>(2 * r.BT)) cols <<= 1;
+    r.tmem_cols = cols;
+    *p = r;
+    return true;
+  }
   const int tiles = r.tiles_n * r.tiles_t;
   r.splits = 1;
   if (tiles < sm_count) {
@@ -575,7 +890,6 @@ bool plan_tc(int T, int N, int k_pad, int sm_count, TcPlan *p) {
   r.units = tiles * r.splits;
   r.grid = r.units < sm_count ? r.units : sm_count;
   r.stage_bytes = kTileWBytes + static_cast<uint32_t>(r.BT) * kBK;
-  const size_t budget = kMaxDynSmem - 1024 - 1024;  // alignment slack + static barriers
   int ns = static_cast<int>(budget / r.stage_bytes);
   if (ns > kMaxStages) ns = kMaxStages;
   const int total_iters = r.ips * ((r.units + r.grid - 1) / r.grid);
@@ -590,14 +904,52 @@ bool plan_tc(int T, int N, int k_pad, int sm_count, TcPlan *p) {
   return true;
 }
 
+// Co-resident clusters of two of the pair kernel at `smem` bytes (per device and size, queried
+// once): the persistent grid is no larger, so no cluster waits for another to finish.
+int pair_clusters(size_t smem, int sm_count) {
+  static std::mutex mu;
+  static int cached_dev[16] = {}, cached_n[16] = {};
+  static size_t cached_smem[16] = {};
+  static int used = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> g(mu);
+  for (int i = 0; i < used; ++i)
+    if (cached_dev[i] == dev && cached_smem[i] == smem) return cached_n[i];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(sm_count / 2 * 2));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_w8a8_tc_pair_kernel, &cfg) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    n = 0;
+  }
+  if (used < 16) {
+    cached_dev[used] = dev;
+    cached_smem[used] = smem;
+    cached_n[used] = n;
+    ++used;
+  }
+  return n;
+}
+
 cudaError_t launch_tc(const TcLaunch &L, const TcPlan &p, cudaStream_t stream) {
   CUtensorMap tm_x;
-  if (!encode_i8_rows(&tm_x, L.x, L.T, L.k_extent_x, L.ldx, p.BT)) {
+  if (!encode_i8_rows(&tm_x, L.x, L.T, L.k_extent_x, L.ldx, p.pair ? p.BT / 2 : p.BT)) {
     set_last_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad operand)");
     return cudaErrorInvalidValue;
   }
   int limit = 0;
-  cudaError_t attr_err = opt_in_dyn_smem<gemm_w8a8_tc_kernel>(&limit);
+  cudaError_t attr_err = p.pair ? opt_in_dyn_smem<gemm_w8a8_tc_pair_kernel>(&limit)
+                                : opt_in_dyn_smem<gemm_w8a8_tc_kernel>(&limit);
   if (attr_err != cudaSuccess) return attr_err;
   if (p.smem > static_cast<size_t>(limit)) return cudaErrorInvalidValue;
   TcArgs a = {};
@@ -616,7 +968,7 @@ cudaError_t launch_tc(const TcLaunch &L, const TcPlan &p, cudaStream_t stream) {
   // Instruction descriptor: D int32 (bits 4-5 = 2), A and B signed int8 (bits 7-9, 10-12 = 1),
   // both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
   a.idesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(p.BT >> 3) << 17) |
-            (static_cast<uint32_t>(kBM >> 4) << 24);
+            (static_cast<uint32_t>((p.pair ? 2 * kBM : kBM) >> 4) << 24);
   a.ep = L.ep;
   a.ws = L.ws;
   a.tile_count = L.tile_count;
@@ -624,8 +976,38 @@ cudaError_t launch_tc(const TcLaunch &L, const TcPlan &p, cudaStream_t stream) {
   a.w_tiles = L.w_tiles;
   a.trace = L.trace;
   a.w_stream = p.tiles_t == 1 ? 1 : 0;
-  return launch_ex(gemm_w8a8_tc_kernel, dim3(p.grid), dim3(kThreads), p.smem, stream, L.pdl, tm_x,
-                   a);
+  if (!p.pair)
+    return launch_ex(gemm_w8a8_tc_kernel, dim3(p.grid), dim3(kThreads), p.smem, stream, L.pdl, tm_x,
+                     a);
+  int sm_count = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+  const int clusters = pair_clusters(p.smem, sm_count);
+  if (clusters < 1) {
+    set_last_error("no cluster of two CTAs of the pair GEMM fits on this device");
+    return cudaErrorInvalidConfiguration;
+  }
+  const int grid = 2 * std::min(p.grid / 2, clusters);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = L.pdl ? 2 : 1;
+  CUtensorMap tm_w;
+  if (!encode_w_tiles(&tm_w, L.w_tiles, static_cast<int64_t>(p.tiles_n) * p.k_iters * kBM)) {
+    set_last_error("cuTensorMapEncodeTiled failed for the weight tiles");
+    return cudaErrorInvalidValue;
+  }
+  return cudaLaunchKernelEx(&cfg, gemm_w8a8_tc_pair_kernel, tm_x, tm_w, a);
 }
 
 size_t tc_tile_bytes(int N, int k_pad) {

@@ -154,6 +154,10 @@ struct TcPlan {
   int ns;          // pipeline depth
   uint32_t stage_bytes, tmem_cols;
   size_t smem;
+  // CTA pairs (clusters of two, tcgen05 cta_group::2): a unit is a 256-channel x BT-token tile;
+  // each CTA of the pair loads its 128 channels and BT / 2 tokens, and the pair's MMAs (M = 256)
+  // read both CTAs' halves, so each SM streams 1.5x fewer operand bytes per MAC.  No split-K.
+  int pair;
 };
 
 struct TcLaunch {
@@ -170,7 +174,8 @@ struct TcLaunch {
   bool pdl;
 };
 
-bool plan_tc(int T, int N, int k_pad, int sm_count, TcPlan *plan);
+// force_pair: CTA pairs whatever the size (otherwise only when they fill the SMs).
+bool plan_tc(int T, int N, int k_pad, int sm_count, TcPlan *plan, bool force_pair = false);
 cudaError_t launch_tc(const TcLaunch &L, const TcPlan &plan, cudaStream_t stream);
 // Weights [N, ldw] (k_pad readable columns) re-laid as contiguous 128 x 128-byte tiles
 // [ceil(N/128)][ceil(k_pad/128)], each stored exactly as the 128-byte-swizzled shared-memory

@@ -11,7 +11,7 @@ import torch
 from oracle import oracle as O
 import romanaccio_b200 as rb
 from romanaccio_b200 import synth
-from romanaccio_b200._lib import PATH_GEMV, PATH_TENSOR
+from romanaccio_b200._lib import PATH_GEMV, PATH_TENSOR, PATH_TENSOR_PAIR
 
 from test_linear_gpu import inputs, make_linear, random_params
 
@@ -56,6 +56,36 @@ def test_tensor_path_bit_exact(ctx, T, K, N, dyntok):
     # fused forward (act quant + contraction + epilogue)
     yf = lin.forward(xd, out_mode=rb.OUT_F32, dyntok=dyntok)
     assert np.array_equal(yf.cpu().numpy(), y)
+
+
+# CTA-pair plans (clusters of two, cta_group::2 MMAs over 256-channel tiles) forced at small and
+# ragged sizes: an odd count of 128-channel blocks (the pair's second half past N), token tiles
+# not a multiple of the pair's halves, K tails, several token blocks and several units per pair.
+PAIR_SHAPES = [(32, 576, 576), (17, 160, 300), (256, 1024, 384), (300, 1536, 1536),
+               (513, 160, 136), (64, 8960, 1536), (96, 2048, 2304)]
+
+
+@pytest.mark.parametrize("T,K,N", PAIR_SHAPES)
+@pytest.mark.parametrize("dyntok", [True, False])
+def test_tensor_pair_path_bit_exact(ctx, T, K, N, dyntok):
+    p = random_params(K, N, seed=T * 137 + K * 5 + N)
+    lin = make_linear(ctx, p)
+    lin.set_path(PATH_TENSOR_PAIR)
+    x = inputs(T, K, seed=T + 2 * K + N)
+    xd = torch.from_numpy(x).cuda()
+    ratio_d = torch.zeros(T, dtype=torch.float32, device="cuda") if dyntok else None
+    qd = lin.pack_npu_input(xd, dyntok_ratios=ratio_d)
+    if dyntok:
+        q, r = O.pack_dyntok(x, 3.0, p["inv_smooth"])
+    else:
+        q, r = O.pack_static(x, 0.05, p["inv_smooth"]), None
+    acc, yq, y, ya = _oracle_outputs(p, q, r)
+    torch.cuda.synchronize()
+    assert np.array_equal(lin.submit(qd, rb.OUT_ACC_I32).cpu().numpy(), acc)
+    assert np.array_equal(lin.submit(qd, rb.OUT_QUANT).cpu().numpy().astype(np.int32), yq)
+    assert np.array_equal(lin.submit(qd, rb.OUT_F32, dyntok_ratios=ratio_d).cpu().numpy(), y)
+    assert np.array_equal(lin.submit(qd, rb.OUT_F32_ACC, dyntok_ratios=ratio_d).cpu().numpy(), ya)
+    ctx.check()
 
 
 @pytest.mark.parametrize("T", [9, 16, 24, 48, 64])
