@@ -179,10 +179,10 @@ w8a8_status w8a8_linear_forward(w8a8_linear *linear, const float *x_dev, int64_t
 /* Contraction engine used by forward / forward_q (no reference counterpart: the reference has
  * one NPU engine).  AUTO streams the weights through the GEMV kernels for small token counts and
  * switches to the tcgen05 tensor-core GEMM above W8A8_TC_MIN_TOKENS; GEMV and TENSOR force one.
- * The tensor-core GEMM runs on CTA pairs (clusters of two SMs sharing each 256-channel tile,
- * tcgen05 cta_group::2) when T >= 256, K >= 1024 and the 256-channel tiles fill the SMs, else one
- * CTA per 128-channel tile; TENSOR_PAIR forces the pairs at any size.  All give bit-identical
- * results. */
+ * TENSOR runs one CTA per 128-channel tile; TENSOR_PAIR runs CTA pairs (clusters of two SMs
+ * sharing each 256-channel tile, tcgen05 cta_group::2 MMAs: 1.5x fewer operand bytes per SM, but
+ * slower on B200 for the prefill shapes measured, so AUTO does not choose it).  All give
+ * bit-identical results. */
 typedef enum {
     W8A8_PATH_AUTO        = 0,
     W8A8_PATH_GEMV        = 1,

@@ -852,10 +852,12 @@ bool plan_tc(int T, int N, int k_pad, int sm_count, TcPlan *p, bool force_pair) 
   r.tiles_n = (N + kBM - 1) / kBM;
   r.k_iters = (k_pad + kBK - 1) / kBK;
   const size_t budget = kMaxDynSmem - 1024 - 1024;  // alignment slack + static barriers
-  // CTA pairs when the 256-channel tiles alone fill the SMs (no split-K) and K is long enough
-  // for the pipeline: half the tokens per CTA, token tiles a multiple of 32.
+  // CTA pairs only on request: half the tokens per CTA, token tiles a multiple of 32.  Measured
+  // on B200 they stream 1.5x fewer L2 -> SM bytes but run slower than single CTAs on the prefill
+  // shapes (2048 x 8192 x 8192: 2127 against 2271 TOPS, GEMM alone), so AUTO / TENSOR keep one
+  // CTA per 128-channel tile.
   const int pair_units = ((r.tiles_n + 1) / 2) * r.tiles_t;
-  if (force_pair || (T >= 256 && r.k_iters >= 8 && 2 * pair_units >= sm_count)) {
+  if (force_pair) {
     r.pair = 1;
     r.BT = (per + 31) / 32 * 32;
     r.splits = 1;
