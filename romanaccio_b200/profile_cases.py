@@ -1,13 +1,14 @@
 """Small, self-contained launches of one kernel each, sized for an ncu capture.
 
     python -m romanaccio_b200.profile_cases chain --layers 4 --vocab 1024 --reps 5
-    python -m romanaccio_b200.profile_cases gemm 2048 8192 8192 --reps 3
+    python -m romanaccio_b200.profile_cases gemm 2048 8192 8192 --reps 3 [--pair]
     python -m romanaccio_b200.profile_cases lmhead 151936 --shards 1 --reps 3
 
 chain   the persistent decode-chain kernel over a Qwen2.5-1.5B-shaped stack of `layers` layers
         and a `vocab`-row LM head (T = 1), launched `reps` times;
 gemm    the tcgen05 tensor-core GEMM of an M x K x N W8A8 linear (int8 input in HBM, int8
-        requantised output), launched `reps` times after one tile-building launch;
+        requantised output), launched `reps` times after one tile-building launch (--pair: the
+        CTA-pair kernel, PATH_TENSOR_PAIR);
 lmhead  the LM-head top-40 GEMV over one shard of a 1536 x `vocab` head (T = 1).
 
 Every case checks the context's device error word at the end (a bounded wait that ran out
@@ -21,6 +22,7 @@ import numpy as np
 import torch
 
 from . import OUT_F32_ACC, OUT_QUANT, PATH_TENSOR, Context, SubgraphScaleInfo, W8A8Linear
+from ._lib import PATH_TENSOR_PAIR
 from . import DTYPE_INT8, synth
 
 
@@ -42,9 +44,9 @@ def run_chain(ctx: Context, layers: int, vocab: int, reps: int) -> None:
         stack.chain.forward()
 
 
-def run_gemm(ctx: Context, M: int, K: int, N: int, reps: int) -> None:
+def run_gemm(ctx: Context, M: int, K: int, N: int, reps: int, pair: bool = False) -> None:
     lin = _random_linear(ctx, K, N)
-    lin.set_path(PATH_TENSOR)
+    lin.set_path(PATH_TENSOR_PAIR if pair else PATH_TENSOR)
     q = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
     y = torch.empty((M, N), dtype=torch.int8, device="cuda")
     for _ in range(reps):
@@ -72,6 +74,7 @@ def main() -> None:
     g.add_argument("K", type=int)
     g.add_argument("N", type=int)
     g.add_argument("--reps", type=int, default=3)
+    g.add_argument("--pair", action="store_true")
     h = sub.add_parser("lmhead")
     h.add_argument("vocab", type=int)
     h.add_argument("--shards", type=int, default=1)
@@ -81,7 +84,7 @@ def main() -> None:
     if args.case == "chain":
         run_chain(ctx, args.layers, args.vocab, args.reps)
     elif args.case == "gemm":
-        run_gemm(ctx, args.M, args.K, args.N, args.reps)
+        run_gemm(ctx, args.M, args.K, args.N, args.reps, args.pair)
     else:
         run_lmhead(ctx, args.vocab, args.shards, args.reps)
     torch.cuda.synchronize()
