@@ -179,6 +179,80 @@ __global__ void __launch_bounds__(kActThreads) act_quant_kernel(const ActArgs a)
   if (a.pub_seq) publish_arrive(a);
 }
 
+// Dyntok quantisation with the token row held in registers (NV float4 of x, and of the
+// smoothing factors, per thread): every load of the row is issued at once and x is read once
+// from memory (act_quant_kernel reads it twice).  The same arithmetic, association and NaN rule
+// as act_quant_kernel<true, SMOOTH, true>; for rows of K <= 4 * kActThreads * NV, no publication.
+template <bool SMOOTH, int NV>
+__global__ void __launch_bounds__(kActThreads) act_quant_dyn_rows_kernel(const ActArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const float4 *x4 = reinterpret_cast<const float4 *>(a.x + t * a.ldx);
+  const float4 *s4 = reinterpret_cast<const float4 *>(a.s);
+  const int n4 = a.K / 4;
+  float4 v[NV], sv[NV];
+#pragma unroll
+  for (int u = 0; u < NV; ++u) {
+    const int c = threadIdx.x + u * kActThreads;
+    v[u] = c < n4 ? x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (SMOOTH) sv[u] = c < n4 ? s4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __shared__ float s_part[kActThreads / 32];
+  float amax = 0.0f;
+#pragma unroll
+  for (int u = 0; u < NV; ++u) {
+    float4 m = v[u];
+    if (SMOOTH) {
+      m.x = v[u].x * sv[u].x; m.y = v[u].y * sv[u].y; m.z = v[u].z * sv[u].z; m.w = v[u].w * sv[u].w;
+    }
+    const float ax = fabsf(m.x), ay = fabsf(m.y), az = fabsf(m.z), aw = fabsf(m.w);
+    if (ax > amax) amax = ax;
+    if (ay > amax) amax = ay;
+    if (az > amax) amax = az;
+    if (aw > amax) amax = aw;
+  }
+  amax = warp_amax(amax);
+  if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kActThreads / 32; ++w) amax = s_part[w] > amax ? s_part[w] : amax;
+  amax = (amax < 1e-8f) ? 1e-8f : amax;
+  if (threadIdx.x == 0) a.ratio[t] = amax / a.safe_thresh;
+  const float inv = 127.0f / amax;
+  char4 *q4 = reinterpret_cast<char4 *>(a.q + t * a.ldq);
+#pragma unroll
+  for (int u = 0; u < NV; ++u) {
+    const int c = threadIdx.x + u * kActThreads;
+    if (c >= n4) break;
+    char4 o;
+    if (SMOOTH) {
+      o.x = static_cast<signed char>(round_clamp(v[u].x * (sv[u].x * inv), 127.0f));
+      o.y = static_cast<signed char>(round_clamp(v[u].y * (sv[u].y * inv), 127.0f));
+      o.z = static_cast<signed char>(round_clamp(v[u].z * (sv[u].z * inv), 127.0f));
+      o.w = static_cast<signed char>(round_clamp(v[u].w * (sv[u].w * inv), 127.0f));
+    } else {
+      o.x = static_cast<signed char>(round_clamp(v[u].x * inv, 127.0f));
+      o.y = static_cast<signed char>(round_clamp(v[u].y * inv, 127.0f));
+      o.z = static_cast<signed char>(round_clamp(v[u].z * inv, 127.0f));
+      o.w = static_cast<signed char>(round_clamp(v[u].w * inv, 127.0f));
+    }
+    q4[c] = o;
+  }
+  int8_t *q = a.q + t * a.ldq;
+  for (int c = a.K + threadIdx.x; c < a.k_fill; c += kActThreads) q[c] = 0;
+}
+
+template <bool SMOOTH>
+cudaError_t act_dyn_rows(const ActArgs &a, int T, int n4, cudaStream_t st, bool pdl) {
+  const dim3 g(T), b(kActThreads);
+  if (n4 <= 1 * kActThreads) return launch_ex(act_quant_dyn_rows_kernel<SMOOTH, 1>, g, b, 0, st, pdl, a);
+  if (n4 <= 2 * kActThreads) return launch_ex(act_quant_dyn_rows_kernel<SMOOTH, 2>, g, b, 0, st, pdl, a);
+  if (n4 <= 4 * kActThreads) return launch_ex(act_quant_dyn_rows_kernel<SMOOTH, 4>, g, b, 0, st, pdl, a);
+  return launch_ex(act_quant_dyn_rows_kernel<SMOOTH, 8>, g, b, 0, st, pdl, a);
+}
+
 template <bool DYN, bool SMOOTH>
 cudaError_t act_dispatch_vec(const ActArgs &a, int T, bool vec, cudaStream_t st, bool pdl) {
   if (vec) return launch_ex(act_quant_kernel<DYN, SMOOTH, true>, dim3(T), dim3(kActThreads), 0, st, pdl, a);
@@ -289,6 +363,9 @@ cudaError_t launch_act_quant(const ActQuantLaunch &L, cudaStream_t st) {
   }
   const bool dyn = L.act_mode == kActDyntok;
   const bool sm = L.inv_smooth != nullptr;
+  // register-resident rows: vector layout, K <= 8192, no publication to other devices
+  if (dyn && vec && L.n_peers == 0 && !L.pub_seq && L.K / 4 <= 8 * kActThreads)
+    return sm ? act_dyn_rows<true>(a, L.T, L.K / 4, st, L.pdl) : act_dyn_rows<false>(a, L.T, L.K / 4, st, L.pdl);
   if (dyn && sm) return act_dispatch_vec<true, true>(a, L.T, vec, st, L.pdl);
   if (dyn) return act_dispatch_vec<true, false>(a, L.T, vec, st, L.pdl);
   if (sm) return act_dispatch_vec<false, true>(a, L.T, vec, st, L.pdl);
