@@ -549,7 +549,7 @@ __device__ void topk_finish(const ChainOp &op, const ChainArgs &a, int tb, int t
     return static_cast<int>(((tile + 1u) * G + num_tiles - 1u) / num_tiles - 1u);
   };
   for (int t = 0; t < a.T; ++t)
-    grid_topk_select<R, kCW>(k, t, st, op.tk.val + t * k, op.tk.idx + t * k, stage, gather, &s_n, warp, lane,
+    grid_topk_select<R, kCW>(static_cast<int>(gridDim.x), k, t, st, op.tk.val + t * k, op.tk.idx + t * k, stage, gather, &s_n, warp, lane,
                              sync, list_of);
   if (tid == 0) *st.arrive = 0u;
 }

@@ -50,6 +50,7 @@ struct GemvArgs {
   ShardSync sync;
   FusedQuant fq;
   uint32_t xres_off;  // fused quantisation: resident [TT][k_pad] int8 slab
+  int split_select;   // top-k of several tokens: the selection runs in topk_select_kernel
 };
 
 // A shard on another device than GPU 0 waits at most this long for GPU 0 to store its
@@ -233,6 +234,14 @@ __device__ void topk_epilogue(const GemvArgs &a, const GridTopkState &st, const 
     if (threadIdx.x == 0) stamp(a, 7);
     return;
   }
+  if (a.split_select) {
+    // every token's lists are written: the selection kernel (one CTA per token) takes over
+    if (threadIdx.x == 0) {
+      *st.arrive = 0u;
+      stamp(a, 7);
+    }
+    return;
+  }
   __shared__ int s_n;
   uint64_t *gather = stage + NW * 64;
   // CTA b owns rows [b * rows_per_cta, (b + 1) * rows_per_cta) of the shard
@@ -250,7 +259,7 @@ __device__ void topk_epilogue(const GemvArgs &a, const GridTopkState &st, const 
       vr = a.tk.val_dst[g / a.tk.dst_tokens] + off;
       ir = a.tk.idx_dst[g / a.tk.dst_tokens] + off;
     }
-    grid_topk_select<R, NW>(a.tk.k, t, st, vr, ir, stage, gather, &s_n, warp, lane, BlockSync{},
+    grid_topk_select<R, NW>(static_cast<int>(gridDim.x), a.tk.k, t, st, vr, ir, stage, gather, &s_n, warp, lane, BlockSync{},
                             list_of);
   }
   if ((a.sync.done || a.sync.done_peers) && !a.sync.hold) {
@@ -588,6 +597,70 @@ bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan
   return true;
 }
 
+namespace {
+
+// The grid top-k selection of a multi-token GEMV, one CTA per token (tokens in parallel instead
+// of one after another in the GEMV's last CTA): token blockIdx.x's top-k over the G per-CTA lists
+// the GEMV wrote, into its output rows (or its owner's gather rows); then, in the last selection
+// CTA to finish, the same publication as the GEMV's last CTA (system-scope fence, forward count,
+// done counters).  The GEMV left st.arrive at zero; it counts the selection CTAs here and the
+// last one re-zeroes it.
+struct SelectArgs {
+  GridTopkState st;
+  int G, k, T, rows_per_cta;
+  TopK tk;
+  ShardSync sync;
+};
+
+constexpr int kSelectWarps = 8;
+constexpr uint32_t kSelectSmemBytes = (kSelectWarps * 64 + kTopkGatherKeys) * 8;
+
+template <int R>
+__global__ void __launch_bounds__(kSelectWarps * 32) topk_select_kernel(const SelectArgs a) {
+  extern __shared__ __align__(16) uint64_t sel_smem[];
+  __shared__ int s_n, s_last;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x;
+  uint64_t *stage = sel_smem;
+  uint64_t *gather = sel_smem + kSelectWarps * 64;
+  const int row_offset = a.tk.row_offset, rows_per_cta = a.rows_per_cta;
+  auto list_of = [row_offset, rows_per_cta](uint64_t key) {
+    return (topk_key_id(key) - row_offset) / rows_per_cta;
+  };
+  float *vr = a.tk.val + t * a.tk.k;
+  int32_t *ir = a.tk.idx + t * a.tk.k;
+  if (a.tk.val_dst) {
+    const int g = a.tk.tok0 + t;
+    const int64_t off = a.tk.dst_row0 + static_cast<int64_t>(g % a.tk.dst_tokens) * a.tk.dst_ld;
+    vr = a.tk.val_dst[g / a.tk.dst_tokens] + off;
+    ir = a.tk.idx_dst[g / a.tk.dst_tokens] + off;
+  }
+  grid_topk_select<R, kSelectWarps>(a.G, a.k, t, a.st, vr, ir, stage, gather, &s_n, warp, lane,
+                                    BlockSync{}, list_of);
+  const bool publish = (a.sync.done || a.sync.done_peers) && !a.sync.hold;
+  if (publish) __threadfence_system();
+  else __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    s_last = atomicAdd(a.st.arrive, 1u) == gridDim.x - 1;
+    if (s_last) {
+      *a.st.arrive = 0u;
+      if (publish) {
+        // every token's rows are stored: count the forward (a release of the rows)
+        __threadfence_system();
+        const unsigned e = *a.sync.seq + 1u;
+        *a.sync.seq = e;
+        if (a.sync.done) st_relaxed_sys(a.sync.done, e);
+        for (int p = 0; p < a.sync.n_done; ++p) st_relaxed_sys(a.sync.done_peers[p], e);
+      }
+    }
+  }
+}
+
+}  // namespace
+
 cudaError_t launch_gemv(const GemvLaunch &L, const GemvPlan &plan, cudaStream_t stream) {
   GemvArgs a;
   a.w = L.w;
@@ -614,12 +687,30 @@ cudaError_t launch_gemv(const GemvLaunch &L, const GemvPlan &plan, cudaStream_t 
   a.fq = L.fq;
   a.xres_off = plan.xres_off;
   if ((L.fq.x != nullptr) != plan.fused_x) return cudaErrorInvalidValue;
+  // several tokens: their selections run in parallel in a kernel of their own
+  a.split_select = (L.topk && L.T >= 2) ? 1 : 0;
+  cudaError_t e;
   switch (plan.tt) {
-    case 1: return dispatch_rpw<1>(a, plan, stream, L.pdl, L.topk);
-    case 2: return dispatch_rpw<2>(a, plan, stream, L.pdl, L.topk);
-    case 4: return dispatch_rpw<4>(a, plan, stream, L.pdl, L.topk);
-    default: return dispatch_rpw<8>(a, plan, stream, L.pdl, L.topk);
+    case 1: e = dispatch_rpw<1>(a, plan, stream, L.pdl, L.topk); break;
+    case 2: e = dispatch_rpw<2>(a, plan, stream, L.pdl, L.topk); break;
+    case 4: e = dispatch_rpw<4>(a, plan, stream, L.pdl, L.topk); break;
+    default: e = dispatch_rpw<8>(a, plan, stream, L.pdl, L.topk); break;
   }
+  if (e != cudaSuccess || !a.split_select) return e;
+  SelectArgs sa;
+  sa.st = GridTopkState{L.tk.counter, L.tk.lists};
+  sa.G = plan.grid;
+  sa.k = L.tk.k;
+  sa.T = L.T;
+  sa.rows_per_cta = plan.tiles_per_cta * plan.rb;
+  sa.tk = L.tk;
+  sa.sync = L.sync;
+  static_assert(kSelectSmemBytes <= 48 * 1024, "within the default dynamic shared memory");
+  if (L.tk.k > 32)
+    return launch_ex(topk_select_kernel<2>, dim3(L.T), dim3(kSelectWarps * 32), kSelectSmemBytes,
+                     stream, true, sa);
+  return launch_ex(topk_select_kernel<1>, dim3(L.T), dim3(kSelectWarps * 32), kSelectSmemBytes,
+                   stream, true, sa);
 }
 
 }  // namespace w8a8

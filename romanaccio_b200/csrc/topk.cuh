@@ -162,16 +162,16 @@ __device__ bool grid_topk_arrive(const GridTopkState &st, int tid, int *s_flag, 
   return last;
 }
 
-// Last CTA: token t's top-k into val_row[0 .. k) / idx_row[0 .. k) (the token's output rows).
-// NW * 32 threads (tid < NW * 32) take part;
+// Last CTA (or a selection CTA of its own): token t's top-k over the G lists of the grid into
+// val_row[0 .. k) / idx_row[0 .. k) (the token's output rows).  NW * 32 threads (tid < NW * 32)
+// take part;
 // `stage` holds NW * 32R keys and `gather` kTopkGatherKeys keys of shared memory; s_int is one
 // shared int.  list_of(key) gives the index of the CTA (list) that owns a key's vocab row.
 // Returns after a sync() over the NW warps.
 template <int R, int NW, typename Sync, typename ListOf>
-__device__ void grid_topk_select(int k, int t, const GridTopkState &st, float *val_row, int32_t *idx_row,
-                                 uint64_t *stage, uint64_t *gather, int *s_int, int warp, int lane,
-                                 Sync sync, ListOf list_of) {
-  const int G = gridDim.x;
+__device__ void grid_topk_select(int G, int k, int t, const GridTopkState &st, float *val_row,
+                                 int32_t *idx_row, uint64_t *stage, uint64_t *gather, int *s_int,
+                                 int warp, int lane, Sync sync, ListOf list_of) {
   const uint64_t *base = st.keys + t * grid_topk_stride(G, k);
   const uint64_t *heads = base + static_cast<size_t>(G) * k;
   // the k largest heads; T0 = the k-th (0 when fewer than k lists are non-empty)
