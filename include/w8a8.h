@@ -360,7 +360,7 @@ w8a8_status w8a8_moe_views(const w8a8_moe *moe, const int32_t **idx_dev, const f
  * tokens' lists.  The exchange is done by this library: peer stores into CUDA-IPC-mapped device
  * memory with counters that only grow, each device-side wait bounded (1 to 2 s, then
  * W8A8_ERR_PEER_TIMEOUT through w8a8_ctx_check) -- no NCCL call and no host round trip, so a
- * forward (three launches on `stream`) can be captured in a CUDA graph.
+ * forward (three launches on `stream`, four when world * T >= 2) can be captured in a CUDA graph.
  *
  * Set-up: every rank calls w8a8_lmhead_rank_create, then w8a8_lmhead_rank_export (64 bytes),
  * the caller exchanges the handles between the processes by any means (they are plain bytes),

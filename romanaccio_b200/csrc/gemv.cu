@@ -224,9 +224,40 @@ __device__ void topk_epilogue(const GemvArgs &a, const GridTopkState &st, const 
                               int rows_here, int rows_per_cta, uint64_t *stage, int *s_last) {
   constexpr int NW = kConsumerWarps + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = 0; t < a.T; ++t)
-    grid_topk_offer<R, NW>(cand + t * a.cand_cap, rows_here, a.tk.k, t, st, stage, warp, lane,
-                           BlockSync{});
+  if (a.T > 1) {
+    // one warp per token: the warps fold different tokens' candidates at once (sort each chunk
+    // of 32R keys, merge it into the running list), where grid_topk_offer would run the tokens
+    // one after another with most warps idle on a CTA's few chunks
+    for (int t = warp; t < a.T; t += NW) {
+      uint64_t v[R];
+      for (int c = 0; c < rows_here; c += 32 * R) {
+        uint64_t b[R];
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+          const int i = c + lane + 32 * j;
+          b[j] = i < rows_here ? cand[t * a.cand_cap + i] : 0ull;
+        }
+        warp_sort_desc<R>(b, lane);
+        if (c == 0) {
+#pragma unroll
+          for (int j = 0; j < R; ++j) v[j] = b[j];
+        } else {
+          warp_merge_desc<R>(v, b, lane);
+        }
+      }
+      uint64_t *base = st.keys + t * grid_topk_stride(gridDim.x, a.tk.k);
+      uint64_t *list = base + static_cast<size_t>(blockIdx.x) * a.tk.k;
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (lane + 32 * j < a.tk.k) list[lane + 32 * j] = v[j];
+      if (lane == 0) base[static_cast<size_t>(gridDim.x) * a.tk.k + blockIdx.x] = v[0];
+    }
+    __syncthreads();
+  } else {
+    for (int t = 0; t < a.T; ++t)
+      grid_topk_offer<R, NW>(cand + t * a.cand_cap, rows_here, a.tk.k, t, st, stage, warp, lane,
+                             BlockSync{});
+  }
   if (threadIdx.x == 0) stamp(a, 4);
   const bool last = grid_topk_arrive(st, threadIdx.x, s_last, BlockSync{});
   if (threadIdx.x == 0) stamp(a, 5);

@@ -353,8 +353,9 @@ w8a8_status w8a8_lmhead_set_trace(w8a8_lmhead *lm, unsigned long long *head_trac
 // ---------------------------------------------------------------------------------------
 // One rank of a vocab-sharded LM head over processes (w8a8_lmhead_rank_*): one process per GPU,
 // the exchange done by this library with peer stores into CUDA-IPC-mapped device memory and
-// counters in device memory, so a rank's whole forward is three stream-ordered launches that a
-// CUDA graph can hold (no NCCL call, no host round trip, no cross-process stream event).
+// counters in device memory, so a rank's whole forward is three (with two or more tokens in all,
+// four) stream-ordered launches that a CUDA graph can hold (no NCCL call, no host round trip, no
+// cross-process stream event).
 //
 // Every rank exports one arena of its device memory:
 //   x_ready[64]  counters: x_ready[p] = forwards whose int8 rows rank p stored here

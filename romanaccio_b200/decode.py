@@ -233,9 +233,10 @@ class DecodeStack:
     def launches_per_step(self) -> int:
         """Kernels of this library launched per step."""
         T_all = self.T * self.world
-        # LM head: act_quant + top-k GEMV per group of 8 tokens (+ merge when sharded, + the
-        # argmax copy when not)
-        lm = 1 + (T_all + 7) // 8 + 1
+        # LM head: act_quant + top-k GEMV per group of 8 tokens, + the per-token selection kernel
+        # after a GEMV of two or more tokens (+ merge when sharded, + the argmax copy when not)
+        groups = [min(8, T_all - g) for g in range(0, T_all, 8)]
+        lm = 1 + len(groups) + sum(1 for g in groups if g >= 2) + 1
         if self.chain is not None:
             return 1 + (1 if self.chain_lm else lm)
         # each linear: act_quant + one tensor-core GEMM, or a GEMV per group of 8 tokens

@@ -219,7 +219,8 @@ class RankLmHead:
     """One rank's part of an LM head vocab-sharded over processes (w8a8_lmhead_rank_*): this
     rank's contiguous vocab rows; the exchange of activations and candidates between the ranks is
     done by the library (peer stores into CUDA-IPC-mapped device memory, device counters), so
-    forward() is three launches on one stream and can be captured in a CUDA graph.
+    forward() is three launches on one stream (four with two or more tokens over all ranks) and
+    can be captured in a CUDA graph.
 
     Set-up: create on every rank, exchange export() bytes (connect(handles) with the list of all
     ranks' handles in rank order), or connect_local(heads) for ranks driven by one process.
