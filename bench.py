@@ -567,8 +567,74 @@ def per_config_records(ctx, dev, headline, args, peak: float) -> dict:
     guarded("c2_prefill_sweep", lambda: prefill_record(ctx, dev, steps, warmup, flush))
     guarded("c3_moe_v2lite", lambda: moe_record(ctx, dev, steps, warmup, peak, flush))
     guarded("c4_gemma_t1", c4)
+    guarded("lmhead_sharded", lambda: sharded_head_record(1, steps, warmup))
     recs["all_parity"] = all(r.get("parity", False) for k, r in recs.items() if isinstance(r, dict))
     return recs
+
+
+# ------------------------------------------------------------- sharded LM head (strong scaling)
+def sharded_head_record(n: int, steps: int, warmup: int) -> dict:
+    """One token's Qwen2.5-1.5B LM head (1536 x 151936, top-40 + argmax) vocab-sharded over GPUs
+    0 .. n-1 by this one process (w8a8_lmhead_*): the reference's dual-die LM-head split, every
+    shard streaming V / n rows of the same token.  Latency: CUDA events on GPU 0 from "h ready"
+    (after a ~100 us GPU delay standing in for the layers, during which the host issues the
+    forward) to the argmax ids in pinned host memory; e2e: the same with GPU 0 idle before it (the
+    host's launches on the clock).  L2 flushed on every GPU before every step.  Parity: top-40 ids
+    and values and the argmax against the oracle's head on the same weights and input."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    from romanaccio_b200 import Context, MultiDeviceLmHead, synth
+    K, V, k, T = synth.QWEN25_15B.hidden, synth.QWEN25_15B.vocab, 40, 1
+    rng = np.random.default_rng(17)
+    wq = rng.integers(-127, 128, size=(V, K), dtype=np.int16).astype(np.int8)
+    w_step = (rng.random(V) * 0.02 / 127 + 1e-5)
+    in_step = float(synth.activations(64, K, 23).abs().max()) / 127.0
+    acc_step = (in_step * w_step).astype(np.float32)
+    h_host = synth.activations(T, K, seed=5)
+    ctxs = [Context(d) for d in range(n)]
+    torch.cuda.set_device(0)
+    h = h_host.cuda()
+    ids_host = torch.empty((T,), dtype=torch.int32).pin_memory()
+    flush = [torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{d}") for d in range(n)]
+    stream = torch.cuda.current_stream()
+    lm = MultiDeviceLmHead(ctxs, wq, acc_step, in_step, max_tokens=8, k_max=k)
+    val = torch.empty((T, k), dtype=torch.float32, device="cuda")
+    idx = torch.empty((T, k), dtype=torch.int32, device="cuda")
+
+    def step(delay: bool) -> float:
+        for f in flush:
+            f.fill_(1)
+        if delay:
+            torch.cuda._sleep(200_000)  # ~100 us at 1.9 GHz
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        lm.forward(h, k, val, idx, ids_host)
+        b.record(stream)
+        b.synchronize()
+        return a.elapsed_time(b) * 1e3
+
+    for _ in range(warmup):
+        step(True)
+    lat = [step(True) for _ in range(steps)]
+    e2e = [step(False) for _ in range(steps)]
+    for d in range(n):
+        torch.cuda.synchronize(d)
+    for c in ctxs:
+        c.check()
+    q = O.pack_static(h_host.numpy(), in_step)
+    want_v, want_i = O.topk(O.dequant_acc(O.gemm_i32(q, wq), acc_step), k)
+    ids_ok = bool(np.array_equal(idx.cpu().numpy(), want_i))
+    vals_ok = bool(np.array_equal(val.cpu().numpy(), want_v))
+    arg_ok = bool(np.array_equal(ids_host.numpy(), want_i[:, 0]))
+    del lm, flush
+    return {"workload": f"LM head {K}x{V} top-{k} + argmax, one token, vocab-sharded over {n} GPU(s) "
+                        "(w8a8_lmhead_*, one process)",
+            "n_gpus": n, "steps": steps, "latency_us": round(statistics.median(lat), 2),
+            "latency_us_min": round(min(lat), 2), "e2e_us": round(statistics.median(e2e), 2),
+            "bytes_per_gpu": (V // n) * K, "l2": "256 MB written on every GPU before every step",
+            "parity": ids_ok and vals_ok and arg_ok,
+            "parity_detail": {"topk_ids_equal": ids_ok, "topk_values_equal": vals_ok,
+                              "argmax_equal": arg_ok}}
 
 
 # ---------------------------------------------------------------------------- GPU path
@@ -770,7 +836,27 @@ def run_ours(args) -> None:
     if world > 1 and not args.no_per_config:
         # every rank takes part in the expert-parallel layer; rank 0 reports it
         rec = moe_ep_record(ctx, dev, rank, world, args.config_steps, 3, peak)
-        per_config = {"c3_moe_v2lite_ep": rec, "all_parity": rec["parity"]}
+        per_config = {"c3_moe_v2lite_ep": rec}
+        # one token's LM head over all N GPUs (strong scaling): rank 0 drives every GPU while the
+        # other ranks wait at a host (gloo) barrier, launching nothing
+        import torch.distributed as dist
+        cpu_group = dist.new_group(backend="gloo")
+        torch.cuda.synchronize()
+        dist.barrier(group=cpu_group)
+        if rank == 0:
+            t0 = time.perf_counter()
+            try:
+                rec = sharded_head_record(world, args.config_steps, 3)
+            except Exception as e:  # reported, not hidden
+                rec = {"error": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}",
+                       "parity": False}
+            rec["wall_s"] = round(time.perf_counter() - t0, 1)
+            per_config["lmhead_sharded"] = rec
+            torch.cuda.set_device(local)
+        dist.barrier(group=cpu_group)
+        if per_config is not None:
+            per_config["all_parity"] = all(r.get("parity", False) for r in per_config.values()
+                                           if isinstance(r, dict))
 
     step_bytes = sb.linear + sb.lm_head
     value = world * T / (ms / 1e3)
