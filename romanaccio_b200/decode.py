@@ -197,7 +197,10 @@ class DecodeStack:
         self.chain_lm = False  # the chain's last step is the (unsharded) LM head
         self.chain = None
         if use_chain and self.T <= 8:
-            if self.world == 1:
+            # one token: the LM head is the chain's last step; several tokens: it runs after the
+            # chain, where each token's top-k selection has a CTA of its own (T = 8: 2.35 against
+            # 2.42 ms per step with the head inside)
+            if self.world == 1 and self.T == 1:
                 try:
                     self.chain = self._build_chain(with_lm=True)
                     self.chain_lm = True

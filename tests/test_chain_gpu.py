@@ -55,6 +55,27 @@ def test_chain_matches_per_linear_path(ctx, shape, T, layers, vocab):
     ctx.check()
 
 
+@pytest.mark.parametrize("shape,T,vocab", [(synth.SMOLLM_135M, 3, 8192), (synth.QWEN25_15B, 8, 20000)])
+def test_chain_lm_step_with_several_tokens(ctx, shape, T, vocab):
+    """The LM head as the chain's last step with several tokens (the decode stack runs it after
+    the chain for T > 1, but the chain supports it): same top-k as the separate head."""
+    st = DecodeStack(ctx, shape, T, layers=1, lm_vocab=vocab, use_chain=True, seed=4)
+    assert not st.chain_lm
+    st.x.copy_(synth.activations(T, shape.hidden, seed=6).to(st.dev))
+    st.run_device()
+    torch.cuda.synchronize()
+    want_val, want_idx = st.top_val.clone(), st.top_idx.clone()
+    chain = st._build_chain(with_lm=True)
+    st.top_val.zero_()
+    st.top_idx.zero_()
+    chain.forward()
+    torch.cuda.synchronize()
+    assert torch.equal(st.top_idx, want_idx)
+    assert torch.equal(st.top_val, want_val)
+    chain.close()
+    ctx.check()
+
+
 def test_chain_oracle_chain_bit_exact(ctx):
     """Two dependent linears with requant outputs checked step by step against the oracle."""
     T = 2
