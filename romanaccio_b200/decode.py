@@ -318,11 +318,36 @@ class DecodeStack:
         else:
             self.run_device()
 
+    def capture_host(self, x_host: torch.Tensor, ids_host: torch.Tensor) -> None:
+        """Captures the end-to-end step for these pinned host buffers as one CUDA graph: the
+        host -> device copy of the activations, the whole step and the device -> host copy of the
+        sampled ids (both copies run on every replay)."""
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            self.x.copy_(x_host, non_blocking=True)
+            self.run_device()
+            ids_host.copy_(self.ids, non_blocking=True)
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        torch.cuda.synchronize(self.dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.x.copy_(x_host, non_blocking=True)
+            self.run_device()
+            ids_host.copy_(self.ids, non_blocking=True)
+        self.host_graph = (g, x_host, ids_host)
+
     def step_host(self, x_host: torch.Tensor, ids_host: torch.Tensor) -> None:
-        """End-to-end step through the public API: pinned host activations in, sampled ids out."""
+        """End-to-end step through the public API: pinned host activations in, sampled ids out
+        (one graph replay when capture_host was called for these buffers)."""
+        hg = getattr(self, "host_graph", None)
+        if hg is not None and hg[1] is x_host and hg[2] is ids_host:
+            hg[0].replay()
+            return
         self.x.copy_(x_host, non_blocking=True)
         self.step()
         ids_host.copy_(self.ids, non_blocking=True)
 
     def release(self) -> None:
         self.graph = None
+        self.host_graph = None
