@@ -87,6 +87,12 @@ struct w8a8_linear {
   uint64_t *lists = nullptr;    // top-k per-CTA candidate lists
   size_t lists_keys = 0;
   unsigned *counter = nullptr;
+  // 16+ token top-k: logits (when the caller passes none) and per-CTA row lists, grown on use
+  // (kept apart from `lists`, whose address a built decode chain holds)
+  float *logit_ws = nullptr;    // [T, N]
+  size_t logit_ws_elems = 0;
+  uint64_t *row_lists = nullptr;
+  size_t row_lists_keys = 0;
   // tensor-core path: tile-ordered weights, split-K partial planes, per-tile arrival counters
   int path = W8A8_PATH_AUTO;
   int8_t *w_tiles = nullptr;    // weights in tensor-core tile order (built on first use)
@@ -137,6 +143,8 @@ void linear_free(w8a8_linear *l) {
   cudaFree(l->ratio);
   cudaFree(l->lists);
   cudaFree(l->counter);
+  cudaFree(l->logit_ws);
+  cudaFree(l->row_lists);
   cudaFree(l->w_tiles);
   cudaFree(l->tc_ws);
   cudaFree(l->tc_count);
@@ -177,6 +185,19 @@ w8a8_status ensure_tc_scratch(w8a8_linear *l, size_t ws_elems, size_t count_n) {
     W8A8_CUDA(cudaMemset(l->tc_count, 0, count_n * sizeof(unsigned)));
     l->tc_count_n = count_n;
   }
+  return W8A8_SUCCESS;
+}
+
+// Grows a device scratch array to at least `need` elements (the old contents are dropped).
+template <typename E>
+w8a8_status grow_scratch(E **p, size_t *have, size_t need) {
+  if (need <= *have) return W8A8_SUCCESS;
+  cudaFree(*p);
+  *p = nullptr;
+  *have = 0;
+  w8a8_status st = dev_alloc(p, need, nullptr);
+  if (st != W8A8_SUCCESS) return st;
+  *have = need;
   return W8A8_SUCCESS;
 }
 
@@ -335,6 +356,10 @@ bool linear_can_fuse(const w8a8_linear *l, int T, int act_mode, FusedQuant *fq) 
   return true;
 }
 
+bool topk_on_tensor_cores(const w8a8_linear *l, int T) {
+  return T >= W8A8_TC_MIN_TOKENS && l->path != W8A8_PATH_GEMV;
+}
+
 w8a8_status linear_topk_quantized(w8a8_linear *l, int T, int act_mode, int out_mode, int k,
                                   int row_offset, float *topk_val, int32_t *topk_idx,
                                   float *logits, int64_t ldl, const ShardSync &sync, bool pdl,
@@ -343,6 +368,35 @@ w8a8_status linear_topk_quantized(w8a8_linear *l, int T, int act_mode, int out_m
   if (((sync.seq && sync.n_ready == 0) || (fq && fq->pub_seq)) && T > 8)
     return fail(W8A8_ERR_INVALID_ARG, "a multi-device LM head takes at most 8 tokens a forward");
   const bool fused = fq && fq->x;
+  if (topk_on_tensor_cores(l, T) && !fused && !route && !sync.seq && !sync.done &&
+      !sync.done_peers) {
+    // 16+ tokens: one tensor-core GEMM writes the logits (the weights stream once), then the
+    // per-CTA row lists and the per-token selection
+    float *lg = logits;
+    int64_t ld = ldl;
+    if (!lg) {
+      w8a8_status st = grow_scratch(&l->logit_ws, &l->logit_ws_elems,
+                                    static_cast<size_t>(T) * l->N);
+      if (st != W8A8_SUCCESS) return st;
+      lg = l->logit_ws;
+      ld = l->N;
+    }
+    w8a8_status st = grow_scratch(&l->row_lists, &l->row_lists_keys,
+                                  static_cast<size_t>(T) * topk_rows_grid(l->N) * (k + 1));
+    if (st != W8A8_SUCCESS) return st;
+    st = run_gemv(l, x_rows ? x_rows : l->xq, l->k_pad, T, act_mode, l->ratio, out_mode, lg, ld,
+                  pdl, s);
+    if (st != W8A8_SUCCESS) return st;
+    TopK tk = {};
+    tk.k = k;
+    tk.row_offset = row_offset;
+    tk.lists = l->row_lists;
+    tk.counter = l->counter;
+    tk.val = topk_val;
+    tk.idx = topk_idx;
+    W8A8_CUDA(launch_topk_rows(lg, ld, T, l->N, tk, true, s));
+    return W8A8_SUCCESS;
+  }
   for (int t0 = 0; t0 < T; t0 += 8) {
     const int tg = std::min(8, T - t0);
     GemvPlan plan;
@@ -741,7 +795,7 @@ w8a8_status w8a8_linear_forward_topk(w8a8_linear *l, const float *x, int64_t ldx
                                        topk_idx, logits, ldl, w8a8::ShardSync{}, true, s);
   }
   w8a8::FusedQuant fq;
-  if (w8a8::linear_can_fuse(l, T, act_mode, &fq)) {
+  if (!w8a8::topk_on_tensor_cores(l, T) && w8a8::linear_can_fuse(l, T, act_mode, &fq)) {
     // static quantisation runs in the GEMV prologue: one launch per 8 tokens
     fq.x = x;
     fq.ldx = ldx;

@@ -690,7 +690,98 @@ __global__ void __launch_bounds__(kSelectWarps * 32) topk_select_kernel(const Se
   }
 }
 
+// One CTA's share of a token's grid top-k over kTopkRowsPerCta rows of fp32 logits (16 per
+// thread, coalesced loads).  A key can be among the CTA's k largest only if it reaches T0, the
+// k-th largest of the 256 threads' maxima (k distinct threads each hold a key >= T0), so only the
+// keys >= T0 are gathered and sorted: on random logits about k + a few of the 4096.  Ties cannot
+// defeat the bound (keys are unique: the vocab id is part of the key); adversarial logits only
+// gather more keys, up to all of them.
+constexpr int kRowsPerThread = kTopkRowsPerCta / (kSelectWarps * 32);
+constexpr uint32_t kRowsOfferSmemBytes = (kSelectWarps * 64 + kTopkRowsPerCta) * 8;
+
+struct RowsOfferArgs {
+  const float *logits;
+  int64_t ldl;
+  int N, k, row_offset;
+  GridTopkState st;
+};
+
+template <int R>
+__global__ void __launch_bounds__(kSelectWarps * 32) topk_rows_offer_kernel(const RowsOfferArgs a) {
+  extern __shared__ __align__(16) uint64_t offer_smem[];
+  __shared__ int s_n;
+  uint64_t *stage = offer_smem;                     // kSelectWarps * 32R keys
+  uint64_t *pool = offer_smem + kSelectWarps * 64;  // the threads' maxima, then the survivors
+  pdl_launch_dependents();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int G = gridDim.x, b = blockIdx.x, t = blockIdx.y;
+  const int n0 = b * kTopkRowsPerCta;
+  const int rows = min(kTopkRowsPerCta, a.N - n0);
+  const float *row = a.logits + static_cast<size_t>(t) * a.ldl + n0;
+  uint64_t key[kRowsPerThread];
+  uint64_t m = 0ull;
+#pragma unroll
+  for (int j = 0; j < kRowsPerThread; ++j) {
+    const int i = tid + j * kSelectWarps * 32;
+    key[j] = i < rows ? topk_key(row[i], static_cast<uint32_t>(a.row_offset + n0 + i)) : 0ull;
+    m = max_u64(m, key[j]);
+  }
+  pool[tid] = m;
+  if (tid == 0) s_n = 0;
+  __syncthreads();
+  cta_top_keys<R, kSelectWarps>(pool, kSelectWarps * 32, false, stage, warp, lane, BlockSync{});
+  // 0 when fewer than k threads hold a row: every key survives
+  const uint64_t t0 = stage[a.k - 1];
+  // append the survivors to the pool (warp-aggregated slots)
+#pragma unroll
+  for (int j = 0; j < kRowsPerThread; ++j) {
+    const bool keep = key[j] != 0ull && key[j] >= t0;
+    const unsigned mask = __ballot_sync(0xFFFFFFFFu, keep);
+    if (mask) {
+      int slot = 0;
+      if (lane == 0) slot = atomicAdd(&s_n, __popc(mask));
+      slot = __shfl_sync(0xFFFFFFFFu, slot, 0);
+      if (keep) pool[slot + __popc(mask & ((1u << lane) - 1u))] = key[j];
+    }
+  }
+  __syncthreads();
+  cta_top_keys<R, kSelectWarps>(pool, s_n, false, stage, warp, lane, BlockSync{});
+  if (warp == 0) {
+    uint64_t *base = a.st.keys + t * grid_topk_stride(G, a.k);
+    uint64_t *list = base + static_cast<size_t>(b) * a.k;
+    for (int e = lane; e < a.k; e += 32) list[e] = stage[e];
+    if (lane == 0) base[static_cast<size_t>(G) * a.k + b] = stage[0];
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_topk_rows(const float *logits, int64_t ldl, int T, int N, const TopK &tk,
+                             bool pdl, cudaStream_t stream) {
+  const int G = topk_rows_grid(N);
+  const GridTopkState st{tk.counter, tk.lists};
+  const RowsOfferArgs oa{logits, ldl, N, tk.k, tk.row_offset, st};
+  static_assert(kRowsOfferSmemBytes <= 48 * 1024, "within the default dynamic shared memory");
+  cudaError_t e =
+      tk.k > 32 ? launch_ex(topk_rows_offer_kernel<2>, dim3(G, T), dim3(kSelectWarps * 32),
+                            kRowsOfferSmemBytes, stream, pdl, oa)
+                : launch_ex(topk_rows_offer_kernel<1>, dim3(G, T), dim3(kSelectWarps * 32),
+                            kRowsOfferSmemBytes, stream, pdl, oa);
+  if (e != cudaSuccess) return e;
+  SelectArgs sa = {};
+  sa.st = st;
+  sa.G = G;
+  sa.k = tk.k;
+  sa.T = T;
+  sa.rows_per_cta = kTopkRowsPerCta;
+  sa.tk = tk;
+  if (tk.k > 32)
+    return launch_ex(topk_select_kernel<2>, dim3(T), dim3(kSelectWarps * 32), kSelectSmemBytes,
+                     stream, true, sa);
+  return launch_ex(topk_select_kernel<1>, dim3(T), dim3(kSelectWarps * 32), kSelectSmemBytes,
+                   stream, true, sa);
+}
 
 cudaError_t launch_gemv(const GemvLaunch &L, const GemvPlan &plan, cudaStream_t stream) {
   GemvArgs a;

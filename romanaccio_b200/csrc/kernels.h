@@ -141,6 +141,17 @@ bool plan_gemv(int T, int N, int k_pad, bool topk, int k, int sm_count, GemvPlan
                bool fused_x = false);
 cudaError_t launch_gemv(const GemvLaunch &L, const GemvPlan &plan, cudaStream_t stream);
 
+// Top-k of fp32 logits already in memory ([T, ldl], N rows, vocab id tk.row_offset + n): the LM
+// head of 16+ tokens, whose logits come from one tensor-core GEMM that reads the weights once
+// (a GEMV top-k streams them again for every 8 tokens).  One CTA per (kTopkRowsPerCta rows,
+// token) writes its sorted k-list and head in the grid top-k layout (tk.lists, G =
+// topk_rows_grid(N) lists per token), then one selection CTA per token merges them into
+// tk.val / tk.idx.  Two launches; tk.counter must be zero and is left zero.
+constexpr int kTopkRowsPerCta = 4096;
+inline int topk_rows_grid(int N) { return (N + kTopkRowsPerCta - 1) / kTopkRowsPerCta; }
+cudaError_t launch_topk_rows(const float *logits, int64_t ldl, int T, int N, const TopK &tk,
+                             bool pdl, cudaStream_t stream);
+
 // Tensor-core (tcgen05 kind::i8) contraction for larger token counts.
 struct TcPlan {
   int BT;          // tokens per tile (multiple of 16, <= 256) = MMA N

@@ -37,6 +37,11 @@ w8a8_status linear_topk_quantized(w8a8_linear *l, int T, int act_mode, int out_m
                                   const int8_t *x_rows = nullptr,
                                   const TopkRoute *route = nullptr);
 
+// True when a top-k forward of T tokens runs as one tensor-core GEMM into fp32 logits followed by
+// the row top-k kernels (launch_topk_rows) rather than as GEMVs of 8 tokens.  That path is taken
+// only without ShardSync, FusedQuant and TopkRoute.
+bool topk_on_tensor_cores(const w8a8_linear *l, int T);
+
 // Whether T tokens of this linear can be quantised in the GEMV prologue (static activation
 // quantisation and a small enough resident slab); fills the linear's static parameters.
 bool linear_can_fuse(const w8a8_linear *l, int T, int act_mode, FusedQuant *fq);

@@ -240,6 +240,9 @@ class DecodeStack:
         # after a GEMV of two or more tokens (+ merge when sharded, + the argmax copy when not)
         groups = [min(8, T_all - g) for g in range(0, T_all, 8)]
         lm = 1 + len(groups) + sum(1 for g in groups if g >= 2) + 1
+        if self.world == 1 and self.T >= TC_MIN_TOKENS:
+            # act_quant, one tensor-core GEMM into the logits, row lists, selection, argmax copy
+            lm = 5
         if self.chain is not None:
             return 1 + (1 if self.chain_lm else lm)
         # each linear: act_quant + one tensor-core GEMM, or a GEMV per group of 8 tokens

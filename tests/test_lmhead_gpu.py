@@ -31,6 +31,9 @@ def oracle_logits(x, wq, in_step, acc_step):
     (49152, 576, 1, 40), (24576, 576, 1, 1), (18992, 1536, 1, 40), (151936, 1536, 1, 40),
     (151936, 1536, 3, 64), (12800, 2048, 8, 40), (32768, 3840, 2, 17), (1000, 64, 5, 64),
     (40, 32, 1, 40), (200, 100, 11, 7),
+    # 16+ tokens: tensor-core GEMM into the logits, per-CTA row lists, per-token selection
+    (151936, 1536, 16, 40), (49152, 576, 64, 64), (12800, 2048, 20, 1), (4097, 128, 33, 33),
+    (1000, 64, 17, 64), (200, 100, 40, 7),
 ])
 def test_shard_topk_matches_oracle(ctx, V, K, T, k):
     wq, w_step = lm_params(V, K, seed=V + K)
@@ -50,7 +53,7 @@ def test_shard_topk_matches_oracle(ctx, V, K, T, k):
         assert idx[t, 0].item() == O.argmax(lg[t]) + off
 
 
-@pytest.mark.parametrize("T,k", [(1, 64), (3, 40)])
+@pytest.mark.parametrize("T,k", [(1, 64), (3, 40), (16, 64), (24, 32)])
 def test_top_keys_concentrated_in_one_cta(ctx, T, k):
     """The whole top-k inside one CTA's rows, with exact ties: one per-CTA list holds every
     winner, so the final selection walks that list far past its head (and breaks the ties by
@@ -76,10 +79,11 @@ def test_top_keys_concentrated_in_one_cta(ctx, T, k):
     assert np.array_equal(val.cpu().numpy(), wv)
 
 
-def test_saturated_int8_logits_tie_rule(ctx):
+@pytest.mark.parametrize("T", [2, 16])
+def test_saturated_int8_logits_tie_rule(ctx, T):
     """LFM3's INT8 LM head requantises logits to int8 (static out_step), so the largest logits
     saturate at +127 and tie; the lowest vocab id must win (FINDINGS.md:2476-2498 case)."""
-    V, K, T, k = 64000, 512, 2, 40
+    V, K, k = 64000, 512, 40
     rng = np.random.default_rng(0)
     wq = rng.integers(-127, 128, size=(V, K)).astype(np.int8)
     qm = np.full(V, 32767, np.int16)
@@ -141,3 +145,33 @@ def test_repeated_topk_calls_reset_scratch(ctx):
         v, i = shard.forward(x, 40)
         assert torch.equal(i, i0) and torch.equal(v, v0)
     ctx.check()
+
+
+@pytest.mark.parametrize("T,k", [(16, 40), (32, 64)])
+def test_tensor_topk_equals_gemv_topk(ctx, T, k):
+    """16+ tokens: the tensor-core top-k (one GEMM into the logits, then row lists) and the GEMV
+    top-k forced on the same linear select the same (value, id) pairs, in the same order."""
+    V, K = 60000, 1024
+    wq, w_step = lm_params(V, K, seed=T)
+    acc_step = (0.029 * w_step).astype(np.float32)
+    shard = rb.LmHeadShard(ctx, wq, acc_step, 0.029, row_offset=7)
+    x = torch.from_numpy(synth.activations(T, K, seed=3).numpy()).cuda()
+    v_tc, i_tc = shard.forward(x, k)
+    shard.linear.set_path(rb.PATH_GEMV)
+    v_gv, i_gv = shard.forward(x, k)
+    assert torch.equal(i_tc, i_gv) and torch.equal(v_tc, v_gv)
+    ctx.check()
+
+
+def test_tensor_topk_equal_logits(ctx):
+    """Every logit equal (zero weights): the order is by vocab id alone, so each CTA's threshold
+    keeps exactly its lowest ids and the selection returns ids row_offset .. row_offset + k - 1."""
+    V, K, T, k = 20000, 256, 16, 64
+    wq = np.zeros((V, K), np.int8)
+    acc_step = np.full(V, 1e-3, np.float32)
+    shard = rb.LmHeadShard(ctx, wq, acc_step, 0.03, row_offset=100)
+    x = torch.from_numpy(synth.activations(T, K, seed=4).numpy()).cuda()
+    v, i = shard.forward(x, k)
+    want = np.broadcast_to(np.arange(100, 100 + k, dtype=np.int32), (T, k))
+    assert np.array_equal(i.cpu().numpy(), want)
+    assert (v.cpu().numpy() == 0).all()
