@@ -191,6 +191,16 @@ typedef enum {
 } w8a8_path;
 #define W8A8_TC_MIN_TOKENS 16
 w8a8_status w8a8_linear_set_path(w8a8_linear *linear, int32_t path);
+/* Set-up call (no reference counterpart: the reference's NPU loadables own fixed buffers).
+ * Allocates, once, every piece of device scratch that forward calls of up to max_tokens tokens
+ * on the linear's current path would otherwise allocate on first use: the activation staging
+ * rows, the tensor-core copy of the weights (built on `stream`), the split-K planes and tile
+ * counters, and with max_k > 0 the logits and row lists of a 16+ token top-k forward with k <=
+ * max_k.  Afterwards forward, forward_q and forward_topk calls within those limits allocate and
+ * synchronise nothing, so a caller can capture them in a CUDA graph.  Call it outside any
+ * capture; set the path first. */
+w8a8_status w8a8_linear_reserve(w8a8_linear *linear, int32_t max_tokens, int32_t max_k,
+                                void *stream);
 /* The LM-head shard's input RMSNorm (fused_emb_norm_broadcast_t1, lfm3_v2.cpp:810-831): when
  * emb_norm_scaled_dev ([K] fp32 = norm weight / in_step, lfm3_v2.cpp:3906-3912) is non-NULL,
  * w8a8_linear_forward_topk with the STATIC act mode packs each row as

@@ -133,6 +133,7 @@ SIGNATURES = {
     "w8a8_linear_destroy": (None, [_P]),
     "w8a8_linear_device_bytes": (_SZ, [_P]),
     "w8a8_linear_set_path": (C.c_int, [_P, _I32]),
+    "w8a8_linear_reserve": (C.c_int, [_P, _I32, _I32, _P]),
     "w8a8_linear_set_input_norm": (C.c_int, [_P, _P, C.c_float]),
     "w8a8_linear_set_trace": (C.c_int, [_P, _P]),
     "w8a8_pack_input": (C.c_int, [_P, _P, _I64, _I32, _I32, _P, _I64, _P, _P]),

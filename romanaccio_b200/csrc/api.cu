@@ -664,6 +664,45 @@ w8a8_status w8a8_linear_set_path(w8a8_linear *l, int32_t path) {
   return W8A8_SUCCESS;
 }
 
+w8a8_status w8a8_linear_reserve(w8a8_linear *l, int32_t max_tokens, int32_t max_k, void *stream) {
+  if (!l) return fail(W8A8_ERR_INVALID_ARG, "linear is NULL");
+  if (max_tokens < 1) return fail(W8A8_ERR_INVALID_ARG, "max_tokens=%d must be >= 1", max_tokens);
+  if (max_k < 0 || max_k > W8A8_TOPK_MAX)
+    return fail(W8A8_ERR_INVALID_ARG, "max_k=%d outside [0, %d]", max_k, W8A8_TOPK_MAX);
+  DeviceGuard g(l->ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  w8a8_status s = ensure_tokens(l, max_tokens);
+  if (s != W8A8_SUCCESS) return s;
+  const bool forced = l->path == W8A8_PATH_TENSOR || l->path == W8A8_PATH_TENSOR_PAIR;
+  const bool any_tc = forced || (l->path == W8A8_PATH_AUTO && max_tokens >= W8A8_TC_MIN_TOKENS);
+  if (!any_tc) return W8A8_SUCCESS;
+  // the largest split-K planes and tile-counter arrays over every token count that takes the
+  // tensor-core path
+  size_t ws = 0, counters = 0;
+  for (int T = forced ? 1 : W8A8_TC_MIN_TOKENS; T <= max_tokens; ++T) {
+    TcPlan plan;
+    if (!plan_tc(T, l->N, l->k_pad, l->ctx->sm_count, &plan, l->path == W8A8_PATH_TENSOR_PAIR))
+      return fail(W8A8_ERR_NOT_SUPPORTED, "no tensor-core plan for T=%d N=%d K=%d", T, l->N, l->K);
+    if (plan.splits > 1) {
+      ws = std::max(ws, static_cast<size_t>(plan.splits) * T * l->N);
+      counters = std::max(counters, static_cast<size_t>(plan.tiles_n) * plan.tiles_t);
+    }
+  }
+  if (ws > 0 && (s = ensure_tc_scratch(l, ws, counters)) != W8A8_SUCCESS) return s;
+  bool built = false;
+  if ((s = ensure_tc_weights(l, st, &built)) != W8A8_SUCCESS) return s;
+  if (max_k > 0 && max_tokens >= W8A8_TC_MIN_TOKENS && l->path != W8A8_PATH_GEMV) {
+    if ((s = grow_scratch(&l->logit_ws, &l->logit_ws_elems,
+                          static_cast<size_t>(max_tokens) * l->N)) != W8A8_SUCCESS)
+      return s;
+    if ((s = grow_scratch(&l->row_lists, &l->row_lists_keys,
+                          static_cast<size_t>(max_tokens) * topk_rows_grid(l->N) * (max_k + 1))) !=
+        W8A8_SUCCESS)
+      return s;
+  }
+  return W8A8_SUCCESS;
+}
+
 w8a8_status w8a8_pack_input(w8a8_linear *l, const float *x, int64_t ldx, int32_t T, int32_t act_mode,
                             int8_t *q, int64_t ldq, float *ratio, void *stream) {
   if (!l || !x || !q) return fail(W8A8_ERR_INVALID_ARG, "linear, x or q is NULL");

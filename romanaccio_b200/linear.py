@@ -153,6 +153,13 @@ class W8A8Linear:
         """Contraction engine: PATH_AUTO, PATH_GEMV (weight streaming) or PATH_TENSOR (tcgen05)."""
         check(self._lib.w8a8_linear_set_path(self.handle, int(path)), "w8a8_linear_set_path")
 
+    def reserve(self, max_tokens: int, max_k: int = 0, stream=None) -> None:
+        """Allocates up front the scratch that forwards of up to max_tokens tokens (top-k
+        forwards with k <= max_k) on the current path would grow on first use, so that those
+        forwards allocate nothing and can be captured in a CUDA graph."""
+        check(self._lib.w8a8_linear_reserve(self.handle, int(max_tokens), int(max_k),
+                                            _stream(stream)), "w8a8_linear_reserve")
+
     def close(self) -> None:
         if getattr(self, "handle", None):
             self._lib.w8a8_linear_destroy(self.handle)
