@@ -5,7 +5,8 @@
 // staging of activations (lfm3_v2.cpp:1186-1225) and WorkerPool::submit_task
 // (worker_pool.hpp:232-254).  Everything runs in-process on CUDA streams; no call allocates
 // device memory after create, except a forward with T above the preallocated token budget and
-// the first tensor-core forward of a linear (its tile-ordered weight copy and split-K scratch).
+// the first tensor-core forward of a linear (its tile-ordered weight copy and split-K scratch),
+// both of which w8a8_linear_reserve allocates ahead at set-up.
 #include "../../include/w8a8.h"
 #include "kernels.h"
 #include "linear_internal.h"
