@@ -236,6 +236,10 @@ struct MoeActLaunch {
   bool pdl;
 };
 
+// Most (expert, 8-pair block) work items a grouped GEMV can have: sum over experts of
+// ceil(count / 8) <= pairs / 8 + experts.
+inline int moe_max_group_items(int n_experts, int pairs) { return n_experts + (pairs + 7) / 8; }
+
 struct MoeGemvLaunch {
   MoePairs pairs;
   const int8_t *q;          // [pairs, ldq]
@@ -250,8 +254,9 @@ struct MoeGemvLaunch {
   void *y;                  // [pairs, N]
   bool pdl;
   // Expert-grouped form (launch_moe_gemv_grouped): the pairs of expert e are
-  // grp_pairs[grp_off[e] .. grp_off[e + 1]) (from launch_moe_group).
-  const int32_t *grp_off;   // [n_experts + 1]
+  // grp_pairs[grp_off[e] .. grp_off[e + 1]) (from launch_moe_group), followed in the same array
+  // by the count of work items and the items (e << 16 | z: pairs 8z .. 8z + 7 of expert e).
+  const int32_t *grp_off;   // [n_experts + 2 + moe_max_group_items(n_experts, pairs)]
   const int32_t *grp_pairs; // [pairs]
   int n_experts;
 };

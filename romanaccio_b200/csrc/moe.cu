@@ -253,7 +253,10 @@ __global__ void __launch_bounds__(kMoeThreads) moe_gemv_kernel(const MoeGemvLaun
 }
 
 // One CTA: the pairs of every expert this rank owns, as lists (counting sort; the order inside an
-// expert's list does not matter: every pair's outputs are computed independently).
+// expert's list does not matter: every pair's outputs are computed independently), then the
+// grouped GEMV's work items after the offsets: off[n_experts + 1] = their count, then one item
+// e << 16 | z per block of up to 8 pairs of expert e, so that no CTA of that GEMV is launched
+// for an empty block.
 __global__ void __launch_bounds__(kMoeThreads) moe_group_kernel(const MoePairs P, int n_experts,
                                                                int32_t *off, int32_t *list) {
   extern __shared__ int s_cnt[];  // [n_experts] counts, then the scatter cursors
@@ -276,6 +279,13 @@ __global__ void __launch_bounds__(kMoeThreads) moe_group_kernel(const MoePairs P
       acc += c;
     }
     off[n_experts] = acc;
+    int32_t *items = off + n_experts + 2;
+    int ni = 0;
+    for (int e = 0; e < n_experts; ++e) {
+      const int c = (e + 1 < n_experts ? s_cnt[e + 1] : acc) - s_cnt[e];
+      for (int z = 0; z * 8 < c; ++z) items[ni++] = (e << 16) | z;
+    }
+    off[n_experts + 1] = ni;
   }
   __syncthreads();
   for (int p = threadIdx.x; p < n; p += kMoeThreads) {
@@ -304,8 +314,8 @@ __device__ __forceinline__ int warp_sum32(int (&v)[32], int lane) {
   return v[0];
 }
 
-// grid (ceil(N / 64), n_experts, ceil(T / 8)).  CTA (rb, e, z) takes pairs 8z .. 8z + 7 of expert
-// e's list, stages their int8 rows in shared memory and streams its 64 weight rows once for all
+// grid (ceil(N / 64), most work items).  CTA (rb, i) takes work item i (if there is one): pairs
+// 8z .. 8z + 7 of expert e's list, stages their int8 rows in shared memory and streams its 64 weight rows once for all
 // of them: each warp owns 8 rows, 4 at a time, each lane its 16-byte chunks of the 4 rows, dp4a
 // against the 8 staged rows; the 32 sums of a pass are reduced together and lane l writes
 // (row l / 8, pair l % 8) through the epilogue of moe_gemv_kernel.
@@ -313,9 +323,11 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_gemv_grouped_kernel(const 
   extern __shared__ __align__(16) int4 s_x[];  // [kGroupTokens][chunks]
   pdl_launch_dependents();
   pdl_wait();
-  const int e = blockIdx.y;
-  if (!expert_owned(L.pairs, e)) return;
-  const int beg = L.grp_off[e] + blockIdx.z * kGroupTokens, end = L.grp_off[e + 1];
+  const int32_t *items = L.grp_off + L.n_experts + 1;  // [0] count, then the items
+  if (static_cast<int>(blockIdx.y) >= items[0]) return;
+  const int item = items[1 + blockIdx.y];
+  const int e = item >> 16;
+  const int beg = L.grp_off[e] + (item & 0xffff) * kGroupTokens, end = L.grp_off[e + 1];
   if (beg >= end) return;
   const int ng = min(kGroupTokens, end - beg);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -521,9 +533,10 @@ cudaError_t launch_moe_group(const MoePairs &P, int n_experts, int32_t *off, int
 cudaError_t launch_moe_gemv_grouped(const MoeGemvLaunch &L, cudaStream_t st) {
   if (L.k_pad <= 0 || L.k_pad % 16 != 0 || L.n_experts <= 0) return cudaErrorInvalidValue;
   if (L.k_pad > kGroupMaxK) return launch_moe_gemv(L, st);  // rows too wide to stage: per pair
-  // an expert holds at most one pair per token, so ceil(T / 8) CTA layers cover every list
-  const dim3 grid((L.N + kRowsPerCta - 1) / kRowsPerCta, L.n_experts,
-                  (L.pairs.T + kGroupTokens - 1) / kGroupTokens);
+  // one CTA row per work item that launch_moe_group can have written
+  const dim3 grid((L.N + kRowsPerCta - 1) / kRowsPerCta,
+                  moe_max_group_items(L.n_experts, L.pairs.T * L.pairs.slots));
+  if (grid.y > 65535u) return cudaErrorInvalidValue;
   const size_t smem = static_cast<size_t>(kGroupTokens) * L.k_pad;
   return launch_ex(moe_gemv_grouped_kernel, grid, dim3(kMoeThreads), smem, st, L.pdl, L);
 }

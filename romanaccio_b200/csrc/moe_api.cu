@@ -45,7 +45,8 @@ struct w8a8_moe {
   float *h = nullptr;              // [P, I]
   int8_t *q2 = nullptr;            // [P, ldi]
   void *yq = nullptr;              // [P, H]
-  int32_t *grp_off = nullptr;      // [E+S+1] pairs of each expert (grouped GEMV, T > 1)
+  int32_t *grp_off = nullptr;      // [E+S+1] pairs of each expert, then the grouped GEMV's work
+                                   // items (T > 1)
   int32_t *grp_pairs = nullptr;    // [P]
   float *route_logits = nullptr;   // [max_T, E]
   int *route_cnt = nullptr;        // [max_T] arrival counters of the routing kernel
@@ -218,7 +219,8 @@ w8a8_status w8a8_moe_create(w8a8_ctx *ctx, const w8a8_moe_desc *d, w8a8_moe **ou
   if (e == cudaSuccess) e = upload(&m->q2, static_cast<const int8_t *>(nullptr), P * m->ldi);
   if (e == cudaSuccess) e = cudaMalloc(&m->yq, P * H * (m->dn_i16 ? 2 : 1));
   if (e == cudaSuccess)
-    e = upload(&m->grp_off, static_cast<const int32_t *>(nullptr), X + 1);
+    e = upload(&m->grp_off, static_cast<const int32_t *>(nullptr),
+               X + 2 + static_cast<size_t>(moe_max_group_items(static_cast<int>(X), static_cast<int>(P))));
   if (e == cudaSuccess) e = upload(&m->grp_pairs, static_cast<const int32_t *>(nullptr), P);
   if (e == cudaSuccess)
     e = upload(&m->route_logits, static_cast<const float *>(nullptr),
