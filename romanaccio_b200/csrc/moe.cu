@@ -354,11 +354,20 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_gemv_grouped_kernel(const 
     int acc[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) acc[i] = 0;
+    // the next chunk's weight loads are issued before this chunk's products (two chunks of
+    // loads in flight per lane)
+    int4 wv[kGroupRows];
+#pragma unroll
+    for (int u = 0; u < kGroupRows; ++u)
+      wv[u] = lane < chunks ? __ldg(reinterpret_cast<const int4 *>(wr[u] + lane * 16))
+                            : make_int4(0, 0, 0, 0);
     for (int ci = lane; ci < chunks; ci += 32) {
-      int4 wv[kGroupRows];
+      const int cn = ci + 32;
+      int4 wn[kGroupRows];
 #pragma unroll
       for (int u = 0; u < kGroupRows; ++u)
-        wv[u] = __ldg(reinterpret_cast<const int4 *>(wr[u] + ci * 16));
+        wn[u] = cn < chunks ? __ldg(reinterpret_cast<const int4 *>(wr[u] + cn * 16))
+                            : make_int4(0, 0, 0, 0);
 #pragma unroll
       for (int t = 0; t < kGroupTokens; ++t) {
         const int4 xv = s_x[t * chunks + ci];
@@ -372,6 +381,8 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_gemv_grouped_kernel(const 
           acc[u * kGroupTokens + t] = s;
         }
       }
+#pragma unroll
+      for (int u = 0; u < kGroupRows; ++u) wv[u] = wn[u];
     }
     const int sum = warp_sum32(acc, lane);
     const int n = n0 + r + my_u;
