@@ -252,6 +252,8 @@ __global__ void __launch_bounds__(kMoeThreads) moe_gemv_kernel(const MoeGemvLaun
   }
 }
 
+constexpr int kGroupTokens = 8;   // pairs of one expert per CTA of the grouped GEMV
+
 // One CTA: the pairs of every expert this rank owns, as lists (counting sort; the order inside an
 // expert's list does not matter: every pair's outputs are computed independently), then the
 // grouped GEMV's work items after the offsets: off[n_experts + 1] = their count, then one item
@@ -259,7 +261,9 @@ __global__ void __launch_bounds__(kMoeThreads) moe_gemv_kernel(const MoeGemvLaun
 // for an empty block.
 __global__ void __launch_bounds__(kMoeThreads) moe_group_kernel(const MoePairs P, int n_experts,
                                                                int32_t *off, int32_t *list) {
-  extern __shared__ int s_cnt[];  // [n_experts] counts, then the scatter cursors
+  // [n_experts] counts (then scatter cursors), [n_experts] list starts, [n_experts] first items
+  extern __shared__ int s_cnt[];
+  int *s_start = s_cnt + n_experts, *s_item = s_start + n_experts;
   pdl_launch_dependents();
   pdl_wait();
   for (int e = threadIdx.x; e < n_experts; e += kMoeThreads) s_cnt[e] = 0;
@@ -270,22 +274,24 @@ __global__ void __launch_bounds__(kMoeThreads) moe_group_kernel(const MoePairs P
     if (expert_owned(P, e)) atomicAdd(&s_cnt[e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0;
+  if (threadIdx.x == 0) {  // prefix sums in shared memory
+    int acc = 0, ni = 0;
     for (int e = 0; e < n_experts; ++e) {
-      off[e] = acc;
-      const int c = s_cnt[e];
-      s_cnt[e] = acc;
-      acc += c;
+      s_start[e] = acc;
+      s_item[e] = ni;
+      acc += s_cnt[e];
+      ni += (s_cnt[e] + kGroupTokens - 1) / kGroupTokens;
     }
     off[n_experts] = acc;
-    int32_t *items = off + n_experts + 2;
-    int ni = 0;
-    for (int e = 0; e < n_experts; ++e) {
-      const int c = (e + 1 < n_experts ? s_cnt[e + 1] : acc) - s_cnt[e];
-      for (int z = 0; z * 8 < c; ++z) items[ni++] = (e << 16) | z;
-    }
     off[n_experts + 1] = ni;
+  }
+  __syncthreads();
+  int32_t *items = off + n_experts + 2;
+  for (int e = threadIdx.x; e < n_experts; e += kMoeThreads) {
+    off[e] = s_start[e];
+    const int nz = (s_cnt[e] + kGroupTokens - 1) / kGroupTokens;
+    for (int z = 0; z < nz; ++z) items[s_item[e] + z] = (e << 16) | z;
+    s_cnt[e] = s_start[e];  // this expert's scatter cursor (each expert has one thread here)
   }
   __syncthreads();
   for (int p = threadIdx.x; p < n; p += kMoeThreads) {
@@ -294,7 +300,6 @@ __global__ void __launch_bounds__(kMoeThreads) moe_group_kernel(const MoePairs P
   }
 }
 
-constexpr int kGroupTokens = 8;   // pairs of one expert per CTA
 constexpr int kGroupRows = 4;     // weight rows a warp streams together
 constexpr int kGroupMaxK = 6144;  // widest staged row (kGroupTokens rows = 48 KB)
 
@@ -538,7 +543,8 @@ cudaError_t launch_moe_gemv(const MoeGemvLaunch &L, cudaStream_t st) {
 cudaError_t launch_moe_group(const MoePairs &P, int n_experts, int32_t *off, int32_t *pairs,
                              bool pdl, cudaStream_t st) {
   return launch_ex(moe_group_kernel, dim3(1), dim3(kMoeThreads),
-                   static_cast<size_t>(n_experts) * sizeof(int), st, pdl, P, n_experts, off, pairs);
+                   3 * static_cast<size_t>(n_experts) * sizeof(int), st, pdl, P, n_experts, off,
+                   pairs);
 }
 
 cudaError_t launch_moe_gemv_grouped(const MoeGemvLaunch &L, cudaStream_t st) {
