@@ -234,6 +234,11 @@ struct MoeActLaunch {
   int64_t ldq;
   float *ratio;              // [pairs] (dyntok)
   bool pdl;
+  // static mode with per-pair rows: when set, row p of the input is computed here as
+  // silu(gu[p, c]) * gu[p, K + c] from the gate|up outputs gu [pairs, 2K] and also stored into
+  // src_out [pairs, K] (the SwiGLU step between the two expert projections, fused)
+  const float *swiglu_gu;
+  float *src_out;
 };
 
 // Most (expert, 8-pair block) work items a grouped GEMV can have: sum over experts of

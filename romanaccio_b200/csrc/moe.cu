@@ -12,7 +12,8 @@
 //   moe_gemv_kernel     the W8A8 contraction of each pair's token against its expert's weights
 //                       with the SDP requant epilogue (QuantM, RNE shift, saturate), then either
 //                       the unpack (F32) or the int16/int8 requantised value (QUANT).
-//   moe_swiglu_kernel   silu(gate) * up between the two expert projections (float).
+//   moe_swiglu_kernel   silu(gate) * up between the two expert projections (float); the layer
+//                       runs it fused into the down projection's moe_act_quant_kernel.
 //   moe_combine_kernel  mlp_out[t, c] += float(y_q[pair, c]) * (w_pair * out_step_chan[e, c]),
 //                       accumulated over the token's pairs in slot order
 //                       (src/LFM2.5-8B-A1B/lfm2_moe.cpp:2300-2318).
@@ -183,8 +184,20 @@ __global__ void __launch_bounds__(kMoeThreads) moe_act_quant_kernel(const MoeAct
     if (threadIdx.x == 0) L.ratio[p] = amax / L.safe_thresh[e];
     inv = 127.0f / amax;
   }
-  for (int c = threadIdx.x; c < L.K; c += kMoeThreads)
-    q[c] = static_cast<int8_t>(round_clamp(x[c] * (s[c] * inv), 127.0f));
+  if (!DYN && L.swiglu_gu) {
+    // SwiGLU fused: the same float steps as moe_swiglu_kernel, h kept for the stage views
+    const float *g = L.swiglu_gu + static_cast<int64_t>(p) * 2 * L.K;
+    float *h = L.src_out + static_cast<int64_t>(p) * L.K;
+    for (int c = threadIdx.x; c < L.K; c += kMoeThreads) {
+      const float gv = g[c];
+      const float xv = (gv / (1.0f + expf(-gv))) * g[L.K + c];
+      h[c] = xv;
+      q[c] = static_cast<int8_t>(round_clamp(xv * (s[c] * inv), 127.0f));
+    }
+  } else {
+    for (int c = threadIdx.x; c < L.K; c += kMoeThreads)
+      q[c] = static_cast<int8_t>(round_clamp(x[c] * (s[c] * inv), 127.0f));
+  }
   for (int c = L.K + threadIdx.x; c < L.ldq; c += kMoeThreads) q[c] = 0;
 }
 

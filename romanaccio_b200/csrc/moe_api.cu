@@ -256,7 +256,6 @@ w8a8_status w8a8_moe_forward(w8a8_moe *m, const float *hidden, int64_t ldh, int3
   w8a8_status s = route(m, hidden, ldh, T, m->idx, m->w, st);
   if (s != W8A8_SUCCESS) return s;
   const MoePairs P = pairs_of(m, T);
-  const int n_pairs = T * m->slots;
   // T > 1: the pairs are grouped by expert so that each expert's weight rows stream once for all
   // of its pairs; T = 1 keeps one CTA column per pair (every expert has at most one pair).
   const bool grouped = T > 1;
@@ -305,11 +304,11 @@ w8a8_status w8a8_moe_forward(w8a8_moe *m, const float *hidden, int64_t ldh, int3
                   "moe gate_up GEMV");
   if (s != W8A8_SUCCESS) return s;
 
-  s = cuda_status(launch_moe_swiglu(m->gu, m->I, n_pairs, m->h, true, st, P), "moe swiglu");
-  if (s != W8A8_SUCCESS) return s;
-
+  // SwiGLU (silu(gate) * up) fused into the down projection's static pack
   MoeActLaunch B = {};
   B.pairs = P;
+  B.swiglu_gu = m->gu;
+  B.src_out = m->h;
   B.src = m->h;
   B.ld = m->I;
   B.per_pair_rows = 1;
