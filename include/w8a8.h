@@ -194,8 +194,8 @@ w8a8_status w8a8_linear_set_path(w8a8_linear *linear, int32_t path);
 /* Set-up call (no reference counterpart: the reference's NPU loadables own fixed buffers).
  * Allocates, once, every piece of device scratch that forward calls of up to max_tokens tokens
  * on the linear's current path would otherwise allocate on first use: the activation staging
- * rows, the tensor-core copy of the weights (built on `stream`), the split-K planes and tile
- * counters, and with max_k > 0 the logits and row lists of a 16+ token top-k forward with k <=
+ * rows, the tensor-core copy of the weights (built on `stream`), the split-K accumulation plane
+ * and tile counters, and with max_k > 0 the logits and row lists of a 16+ token top-k forward with k <=
  * max_k.  Afterwards forward, forward_q and forward_topk calls within those limits allocate and
  * synchronise nothing, so a caller can capture them in a CUDA graph.  Call it outside any
  * capture; set the path first. */

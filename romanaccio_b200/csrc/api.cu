@@ -94,7 +94,7 @@ struct w8a8_linear {
   size_t logit_ws_elems = 0;
   uint64_t *row_lists = nullptr;
   size_t row_lists_keys = 0;
-  // tensor-core path: tile-ordered weights, split-K partial planes, per-tile arrival counters
+  // tensor-core path: tile-ordered weights, split-K accumulation plane, per-tile arrival counters
   int path = W8A8_PATH_AUTO;
   int8_t *w_tiles = nullptr;    // weights in tensor-core tile order (built on first use)
   unsigned long long *tc_trace = nullptr;  // optional per-CTA timeline of tensor-core launches
@@ -165,8 +165,8 @@ w8a8_status ensure_tc_weights(w8a8_linear *l, cudaStream_t st, bool *built) {
   return W8A8_SUCCESS;
 }
 
-// Grows the split-K partial planes / per-tile arrival counters of the tensor-core path (the
-// counters start at zero and the kernel leaves them zero again).
+// Grows the split-K accumulation plane / per-tile arrival counters of the tensor-core path (both
+// start at zero and the kernel leaves them zero again).
 w8a8_status ensure_tc_scratch(w8a8_linear *l, size_t ws_elems, size_t count_n) {
   if (ws_elems > l->tc_ws_elems) {
     cudaFree(l->tc_ws);
@@ -260,7 +260,7 @@ w8a8_status run_gemv(w8a8_linear *l, const int8_t *xq, int64_t ldx, int T, int a
     if (!plan_tc(T, l->N, l->k_pad, l->ctx->sm_count, &plan, l->path == W8A8_PATH_TENSOR_PAIR))
       return fail(W8A8_ERR_NOT_SUPPORTED, "no tensor-core plan for T=%d N=%d K=%d", T, l->N, l->K);
     if (plan.splits > 1) {
-      w8a8_status s = ensure_tc_scratch(l, static_cast<size_t>(plan.splits) * T * l->N,
+      w8a8_status s = ensure_tc_scratch(l, static_cast<size_t>(T) * l->N,
                                         static_cast<size_t>(plan.tiles_n) * plan.tiles_t);
       if (s != W8A8_SUCCESS) return s;
     }
@@ -677,15 +677,15 @@ w8a8_status w8a8_linear_reserve(w8a8_linear *l, int32_t max_tokens, int32_t max_
   const bool forced = l->path == W8A8_PATH_TENSOR || l->path == W8A8_PATH_TENSOR_PAIR;
   const bool any_tc = forced || (l->path == W8A8_PATH_AUTO && max_tokens >= W8A8_TC_MIN_TOKENS);
   if (!any_tc) return W8A8_SUCCESS;
-  // the largest split-K planes and tile-counter arrays over every token count that takes the
-  // tensor-core path
+  // the largest split-K accumulation plane and tile-counter arrays over every token count that
+  // takes the tensor-core path
   size_t ws = 0, counters = 0;
   for (int T = forced ? 1 : W8A8_TC_MIN_TOKENS; T <= max_tokens; ++T) {
     TcPlan plan;
     if (!plan_tc(T, l->N, l->k_pad, l->ctx->sm_count, &plan, l->path == W8A8_PATH_TENSOR_PAIR))
       return fail(W8A8_ERR_NOT_SUPPORTED, "no tensor-core plan for T=%d N=%d K=%d", T, l->N, l->K);
     if (plan.splits > 1) {
-      ws = std::max(ws, static_cast<size_t>(plan.splits) * T * l->N);
+      ws = std::max(ws, static_cast<size_t>(T) * l->N);
       counters = std::max(counters, static_cast<size_t>(plan.tiles_n) * plan.tiles_t);
     }
   }

@@ -17,9 +17,9 @@
 // Work split: units of (channel block, token block, K split), walked persistently by the CTAs
 // (unit = blockIdx.x + i * gridDim.x).  The accumulator is double-buffered in TMEM, so the
 // epilogue of one unit overlaps the main loop of the next.  When the channel x token tiles do not
-// fill the SMs, K is split: each split stores its int32 partial tile into its own plane of a
-// workspace, and the last split of a tile to arrive (an arrival counter per tile) adds the other
-// planes to its TMEM accumulator and runs the epilogue.  Integer sums are exact in any order.
+// fill the SMs, K is split: each split adds its int32 partial tile into one accumulation plane
+// (L2 reductions), and the last split of a tile to arrive (an arrival counter per tile) reads the
+// totals, resets them to zero and runs the epilogue.  Integer sums are exact in any order.
 //
 // Warp roles (576 threads): warp 0 issues the TMA copies, warp 1 owns TMEM and issues the MMAs
 // (one thread), warps 2..17 run the epilogue; warp w reads TMEM lanes 32*(w%4)..+31 (the lane
@@ -55,7 +55,7 @@ struct TcArgs {
   uint32_t stage_bytes, buf_stride, tmem_cols, idesc;
   Epilogue ep;
   const int8_t *w_tiles;  // [tiles_n][k_iters] contiguous 16 KB swizzled weight tiles
-  int32_t *ws;            // split-K partial planes [splits, T, N]
+  int32_t *ws;            // split-K accumulation plane [T, N] (all zero between launches)
   unsigned *tile_count;   // split-K arrival counters [tiles] (all zero between launches)
   int *err;
   int w_stream;           // weights read once (one token block): evict-first L2 policy
@@ -320,10 +320,11 @@ __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[CW]) {
   tmem_ld16(taddr, v);
 }
 
-// Split-K: this split's partial tile into its plane of the workspace.
+// Split-K: this split's partial tile added into the workspace's accumulation plane (reductions
+// in L2, no result awaited; int32 sums wrap, so their order does not change the total).
 template <int CW>
-__device__ __forceinline__ void store_partials(int32_t *plane_n, int N, uint32_t trow, int c_first,
-                                               int t_base, int t_lim, bool n_ok) {
+__device__ __forceinline__ void add_partials(int32_t *plane_n, int N, uint32_t trow, int c_first,
+                                             int t_base, int t_lim, bool n_ok) {
   for (int c = c_first; c < t_lim; c += kColGroups * CW) {
     uint32_t v[CW];
     tmem_ld<CW>(trow + c, v);
@@ -331,17 +332,17 @@ __device__ __forceinline__ void store_partials(int32_t *plane_n, int N, uint32_t
     int32_t *p = plane_n + static_cast<size_t>(t_base + c) * N;
 #pragma unroll
     for (int i = 0; i < CW; ++i)
-      if (c + i < t_lim) __stcg(p + static_cast<size_t>(i) * N, static_cast<int32_t>(v[i]));
+      if (c + i < t_lim) atomicAdd(p + static_cast<size_t>(i) * N, static_cast<int32_t>(v[i]));
   }
 }
 
-// Final values of this thread's channel for its columns: accumulator (+ the other splits'
-// partial planes) through the output mode.
+// Final values of this thread's channel for its columns through the output mode: the
+// accumulator, or with split-K the accumulation plane's totals (every split's partial tile, this
+// one's included), which are read once and reset to zero for the next launch.
 template <int MODE, int CW>
 __device__ __forceinline__ void finish_columns(const Epilogue &ep, const ChanParams &cp,
                                                uint32_t trow, int c_first, int t_base, int t_lim,
-                                               int n, bool n_ok, const int32_t *ws, int N,
-                                               int splits, int split, size_t plane) {
+                                               int n, bool n_ok, int32_t *ws, int N, int splits) {
   const int esize = out_size<MODE>(ep);
   char *col = static_cast<char *>(ep.y) + static_cast<size_t>(n) * esize;
   const size_t ldb = static_cast<size_t>(ep.ldy) * esize;
@@ -350,18 +351,13 @@ __device__ __forceinline__ void finish_columns(const Epilogue &ep, const ChanPar
     tmem_ld<CW>(trow + c, v);
     if (!n_ok) continue;
     if (splits > 1) {
-      // One plane at a time, all CW loads of it in flight together.
-      const int32_t *p = ws + static_cast<size_t>(t_base + c) * N + n;
-      for (int s = 0; s < splits; ++s) {
-        if (s == split) continue;
-        const int32_t *ps = p + s * plane;
-        int32_t part[CW];
+      int32_t *p = ws + static_cast<size_t>(t_base + c) * N + n;
 #pragma unroll
-        for (int i = 0; i < CW; ++i)
-          part[i] = (c + i < t_lim) ? __ldcg(ps + static_cast<size_t>(i) * N) : 0;
+      for (int i = 0; i < CW; ++i)
+        if (c + i < t_lim) v[i] = static_cast<uint32_t>(__ldcg(p + static_cast<size_t>(i) * N));
 #pragma unroll
-        for (int i = 0; i < CW; ++i) v[i] += static_cast<uint32_t>(part[i]);
-      }
+      for (int i = 0; i < CW; ++i)
+        if (c + i < t_lim) __stcg(p + static_cast<size_t>(i) * N, 0);
     }
 #pragma unroll
     for (int i = 0; i < CW; ++i) {
@@ -409,7 +405,6 @@ __device__ __forceinline__ void epilogue_role(const TcArgs &a, uint32_t tmem, ui
   const Epilogue &ep = a.ep;
   const int q = warp & 3;
   const int group = (warp - 2) >> 2;  // column group of this warp
-  const size_t plane = static_cast<size_t>(a.T) * a.N;
   const uint32_t rank = PAIR ? cluster_rank() : 0u;
   bool ok = true;
   int j = 0;
@@ -430,13 +425,10 @@ __device__ __forceinline__ void epilogue_role(const TcArgs &a, uint32_t tmem, ui
     const uint32_t trow = tmem + buf * a.buf_stride + (static_cast<uint32_t>(q * 32) << 16);
     bool finish = true;
     if (a.splits > 1) {
-      // Split-K: every split stores its partial tile (plain coalesced stores into its own plane
-      // of the workspace); the last split of the tile to arrive adds the other planes to its
-      // own accumulator, still in TMEM, and runs the epilogue.
-      if (ok) {
-        int32_t *mine = a.ws + un.split * plane + n;
-        store_partials<kCW>(mine, a.N, trow, group * kCW, t_base, t_lim, n_ok);
-      }
+      // Split-K: every split adds its partial tile into the accumulation plane (coalesced L2
+      // reductions); the last split of the tile to arrive reads the totals in one pass, resets
+      // them to zero and runs the epilogue.
+      if (ok) add_partials<kCW>(a.ws + n, a.N, trow, group * kCW, t_base, t_lim, n_ok);
       __threadfence();
       epi_bar_sync();
       if (threadIdx.x == 64) {
@@ -451,7 +443,7 @@ __device__ __forceinline__ void epilogue_role(const TcArgs &a, uint32_t tmem, ui
     if (ok && finish) {
       const ChanParams cp = chan_params<MODE>(ep, n, n_ok);
       finish_columns<MODE, kCW>(ep, cp, trow, group * kCW, t_base, t_lim, n, n_ok, a.ws, a.N,
-                                a.splits, un.split, plane);
+                                a.splits);
     }
     // TMEM buffer free for the next unit's MMAs.
     tc_fence_before();

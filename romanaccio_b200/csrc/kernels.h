@@ -178,7 +178,7 @@ struct TcLaunch {
   int k_extent_x;           // readable columns of x; columns beyond read as zero
   int T, N;
   Epilogue ep;
-  int32_t *ws;              // split-K partial planes [splits, T, N] (plan.splits > 1)
+  int32_t *ws;              // split-K accumulation plane [T, N], zero between launches (splits > 1)
   unsigned *tile_count;     // split-K counters [tiles_n * tiles_t], zero between launches
   int *err;
   unsigned long long *trace;  // optional per-CTA timeline [grid, 8]
