@@ -45,6 +45,8 @@ def test_null_arguments_are_rejected():
     assert lib.w8a8_linear_forward(None, None, 0, 1, 0, 0, None, 0, None, None) == _lib.ERR_INVALID_ARG
     assert lib.w8a8_topk_merge(None, None, None, 1, 1, 1, 1, 1, 1, None, None, None, None) == \
         _lib.ERR_INVALID_ARG
+    assert lib.w8a8_linear_reserve(None, 64, 40, None) == _lib.ERR_INVALID_ARG
+    assert "NULL" in lib.w8a8_last_error().decode()
     lib.w8a8_linear_destroy(None)  # NULL-safe like es_*_free
     lib.w8a8_ctx_destroy(None)
 
