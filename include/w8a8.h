@@ -104,7 +104,9 @@ int         w8a8_ctx_sm_count(const w8a8_ctx *ctx);
 int         w8a8_ctx_device(const w8a8_ctx *ctx);
 /* Synchronises the context's device and reports a device-side failure recorded by a kernel
  * (a bounded wait that ran out: W8A8_ERR_TIMEOUT / W8A8_ERR_PEER_TIMEOUT), then clears it.
- * Plays the role of the worker liveness checks of worker_pool.cpp:180-193. */
+ * Plays the role of the worker liveness checks of worker_pool.cpp:180-193.  After a timeout,
+ * destroy and recreate the linears whose forwards were in flight: a tensor-core forward cut short
+ * may leave its split-K accumulation plane non-zero. */
 w8a8_status w8a8_ctx_check(w8a8_ctx *ctx);
 
 /* ---------------------------------------------------------------------------------------
